@@ -1,0 +1,302 @@
+"""``CudaBackend``: the host-side mirror of ``laya_core::Backend`` over ``libs1c.so``.
+
+Same methods and meanings as the reference trait (``runtime/crates/laya-core/src/backend.rs:109-133``):
+``name``, ``forward(batch) -> BackendOutput``, ``active_kernels``, ``padded_len``, ``warmup``,
+``encoder_hidden``. Errors surface as ``BackendError`` (``Error::Backend``), weight problems as
+``WeightsError`` and config problems as ``ConfigError``, like the reference's ``Error`` enum.
+
+There is no CPU fallback: constructing a backend needs the CUDA library and an sm_100 GPU, and
+fails loudly otherwise.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Tuple
+
+import numpy as np
+
+from .batch import Batch, Varlen
+from .config import ConfigError, ModelConfig
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libs1c.so")
+HEADER = os.path.join(os.path.dirname(HERE), "include", "s1c.h")
+
+S1C_OK, S1C_ERR_ARG, S1C_ERR_CUDA, S1C_ERR_WEIGHTS, S1C_ERR_CONFIG, S1C_ERR_DEVICE_TIMEOUT, S1C_ERR_UNSUPPORTED = \
+    0, -1, -2, -3, -4, -5, -6
+DT_F32, DT_F16, DT_BF16 = 0, 1, 2
+
+
+class BackendError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"backend error {code}: {msg}")
+        self.code = code
+
+
+class WeightsError(BackendError):
+    pass
+
+
+class DeviceTimeout(BackendError):
+    pass
+
+
+class ModelDesc(C.Structure):
+    _fields_ = [("vocab_size", C.c_int32), ("hidden_size", C.c_int32), ("num_layers", C.c_int32),
+                ("num_heads", C.c_int32), ("intermediate_size", C.c_int32), ("norm_eps", C.c_float),
+                ("local_attention", C.c_int32), ("global_rope_theta", C.c_float),
+                ("local_rope_theta", C.c_float), ("layer_is_local", C.POINTER(C.c_uint8)),
+                ("head_layers", C.c_int32), ("max_position", C.c_int32), ("max_tokens", C.c_int32)]
+
+
+class Tensor(C.Structure):
+    _fields_ = [("name", C.c_char_p), ("dtype", C.c_int32), ("ndim", C.c_int32),
+                ("shape", C.c_int64 * 4), ("data", C.c_void_p)]
+
+
+class CBatch(C.Structure):
+    _fields_ = [("n", C.c_size_t), ("len", C.c_size_t), ("kmax", C.c_size_t),
+                ("input_ids", C.c_void_p), ("attention_mask", C.c_void_p), ("seq_lens", C.c_void_p),
+                ("marker_pos", C.c_void_p), ("marker_count", C.c_void_p), ("qtype", C.c_void_p)]
+
+
+class CVarlen(C.Structure):
+    _fields_ = [("n", C.c_int32), ("kmax", C.c_int32), ("ids", C.c_void_p), ("cu_seqlens", C.c_void_p),
+                ("marker_pos", C.c_void_p), ("marker_count", C.c_void_p), ("qtype", C.c_void_p)]
+
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    """Load ``libs1c.so`` (built in-tree by ``sys1rust_b200.build``); raises when it is missing."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError(f"{LIB_PATH} is missing: build it with `python -m sys1rust_b200.build`")
+    L = C.CDLL(LIB_PATH)
+    P, I32, I64, F32, SZ = C.c_void_p, C.c_int32, C.c_int64, C.c_float, C.c_size_t
+    sig = {
+        "s1c_create": (I32, [C.POINTER(ModelDesc), C.POINTER(Tensor), I32, I32, C.POINTER(P)]),
+        "s1c_destroy": (None, [P]),
+        "s1c_last_error": (C.c_char_p, [P]),
+        "s1c_create_error": (C.c_char_p, []),
+        "s1c_name": (C.c_char_p, [P]),
+        "s1c_active_kernels": (C.c_char_p, [P]),
+        "s1c_padded_len": (SZ, [P, SZ, SZ]),
+        "s1c_warmup": (I32, [P]),
+        "s1c_forward_padded": (I32, [P, C.POINTER(CBatch), P, P]),
+        "s1c_forward_varlen": (I32, [P, C.POINTER(CVarlen), P, P, P]),
+        "s1c_forward_device": (I32, [P, C.POINTER(CVarlen), P, P, P, P]),
+        "s1c_encoder_hidden": (I32, [P, C.POINTER(CBatch), P]),
+        "s1c_gemm": (I32, [I32, P, P, P, I32, I32, I32, P, I32, I32, P, F32, I32, I32, P]),
+        "s1c_attention": (I32, [P, P, P, P, I32, I32, I32, I32, I32, P, I32, I32, F32, P]),
+        "s1c_last_launch_count": (I64, [P]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L
+
+
+def header_functions() -> List[str]:
+    """Every function ``include/s1c.h`` declares."""
+    with open(HEADER) as f:
+        text = re.sub(r"/\*.*?\*/", "", f.read(), flags=re.S)
+    return sorted(set(re.findall(r"\b(s1c_[a-z_]+)\s*\(", text)))
+
+
+def _ptr(a: np.ndarray) -> int:
+    return a.ctypes.data
+
+
+def _raise(code: int, msg: str) -> None:
+    if code == S1C_OK:
+        return
+    if code == S1C_ERR_WEIGHTS:
+        raise WeightsError(code, msg)
+    if code == S1C_ERR_CONFIG:
+        raise ConfigError(msg)
+    if code == S1C_ERR_DEVICE_TIMEOUT:
+        raise DeviceTimeout(code, msg)
+    raise BackendError(code, msg)
+
+
+@dataclass
+class BackendOutput:
+    """``BackendOutput`` (``backend.rs:100-108``): masked logits ``[n * kmax]``, pooled ``[n * d]``."""
+    logits: np.ndarray
+    pooled: np.ndarray
+    hidden: Optional[np.ndarray] = None
+
+
+class CudaBackend:
+    """One model on one GPU. Calls on one instance must be serialised."""
+
+    def __init__(self, cfg: ModelConfig, tensors: Dict[str, Tuple[str, Tuple[int, ...], np.ndarray]],
+                 device: int = 0, max_tokens: int = 16384):
+        L = lib()
+        e = cfg.encoder
+        self.cfg = cfg
+        self.hidden = e.hidden_size
+        self._local = np.array([1 if x else 0 for x in e.layer_is_local], dtype=np.uint8)
+        desc = ModelDesc(e.vocab_size, e.hidden_size, e.num_hidden_layers, e.num_attention_heads,
+                         e.intermediate_size, e.norm_eps, e.local_attention, e.global_rope_theta,
+                         e.local_rope_theta, self._local.ctypes.data_as(C.POINTER(C.c_uint8)),
+                         cfg.head_layers, e.max_position_embeddings, max_tokens)
+        keep = []
+        arr = (Tensor * len(tensors))()
+        for i, (name, (dt, shape, data)) in enumerate(tensors.items()):
+            data = np.ascontiguousarray(data)
+            keep.append(data)
+            nb = name.encode()
+            keep.append(nb)
+            code = {"F32": DT_F32, "F16": DT_F16, "BF16": DT_BF16}[dt]
+            sh = (C.c_int64 * 4)(*(list(shape) + [0] * (4 - len(shape))))
+            arr[i] = Tensor(nb, code, len(shape), sh, data.ctypes.data)
+        h = C.c_void_p()
+        rc = L.s1c_create(C.byref(desc), arr, len(tensors), device, C.byref(h))
+        if rc != S1C_OK:
+            _raise(rc, L.s1c_create_error().decode())
+        self._h = h
+        self.device = device
+
+    @staticmethod
+    def from_synthetic(cfg: ModelConfig, weights, device: int = 0, max_tokens: int = 16384) -> "CudaBackend":
+        t = {name: ("BF16", bits.shape, bits) for name, bits in weights.items()}
+        return CudaBackend(cfg, t, device=device, max_tokens=max_tokens)
+
+    @staticmethod
+    def from_dir(model_dir: str, device: int = 0, max_tokens: int = 16384) -> "CudaBackend":
+        """Load ``model.safetensors`` + configs from a checkpoint directory (``Agent::load``)."""
+        from .weights import load_safetensors_bits
+        cfg = ModelConfig.load(model_dir)
+        t = load_safetensors_bits(os.path.join(model_dir, "model.safetensors"))
+        cfg.head_ffn = t["head.layers.0.linear1.weight"][1][0]
+        cfg.scorer_hidden = t["scorer.1.weight"][1][0]
+        return CudaBackend(cfg, t, device=device, max_tokens=max_tokens)
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib().s1c_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _err(self) -> str:
+        return lib().s1c_last_error(self._h).decode()
+
+    def _check(self, rc: int) -> None:
+        if rc != S1C_OK:
+            _raise(rc, self._err())
+
+    # -- the Backend trait ------------------------------------------------------------------
+    def name(self) -> str:
+        return lib().s1c_name(self._h).decode()
+
+    def active_kernels(self) -> List[str]:
+        s = lib().s1c_active_kernels(self._h).decode()
+        return re.findall(r"[a-z0-9_]+(?:\([^)]*\))?", s)
+
+    def padded_len(self, length: int, rows: int) -> int:
+        return int(lib().s1c_padded_len(self._h, length, rows))
+
+    def warmup(self) -> None:
+        self._check(lib().s1c_warmup(self._h))
+
+    def forward(self, batch: Batch) -> BackendOutput:
+        cb, keep = self._cbatch(batch)
+        logits = np.empty(batch.n * batch.kmax, dtype=np.float32)
+        pooled = np.empty(batch.n * self.hidden, dtype=np.float32)
+        self._check(lib().s1c_forward_padded(self._h, C.byref(cb), _ptr(logits), _ptr(pooled)))
+        return BackendOutput(logits, pooled)
+
+    def encoder_hidden(self, batch: Batch) -> np.ndarray:
+        cb, keep = self._cbatch(batch)
+        out = np.empty(batch.n * batch.len * self.hidden, dtype=np.float32)
+        self._check(lib().s1c_encoder_hidden(self._h, C.byref(cb), _ptr(out)))
+        return out
+
+    # -- unpadded entry points --------------------------------------------------------------
+    def forward_varlen(self, v: Varlen, hidden: bool = False) -> BackendOutput:
+        cv, keep = self._cvarlen(v)
+        logits = np.empty(v.n * v.kmax, dtype=np.float32)
+        pooled = np.empty(v.n * self.hidden, dtype=np.float32)
+        hid = np.empty(v.total * self.hidden, dtype=np.float32) if hidden else None
+        self._check(lib().s1c_forward_varlen(self._h, C.byref(cv), _ptr(logits), _ptr(pooled),
+                                             _ptr(hid) if hidden else None))
+        return BackendOutput(logits, pooled, hid)
+
+    def forward_device(self, v: Varlen, d_ids: int, d_logits: int, d_pooled: int, d_hidden: int = 0) -> None:
+        """Device-resident inputs/outputs (raw device pointers, e.g. ``tensor.data_ptr()``)."""
+        cv, keep = self._cvarlen(v)
+        self._check(lib().s1c_forward_device(self._h, C.byref(cv), d_ids, d_logits, d_pooled, d_hidden or None))
+
+    def last_launch_count(self) -> int:
+        return int(lib().s1c_last_launch_count(self._h))
+
+    # -- marshalling ------------------------------------------------------------------------
+    @staticmethod
+    def _cbatch(b: Batch):
+        arrs = [np.ascontiguousarray(b.input_ids, dtype=np.uint32),
+                np.ascontiguousarray(b.attention_mask, dtype=np.uint32),
+                np.ascontiguousarray(b.seq_lens, dtype=np.uint64),
+                np.ascontiguousarray(b.marker_pos, dtype=np.uint32),
+                np.ascontiguousarray(b.marker_count, dtype=np.uint64),
+                np.ascontiguousarray(b.qtype, dtype=np.uint32)]
+        cb = CBatch(b.n, b.len, b.kmax, *[_ptr(a) for a in arrs])
+        return cb, arrs
+
+    @staticmethod
+    def _cvarlen(v: Varlen):
+        arrs = [np.ascontiguousarray(v.ids, dtype=np.uint32), np.ascontiguousarray(v.cu_seqlens, dtype=np.int32),
+                np.ascontiguousarray(v.marker_pos, dtype=np.uint32),
+                np.ascontiguousarray(v.marker_count, dtype=np.int32), np.ascontiguousarray(v.qtype, dtype=np.uint32)]
+        cv = CVarlen(v.n, v.kmax, *[_ptr(a) for a in arrs])
+        return cv, arrs
+
+
+# -- isolated kernels (tests, GEMM sweep) ---------------------------------------------------
+EPI_STORE, EPI_ROPE, EPI_GEGLU, EPI_RESID = 0, 1, 2, 3
+
+
+def gemm(epi: int, a_ptr: int, b_ptr: int, out_ptr: int, M: int, N: int, K: int, bias_ptr: int = 0, act: int = 0,
+         out_f32: int = 0, pos_ptr: int = 0, rope_theta: float = 10000.0, rope_cols: int = 0, out_cols: int = 0,
+         stream: int = 0) -> None:
+    L = lib()
+    rc = L.s1c_gemm(epi, a_ptr, b_ptr, out_ptr, M, N, K, bias_ptr or None, act, out_f32, pos_ptr or None,
+                    rope_theta, rope_cols, out_cols, stream or None)
+    if rc != S1C_OK:
+        _raise(rc, L.s1c_create_error().decode())
+
+
+def attention(q_ptr: int, k_ptr: int, v_ptr: int, o_ptr: int, q_stride: int, k_stride: int, v_stride: int,
+              o_stride: int, heads: int, cu_seqlens: np.ndarray, window: int, scale: float, stream: int = 0) -> None:
+    L = lib()
+    cu = np.ascontiguousarray(cu_seqlens, dtype=np.int32)
+    rc = L.s1c_attention(q_ptr, k_ptr, v_ptr, o_ptr, q_stride, k_stride, v_stride, o_stride, heads, _ptr(cu),
+                         len(cu) - 1, window, scale, stream or None)
+    if rc != S1C_OK:
+        _raise(rc, L.s1c_create_error().decode())
+
+
+def interleave_wi(wi: np.ndarray, I: int) -> np.ndarray:
+    """The row order the GeGLU epilogue expects (what ``s1c_create`` does to ``mlp.Wi``): per
+    256-row tile, 128 input rows then the matching 128 gate rows, zero rows past ``I``."""
+    tiles = (I + 127) // 128
+    out = np.zeros((tiles * 256, wi.shape[1]), dtype=wi.dtype)
+    for t in range(tiles):
+        c0, c1 = 128 * t, min(128 * t + 128, I)
+        out[256 * t: 256 * t + (c1 - c0)] = wi[c0:c1]
+        out[256 * t + 128: 256 * t + 128 + (c1 - c0)] = wi[I + c0: I + c1]
+    return out

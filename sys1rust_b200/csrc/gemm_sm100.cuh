@@ -1,0 +1,330 @@
+// Persistent bf16 GEMM for sm_100a on the 5th-generation tensor cores:
+//   out = epilogue( A[M, K] * B[N, K]^T )   (A and B K-major, as the weights are stored [out, in])
+//
+// Encoder GEMMs of the reference forward (runtime/crates/laya-mlx/src/lib.rs:1363-1390 `mm` and
+// `lin_add`, :1600-1675 the layer loop) and the head's biased linears (:1726-1760) all run here.
+//
+// Structure (one CTA per SM, 192 threads):
+//   warp 0      TMA producer: 128x64 A tile + BNx64 B tile per stage, 128-byte swizzle,
+//               4-stage ring of shared-memory buffers guarded by full/empty mbarriers.
+//   warp 1      allocates 2*BN TMEM columns and issues tcgen05.mma (M=128, N=BN, K=16 per
+//               instruction, fp32 accumulation in TMEM); tcgen05.commit releases a stage when
+//               the MMAs reading it are done and hands a finished accumulator to the epilogue.
+//   warps 2..5  epilogue: tcgen05.ld of the accumulator (one row per thread), the fused
+//               epilogue math, stores to global memory. Two accumulators alternate, so the
+//               epilogue of tile i overlaps the MMAs of tile i+1.
+// Tiles are walked n-fastest (tile = m_block * n_blocks + n_block) so CTAs running together
+// share their A rows and stream the whole weight from L2.
+//
+// Epilogues:
+//   EPI_STORE  bias (optional), then identity / ReLU / erf-GELU, stored bf16 (or fp32).
+//   EPI_ROPE   the encoder's qkv: rotate-half RoPE of the q and k heads at each row's position
+//              (split_rope.metal:46-76), v copied; stored bf16 [M, 3d] (q | k | v, head-major).
+//   EPI_GEGLU  the encoder's Wi with its rows interleaved per 128 (input 128 | gate 128 per
+//              256-wide tile): out = gelu_erf(input) * gate (lib.rs:367-368, :494-510), bf16 [M, I].
+//   EPI_RESID  fp32 residual stream update in place: out += acc (+ bias)  (lib.rs:1375-1390).
+#pragma once
+#include <cuda.h>
+#include "common.cuh"
+
+namespace s1c {
+
+enum Epi : int { EPI_STORE = 0, EPI_ROPE = 1, EPI_GEGLU = 2, EPI_RESID = 3 };
+enum Act : int { ACT_NONE = 0, ACT_RELU = 1, ACT_GELU = 2 };
+
+struct GemmArgs {
+  int M, N, K;
+  void* out;
+  int ldo;                // row pitch of `out`, elements
+  const float* bias;      // [N] or null (EPI_STORE, EPI_RESID)
+  int act;                // EPI_STORE activation
+  int out_f32;            // EPI_STORE: fp32 output
+  const int* pos;         // EPI_ROPE: position of each row inside its sequence
+  const float2* rope_cs;  // EPI_ROPE: [max_pos][32] (cos, sin) of the layer's theta
+  int rope_cols;          // EPI_ROPE: columns [0, rope_cols) hold q and k heads
+  int out_cols;           // EPI_GEGLU: output width I
+  int* status;
+};
+
+constexpr int GEMM_BM = 128;
+constexpr int GEMM_BK = 64;
+constexpr int GEMM_STAGES = 4;
+constexpr int GEMM_THREADS = 192;
+
+__host__ __device__ constexpr size_t gemm_smem_bytes(int BN) {
+  return (size_t)GEMM_STAGES * (GEMM_BM * GEMM_BK * 2 + BN * GEMM_BK * 2) + 1024 /*align*/ + 256 /*barriers*/;
+}
+
+S1C_DEV float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
+
+S1C_DEV void store_bf16x32(__nv_bfloat16* dst, const float (&v)[32]) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint4 u;
+    u.x = pack_bf16x2(v[8 * i + 0], v[8 * i + 1]);
+    u.y = pack_bf16x2(v[8 * i + 2], v[8 * i + 3]);
+    u.z = pack_bf16x2(v[8 * i + 4], v[8 * i + 5]);
+    u.w = pack_bf16x2(v[8 * i + 6], v[8 * i + 7]);
+    d[i] = u;
+  }
+}
+
+// Warp-collective bounded wait: every lane polls, the warp leaves together.
+S1C_DEV bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int* status, int code, volatile int* abort) {
+  const uint32_t a = smem_u32(bar);
+  const int lane = threadIdx.x & 31;
+  uint64_t t0 = 0;
+  for (uint32_t it = 0;; ++it) {
+    const bool done = mbar_try_wait(a, parity);
+    if (__all_sync(0xffffffffu, done)) return true;
+    if ((it & 63u) == 63u) {
+      int give_up = 0;
+      if (lane == 0) {
+        const uint64_t now = globaltimer();
+        if (t0 == 0) t0 = now;
+        if ((abort && *abort) || now - t0 > S1C_WAIT_BUDGET_NS) give_up = 1;
+      }
+      give_up = __shfl_sync(0xffffffffu, give_up, 0);
+      if (give_up) {
+        if (lane == 0) {
+          if (!(abort && *abort)) report(status, code);
+          if (abort) *abort = 1;
+        }
+        return false;
+      }
+    }
+  }
+}
+
+template <int BN, int EPI>
+__device__ __forceinline__ void gemm_epilogue_tile(const GemmArgs& args, uint32_t t, int row, int m_ok, int n0,
+                                                   int n_block) {
+  if constexpr (EPI == EPI_STORE || EPI == EPI_RESID) {
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      float v[32];
+      tmem_ld32(t + c * 32, v);
+      const int col = n0 + c * 32;
+      if (!m_ok || col >= args.N) continue;
+      if (args.bias) {
+        const float4* b4 = reinterpret_cast<const float4*>(args.bias + col);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 b = __ldg(b4 + i);
+          v[4 * i] += b.x; v[4 * i + 1] += b.y; v[4 * i + 2] += b.z; v[4 * i + 3] += b.w;
+        }
+      }
+      if constexpr (EPI == EPI_RESID) {
+        float4* p = reinterpret_cast<float4*>(static_cast<float*>(args.out) + (size_t)row * args.ldo + col);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          float4 r = p[i];
+          r.x += v[4 * i]; r.y += v[4 * i + 1]; r.z += v[4 * i + 2]; r.w += v[4 * i + 3];
+          p[i] = r;
+        }
+      } else {
+        if (args.act == ACT_RELU) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.0f);
+        } else if (args.act == ACT_GELU) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
+        }
+        if (args.out_f32) {
+          float4* p = reinterpret_cast<float4*>(static_cast<float*>(args.out) + (size_t)row * args.ldo + col);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) p[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        } else {
+          store_bf16x32(static_cast<__nv_bfloat16*>(args.out) + (size_t)row * args.ldo + col, v);
+        }
+      }
+    }
+  } else if constexpr (EPI == EPI_ROPE) {
+    const int p = m_ok ? __ldg(args.pos + row) : 0;
+    const float2* cs = args.rope_cs + (size_t)p * 32;
+#pragma unroll 1
+    for (int hh = 0; hh < BN / 64; ++hh) {
+      float x1[32], x2[32];
+      tmem_ld32(t + hh * 64, x1);
+      tmem_ld32(t + hh * 64 + 32, x2);
+      const int col = n0 + hh * 64;
+      if (!m_ok || col >= args.N) continue;
+      if (col < args.rope_cols) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float2 c = __ldg(cs + j);
+          const float a = x1[j], b = x2[j];
+          x1[j] = a * c.x - b * c.y;
+          x2[j] = a * c.y + b * c.x;
+        }
+      }
+      __nv_bfloat16* o = static_cast<__nv_bfloat16*>(args.out) + (size_t)row * args.ldo + col;
+      store_bf16x32(o, x1);
+      store_bf16x32(o + 32, x2);
+    }
+  } else {  // EPI_GEGLU, BN == 256: columns [0,128) input, [128,256) gate
+    static_assert(EPI != EPI_GEGLU || BN == 256, "GeGLU tiles are 128 input + 128 gate columns");
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      float a[32], g[32];
+      tmem_ld32(t + c * 32, a);
+      tmem_ld32(t + 128 + c * 32, g);
+      const int ocol = n_block * 128 + c * 32;
+      if (!m_ok || ocol >= args.out_cols) continue;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) a[j] = gelu_erf(a[j]) * g[j];
+      store_bf16x32(static_cast<__nv_bfloat16*>(args.out) + (size_t)row * args.ldo + ocol, a);
+    }
+  }
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    gemm_bf16_sm100(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const GemmArgs args) {
+  constexpr int BM = GEMM_BM, BK = GEMM_BK, STAGES = GEMM_STAGES;
+  constexpr uint32_t A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2, STAGE_BYTES = A_BYTES + B_BYTES;
+  constexpr uint32_t TMEM_COLS = 2 * BN;
+  static_assert(TMEM_COLS == 32 || TMEM_COLS == 64 || TMEM_COLS == 128 || TMEM_COLS == 256 || TMEM_COLS == 512,
+                "TMEM allocations are powers of two from 32 to 512 columns");
+  static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "tcgen05 M=128 needs N % 16 == 0, 16..256");
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_u = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_u + 1023u) & ~1023u) - raw_u);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_m = (args.M + BM - 1) / BM, num_n = (args.N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int nk = (args.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&tmA);
+      prefetch_tmap(&tmB);
+      int s = 0, issued = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+        const int m0 = (tile / num_n) * BM, n0 = (tile % num_n) * BN;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&empty[s], ph ^ 1u, args.status, DEV_TIMEOUT_PRODUCER, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+          tma_load_2d(sA + s * A_BYTES, &tmA, &full[s], kb * BK, m0);
+          tma_load_2d(sB + s * B_BYTES, &tmB, &full[s], kb * BK, n0);
+          ++issued;
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      // Every load this thread issued must land before the CTA exits; only the last STAGES
+      // can still be in flight.
+      int back = issued < STAGES ? issued : STAGES;
+      int ss = s;
+      uint32_t pp = ph;
+      for (int i = 0; i < back; ++i) {
+        if (--ss < 0) {
+          ss = STAGES - 1;
+          pp ^= 1u;
+        }
+        mbar_wait(&full[ss], pp, args.status, DEV_TIMEOUT_DRAIN, nullptr);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
+      int s = 0, acc = 0;
+      uint32_t ph = 0, aph = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], aph ^ 1u, args.status, DEV_TIMEOUT_MMA_TEMPTY, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&full[s], ph, args.status, DEV_TIMEOUT_MMA_FULL, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + s * A_BYTES), b0 = smem_u32(sB + s * B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            umma_bf16(d, sdesc_kmajor_sw128(a0 + k * 32), sdesc_kmajor_sw128(b0 + k * 32), idesc,
+                      (kb | k) != 0 ? 1u : 0u);
+          umma_commit(&empty[s]);
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+        acc ^= 1;
+        if (acc == 0) aph ^= 1u;
+      }
+      // All MMAs this thread issued complete before TMEM is released.
+      umma_commit(drain);
+      mbar_wait(drain, 0, args.status, DEV_TIMEOUT_DRAIN, nullptr);
+    }
+  } else {
+    const int quad = warp & 3;  // TMEM lanes this warp may read: [32*quad, 32*quad + 32)
+    int acc = 0;
+    uint32_t aph = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      if (!mbar_wait_warp(&tfull[acc], aph, args.status, DEV_TIMEOUT_EPILOGUE, abort_flag)) break;
+      tc_fence_after();
+      const int m0 = (tile / num_n) * BM, n_block = tile % num_n;
+      const int row = m0 + quad * 32 + lane;
+      const uint32_t t = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
+      gemm_epilogue_tile<BN, EPI>(args, t, row, row < args.M, n_block * BN, n_block);
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+      acc ^= 1;
+      if (acc == 0) aph ^= 1u;
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+}  // namespace s1c

@@ -1,0 +1,1079 @@
+// libs1c: the C ABI of include/s1c.h and the host runtime that drives the sm_100a kernels.
+//
+// One s1c_backend per GPU: weights resident in HBM (bf16 matrices, fp32 vectors), activation
+// buffers sized for a packed-token capacity, TMA descriptors built once per buffer, one CUDA
+// stream. A forward packs the batch on the host (Packing::new, laya-mlx/src/lib.rs:906-930),
+// uploads a small metadata arena, and enqueues the whole model on the stream:
+//   embed_ln -> 28 x [LN, GEMM+RoPE, attention, GEMM+residual, LN, GEMM+GeGLU, GEMM+residual]
+//   -> final LN + type embedding + head norm1 -> head layers (last one pruned to the scorer's
+//   rows, lib.rs:1728-1748) -> scorer -> logits / pooled.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "../../include/s1c.h"
+#include "attention.cuh"
+#include "gemm_sm100.cuh"
+#include "rowwise.cuh"
+
+using namespace s1c;
+typedef __nv_bfloat16 bf16;
+
+namespace {
+
+// ---------------------------------------------------------------------------------------------
+// errors
+
+struct S1cError : std::runtime_error {
+  s1c_status code;
+  S1cError(s1c_status c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+
+#define CK(call)                                                                                  \
+  do {                                                                                            \
+    cudaError_t e_ = (call);                                                                      \
+    if (e_ != cudaSuccess)                                                                        \
+      throw S1cError(S1C_ERR_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_));          \
+  } while (0)
+
+thread_local std::string g_create_error;
+
+// ---------------------------------------------------------------------------------------------
+// host numerics
+
+uint16_t f32_to_bf16_bits(float f) {
+  uint32_t u;
+  std::memcpy(&u, &f, 4);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x40);  // quiet NaN
+  u += 0x7fffu + ((u >> 16) & 1u);
+  return (uint16_t)(u >> 16);
+}
+float f16_bits_to_f32(uint16_t h) {
+  const uint32_t s = (uint32_t)(h & 0x8000u) << 16;
+  uint32_t e = (h >> 10) & 0x1fu, m = h & 0x3ffu;
+  uint32_t u;
+  if (e == 0) {
+    if (m == 0) {
+      u = s;
+    } else {  // subnormal
+      int sh = 0;
+      while (!(m & 0x400u)) {
+        m <<= 1;
+        ++sh;
+      }
+      m &= 0x3ffu;
+      u = s | ((uint32_t)(127 - 15 - sh + 1) << 23) | (m << 13);
+    }
+  } else if (e == 31) {
+    u = s | 0x7f800000u | (m << 13);
+  } else {
+    u = s | ((e + 127 - 15) << 23) | (m << 13);
+  }
+  float f;
+  std::memcpy(&f, &u, 4);
+  return f;
+}
+float bf16_bits_to_f32(uint16_t b) {
+  uint32_t u = (uint32_t)b << 16;
+  float f;
+  std::memcpy(&f, &u, 4);
+  return f;
+}
+float elem_f32(const s1c_tensor& t, size_t i) {
+  switch (t.dtype) {
+    case S1C_DT_F32: return static_cast<const float*>(t.data)[i];
+    case S1C_DT_F16: return f16_bits_to_f32(static_cast<const uint16_t*>(t.data)[i]);
+    case S1C_DT_BF16: return bf16_bits_to_f32(static_cast<const uint16_t*>(t.data)[i]);
+  }
+  throw S1cError(S1C_ERR_WEIGHTS, std::string(t.name) + ": unsupported dtype");
+}
+
+// ---------------------------------------------------------------------------------------------
+// TMA descriptors
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  if (!fn) throw S1cError(S1C_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  return fn;
+}
+
+// K-major bf16 matrix [rows, k] with row pitch `ld` elements, tiles of box_rows x 64, 128-byte swizzle.
+CUtensorMap make_tmap(const void* ptr, uint64_t rows, uint64_t k, uint64_t ld, uint32_t box_rows) {
+  if ((reinterpret_cast<uintptr_t>(ptr) & 15) || (ld * 2) % 16)
+    throw S1cError(S1C_ERR_ARG, "TMA operand must be 16-byte aligned with a 16-byte multiple row pitch");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {k, rows};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = get_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box,
+                               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw S1cError(S1C_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+  return m;
+}
+
+// ---------------------------------------------------------------------------------------------
+// kernel launch helpers
+
+constexpr int GEMM_BN = 256;
+
+template <int EPI>
+void set_gemm_smem() {
+  CK(cudaFuncSetAttribute(gemm_bf16_sm100<GEMM_BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                          (int)gemm_smem_bytes(GEMM_BN)));
+}
+void set_all_gemm_smem() {
+  set_gemm_smem<EPI_STORE>();
+  set_gemm_smem<EPI_ROPE>();
+  set_gemm_smem<EPI_GEGLU>();
+  set_gemm_smem<EPI_RESID>();
+}
+
+template <int EPI>
+void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int num_sms, cudaStream_t st) {
+  if (a.M <= 0) return;
+  const int tiles = ((a.M + GEMM_BM - 1) / GEMM_BM) * ((a.N + GEMM_BN - 1) / GEMM_BN);
+  const int grid = std::min(tiles, num_sms);
+  gemm_bf16_sm100<GEMM_BN, EPI><<<grid, GEMM_THREADS, gemm_smem_bytes(GEMM_BN), st>>>(ta, tb, a);
+  CK(cudaGetLastError());
+}
+
+template <int D>
+void launch_ln(const float* in, const int* gather, int rows, const float* w, const float* b, float eps, bf16* out,
+               cudaStream_t st) {
+  if (rows <= 0) return;
+  layernorm_kernel<D><<<(rows + 7) / 8, 256, 0, st>>>(in, gather, rows, w, b, eps, out);
+  CK(cudaGetLastError());
+}
+
+__global__ void prep_tokens_kernel(const int* __restrict__ cu, int n, int T, int* __restrict__ pos,
+                                   int* __restrict__ row) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= T) return;
+  int lo = 0, hi = n - 1;  // largest r with cu[r] <= t
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (cu[mid] <= t) lo = mid; else hi = mid - 1;
+  }
+  pos[t] = t - cu[lo];
+  row[t] = lo;
+}
+
+// ---------------------------------------------------------------------------------------------
+// the backend
+
+struct DevBuf {
+  void* p = nullptr;
+  size_t bytes = 0;
+  ~DevBuf() { if (p) cudaFree(p); }
+  void ensure(size_t b) {
+    if (b <= bytes) return;
+    if (p) cudaFree(p);
+    p = nullptr;
+    bytes = 0;
+    CK(cudaMalloc(&p, b));
+    bytes = b;
+  }
+  template <class T> T* as() const { return static_cast<T*>(p); }
+};
+
+struct EncLayer {
+  bf16 *wqkv = nullptr, *wo = nullptr, *wi = nullptr, *wo2 = nullptr;
+  float *attn_norm = nullptr, *mlp_norm = nullptr;
+  bool local = false;
+  CUtensorMap tm_wqkv, tm_wo, tm_wi, tm_wo2;
+};
+
+struct HeadLayer {
+  bf16 *in_w = nullptr, *out_w = nullptr, *l1_w = nullptr, *l2_w = nullptr;
+  float *in_b = nullptr, *out_b = nullptr, *l1_b = nullptr, *l2_b = nullptr;
+  float *n1w = nullptr, *n1b = nullptr, *n2w = nullptr, *n2b = nullptr;
+  CUtensorMap tm_in, tm_in_q, tm_in_kv, tm_out, tm_l1, tm_l2;
+};
+
+}  // namespace
+
+struct s1c_backend {
+  int device = 0;
+  int num_sms = 148;
+  cudaStream_t stream = nullptr;
+  std::string name = "cuda(sm_100a,bf16)";
+  std::string kernels =
+      "gemm_tcgen05_tma(rope,geglu,residual,bias_act),attention_varlen_mma,embed_ln,layernorm,final_to_head,"
+      "scorer_logits";
+  std::string last_error;
+  int64_t launches = 0;
+
+  // config
+  int V = 0, d = 0, L = 0, H = 0, I = 0, Ipad = 0, F = 0, S = 0, n_head = 0, window = 64, max_pos = 0;
+  float eps = 1e-5f;
+  std::vector<uint8_t> local;
+
+  // weights
+  std::vector<void*> allocs;
+  bf16* tok_emb = nullptr;
+  float *emb_norm = nullptr, *final_norm = nullptr, *type_emb = nullptr;
+  std::vector<EncLayer> layers;
+  std::vector<HeadLayer> head;
+  float *sc_nw = nullptr, *sc_nb = nullptr, *sc_b1 = nullptr, *sc_w3 = nullptr, *sc_b3 = nullptr;
+  bf16* sc_w1 = nullptr;
+  CUtensorMap tm_sc1;
+  float2* rope_cs[2] = {nullptr, nullptr};  // 0 global theta, 1 local theta
+
+  // activations (capacity in rows, multiples of 128)
+  int cap_T = 0, cap_R = 0;
+  DevBuf h, x, qkv, att, act;          // [cap_T, ...]
+  DevBuf h2;                           // head residual stream [cap_T, d] fp32
+  DevBuf xs, qs, atts, hs, fs, xm, sh; // scorer rows [cap_R, ...]
+  CUtensorMap tm_x, tm_att, tm_act_i, tm_act_f, tm_xs, tm_atts, tm_fs, tm_xm;
+
+  // metadata
+  DevBuf meta;        // device arena
+  void* meta_host = nullptr;  // pinned staging
+  size_t meta_host_bytes = 0;
+  DevBuf tok;         // pos [cap_T] + token_row [cap_T] int32
+  int* d_status = nullptr;
+  int* h_status = nullptr;
+  DevBuf out_stage;   // device outputs for the host-buffer entry points
+  float* h_out = nullptr;  // pinned host outputs
+  size_t h_out_bytes = 0;
+
+  ~s1c_backend() {
+    if (stream) cudaStreamSynchronize(stream);
+    for (void* p : allocs) cudaFree(p);
+    if (d_status) cudaFree(d_status);
+    if (h_status) cudaFreeHost(h_status);
+    if (meta_host) cudaFreeHost(meta_host);
+    if (h_out) cudaFreeHost(h_out);
+    if (stream) cudaStreamDestroy(stream);
+  }
+
+  template <class T>
+  T* dalloc(size_t n) {
+    void* p = nullptr;
+    CK(cudaMalloc(&p, std::max<size_t>(n, 1) * sizeof(T)));
+    allocs.push_back(p);
+    return static_cast<T*>(p);
+  }
+};
+
+namespace {
+
+struct TensorTable {
+  std::map<std::string, const s1c_tensor*> by_name;
+  const s1c_tensor& get(const std::string& n, std::vector<int64_t> shape) const {
+    auto it = by_name.find(n);
+    if (it == by_name.end()) throw S1cError(S1C_ERR_WEIGHTS, n + ": missing tensor");
+    const s1c_tensor& t = *it->second;
+    bool ok = (int)shape.size() == t.ndim;
+    for (size_t i = 0; ok && i < shape.size(); ++i) ok = shape[i] == t.shape[i];
+    if (!ok) {
+      std::string want, got;
+      for (auto s : shape) want += std::to_string(s) + ",";
+      for (int i = 0; i < t.ndim; ++i) got += std::to_string(t.shape[i]) + ",";
+      throw S1cError(S1C_ERR_WEIGHTS, n + ": shape [" + got + "] where [" + want + "] is needed");
+    }
+    if (!t.data) throw S1cError(S1C_ERR_WEIGHTS, n + ": null data");
+    return t;
+  }
+  bool has(const std::string& n) const { return by_name.count(n) != 0; }
+};
+
+// Matrix [rows, cols] -> bf16 on the device, rows padded with zeros to a multiple of 256 so
+// that every TMA box lies inside the tensor.
+bf16* upload_matrix(s1c_backend& B, const s1c_tensor& t, int64_t rows, int64_t cols, const int64_t* row_map = nullptr,
+                    int64_t out_rows = -1) {
+  if (out_rows < 0) out_rows = rows;
+  const int64_t padded = (out_rows + 255) / 256 * 256;
+  std::vector<uint16_t> hbuf((size_t)padded * cols, 0);
+  for (int64_t r = 0; r < out_rows; ++r) {
+    const int64_t src = row_map ? row_map[r] : r;
+    if (src < 0) continue;
+    for (int64_t c = 0; c < cols; ++c) hbuf[(size_t)r * cols + c] = f32_to_bf16_bits(elem_f32(t, (size_t)src * cols + c));
+  }
+  bf16* d = B.dalloc<bf16>(hbuf.size());
+  CK(cudaMemcpy(d, hbuf.data(), hbuf.size() * 2, cudaMemcpyHostToDevice));
+  return d;
+}
+float* upload_vector(s1c_backend& B, const s1c_tensor& t, int64_t n, int64_t offset = 0) {
+  std::vector<float> hbuf((size_t)n);
+  for (int64_t i = 0; i < n; ++i) hbuf[i] = elem_f32(t, (size_t)(offset + i));
+  float* d = B.dalloc<float>(n);
+  CK(cudaMemcpy(d, hbuf.data(), n * 4, cudaMemcpyHostToDevice));
+  return d;
+}
+
+// RoPE (cos, sin) table: inverse frequency exp2(-(i / 32) * log2(theta)) and angle p * inv_freq
+// in fp32 as the reference kernel computes them (split_rope.metal:46-76); cos/sin of that fp32
+// angle evaluated in double and rounded once. Returns a fresh device allocation.
+float2* make_rope_table_raw(float theta, int max_pos) {
+  std::vector<float2> t((size_t)max_pos * 32);
+  const float lbase = std::log2(theta);
+  for (int i = 0; i < 32; ++i) {
+    const float inv = std::exp2(-((float)i / 32.0f) * lbase);
+    for (int p = 0; p < max_pos; ++p) {
+      const float ang = (float)p * inv;
+      t[(size_t)p * 32 + i] = make_float2((float)std::cos((double)ang), (float)std::sin((double)ang));
+    }
+  }
+  float2* d = nullptr;
+  CK(cudaMalloc(&d, t.size() * sizeof(float2)));
+  cudaError_t e = cudaMemcpy(d, t.data(), t.size() * sizeof(float2), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    cudaFree(d);
+    throw S1cError(S1C_ERR_CUDA, std::string("rope table upload: ") + cudaGetErrorString(e));
+  }
+  return d;
+}
+float2* make_rope_table(s1c_backend& B, float theta, int max_pos) {
+  float2* d = make_rope_table_raw(theta, max_pos);
+  B.allocs.push_back(d);
+  return d;
+}
+
+void ensure_capacity(s1c_backend& B, int T, int R) {
+  const int want_T = (std::max(T, 128) + 127) / 128 * 128;
+  const int want_R = (std::max(R, 128) + 127) / 128 * 128;
+  if (want_T > B.cap_T) {
+    const int cap = std::max(want_T, B.cap_T + B.cap_T / 2 / 128 * 128);
+    CK(cudaStreamSynchronize(B.stream));
+    const size_t wide = (size_t)std::max(B.Ipad / 2, B.F);
+    B.h.ensure((size_t)cap * B.d * 4);
+    B.h2.ensure((size_t)cap * B.d * 4);
+    B.x.ensure((size_t)cap * B.d * 2);
+    B.qkv.ensure((size_t)cap * 3 * B.d * 2);
+    B.att.ensure((size_t)cap * B.d * 2);
+    B.act.ensure((size_t)cap * wide * 2);
+    B.tok.ensure((size_t)cap * 2 * 4);
+    B.cap_T = cap;
+    B.tm_x = make_tmap(B.x.p, cap, B.d, B.d, GEMM_BM);
+    B.tm_att = make_tmap(B.att.p, cap, B.d, B.d, GEMM_BM);
+    B.tm_act_i = make_tmap(B.act.p, cap, B.I, B.I, GEMM_BM);
+    B.tm_act_f = make_tmap(B.act.p, cap, B.F, B.F, GEMM_BM);
+  }
+  if (want_R > B.cap_R) {
+    const int cap = std::max(want_R, B.cap_R + B.cap_R / 2 / 128 * 128);
+    CK(cudaStreamSynchronize(B.stream));
+    B.xs.ensure((size_t)cap * B.d * 2);
+    B.qs.ensure((size_t)cap * B.d * 2);
+    B.atts.ensure((size_t)cap * B.d * 2);
+    B.hs.ensure((size_t)cap * B.d * 4);
+    B.fs.ensure((size_t)cap * B.F * 2);
+    B.xm.ensure((size_t)cap * B.d * 2);
+    B.sh.ensure((size_t)cap * B.S * 4);
+    B.cap_R = cap;
+    B.tm_xs = make_tmap(B.xs.p, cap, B.d, B.d, GEMM_BM);
+    B.tm_atts = make_tmap(B.atts.p, cap, B.d, B.d, GEMM_BM);
+    B.tm_fs = make_tmap(B.fs.p, cap, B.F, B.F, GEMM_BM);
+    B.tm_xm = make_tmap(B.xm.p, cap, B.d, B.d, GEMM_BM);
+  }
+}
+
+void build(s1c_backend& B, const s1c_model_desc& D, const s1c_tensor* tensors, int n_tensors) {
+  B.V = D.vocab_size;
+  B.d = D.hidden_size;
+  B.L = D.num_layers;
+  B.H = D.num_heads;
+  B.I = D.intermediate_size;
+  B.eps = D.norm_eps;
+  B.window = D.local_attention / 2;
+  B.max_pos = D.max_position > 0 ? D.max_position : 8192;
+  B.n_head = D.head_layers;
+  if (B.d != 256 && B.d != 768 && B.d != 1024)
+    throw S1cError(S1C_ERR_CONFIG, "hidden_size " + std::to_string(B.d) + " is not one of 256, 768, 1024");
+  if (B.H <= 0 || B.d % B.H || B.d / B.H != 64)
+    throw S1cError(S1C_ERR_CONFIG, "the attention kernels need head_dim 64 (hidden_size / num_heads)");
+  if (B.I <= 0 || B.I % 32) throw S1cError(S1C_ERR_CONFIG, "intermediate_size must be a positive multiple of 32");
+  if (D.local_attention < 2) throw S1cError(S1C_ERR_CONFIG, "local_attention must be at least 2");
+  if (B.n_head < 1) throw S1cError(S1C_ERR_CONFIG, "head_layers must be at least 1");
+  if (B.L < 1 || !D.layer_is_local) throw S1cError(S1C_ERR_CONFIG, "num_layers / layer_is_local");
+  B.local.assign(D.layer_is_local, D.layer_is_local + B.L);
+  B.Ipad = (B.I + 127) / 128 * 256;
+
+  TensorTable tt;
+  for (int i = 0; i < n_tensors; ++i) {
+    if (!tensors[i].name) throw S1cError(S1C_ERR_ARG, "tensor with a null name");
+    tt.by_name[tensors[i].name] = &tensors[i];
+  }
+  const int64_t d = B.d, I = B.I;
+  B.tok_emb = upload_matrix(B, tt.get("encoder.embeddings.tok_embeddings.weight", {B.V, d}), B.V, d);
+  B.emb_norm = upload_vector(B, tt.get("encoder.embeddings.norm.weight", {d}), d);
+  B.final_norm = upload_vector(B, tt.get("encoder.final_norm.weight", {d}), d);
+  B.type_emb = upload_vector(B, tt.get("type_emb.weight", {3, d}), 3 * d);
+
+  // Wi rows interleaved per 128: tile t holds input rows [128t, 128t+128) then gate rows
+  // [I + 128t, ...), zero past the end, so one 256-wide output tile carries both GeGLU halves.
+  std::vector<int64_t> wi_map((size_t)B.Ipad);
+  for (int64_t r = 0; r < B.Ipad; ++r) {
+    const int64_t t = r / 256, j = r % 256;
+    const int64_t c = 128 * t + (j < 128 ? j : j - 128);  // output column this row feeds
+    wi_map[r] = c < I ? (j < 128 ? c : I + c) : -1;
+  }
+  B.layers.resize(B.L);
+  for (int i = 0; i < B.L; ++i) {
+    const std::string p = "encoder.layers." + std::to_string(i);
+    EncLayer& l = B.layers[i];
+    l.local = B.local[i] != 0;
+    if (i > 0) l.attn_norm = upload_vector(B, tt.get(p + ".attn_norm.weight", {d}), d);
+    l.mlp_norm = upload_vector(B, tt.get(p + ".mlp_norm.weight", {d}), d);
+    l.wqkv = upload_matrix(B, tt.get(p + ".attn.Wqkv.weight", {3 * d, d}), 3 * d, d);
+    l.wo = upload_matrix(B, tt.get(p + ".attn.Wo.weight", {d, d}), d, d);
+    l.wi = upload_matrix(B, tt.get(p + ".mlp.Wi.weight", {2 * I, d}), 2 * I, d, wi_map.data(), B.Ipad);
+    l.wo2 = upload_matrix(B, tt.get(p + ".mlp.Wo.weight", {d, I}), d, I);
+    l.tm_wqkv = make_tmap(l.wqkv, 3 * d, d, d, GEMM_BN);
+    l.tm_wo = make_tmap(l.wo, (d + 255) / 256 * 256, d, d, GEMM_BN);
+    l.tm_wi = make_tmap(l.wi, B.Ipad, d, d, GEMM_BN);
+    l.tm_wo2 = make_tmap(l.wo2, (d + 255) / 256 * 256, I, I, GEMM_BN);
+  }
+  const std::string h0 = "head.layers.0.linear1.weight";
+  if (!tt.has(h0)) throw S1cError(S1C_ERR_WEIGHTS, h0 + ": missing tensor");
+  B.F = (int)tt.by_name[h0]->shape[0];
+  if (B.F <= 0 || B.F % 256) throw S1cError(S1C_ERR_CONFIG, "head FFN width must be a multiple of 256");
+  B.head.resize(B.n_head);
+  for (int j = 0; j < B.n_head; ++j) {
+    const std::string p = "head.layers." + std::to_string(j);
+    HeadLayer& hl = B.head[j];
+    const s1c_tensor& inw = tt.get(p + ".self_attn.in_proj_weight", {3 * d, d});
+    hl.in_w = upload_matrix(B, inw, 3 * d, d);
+    hl.in_b = upload_vector(B, tt.get(p + ".self_attn.in_proj_bias", {3 * d}), 3 * d);
+    hl.out_w = upload_matrix(B, tt.get(p + ".self_attn.out_proj.weight", {d, d}), d, d);
+    hl.out_b = upload_vector(B, tt.get(p + ".self_attn.out_proj.bias", {d}), d);
+    hl.l1_w = upload_matrix(B, tt.get(p + ".linear1.weight", {B.F, d}), B.F, d);
+    hl.l1_b = upload_vector(B, tt.get(p + ".linear1.bias", {B.F}), B.F);
+    hl.l2_w = upload_matrix(B, tt.get(p + ".linear2.weight", {d, B.F}), d, B.F);
+    hl.l2_b = upload_vector(B, tt.get(p + ".linear2.bias", {d}), d);
+    hl.n1w = upload_vector(B, tt.get(p + ".norm1.weight", {d}), d);
+    hl.n1b = upload_vector(B, tt.get(p + ".norm1.bias", {d}), d);
+    hl.n2w = upload_vector(B, tt.get(p + ".norm2.weight", {d}), d);
+    hl.n2b = upload_vector(B, tt.get(p + ".norm2.bias", {d}), d);
+    hl.tm_in = make_tmap(hl.in_w, 3 * d, d, d, GEMM_BN);
+    hl.tm_in_q = make_tmap(hl.in_w, d, d, d, GEMM_BN);
+    hl.tm_in_kv = make_tmap(hl.in_w + d * d, 2 * d, d, d, GEMM_BN);
+    hl.tm_out = make_tmap(hl.out_w, (d + 255) / 256 * 256, d, d, GEMM_BN);
+    hl.tm_l1 = make_tmap(hl.l1_w, B.F, d, d, GEMM_BN);
+    hl.tm_l2 = make_tmap(hl.l2_w, (d + 255) / 256 * 256, B.F, B.F, GEMM_BN);
+  }
+  if (!tt.has("scorer.1.weight")) throw S1cError(S1C_ERR_WEIGHTS, "scorer.1.weight: missing tensor");
+  B.S = (int)tt.by_name["scorer.1.weight"]->shape[0];
+  if (B.S <= 0 || B.S % 32) throw S1cError(S1C_ERR_CONFIG, "scorer hidden width must be a multiple of 32");
+  B.sc_nw = upload_vector(B, tt.get("scorer.0.weight", {d}), d);
+  B.sc_nb = upload_vector(B, tt.get("scorer.0.bias", {d}), d);
+  B.sc_w1 = upload_matrix(B, tt.get("scorer.1.weight", {B.S, d}), B.S, d);
+  B.sc_b1 = upload_vector(B, tt.get("scorer.1.bias", {B.S}), B.S);
+  B.sc_w3 = upload_vector(B, tt.get("scorer.3.weight", {1, B.S}), B.S);
+  B.sc_b3 = upload_vector(B, tt.get("scorer.3.bias", {1}), 1);
+  B.tm_sc1 = make_tmap(B.sc_w1, (B.S + 255) / 256 * 256, d, d, GEMM_BN);
+
+  B.rope_cs[0] = make_rope_table(B, D.global_rope_theta, B.max_pos);
+  B.rope_cs[1] = make_rope_table(B, D.local_rope_theta, B.max_pos);
+  CK(cudaMalloc(&B.d_status, sizeof(int)));
+  CK(cudaMemset(B.d_status, 0, sizeof(int)));
+  CK(cudaMallocHost(&B.h_status, sizeof(int)));
+  ensure_capacity(B, std::max(D.max_tokens, 128), 128);
+}
+
+// ---------------------------------------------------------------------------------------------
+// forward
+
+struct HostMeta {
+  int n = 0, kmax = 0, T = 0, R = 0, M = 0;  // rows, kmax, tokens, scorer rows n(1+kmax), markers n*kmax
+  std::vector<int> cu, srows, mrows, prows, mcount;
+  std::vector<uint32_t> qtype;
+  std::vector<int4> items_full, items_rows;
+};
+
+void validate_varlen(const s1c_backend& B, const s1c_varlen& in) {
+  if (in.n < 0 || in.kmax < 0) throw S1cError(S1C_ERR_ARG, "n and kmax must be non-negative");
+  if (in.n == 0) return;
+  if (!in.cu_seqlens || !in.marker_count || !in.qtype || (in.kmax > 0 && !in.marker_pos))
+    throw S1cError(S1C_ERR_ARG, "null batch array");
+  if (in.cu_seqlens[0] != 0) throw S1cError(S1C_ERR_ARG, "cu_seqlens[0] must be 0");
+  for (int r = 0; r < in.n; ++r) {
+    const int len = in.cu_seqlens[r + 1] - in.cu_seqlens[r];
+    if (len < 1) throw S1cError(S1C_ERR_ARG, "row " + std::to_string(r) + ": every row needs at least one token");
+    if (len > B.max_pos)
+      throw S1cError(S1C_ERR_ARG, "row " + std::to_string(r) + ": length " + std::to_string(len) +
+                                      " exceeds max_position " + std::to_string(B.max_pos));
+    if (in.qtype[r] > 2) throw S1cError(S1C_ERR_ARG, "row " + std::to_string(r) + ": qtype must be 0, 1 or 2");
+    const int mc = in.marker_count[r];
+    if (mc < 0 || mc > in.kmax) throw S1cError(S1C_ERR_ARG, "row " + std::to_string(r) + ": marker_count outside 0..kmax");
+    for (int k = 0; k < in.kmax; ++k)
+      if ((int64_t)in.marker_pos[(size_t)r * in.kmax + k] >= len)
+        throw S1cError(S1C_ERR_ARG, "row " + std::to_string(r) + ": marker position past the row");
+  }
+}
+
+HostMeta make_meta(const s1c_varlen& in) {
+  HostMeta m;
+  m.n = in.n;
+  m.kmax = in.kmax;
+  m.T = in.n ? in.cu_seqlens[in.n] : 0;
+  m.R = in.n * (1 + in.kmax);
+  m.M = in.n * in.kmax;
+  m.cu.assign(in.cu_seqlens, in.cu_seqlens + in.n + 1);
+  m.qtype.assign(in.qtype, in.qtype + in.n);
+  m.mcount.assign(in.marker_count, in.marker_count + in.n);
+  m.srows.resize(m.R);
+  m.prows.resize(in.n);
+  m.mrows.resize(m.M);
+  for (int r = 0; r < in.n; ++r) {
+    const int base = m.cu[r];
+    m.srows[r * (1 + in.kmax)] = base;
+    m.prows[r] = r * (1 + in.kmax);
+    for (int k = 0; k < in.kmax; ++k) {
+      m.srows[r * (1 + in.kmax) + 1 + k] = base + (int)in.marker_pos[(size_t)r * in.kmax + k];
+      m.mrows[r * in.kmax + k] = r * (1 + in.kmax) + 1 + k;
+    }
+    const int len = m.cu[r + 1] - base;
+    for (int q = 0; q < len; q += ATT_BQ) m.items_full.push_back(make_int4(r, base + q, std::min(ATT_BQ, len - q), 0));
+    const int rows = 1 + in.kmax;
+    for (int q = 0; q < rows; q += ATT_BQ)
+      m.items_rows.push_back(make_int4(r, r * rows + q, std::min(ATT_BQ, rows - q), 1));
+  }
+  return m;
+}
+
+struct DevMeta {
+  const uint32_t* ids;
+  const int* cu;
+  const int* srows;
+  const int* mrows;
+  const int* prows;
+  const int* mcount;
+  const uint32_t* qtype;
+  const int4* items_full;
+  const int4* items_rows;
+};
+
+// Stage the metadata (and optionally the ids) in pinned memory and copy it in one transfer.
+DevMeta upload_meta(s1c_backend& B, const HostMeta& m, const uint32_t* host_ids) {
+  struct Part {
+    const void* src;
+    size_t bytes;
+  };
+  std::vector<Part> parts = {
+      {host_ids, host_ids ? (size_t)m.T * 4 : 0},
+      {m.cu.data(), m.cu.size() * 4},
+      {m.srows.data(), m.srows.size() * 4},
+      {m.mrows.data(), m.mrows.size() * 4},
+      {m.prows.data(), m.prows.size() * 4},
+      {m.mcount.data(), m.mcount.size() * 4},
+      {m.qtype.data(), m.qtype.size() * 4},
+      {m.items_full.data(), m.items_full.size() * 16},
+      {m.items_rows.data(), m.items_rows.size() * 16},
+  };
+  std::vector<size_t> off(parts.size());
+  size_t total = 0;
+  for (size_t i = 0; i < parts.size(); ++i) {
+    off[i] = total;
+    total += (parts[i].bytes + 255) / 256 * 256;
+  }
+  total = std::max<size_t>(total, 256);
+  if (total > B.meta_host_bytes) {
+    CK(cudaStreamSynchronize(B.stream));
+    if (B.meta_host) cudaFreeHost(B.meta_host);
+    B.meta_host = nullptr;
+    B.meta_host_bytes = 0;
+    CK(cudaMallocHost(&B.meta_host, total * 2));
+    B.meta_host_bytes = total * 2;
+  }
+  // The staging buffer may still feed a copy of the previous forward.
+  CK(cudaStreamSynchronize(B.stream));
+  B.meta.ensure(B.meta_host_bytes);
+  char* hs = static_cast<char*>(B.meta_host);
+  for (size_t i = 0; i < parts.size(); ++i)
+    if (parts[i].bytes) std::memcpy(hs + off[i], parts[i].src, parts[i].bytes);
+  CK(cudaMemcpyAsync(B.meta.p, B.meta_host, total, cudaMemcpyHostToDevice, B.stream));
+  char* dv = B.meta.as<char>();
+  DevMeta dm;
+  dm.ids = reinterpret_cast<const uint32_t*>(dv + off[0]);
+  dm.cu = reinterpret_cast<const int*>(dv + off[1]);
+  dm.srows = reinterpret_cast<const int*>(dv + off[2]);
+  dm.mrows = reinterpret_cast<const int*>(dv + off[3]);
+  dm.prows = reinterpret_cast<const int*>(dv + off[4]);
+  dm.mcount = reinterpret_cast<const int*>(dv + off[5]);
+  dm.qtype = reinterpret_cast<const uint32_t*>(dv + off[6]);
+  dm.items_full = reinterpret_cast<const int4*>(dv + off[7]);
+  dm.items_rows = reinterpret_cast<const int4*>(dv + off[8]);
+  return dm;
+}
+
+template <int D>
+void run_rowwise_embed(s1c_backend& B, const uint32_t* ids, int T) {
+  embed_ln_kernel<D><<<(T + 7) / 8, 256, 0, B.stream>>>(ids, T, B.tok_emb, B.V, B.emb_norm, B.eps, B.h.as<float>(),
+                                                        B.x.as<bf16>(), B.d_status);
+  CK(cudaGetLastError());
+}
+
+template <int D>
+void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uint32_t* d_ids, float* d_logits,
+                 float* d_pooled, float* d_hidden) {
+  cudaStream_t st = B.stream;
+  const int T = m.T, d = B.d, nsm = B.num_sms;
+  int64_t nl = 0;
+  int* pos = B.tok.as<int>();
+  int* trow = pos + B.cap_T;
+  float* h = B.h.as<float>();
+  float* h2 = B.h2.as<float>();
+  bf16* x = B.x.as<bf16>();
+  bf16* qkv = B.qkv.as<bf16>();
+  bf16* att = B.att.as<bf16>();
+  bf16* act = B.act.as<bf16>();
+  const float scale_log2 = (1.0f / 8.0f) * 1.4426950408889634f;  // 1/sqrt(64) * log2(e)
+
+  prep_tokens_kernel<<<(T + 255) / 256, 256, 0, st>>>(dm.cu, m.n, T, pos, trow);
+  CK(cudaGetLastError());
+  run_rowwise_embed<D>(B, d_ids, T);
+  nl += 2;
+
+  auto attn = [&](const bf16* q, const bf16* k, const bf16* v, bf16* o, int qs, int ks, int vs, int os,
+                  const int4* items, int n_items, int window) {
+    if (n_items == 0) return;
+    AttnArgs a{q, k, v, o, qs, ks, vs, os, dm.cu, items, window, scale_log2};
+    attention_varlen_kernel<<<dim3(n_items, d / 64), ATT_THREADS, 0, st>>>(a);
+    CK(cudaGetLastError());
+    ++nl;
+  };
+  auto gemm_args = [&](int M, int N, int K, void* out, int ldo) {
+    GemmArgs a{};
+    a.M = M; a.N = N; a.K = K; a.out = out; a.ldo = ldo; a.status = B.d_status;
+    return a;
+  };
+
+  for (int i = 0; i < B.L; ++i) {
+    const EncLayer& l = B.layers[i];
+    if (i > 0) { launch_ln<D>(h, nullptr, T, l.attn_norm, nullptr, B.eps, x, st); ++nl; }
+    GemmArgs g = gemm_args(T, 3 * d, d, qkv, 3 * d);
+    g.pos = pos;
+    g.rope_cs = B.rope_cs[l.local ? 1 : 0];
+    g.rope_cols = 2 * d;
+    launch_gemm<EPI_ROPE>(B.tm_x, l.tm_wqkv, g, nsm, st); ++nl;
+    attn(qkv, qkv + d, qkv + 2 * d, att, 3 * d, 3 * d, 3 * d, d, dm.items_full, (int)m.items_full.size(),
+         l.local ? B.window : -1);
+    launch_gemm<EPI_RESID>(B.tm_att, l.tm_wo, gemm_args(T, d, d, h, d), nsm, st); ++nl;
+    launch_ln<D>(h, nullptr, T, l.mlp_norm, nullptr, B.eps, x, st); ++nl;
+    GemmArgs gi = gemm_args(T, B.Ipad, d, act, B.I);
+    gi.out_cols = B.I;
+    launch_gemm<EPI_GEGLU>(B.tm_x, l.tm_wi, gi, nsm, st); ++nl;
+    launch_gemm<EPI_RESID>(B.tm_act_i, l.tm_wo2, gemm_args(T, d, B.I, h, d), nsm, st); ++nl;
+  }
+
+  // final_norm, + type embedding, head layer 0's norm1
+  final_to_head_kernel<D><<<(T + 7) / 8, 256, 0, st>>>(h, T, B.final_norm, B.eps, d_hidden, trow, dm.qtype,
+                                                       B.type_emb, B.head[0].n1w, B.head[0].n1b, h2, x);
+  CK(cudaGetLastError());
+  ++nl;
+
+  // full head layers (all but the last)
+  for (int j = 0; j + 1 < B.n_head; ++j) {
+    const HeadLayer& hl = B.head[j];
+    GemmArgs g = gemm_args(T, 3 * d, d, qkv, 3 * d);
+    g.bias = hl.in_b;
+    launch_gemm<EPI_STORE>(B.tm_x, hl.tm_in, g, nsm, st); ++nl;
+    attn(qkv, qkv + d, qkv + 2 * d, att, 3 * d, 3 * d, 3 * d, d, dm.items_full, (int)m.items_full.size(), -1);
+    GemmArgs go = gemm_args(T, d, d, h2, d);
+    go.bias = hl.out_b;
+    launch_gemm<EPI_RESID>(B.tm_att, hl.tm_out, go, nsm, st); ++nl;
+    launch_ln<D>(h2, nullptr, T, hl.n2w, hl.n2b, 1e-5f, x, st); ++nl;
+    GemmArgs g1 = gemm_args(T, B.F, d, act, B.F);
+    g1.bias = hl.l1_b;
+    g1.act = ACT_RELU;
+    launch_gemm<EPI_STORE>(B.tm_x, hl.tm_l1, g1, nsm, st); ++nl;
+    GemmArgs g2 = gemm_args(T, d, B.F, h2, d);
+    g2.bias = hl.l2_b;
+    launch_gemm<EPI_RESID>(B.tm_act_f, hl.tm_l2, g2, nsm, st); ++nl;
+    const HeadLayer& nx = B.head[j + 1];
+    launch_ln<D>(h2, nullptr, T, nx.n1w, nx.n1b, 1e-5f, x, st); ++nl;
+  }
+
+  // last head layer, pruned to the scorer's rows: keys/values from every token, the rest at
+  // position 0 and the marker slots only (lib.rs:1728-1748)
+  {
+    const HeadLayer& hl = B.head[B.n_head - 1];
+    const int R = m.R;
+    bf16* kv = qkv;  // [T, 2d]
+    GemmArgs gkv = gemm_args(T, 2 * d, d, kv, 2 * d);
+    gkv.bias = hl.in_b + d;
+    launch_gemm<EPI_STORE>(B.tm_x, hl.tm_in_kv, gkv, nsm, st); ++nl;
+    gather_rows_bf16_kernel<<<R, 128, 0, st>>>(x, dm.srows, R, d, B.xs.as<bf16>()); ++nl;
+    gather_rows_f32_kernel<<<R, 256, 0, st>>>(h2, dm.srows, R, d, B.hs.as<float>()); ++nl;
+    CK(cudaGetLastError());
+    GemmArgs gq = gemm_args(R, d, d, B.qs.p, d);
+    gq.bias = hl.in_b;
+    launch_gemm<EPI_STORE>(B.tm_xs, hl.tm_in_q, gq, nsm, st); ++nl;
+    attn(B.qs.as<bf16>(), kv, kv + d, B.atts.as<bf16>(), d, 2 * d, 2 * d, d, dm.items_rows,
+         (int)m.items_rows.size(), -1);
+    GemmArgs go = gemm_args(R, d, d, B.hs.p, d);
+    go.bias = hl.out_b;
+    launch_gemm<EPI_RESID>(B.tm_atts, hl.tm_out, go, nsm, st); ++nl;
+    launch_ln<D>(B.hs.as<float>(), nullptr, R, hl.n2w, hl.n2b, 1e-5f, B.xs.as<bf16>(), st); ++nl;
+    GemmArgs g1 = gemm_args(R, B.F, d, B.fs.p, B.F);
+    g1.bias = hl.l1_b;
+    g1.act = ACT_RELU;
+    launch_gemm<EPI_STORE>(B.tm_xs, hl.tm_l1, g1, nsm, st); ++nl;
+    GemmArgs g2 = gemm_args(R, d, B.F, B.hs.p, d);
+    g2.bias = hl.l2_b;
+    launch_gemm<EPI_RESID>(B.tm_fs, hl.tm_l2, g2, nsm, st); ++nl;
+  }
+
+  // scorer at the marker slots, pooled at position 0
+  if (m.M > 0) {
+    launch_ln<D>(B.hs.as<float>(), dm.mrows, m.M, B.sc_nw, B.sc_nb, 1e-5f, B.xm.as<bf16>(), st); ++nl;
+    GemmArgs gs = gemm_args(m.M, B.S, d, B.sh.p, B.S);
+    gs.bias = B.sc_b1;
+    gs.act = ACT_GELU;
+    gs.out_f32 = 1;
+    launch_gemm<EPI_STORE>(B.tm_xm, B.tm_sc1, gs, nsm, st); ++nl;
+    scorer_logits_kernel<<<(m.M + 7) / 8, 256, 0, st>>>(B.sh.as<float>(), m.M, B.S, B.sc_w3, B.sc_b3, dm.mcount,
+                                                        m.kmax, d_logits);
+    CK(cudaGetLastError());
+    ++nl;
+  }
+  if (m.n > 0) {
+    gather_rows_f32_kernel<<<m.n, 256, 0, st>>>(B.hs.as<float>(), dm.prows, m.n, d, d_pooled);
+    CK(cudaGetLastError());
+    ++nl;
+  }
+  B.launches = nl;
+}
+
+void forward_enqueue(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uint32_t* d_ids, float* d_logits,
+                     float* d_pooled, float* d_hidden) {
+  switch (B.d) {
+    case 256: run_forward<256>(B, m, dm, d_ids, d_logits, d_pooled, d_hidden); break;
+    case 768: run_forward<768>(B, m, dm, d_ids, d_logits, d_pooled, d_hidden); break;
+    case 1024: run_forward<1024>(B, m, dm, d_ids, d_logits, d_pooled, d_hidden); break;
+    default: throw S1cError(S1C_ERR_CONFIG, "unsupported hidden size");
+  }
+}
+
+void check_status(s1c_backend& B) {
+  CK(cudaMemcpyAsync(B.h_status, B.d_status, sizeof(int), cudaMemcpyDeviceToHost, B.stream));
+  CK(cudaStreamSynchronize(B.stream));
+  if (*B.h_status != 0) {
+    const int code = *B.h_status;
+    CK(cudaMemsetAsync(B.d_status, 0, sizeof(int), B.stream));
+    CK(cudaStreamSynchronize(B.stream));
+    if (code == DEV_BAD_INDEX) throw S1cError(S1C_ERR_ARG, "a token id is outside the vocabulary");
+    throw S1cError(S1C_ERR_DEVICE_TIMEOUT, "device-side wait ran out (code " + std::to_string(code) + ")");
+  }
+}
+
+// Host-buffer forward: ids and metadata copied in, logits / pooled / hidden copied out.
+void forward_host(s1c_backend& B, const s1c_varlen& in, float* logits, float* pooled, float* hidden) {
+  validate_varlen(B, in);
+  if (in.n == 0) return;
+  const int T = in.cu_seqlens[in.n];
+  for (int t = 0; t < T; ++t)
+    if (in.ids[t] >= (uint32_t)B.V) throw S1cError(S1C_ERR_ARG, "token " + std::to_string(t) + ": id outside the vocabulary");
+  HostMeta m = make_meta(in);
+  ensure_capacity(B, m.T, m.R);
+  const size_t nl = (size_t)m.M, np = (size_t)m.n * B.d, nh = hidden ? (size_t)m.T * B.d : 0;
+  B.out_stage.ensure((nl + np + nh + 64) * 4);
+  float* d_logits = B.out_stage.as<float>();
+  float* d_pooled = d_logits + (nl + 15) / 16 * 16;
+  float* d_hidden = hidden ? d_pooled + (np + 15) / 16 * 16 : nullptr;
+  DevMeta dm = upload_meta(B, m, in.ids);
+  forward_enqueue(B, m, dm, dm.ids, d_logits, d_pooled, d_hidden);
+  const size_t out_bytes = (nl + np + nh) * 4;
+  if (out_bytes > B.h_out_bytes) {
+    if (B.h_out) cudaFreeHost(B.h_out);
+    B.h_out = nullptr;
+    B.h_out_bytes = 0;
+    CK(cudaMallocHost(&B.h_out, out_bytes * 2 + 64));
+    B.h_out_bytes = out_bytes * 2 + 64;
+  }
+  float* ho = B.h_out;
+  if (nl) CK(cudaMemcpyAsync(ho, d_logits, nl * 4, cudaMemcpyDeviceToHost, B.stream));
+  CK(cudaMemcpyAsync(ho + nl, d_pooled, np * 4, cudaMemcpyDeviceToHost, B.stream));
+  if (nh) CK(cudaMemcpyAsync(ho + nl + np, d_hidden, nh * 4, cudaMemcpyDeviceToHost, B.stream));
+  check_status(B);
+  if (nl) std::memcpy(logits, ho, nl * 4);
+  std::memcpy(pooled, ho + nl, np * 4);
+  if (nh) std::memcpy(hidden, ho + nl + np, nh * 4);
+}
+
+// Padded Batch -> varlen (Packing::new, lib.rs:906-930): real tokens row-major; positions are
+// indices inside the row; markers keep their in-row positions.
+struct PackedBatch {
+  std::vector<uint32_t> ids;
+  std::vector<int32_t> cu, mcount;
+  std::vector<uint32_t> mpos, qtype;
+  s1c_varlen v{};
+};
+void pack_batch(const s1c_batch& b, PackedBatch& p) {
+  if (!b.input_ids || !b.attention_mask || !b.seq_lens || !b.marker_count || !b.qtype || (b.kmax && !b.marker_pos))
+    throw S1cError(S1C_ERR_ARG, "null batch array");
+  p.cu.assign(1, 0);
+  for (size_t r = 0; r < b.n; ++r) {
+    const size_t s = b.seq_lens[r];
+    if (s < 1 || s > b.len) throw S1cError(S1C_ERR_ARG, "row " + std::to_string(r) + ": seq_len outside 1..len");
+    for (size_t pos = 0; pos < b.len; ++pos) {
+      const uint32_t mk = b.attention_mask[r * b.len + pos];
+      if (mk != (pos < s ? 1u : 0u))
+        throw S1cError(S1C_ERR_ARG, "row " + std::to_string(r) + ": attention mask does not match seq_len " +
+                                        std::to_string(s));
+      if (mk == 1) p.ids.push_back(b.input_ids[r * b.len + pos]);
+    }
+    p.cu.push_back((int32_t)p.ids.size());
+    if (b.marker_count[r] > b.kmax) throw S1cError(S1C_ERR_ARG, "row " + std::to_string(r) + ": marker_count > kmax");
+    p.mcount.push_back((int32_t)b.marker_count[r]);
+    p.qtype.push_back(b.qtype[r]);
+  }
+  p.mpos.assign(b.marker_pos, b.marker_pos + b.n * b.kmax);
+  p.v.n = (int32_t)b.n;
+  p.v.kmax = (int32_t)b.kmax;
+  p.v.ids = p.ids.data();
+  p.v.cu_seqlens = p.cu.data();
+  p.v.marker_pos = p.mpos.data();
+  p.v.marker_count = p.mcount.data();
+  p.v.qtype = p.qtype.data();
+}
+
+template <class F>
+s1c_status guarded(s1c_backend* b, F&& f) {
+  if (!b) return S1C_ERR_ARG;
+  try {
+    CK(cudaSetDevice(b->device));
+    f();
+    return S1C_OK;
+  } catch (const S1cError& e) {
+    b->last_error = e.what();
+    return e.code;
+  } catch (const std::exception& e) {
+    b->last_error = e.what();
+    return S1C_ERR_ARG;
+  } catch (...) {
+    b->last_error = "unknown error";
+    return S1C_ERR_ARG;
+  }
+}
+
+}  // namespace
+
+// =============================================================================================
+// C ABI
+
+extern "C" {
+
+s1c_status s1c_create(const s1c_model_desc* desc, const s1c_tensor* tensors, int32_t n_tensors, int32_t device,
+                      s1c_backend** out) {
+  g_create_error.clear();
+  if (!desc || !out || (n_tensors > 0 && !tensors)) {
+    g_create_error = "null argument";
+    return S1C_ERR_ARG;
+  }
+  *out = nullptr;
+  std::unique_ptr<s1c_backend> b(new s1c_backend());
+  try {
+    int n_dev = 0;
+    CK(cudaGetDeviceCount(&n_dev));
+    if (device < 0 || device >= n_dev) throw S1cError(S1C_ERR_ARG, "no CUDA device " + std::to_string(device));
+    CK(cudaSetDevice(device));
+    cudaDeviceProp prop;
+    CK(cudaGetDeviceProperties(&prop, device));
+    if (prop.major != 10)
+      throw S1cError(S1C_ERR_UNSUPPORTED, std::string("the kernels are built for sm_100a; device is ") + prop.name);
+    b->device = device;
+    b->num_sms = prop.multiProcessorCount;
+    CK(cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking));
+    set_all_gemm_smem();
+    build(*b, *desc, tensors, n_tensors);
+    CK(cudaDeviceSynchronize());
+  } catch (const S1cError& e) {
+    g_create_error = e.what();
+    return e.code;
+  } catch (const std::exception& e) {
+    g_create_error = e.what();
+    return S1C_ERR_ARG;
+  }
+  *out = b.release();
+  return S1C_OK;
+}
+
+void s1c_destroy(s1c_backend* b) {
+  if (!b) return;
+  cudaSetDevice(b->device);
+  delete b;
+}
+
+const char* s1c_last_error(const s1c_backend* b) { return b ? b->last_error.c_str() : "null backend"; }
+const char* s1c_create_error(void) { return g_create_error.c_str(); }
+const char* s1c_name(const s1c_backend* b) { return b ? b->name.c_str() : ""; }
+const char* s1c_active_kernels(const s1c_backend* b) { return b ? b->kernels.c_str() : ""; }
+size_t s1c_padded_len(const s1c_backend*, size_t len, size_t) { return len; }
+int64_t s1c_last_launch_count(const s1c_backend* b) { return b ? b->launches : 0; }
+
+s1c_status s1c_warmup(s1c_backend* b) {
+  return guarded(b, [&] {
+    // One forward per shape class: a single short row and a multi-row batch.
+    for (int n : {1, 4}) {
+      std::vector<int32_t> cu(n + 1);
+      for (int r = 0; r <= n; ++r) cu[r] = r * 64;
+      std::vector<uint32_t> ids((size_t)n * 64, 0), mpos((size_t)n * 2), qt(n, 0);
+      std::vector<int32_t> mc(n, 2);
+      for (int r = 0; r < n; ++r) { mpos[2 * r] = 1; mpos[2 * r + 1] = 2; }
+      s1c_varlen v{n, 2, ids.data(), cu.data(), mpos.data(), mc.data(), qt.data()};
+      std::vector<float> lg((size_t)n * 2), pl((size_t)n * b->d);
+      forward_host(*b, v, lg.data(), pl.data(), nullptr);
+    }
+  });
+}
+
+s1c_status s1c_forward_varlen(s1c_backend* b, const s1c_varlen* in, float* logits, float* pooled, float* hidden) {
+  return guarded(b, [&] {
+    if (!in || !pooled || (in->n > 0 && in->kmax > 0 && !logits)) throw S1cError(S1C_ERR_ARG, "null argument");
+    forward_host(*b, *in, logits, pooled, hidden);
+  });
+}
+
+s1c_status s1c_forward_padded(s1c_backend* b, const s1c_batch* batch, float* logits, float* pooled) {
+  return guarded(b, [&] {
+    if (!batch || !pooled || (batch->n > 0 && batch->kmax > 0 && !logits)) throw S1cError(S1C_ERR_ARG, "null argument");
+    PackedBatch p;
+    pack_batch(*batch, p);
+    forward_host(*b, p.v, logits, pooled, nullptr);
+  });
+}
+
+s1c_status s1c_encoder_hidden(s1c_backend* b, const s1c_batch* batch, float* out) {
+  return guarded(b, [&] {
+    if (!batch || !out) throw S1cError(S1C_ERR_ARG, "null argument");
+    PackedBatch p;
+    pack_batch(*batch, p);
+    const size_t d = b->d;
+    std::vector<float> lg(batch->n * batch->kmax), pl(batch->n * d), hid((size_t)p.ids.size() * d);
+    forward_host(*b, p.v, lg.data(), pl.data(), hid.data());
+    std::memset(out, 0, batch->n * batch->len * d * sizeof(float));
+    for (size_t r = 0; r < batch->n; ++r) {
+      const size_t s = batch->seq_lens[r];
+      std::memcpy(out + r * batch->len * d, hid.data() + (size_t)p.cu[r] * d, s * d * sizeof(float));
+    }
+  });
+}
+
+s1c_status s1c_forward_device(s1c_backend* b, const s1c_varlen* in, const uint32_t* d_ids, float* d_logits,
+                              float* d_pooled, float* d_hidden) {
+  return guarded(b, [&] {
+    if (!in || !d_ids || !d_pooled || (in->n > 0 && in->kmax > 0 && !d_logits))
+      throw S1cError(S1C_ERR_ARG, "null argument");
+    validate_varlen(*b, *in);
+    if (in->n == 0) return;
+    HostMeta m = make_meta(*in);
+    ensure_capacity(*b, m.T, m.R);
+    DevMeta dm = upload_meta(*b, m, nullptr);
+    forward_enqueue(*b, m, dm, d_ids, d_logits, d_pooled, d_hidden);
+    check_status(*b);
+  });
+}
+
+s1c_status s1c_gemm(int32_t epi, const void* d_A, const void* d_B, void* d_out, int32_t M, int32_t N, int32_t K,
+                    const float* d_bias, int32_t act, int32_t out_f32, const int32_t* d_pos, float rope_theta,
+                    int32_t rope_cols, int32_t out_cols, void* stream) {
+  static std::mutex mu;
+  static std::map<std::pair<int, float>, float2*> tables;  // (device, theta) -> RoPE table
+  static int* d_status_dummy[64] = {nullptr};
+  try {
+    if (!d_A || !d_B || !d_out || M <= 0 || N <= 0 || K <= 0 || K % 8 || N % 32)
+      throw S1cError(S1C_ERR_ARG, "bad GEMM arguments (K must be a multiple of 8, N of 32)");
+    int dev = 0;
+    CK(cudaGetDevice(&dev));
+    cudaDeviceProp prop;
+    CK(cudaGetDeviceProperties(&prop, dev));
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    GemmArgs a{};
+    a.M = M; a.N = N; a.K = K; a.out = d_out; a.bias = d_bias; a.act = act; a.out_f32 = out_f32;
+    a.pos = d_pos; a.rope_cols = rope_cols; a.out_cols = out_cols;
+    {
+      std::lock_guard<std::mutex> g(mu);
+      static bool smem_set[64] = {false};
+      if (!smem_set[dev]) { set_all_gemm_smem(); smem_set[dev] = true; }
+      if (!d_status_dummy[dev]) {
+        CK(cudaMalloc(&d_status_dummy[dev], sizeof(int)));
+        CK(cudaMemset(d_status_dummy[dev], 0, sizeof(int)));
+      }
+      a.status = d_status_dummy[dev];
+      if (epi == EPI_ROPE) {
+        auto key = std::make_pair(dev, rope_theta);
+        if (!tables.count(key)) tables[key] = make_rope_table_raw(rope_theta, 8192);
+        a.rope_cs = tables[key];
+        if (!d_pos) throw S1cError(S1C_ERR_ARG, "RoPE needs positions");
+      }
+    }
+    const int ldo = (epi == EPI_GEGLU) ? out_cols : N;
+    a.ldo = ldo;
+    const CUtensorMap ta = make_tmap(d_A, (uint64_t)M, K, K, GEMM_BM);
+    const CUtensorMap tb = make_tmap(d_B, N, K, K, GEMM_BN);
+    switch (epi) {
+      case EPI_STORE: launch_gemm<EPI_STORE>(ta, tb, a, prop.multiProcessorCount, st); break;
+      case EPI_ROPE: launch_gemm<EPI_ROPE>(ta, tb, a, prop.multiProcessorCount, st); break;
+      case EPI_GEGLU: launch_gemm<EPI_GEGLU>(ta, tb, a, prop.multiProcessorCount, st); break;
+      case EPI_RESID: launch_gemm<EPI_RESID>(ta, tb, a, prop.multiProcessorCount, st); break;
+      default: throw S1cError(S1C_ERR_ARG, "unknown epilogue");
+    }
+    return S1C_OK;
+  } catch (const S1cError& e) {
+    g_create_error = e.what();
+    return e.code;
+  } catch (const std::exception& e) {
+    g_create_error = e.what();
+    return S1C_ERR_ARG;
+  }
+}
+
+s1c_status s1c_attention(const void* d_q, const void* d_k, const void* d_v, void* d_o, int32_t q_stride,
+                         int32_t k_stride, int32_t v_stride, int32_t o_stride, int32_t heads,
+                         const int32_t* cu_seqlens, int32_t n, int32_t window, float scale, void* stream) {
+  try {
+    if (!d_q || !d_k || !d_v || !d_o || !cu_seqlens || n <= 0 || heads <= 0)
+      throw S1cError(S1C_ERR_ARG, "bad attention arguments");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    std::vector<int4> items;
+    for (int r = 0; r < n; ++r) {
+      const int base = cu_seqlens[r], len = cu_seqlens[r + 1] - base;
+      for (int q = 0; q < len; q += ATT_BQ) items.push_back(make_int4(r, base + q, std::min(ATT_BQ, len - q), 0));
+    }
+    int* d_cu = nullptr;
+    int4* d_items = nullptr;
+    CK(cudaMalloc(&d_cu, (n + 1) * 4));
+    CK(cudaMalloc(&d_items, items.size() * 16));
+    CK(cudaMemcpy(d_cu, cu_seqlens, (n + 1) * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(d_items, items.data(), items.size() * 16, cudaMemcpyHostToDevice));
+    AttnArgs a{static_cast<const bf16*>(d_q), static_cast<const bf16*>(d_k), static_cast<const bf16*>(d_v),
+               static_cast<bf16*>(d_o), q_stride, k_stride, v_stride, o_stride, d_cu, d_items, window,
+               scale * 1.4426950408889634f};
+    attention_varlen_kernel<<<dim3((unsigned)items.size(), heads), ATT_THREADS, 0, st>>>(a);
+    cudaError_t e = cudaGetLastError();
+    cudaError_t e2 = cudaStreamSynchronize(st);
+    cudaFree(d_cu);
+    cudaFree(d_items);
+    if (e != cudaSuccess) throw S1cError(S1C_ERR_CUDA, cudaGetErrorString(e));
+    if (e2 != cudaSuccess) throw S1cError(S1C_ERR_CUDA, cudaGetErrorString(e2));
+    return S1C_OK;
+  } catch (const S1cError& e) {
+    g_create_error = e.what();
+    return e.code;
+  }
+}
+
+}  // extern "C"

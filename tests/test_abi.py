@@ -1,0 +1,58 @@
+"""The C-ABI library builds, loads without a GPU, and exports every function ``include/s1c.h``
+declares. No compute calls are made here."""
+import ctypes
+import os
+import subprocess
+
+import pytest
+
+from sys1rust_b200 import build as b
+from sys1rust_b200.backend import header_functions, lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+@pytest.fixture(scope="module")
+def built():
+    return b.build()
+
+
+def test_header_declares_the_backend_surface():
+    fns = header_functions()
+    for want in ["s1c_create", "s1c_destroy", "s1c_forward_padded", "s1c_forward_varlen", "s1c_forward_device",
+                 "s1c_encoder_hidden", "s1c_name", "s1c_active_kernels", "s1c_padded_len", "s1c_warmup",
+                 "s1c_last_error"]:
+        assert want in fns
+
+
+def test_library_exports_every_declared_symbol(built):
+    L = ctypes.CDLL(built)
+    missing = [f for f in header_functions() if not hasattr(L, f)]
+    assert not missing, missing
+
+
+def test_only_declared_symbols_are_exported(built):
+    out = subprocess.run(["nm", "-D", "--defined-only", built], capture_output=True, text=True, check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if " T " in line}
+    s1c = {s for s in exported if s.startswith("s1c_")}
+    assert s1c == set(header_functions())
+
+
+def test_library_is_built_for_sm100a(built):
+    """The embedded device code targets sm_100a only (checked from the build flags)."""
+    assert "arch=compute_100a,code=sm_100a" in " ".join(b.NVCC_FLAGS)
+    assert os.path.getsize(built) > 100_000
+
+
+def test_create_without_gpu_fails_cleanly(built):
+    """With no usable device the library returns an error code, not a crash."""
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    from sys1rust_b200.backend import ModelDesc, Tensor
+    L = lib()
+    desc = ModelDesc()
+    h = ctypes.c_void_p()
+    rc = L.s1c_create(ctypes.byref(desc), (Tensor * 1)(), 0, 0, ctypes.byref(h))
+    assert rc < 0
+    assert L.s1c_create_error()

@@ -1,0 +1,170 @@
+"""Full-forward parity on the GPU: ``CudaBackend.forward`` (through the C ABI) against the CPU
+oracle of the reference forward on identical seeded weights and token ids.
+
+Tolerances (stated by the task for this path, tighter than the reference's own
+``laya-mlx/tests/parity.rs:29-39`` logits < 0.15 / probs < 0.02):
+  * per-question probabilities within 1e-2 absolute,
+  * final encoder hidden states within 2e-2 relative (Frobenius, over the real tokens),
+  * choice argmax equal wherever the fp32 top-two margin exceeds the measured logit error,
+  * masked marker slots exactly -1e4.
+"""
+import numpy as np
+import pytest
+
+from sys1rust_b200.batch import Batch, EncodedItem, Varlen, collate_to
+
+pytestmark = pytest.mark.gpu
+
+HIDDEN_REL = 2e-2
+PROB_ABS = 1e-2
+
+
+def make_rows(cfg, seed, lens, ks, qtypes=None):
+    rng = np.random.Generator(np.random.PCG64(seed))
+    items = []
+    for i, (L, k) in enumerate(zip(lens, ks)):
+        ids = rng.integers(4, cfg.encoder.vocab_size, size=L).astype(np.uint32)
+        ids[0] = 1
+        if L > 1:
+            ids[-1] = 2
+        k = min(k, max(L - 1, 0))
+        markers = sorted(rng.choice(np.arange(1, L), size=k, replace=False).tolist()) if k else []
+        qt = int(qtypes[i]) if qtypes is not None else int(rng.integers(0, 3))
+        items.append(EncodedItem(ids.tolist(), markers, qt))
+    return items
+
+
+def oracle(cfg, w, batch, emulate=False):
+    from oracle.forward_ref import OracleModel
+    return OracleModel(cfg, w.tensors, emulate_bf16=emulate).forward(batch)
+
+
+def question_probs(logits, batch):
+    out = []
+    for r in range(batch.n):
+        c = int(batch.marker_count[r])
+        if c:
+            z = logits[r * batch.kmax: r * batch.kmax + c].astype(np.float64)
+            z = np.exp(z - z.max())
+            out.append(z / z.sum())
+    return out
+
+
+def check_against_oracle(cfg, w, be, batch):
+    got = be.forward(batch)
+    hid = be.encoder_hidden(batch).reshape(batch.n, batch.len, -1)
+    lo, po, ho = oracle(cfg, w, batch)
+    am = batch.attention_mask.reshape(batch.n, batch.len).astype(bool)
+    # hidden state
+    rel = np.linalg.norm(hid[am] - ho[am]) / np.linalg.norm(ho[am])
+    assert rel < HIDDEN_REL, f"hidden rel err {rel}"
+    # masked slots
+    for r in range(batch.n):
+        for k in range(int(batch.marker_count[r]), batch.kmax):
+            assert got.logits[r * batch.kmax + k] == np.float32(-1e4)
+    # probabilities per question
+    for pg, pw in zip(question_probs(got.logits, batch), question_probs(lo, batch)):
+        assert np.abs(pg - pw).max() < PROB_ABS
+    # argmax where the margin is clear
+    err = np.abs(got.logits - lo).max()
+    for r in range(batch.n):
+        c = int(batch.marker_count[r])
+        if c >= 2:
+            z = lo[r * batch.kmax: r * batch.kmax + c]
+            srt = np.sort(z)
+            if srt[-1] - srt[-2] > 2 * err:
+                assert np.argmax(got.logits[r * batch.kmax: r * batch.kmax + c]) == np.argmax(z)
+    assert np.all(np.isfinite(got.pooled))
+    prel = np.linalg.norm(got.pooled - po) / np.linalg.norm(po)
+    assert prel < 5e-2, f"pooled rel err {prel}"
+    return rel, err
+
+
+def test_small_model_matches_oracle(cuda_lib):
+    from conftest import get_backend
+    cfg, w, be = get_backend("small:3")
+    items = make_rows(cfg, 21, [1, 2, 9, 17, 40, 64, 65, 130, 300], [0, 1, 2, 3, 4, 2, 5, 3, 6])
+    batch = collate_to(items, cfg.encoder.pad_token_id)
+    check_against_oracle(cfg, w, be, batch)
+
+
+def test_large_model_matches_oracle(cuda_lib):
+    from conftest import get_backend
+    cfg, w, be = get_backend("large:0")
+    items = make_rows(cfg, 22, [128, 37, 200, 300], [2, 3, 4, 9], qtypes=[2, 0, 1, 0])
+    batch = collate_to(items, cfg.encoder.pad_token_id)
+    rel, err = check_against_oracle(cfg, w, be, batch)
+    print(f"large: hidden rel {rel:.4g}, logit max err {err:.4g}")
+
+
+def test_large_model_long_rows(cuda_lib):
+    """Rows at 511/512/513 tokens and one long row (window and global paths over many tiles)."""
+    from conftest import get_backend
+    cfg, w, be = get_backend("large:0")
+    items = make_rows(cfg, 23, [511, 512, 513, 1024], [3, 1, 2, 10])
+    batch = collate_to(items, cfg.encoder.pad_token_id)
+    check_against_oracle(cfg, w, be, batch)
+
+
+def test_rows_do_not_depend_on_batch(cuda_lib):
+    """A row's outputs are the same, bit for bit, alone or batched with other rows
+    (``laya-core/src/agent.rs:400-442`` checks batch-vs-single equality)."""
+    from conftest import get_backend
+    cfg, w, be = get_backend("large:0")
+    items = make_rows(cfg, 24, [50, 129, 7, 260], [2, 3, 1, 4])
+    batch = collate_to(items, cfg.encoder.pad_token_id)
+    full = be.forward(batch)
+    d = cfg.encoder.hidden_size
+    for r, it in enumerate(items):
+        one = collate_to([it], cfg.encoder.pad_token_id, min_len=0)
+        o = be.forward(one)
+        k = len(it.markers)
+        assert np.array_equal(o.logits[:k], full.logits[r * batch.kmax: r * batch.kmax + k])
+        assert np.array_equal(o.pooled, full.pooled[r * d:(r + 1) * d])
+
+
+def test_padded_and_varlen_entry_points_agree(cuda_lib):
+    from conftest import get_backend
+    cfg, w, be = get_backend("small:3")
+    items = make_rows(cfg, 25, [5, 33, 12], [2, 0, 3])
+    batch = collate_to(items, cfg.encoder.pad_token_id)
+    a = be.forward(batch)
+    b = be.forward_varlen(Varlen.from_batch(batch), hidden=True)
+    assert np.array_equal(a.logits, b.logits) and np.array_equal(a.pooled, b.pooled)
+    hid = be.encoder_hidden(batch).reshape(batch.n, batch.len, -1)
+    am = batch.attention_mask.reshape(batch.n, batch.len).astype(bool)
+    assert np.array_equal(hid[am], b.hidden.reshape(-1, cfg.encoder.hidden_size))
+    assert np.all(hid[~am] == 0)
+
+
+def test_batch_without_markers(cuda_lib):
+    from conftest import get_backend
+    cfg, w, be = get_backend("small:3")
+    batch = collate_to(make_rows(cfg, 26, [10, 3], [0, 0]), cfg.encoder.pad_token_id)
+    assert batch.kmax == 0
+    out = be.forward(batch)
+    assert out.logits.size == 0 and out.pooled.size == 2 * cfg.encoder.hidden_size
+    _, po, _ = oracle(cfg, w, batch)
+    assert np.linalg.norm(out.pooled - po) / np.linalg.norm(po) < 5e-2
+
+
+def test_malformed_batches_are_errors(cuda_lib):
+    from conftest import get_backend
+    from sys1rust_b200.backend import BackendError
+    cfg, w, be = get_backend("small:3")
+    good = collate_to(make_rows(cfg, 27, [6, 4], [2, 1]), cfg.encoder.pad_token_id)
+    bad_mask = Batch(**{**good.__dict__, "attention_mask": good.attention_mask.copy()})
+    bad_mask.attention_mask[good.len - 1] = 0  # row 0 is full length: mask no longer matches
+    with pytest.raises(BackendError, match="attention mask"):
+        be.forward(bad_mask)
+    bad_id = Batch(**{**good.__dict__, "input_ids": good.input_ids.copy()})
+    bad_id.input_ids[1] = cfg.encoder.vocab_size + 5
+    with pytest.raises(BackendError, match="vocabulary"):
+        be.forward(bad_id)
+    bad_marker = Batch(**{**good.__dict__, "marker_pos": good.marker_pos.copy()})
+    bad_marker.marker_pos[good.kmax] = 10  # row 1 has 4 tokens
+    with pytest.raises(BackendError, match="marker"):
+        be.forward(bad_marker)
+    # the handle stays usable after an error
+    out = be.forward(good)
+    assert np.all(np.isfinite(out.pooled))

@@ -1,0 +1,135 @@
+"""Kernel-level parity on the GPU: each sm_100a kernel against a plain PyTorch fp32 reference of
+the same op, through the C ABI (``s1c_gemm``, ``s1c_attention``).
+
+Tolerances: outputs stored as bf16 carry a relative rounding error of 2^-9; the bound used is
+``max|out - ref| <= 1e-2 * max|ref|`` (fp32 outputs: 1e-4 relative to the accumulation).
+"""
+import math
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+
+def _rel_err(out, ref):
+    return (out.float() - ref.float()).abs().max().item() / max(ref.float().abs().max().item(), 1e-30)
+
+
+def _rand(shape, seed, scale=1.0):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    return (torch.randn(*shape, generator=g) * scale).to(torch.bfloat16).cuda()
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (300, 768, 1024), (1024, 3072, 1024), (77, 1024, 2624),
+                                   (513, 256, 4096)])
+def test_gemm_store_matches_torch(cuda_lib, M, N, K):
+    from sys1rust_b200.backend import EPI_STORE, gemm
+    a, b = _rand((M, K), 1), _rand((N, K), 2)
+    out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    gemm(EPI_STORE, a.data_ptr(), b.data_ptr(), out.data_ptr(), M, N, K)
+    torch.cuda.synchronize()
+    ref = a.float() @ b.float().t()
+    assert _rel_err(out, ref) < 1e-2
+
+
+@pytest.mark.parametrize("act", [0, 1, 2])
+def test_gemm_bias_activation_fp32_out(cuda_lib, act):
+    from sys1rust_b200.backend import EPI_STORE, gemm
+    M, N, K = 200, 512, 1024
+    a, b = _rand((M, K), 3), _rand((N, K), 4)
+    bias = torch.randn(N, generator=torch.Generator().manual_seed(5)).float().cuda()
+    out = torch.empty(M, N, dtype=torch.float32, device="cuda")
+    gemm(EPI_STORE, a.data_ptr(), b.data_ptr(), out.data_ptr(), M, N, K, bias_ptr=bias.data_ptr(), act=act, out_f32=1)
+    torch.cuda.synchronize()
+    ref = a.float() @ b.float().t() + bias
+    ref = [ref, torch.relu(ref), torch.nn.functional.gelu(ref)][act]
+    assert _rel_err(out, ref) < 1e-4
+
+
+def test_gemm_residual_in_place(cuda_lib):
+    from sys1rust_b200.backend import EPI_RESID, gemm
+    M, N, K = 333, 1024, 2624
+    a, b = _rand((M, K), 6), _rand((N, K), 7)
+    h = torch.randn(M, N, generator=torch.Generator().manual_seed(8)).float().cuda()
+    ref = h + a.float() @ b.float().t()
+    gemm(EPI_RESID, a.data_ptr(), b.data_ptr(), h.data_ptr(), M, N, K)
+    torch.cuda.synchronize()
+    assert _rel_err(h, ref) < 1e-4
+
+
+def _rope_ref(x, pos, theta):
+    """Rotate-half RoPE per 64-wide head of x [M, C] at positions pos [M] (split_rope.metal:46-76)."""
+    M, Cc = x.shape
+    half = 32
+    lbase = torch.log2(torch.tensor(theta, dtype=torch.float32))
+    inv = torch.exp2(-(torch.arange(half, dtype=torch.float32) / half) * lbase)
+    ang = pos.float().cpu()[:, None] * inv[None, :]
+    c, s = torch.cos(ang).cuda(), torch.sin(ang).cuda()
+    xh = x.view(M, Cc // 64, 64)
+    x1, x2 = xh[..., :half], xh[..., half:]
+    return torch.cat([x1 * c[:, None] - x2 * s[:, None], x1 * s[:, None] + x2 * c[:, None]], -1).view(M, Cc)
+
+
+@pytest.mark.parametrize("theta", [160000.0, 10000.0])
+def test_gemm_rope_epilogue(cuda_lib, theta):
+    from sys1rust_b200.backend import EPI_ROPE, gemm
+    d = 1024
+    M, N, K = 700, 3 * d, d
+    a, b = _rand((M, K), 9), _rand((N, K), 10)
+    pos = torch.from_numpy(np.concatenate([np.arange(500), np.arange(200)]).astype(np.int32)).cuda()
+    out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    gemm(EPI_ROPE, a.data_ptr(), b.data_ptr(), out.data_ptr(), M, N, K, pos_ptr=pos.data_ptr(), rope_theta=theta,
+         rope_cols=2 * d)
+    torch.cuda.synchronize()
+    acc = a.float() @ b.float().t()
+    ref = torch.cat([_rope_ref(acc[:, :2 * d], pos, theta), acc[:, 2 * d:]], 1)
+    assert _rel_err(out, ref) < 1e-2
+
+
+@pytest.mark.parametrize("I", [2624, 384])
+def test_gemm_geglu_epilogue(cuda_lib, I):
+    from sys1rust_b200.backend import EPI_GEGLU, gemm, interleave_wi
+    M, K = 260, 1024
+    a = _rand((M, K), 11)
+    wi = _rand((2 * I, K), 12)
+    wil = torch.from_numpy(interleave_wi(wi.cpu().view(torch.int16).numpy(), I)).view(torch.bfloat16).cuda()
+    out = torch.empty(M, I, dtype=torch.bfloat16, device="cuda")
+    gemm(EPI_GEGLU, a.data_ptr(), wil.data_ptr(), out.data_ptr(), M, wil.shape[0], K, out_cols=I)
+    torch.cuda.synchronize()
+    y = a.float() @ wi.float().t()
+    ref = torch.nn.functional.gelu(y[:, :I]) * y[:, I:]
+    assert _rel_err(out, ref) < 1e-2
+
+
+def _attn_ref(q, k, v, cu, window, scale, heads):
+    out = torch.zeros_like(q, dtype=torch.float32)
+    for r in range(len(cu) - 1):
+        s, e = int(cu[r]), int(cu[r + 1])
+        L = e - s
+        qh = q[s:e].float().view(L, heads, 64).transpose(0, 1)
+        kh = k[s:e].float().view(L, heads, 64).transpose(0, 1)
+        vh = v[s:e].float().view(L, heads, 64).transpose(0, 1)
+        sc = qh @ kh.transpose(1, 2) * scale
+        if window >= 0:
+            p = torch.arange(L, device=q.device)
+            sc = sc.masked_fill((p[:, None] - p[None, :]).abs() > window, float("-inf"))
+        out[s:e] = (torch.softmax(sc, -1) @ vh).transpose(0, 1).reshape(L, heads * 64)
+    return out
+
+
+@pytest.mark.parametrize("window", [-1, 64, 3])
+def test_attention_varlen_matches_torch(cuda_lib, window):
+    from sys1rust_b200.backend import attention
+    heads, d = 16, 1024
+    lens = [1, 2, 63, 64, 65, 129, 300, 1024]
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    T = int(cu[-1])
+    qkv = _rand((T, 3 * d), 13)
+    o = torch.empty(T, d, dtype=torch.bfloat16, device="cuda")
+    attention(qkv.data_ptr(), qkv[:, d:].data_ptr(), qkv[:, 2 * d:].data_ptr(), o.data_ptr(), 3 * d, 3 * d, 3 * d, d,
+              heads, cu, window, 0.125)
+    ref = _attn_ref(qkv[:, :d], qkv[:, d:2 * d], qkv[:, 2 * d:], cu, window, 0.125, heads)
+    assert _rel_err(o, ref) < 1e-2
