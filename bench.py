@@ -1,0 +1,371 @@
+"""Benchmark of the sys1rust model forward on B200: encoder tokens/s on packed varlen batches.
+
+    python bench.py --gpus N --steps K --warmup W            # this implementation
+    python bench.py --impl reference --steps K --warmup W    # the reference's CPU path (oracle port)
+
+A step is one pass over this GPU's share of the cfg5 serving workload: 1024 requests per GPU
+(lognormal lengths, median 200, sigma 0.6, clipped to [32, 1024]; 1-10 questions each), packed
+into varlen batches of at most 16384 tokens, each batch one full forward (encoder + decision head +
+scorer). At N GPUs the job is the first N x 1024 requests of the cfg5 stream, shard-balanced by
+tokens (LPT): weak scaling, and at N = 8 exactly cfg5's 8192 requests. Ranks share nothing on the
+data path (replicas, no collective); the barrier and the max-over-ranks reduction are the only
+collectives. ``value`` is the whole job's tokens / max-over-ranks device time.
+
+Rank 0 prints one JSON line. Extra keys: ``e2e`` (the same metric through the host-buffer C ABI,
+copies included), ``roofline`` (dominant kernel, from per-launch CUDA events over the timed
+region), ``cpu_baseline`` (the CPU oracle on a bounded sample, N = 1 only), ``latency_cfg1`` (p50 ms
+of one 128-token request through the host API), ``clocks`` (nvidia-smi during the timed region).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "encoder tokens/sec/GPU (packed varlen) at 1/2/4/8 B200; p50 ms per 128-tok request"
+REQ_PER_GPU = 1024
+BATCH_TOKENS = 16384
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def workload(world: int, rank: int):
+    from sys1rust_b200.workloads import cfg5_requests, shard_lpt
+    reqs = cfg5_requests(n=REQ_PER_GPU * world, seed=1)
+    return reqs, shard_lpt(reqs, world)[rank]
+
+
+def cpu_oracle_sample(cfg, weights, items, budget_s: float):
+    """tokens/s of the CPU oracle (fp32, all host threads) over requests of the workload, one row per
+    forward, until ``budget_s`` seconds have passed (at least one request)."""
+    import torch
+    from oracle.forward_ref import OracleModel
+    from sys1rust_b200.batch import collate_to
+    torch.set_num_threads(os.cpu_count() or 1)
+    om = OracleModel(cfg, weights.tensors)
+    om.forward(collate_to([items[0]], cfg.encoder.pad_token_id))  # warm
+    t0 = time.perf_counter()
+    tok = nreq = 0
+    for it in items:
+        om.forward(collate_to([it], cfg.encoder.pad_token_id))
+        tok += len(it.ids)
+        nreq += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return tok / dt, {"cores": torch.get_num_threads(), "tokens": tok, "requests": nreq, "seconds": dt}
+
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in getattr(self, "lines", []):
+            p = [x.strip() for x in l.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                sm.append(float(p[1]))
+                mx = float(p[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, p[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return None
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def run_reference(args):
+    """The reference arm: the CPU restatement of the forward (the reference's MLX-CPU path does
+    not build here), all host threads, on this arm's workload, each step a bounded sample."""
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    from sys1rust_b200.config import large_model
+    from sys1rust_b200.weights import SyntheticWeights
+    cfg = large_model()
+    w = SyntheticWeights(cfg, seed=0)
+    _, mine = workload(1, 0)
+    vals = []
+    steps = args.steps
+    per_step = max(2.0, min(20.0, 90.0 / max(steps + args.warmup, 1)))
+    for s in range(args.warmup + steps):
+        v, info = cpu_oracle_sample(cfg, w, mine[s * 3:] + mine[:s * 3], per_step)
+        if s >= args.warmup:
+            vals.append(v)
+    v = float(np.median(vals))
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": world,
+        "steps": steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"cfg5 shard sample ({REQ_PER_GPU} lognormal requests per GPU), one row per forward",
+                   "model": "ModernBERT-large encoder + decision head + scorer (seeded weights)"},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": info["cores"], "kind": "port",
+                         "sample": f"~{per_step:.0f} s of requests per step ({info['requests']} requests, "
+                                   f"{info['tokens']} tokens in the last step); the reference's MLX-CPU path "
+                                   "needs cargo + MLX, absent here"},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    args.warmup = max(args.warmup, 3)
+
+    import torch
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+
+    from sys1rust_b200.backend import CudaBackend
+    from sys1rust_b200.config import large_model
+    from sys1rust_b200.weights import SyntheticWeights
+    from sys1rust_b200.workloads import cfg1, cfg3, pack_batches
+    from sys1rust_b200.batch import Varlen
+
+    cfg = large_model()
+    t0 = time.time()
+    w = SyntheticWeights(cfg, seed=0)
+    be = CudaBackend.from_synthetic(cfg, w.tensors, device=local, max_tokens=BATCH_TOKENS)
+    log(f"[rank {rank}] model ready in {time.time() - t0:.1f}s: {be.name()}")
+    stream = torch.cuda.current_stream()
+    be.set_stream(stream.cuda_stream)
+
+    all_reqs, mine = workload(world, rank)
+    batches = pack_batches(mine, BATCH_TOKENS)
+    tokens_mine = sum(b.total for b in batches)
+    # inputs resident in HBM before timing
+    d_ids = [torch.from_numpy(b.ids.astype(np.int32)).cuda() for b in batches]
+    max_n = max(b.n for b in batches)
+    max_m = max(b.n * b.kmax for b in batches)
+    d_logits = torch.empty(max(max_m, 1), dtype=torch.float32, device="cuda")
+    d_pooled = torch.empty(max_n * cfg.encoder.hidden_size, dtype=torch.float32, device="cuda")
+
+    def step():
+        for b, ids in zip(batches, d_ids):
+            be.forward_device(b, ids.data_ptr(), d_logits.data_ptr(), d_pooled.data_ptr())
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        step()
+    # ---- timed region: device-resident inputs --------------------------------------------
+    be.profile(True)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches = 0
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+            launches += be.last_launch_count() * len(batches)
+        e1.record(stream)
+        barrier()
+    ms = e0.elapsed_time(e1)
+    prof = be.profile_report()
+    be.profile(False)
+    ms_max = max_over_ranks(ms)
+    tokens_total = sum(len(r.ids) for r in all_reqs)
+    value = tokens_total * args.steps / (ms_max / 1e3)
+
+    # ---- e2e: host buffers through the C ABI, copies inside the timed region --------------
+    be.set_stream(0)
+    for b in batches[:2]:
+        be.forward_varlen(b)
+    barrier()
+    h2d = sum(b.ids.nbytes + b.cu_seqlens.nbytes + b.marker_pos.nbytes + b.marker_count.nbytes + b.qtype.nbytes
+              for b in batches)
+    d2h = sum(4 * (b.n * b.kmax + b.n * cfg.encoder.hidden_size) for b in batches)
+    e2e_steps = max(1, min(args.steps, 3))
+    t_e2e = time.perf_counter()
+    for _ in range(e2e_steps):
+        for b in batches:
+            be.forward_varlen(b)
+    e2e_s = time.perf_counter() - t_e2e
+    e2e_s = max_over_ranks(e2e_s)
+    e2e_value = tokens_total * e2e_steps / e2e_s
+
+    # ---- latency of one 128-token request (cfg1), host API ---------------------------------
+    lat = None
+    one = Varlen.from_rows(cfg1())
+    for _ in range(5):
+        be.forward_varlen(one)
+    ts = []
+    for _ in range(50):
+        t = time.perf_counter()
+        be.forward_varlen(one)
+        ts.append((time.perf_counter() - t) * 1e3)
+    lat = {"p50_ms": float(np.median(ts)), "p90_ms": float(np.percentile(ts, 90)), "n": len(ts),
+           "path": "s1c_forward_varlen, host buffers, copies included"}
+
+    # ---- cfg3: 64 requests U[64,512] in one varlen batch, device-resident -----------------
+    c3 = Varlen.from_rows(cfg3())
+    c3_ids = torch.from_numpy(c3.ids.astype(np.int32)).cuda()
+    c3_l = torch.empty(c3.n * c3.kmax, dtype=torch.float32, device="cuda")
+    c3_p = torch.empty(c3.n * cfg.encoder.hidden_size, dtype=torch.float32, device="cuda")
+    be.set_stream(stream.cuda_stream)
+    for _ in range(3):
+        be.forward_device(c3, c3_ids.data_ptr(), c3_l.data_ptr(), c3_p.data_ptr())
+    torch.cuda.synchronize()
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record(stream)
+    for _ in range(10):
+        be.forward_device(c3, c3_ids.data_ptr(), c3_l.data_ptr(), c3_p.data_ptr())
+    a1.record(stream)
+    torch.cuda.synchronize()
+    cfg3_tps = c3.total * 10 / (a0.elapsed_time(a1) / 1e3)
+
+    # ---- roofline of the dominant kernel ------------------------------------------------
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except OSError:
+        pass
+    total_ms = sum(v["ms"] for v in prof.values()) or 1.0
+    dom_name, dom = max(prof.items(), key=lambda kv: kv[1]["ms"])
+    per_launch_ms = dom["ms"] / dom["launches"]
+    traffic = None
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            tr = json.load(f).get(dom_name)
+        if tr:
+            traffic = tr["dram_bytes_per_flop"] * dom["flops"] / dom["launches"]
+    except (OSError, ValueError, KeyError):
+        pass
+    if dom["flops"] > 0:
+        achieved = dom["flops"] / dom["launches"] / (per_launch_ms / 1e3) / 1e12
+        peak = peaks.get("bf16_tflops_sustained")
+        roof = {"kernel": dom_name, "bound": "tensor", "achieved": achieved, "unit": "TFLOP/s",
+                "peak": peak if peak else 1400.0, "peak_source": "measured (sustained)" if peak else "fallback",
+                "frac": achieved / (peak if peak else 1400.0), "traffic": traffic,
+                "flops_per_launch": dom["flops"] / dom["launches"], "ms_per_launch": per_launch_ms,
+                "share_of_device_time": dom["ms"] / total_ms}
+    else:
+        achieved = dom["bytes"] / dom["launches"] / (per_launch_ms / 1e3) / 1e9
+        peak = peaks.get("hbm_gbs", 6650.0)
+        roof = {"kernel": dom_name, "bound": "hbm", "achieved": achieved, "unit": "GB/s", "peak": peak,
+                "frac": achieved / peak, "traffic": traffic, "share_of_device_time": dom["ms"] / total_ms}
+    enc = [k for k in prof if k.startswith("gemm_")]
+    enc_tflops = sum(prof[k]["flops"] for k in enc) / (sum(prof[k]["ms"] for k in enc) / 1e3) / 1e12 if enc else None
+    kernels = {k: {"launches": v["launches"], "share": v["ms"] / total_ms,
+                   "tflops": (v["flops"] / (v["ms"] / 1e3) / 1e12) if v["flops"] else None,
+                   "gbs": (v["bytes"] / (v["ms"] / 1e3) / 1e9) if v["bytes"] else None}
+               for k, v in sorted(prof.items(), key=lambda kv: -kv[1]["ms"])}
+
+    # ---- CPU baseline (rank 0, N = 1) -----------------------------------------------------
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, info = cpu_oracle_sample(cfg, w, mine, 15.0)
+        cpu = {"value": v, "unit": "tokens/s", "cores": info["cores"], "kind": "port",
+               "sample": f"{info['requests']} requests / {info['tokens']} tokens of this workload, one row per "
+                         f"forward, {info['seconds']:.1f} s, torch fp32 oracle"}
+
+    if world > 1:
+        torch.distributed.barrier()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "value_per_gpu": value / world,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": f"cfg5 shard: {REQ_PER_GPU} lognormal requests per GPU (first "
+                                   f"{REQ_PER_GPU * world} of cfg5's stream, LPT by tokens), varlen batches "
+                                   f"<= {BATCH_TOKENS} tokens, full forward (encoder + head + scorer)",
+                       "model": "ModernBERT-large encoder (28 layers, d 1024, 16x64 heads, GeGLU 2x2624) + "
+                                "2 decision-head layers + scorer, seeded N(0,0.02) bf16 weights",
+                       "tokens_per_step": tokens_total, "batches_per_gpu_step": len(batches),
+                       "l2": "inputs larger than L2: 686 MB of encoder weights stream every forward",
+                       "parallelism": f"dp{world} replicas, no data-path collective"},
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": int(h2d),
+                    "d2h_bytes_per_step": int(d2h), "steps": e2e_steps,
+                    "path": "s1c_forward_varlen (pageable host arrays -> pinned staging -> device; logits and "
+                            "pooled back to host)"},
+            "roofline": roof,
+            "encoder_gemm_tflops": enc_tflops,
+            "cpu_baseline": cpu,
+            "latency_cfg1": lat,
+            "cfg3_tokens_per_s": cfg3_tps,
+            "clocks": clk.summary(),
+            "gpu_launches": int(launches),
+            "kernels": kernels,
+        }
+        print(json.dumps(line), flush=True)
+    be.close()
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

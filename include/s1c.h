@@ -153,6 +153,18 @@ S1C_API s1c_status s1c_attention(const void* d_q, const void* d_k, const void* d
                          int32_t k_stride, int32_t v_stride, int32_t o_stride, int32_t heads,
                          const int32_t* cu_seqlens, int32_t n, int32_t window, float scale, void* stream);
 
+/* Run this handle's forwards on `stream` (a cudaStream_t of the handle's device); NULL returns
+ * to the handle's own stream. Lets a caller order forwards with its own work and time them with
+ * events on that stream. */
+S1C_API s1c_status s1c_set_stream(s1c_backend* b, void* stream);
+
+/* Per-kernel timing: with `on` = 1 every launch of later forwards is bracketed by CUDA events on
+ * the forward's stream (statistics cleared); 0 turns it off. */
+S1C_API s1c_status s1c_profile(s1c_backend* b, int32_t on);
+/* Text report of the profile, one line per kernel: "name launches total_ms flops bytes" (FLOPs and
+ * bytes are algorithmic). Returns the size needed including the terminating 0. */
+S1C_API size_t s1c_profile_report(const s1c_backend* b, char* buf, size_t cap);
+
 /* Number of this library's kernel launches the last forward on this handle enqueued. */
 S1C_API int64_t s1c_last_launch_count(const s1c_backend* b);
 

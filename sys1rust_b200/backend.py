@@ -96,6 +96,9 @@ def lib() -> C.CDLL:
         "s1c_gemm": (I32, [I32, P, P, P, I32, I32, I32, P, I32, I32, P, F32, I32, I32, P]),
         "s1c_attention": (I32, [P, P, P, P, I32, I32, I32, I32, I32, P, I32, I32, F32, P]),
         "s1c_last_launch_count": (I64, [P]),
+        "s1c_set_stream": (I32, [P, P]),
+        "s1c_profile": (I32, [P, I32]),
+        "s1c_profile_report": (SZ, [P, C.c_char_p, SZ]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -244,6 +247,24 @@ class CudaBackend:
 
     def last_launch_count(self) -> int:
         return int(lib().s1c_last_launch_count(self._h))
+
+    def set_stream(self, stream: int) -> None:
+        """Run forwards on ``stream`` (a raw ``cudaStream_t``, e.g. ``torch.cuda.current_stream().cuda_stream``)."""
+        self._check(lib().s1c_set_stream(self._h, stream or None))
+
+    def profile(self, on: bool) -> None:
+        self._check(lib().s1c_profile(self._h, 1 if on else 0))
+
+    def profile_report(self) -> Dict[str, Dict[str, float]]:
+        """Per-kernel totals since ``profile(True)``: launches, ms, algorithmic flops and bytes."""
+        n = int(lib().s1c_profile_report(self._h, None, 0))
+        buf = C.create_string_buffer(n)
+        lib().s1c_profile_report(self._h, buf, n)
+        out = {}
+        for line in buf.value.decode().splitlines():
+            name, launches, ms, flops, nbytes = line.split()
+            out[name] = {"launches": int(launches), "ms": float(ms), "flops": float(flops), "bytes": float(nbytes)}
+        return out
 
     # -- marshalling ------------------------------------------------------------------------
     @staticmethod

@@ -197,6 +197,16 @@ struct DevBuf {
   template <class T> T* as() const { return static_cast<T*>(p); }
 };
 
+struct ProfRec {
+  const char* name;
+  double flops, bytes;
+  size_t ev;
+};
+struct ProfStat {
+  int64_t launches = 0;
+  double ms = 0, flops = 0, bytes = 0;
+};
+
 struct EncLayer {
   bf16 *wqkv = nullptr, *wo = nullptr, *wi = nullptr, *wo2 = nullptr;
   float *attn_norm = nullptr, *mlp_norm = nullptr;
@@ -223,6 +233,14 @@ struct s1c_backend {
       "scorer_logits";
   std::string last_error;
   int64_t launches = 0;
+  cudaStream_t own_stream = nullptr;
+
+  // per-launch profiling (s1c_profile)
+  bool prof_on = false;
+  std::vector<cudaEvent_t> ev_pool;
+  size_t ev_used = 0;
+  std::vector<ProfRec> prof_pending;
+  std::map<std::string, ProfStat> prof_stats;
 
   // config
   int V = 0, d = 0, L = 0, H = 0, I = 0, Ipad = 0, F = 0, S = 0, n_head = 0, window = 64, max_pos = 0;
@@ -260,12 +278,14 @@ struct s1c_backend {
 
   ~s1c_backend() {
     if (stream) cudaStreamSynchronize(stream);
+    if (own_stream) cudaStreamSynchronize(own_stream);
+    for (cudaEvent_t e : ev_pool) cudaEventDestroy(e);
     for (void* p : allocs) cudaFree(p);
     if (d_status) cudaFree(d_status);
     if (h_status) cudaFreeHost(h_status);
     if (meta_host) cudaFreeHost(meta_host);
     if (h_out) cudaFreeHost(h_out);
-    if (stream) cudaStreamDestroy(stream);
+    if (own_stream) cudaStreamDestroy(own_stream);
   }
 
   template <class T>
@@ -497,6 +517,7 @@ void build(s1c_backend& B, const s1c_model_desc& D, const s1c_tensor* tensors, i
 
 struct HostMeta {
   int n = 0, kmax = 0, T = 0, R = 0, M = 0;  // rows, kmax, tokens, scorer rows n(1+kmax), markers n*kmax
+  double pairs_global = 0, pairs_local = 0, pairs_rows = 0;  // attended (query, key) pairs per head-set
   std::vector<int> cu, srows, mrows, prows, mcount;
   std::vector<uint32_t> qtype;
   std::vector<int4> items_full, items_rows;
@@ -523,7 +544,7 @@ void validate_varlen(const s1c_backend& B, const s1c_varlen& in) {
   }
 }
 
-HostMeta make_meta(const s1c_varlen& in) {
+HostMeta make_meta(const s1c_varlen& in, int window) {
   HostMeta m;
   m.n = in.n;
   m.kmax = in.kmax;
@@ -545,6 +566,9 @@ HostMeta make_meta(const s1c_varlen& in) {
       m.mrows[r * in.kmax + k] = r * (1 + in.kmax) + 1 + k;
     }
     const int len = m.cu[r + 1] - base;
+    m.pairs_global += (double)len * len;
+    m.pairs_rows += (double)(1 + in.kmax) * len;
+    for (int i = 0; i < len; ++i) m.pairs_local += std::min(i, window) + std::min(len - 1 - i, window) + 1;
     for (int q = 0; q < len; q += ATT_BQ) m.items_full.push_back(make_int4(r, base + q, std::min(ATT_BQ, len - q), 0));
     const int rows = 1 + in.kmax;
     for (int q = 0; q < rows; q += ATT_BQ)
@@ -618,11 +642,45 @@ DevMeta upload_meta(s1c_backend& B, const HostMeta& m, const uint32_t* host_ids)
   return dm;
 }
 
-template <int D>
-void run_rowwise_embed(s1c_backend& B, const uint32_t* ids, int T) {
-  embed_ln_kernel<D><<<(T + 7) / 8, 256, 0, B.stream>>>(ids, T, B.tok_emb, B.V, B.emb_norm, B.eps, B.h.as<float>(),
-                                                        B.x.as<bf16>(), B.d_status);
+// Per-launch CUDA-event timing (s1c_profile): every launch of a forward is bracketed by two
+// events on the forward's stream and attributed to a named kernel with its algorithmic FLOPs
+// and bytes; the totals are read back after the forward's final synchronisation.
+void prof_collect(s1c_backend& B) {
+  for (const auto& r : B.prof_pending) {
+    float ms = 0.f;
+    CK(cudaEventElapsedTime(&ms, B.ev_pool[r.ev], B.ev_pool[r.ev + 1]));
+    ProfStat& st = B.prof_stats[r.name];
+    st.launches += 1;
+    st.ms += ms;
+    st.flops += r.flops;
+    st.bytes += r.bytes;
+  }
+  B.prof_pending.clear();
+  B.ev_used = 0;
+}
+
+template <class F>
+void launch(s1c_backend& B, int64_t& nl, const char* name, double flops, double bytes, F&& f) {
+  size_t ev = 0;
+  if (B.prof_on) {
+    if (B.ev_used + 2 > B.ev_pool.size()) {
+      for (int i = 0; i < 64; ++i) {
+        cudaEvent_t e;
+        CK(cudaEventCreate(&e));
+        B.ev_pool.push_back(e);
+      }
+    }
+    ev = B.ev_used;
+    B.ev_used += 2;
+    CK(cudaEventRecord(B.ev_pool[ev], B.stream));
+  }
+  f();
   CK(cudaGetLastError());
+  if (B.prof_on) {
+    CK(cudaEventRecord(B.ev_pool[ev + 1], B.stream));
+    B.prof_pending.push_back(ProfRec{name, flops, bytes, ev});
+  }
+  ++nl;
 }
 
 template <int D>
@@ -630,6 +688,7 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
                  float* d_pooled, float* d_hidden) {
   cudaStream_t st = B.stream;
   const int T = m.T, d = B.d, nsm = B.num_sms;
+  const double Td = (double)T * d;
   int64_t nl = 0;
   int* pos = B.tok.as<int>();
   int* trow = pos + B.cap_T;
@@ -641,69 +700,81 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
   bf16* act = B.act.as<bf16>();
   const float scale_log2 = (1.0f / 8.0f) * 1.4426950408889634f;  // 1/sqrt(64) * log2(e)
 
-  prep_tokens_kernel<<<(T + 255) / 256, 256, 0, st>>>(dm.cu, m.n, T, pos, trow);
-  CK(cudaGetLastError());
-  run_rowwise_embed<D>(B, d_ids, T);
-  nl += 2;
+  launch(B, nl, "prep_tokens", 0, 8.0 * T, [&] {
+    prep_tokens_kernel<<<(T + 255) / 256, 256, 0, st>>>(dm.cu, m.n, T, pos, trow);
+  });
+  launch(B, nl, "embed_ln", 0, 8.0 * Td, [&] {
+    embed_ln_kernel<D><<<(T + 7) / 8, 256, 0, st>>>(d_ids, T, B.tok_emb, B.V, B.emb_norm, B.eps, h, x, B.d_status);
+  });
 
-  auto attn = [&](const bf16* q, const bf16* k, const bf16* v, bf16* o, int qs, int ks, int vs, int os,
-                  const int4* items, int n_items, int window) {
+  auto attn = [&](const char* name, const bf16* q, const bf16* k, const bf16* v, bf16* o, int qs, int ks, int vs,
+                  int os, const int4* items, int n_items, int window, double pairs) {
     if (n_items == 0) return;
     AttnArgs a{q, k, v, o, qs, ks, vs, os, dm.cu, items, window, scale_log2};
-    attention_varlen_kernel<<<dim3(n_items, d / 64), ATT_THREADS, 0, st>>>(a);
-    CK(cudaGetLastError());
-    ++nl;
+    launch(B, nl, name, 4.0 * d * pairs, 0, [&] {
+      attention_varlen_kernel<<<dim3(n_items, d / 64), ATT_THREADS, 0, st>>>(a);
+    });
   };
   auto gemm_args = [&](int M, int N, int K, void* out, int ldo) {
     GemmArgs a{};
     a.M = M; a.N = N; a.K = K; a.out = out; a.ldo = ldo; a.status = B.d_status;
     return a;
   };
+  auto ln = [&](const char* name, const float* in, const int* gather, int rows, const float* w, const float* b,
+                float eps, bf16* out) {
+    launch(B, nl, name, 0, (double)rows * d * 6.0, [&] { launch_ln<D>(in, gather, rows, w, b, eps, out, st); });
+  };
+  const double fl = 2.0 * T;  // GEMM FLOPs per (output column x reduction element)
 
   for (int i = 0; i < B.L; ++i) {
     const EncLayer& l = B.layers[i];
-    if (i > 0) { launch_ln<D>(h, nullptr, T, l.attn_norm, nullptr, B.eps, x, st); ++nl; }
+    if (i > 0) ln("ln_attn", h, nullptr, T, l.attn_norm, nullptr, B.eps, x);
     GemmArgs g = gemm_args(T, 3 * d, d, qkv, 3 * d);
     g.pos = pos;
     g.rope_cs = B.rope_cs[l.local ? 1 : 0];
     g.rope_cols = 2 * d;
-    launch_gemm<EPI_ROPE>(B.tm_x, l.tm_wqkv, g, nsm, st); ++nl;
-    attn(qkv, qkv + d, qkv + 2 * d, att, 3 * d, 3 * d, 3 * d, d, dm.items_full, (int)m.items_full.size(),
-         l.local ? B.window : -1);
-    launch_gemm<EPI_RESID>(B.tm_att, l.tm_wo, gemm_args(T, d, d, h, d), nsm, st); ++nl;
-    launch_ln<D>(h, nullptr, T, l.mlp_norm, nullptr, B.eps, x, st); ++nl;
+    launch(B, nl, "gemm_qkv_rope", fl * 3 * d * d, 0, [&] { launch_gemm<EPI_ROPE>(B.tm_x, l.tm_wqkv, g, nsm, st); });
+    attn(l.local ? "attn_local" : "attn_global", qkv, qkv + d, qkv + 2 * d, att, 3 * d, 3 * d, 3 * d, d,
+         dm.items_full, (int)m.items_full.size(), l.local ? B.window : -1, l.local ? m.pairs_local : m.pairs_global);
+    GemmArgs go = gemm_args(T, d, d, h, d);
+    launch(B, nl, "gemm_wo_resid", fl * d * d, 0, [&] { launch_gemm<EPI_RESID>(B.tm_att, l.tm_wo, go, nsm, st); });
+    ln("ln_mlp", h, nullptr, T, l.mlp_norm, nullptr, B.eps, x);
     GemmArgs gi = gemm_args(T, B.Ipad, d, act, B.I);
     gi.out_cols = B.I;
-    launch_gemm<EPI_GEGLU>(B.tm_x, l.tm_wi, gi, nsm, st); ++nl;
-    launch_gemm<EPI_RESID>(B.tm_act_i, l.tm_wo2, gemm_args(T, d, B.I, h, d), nsm, st); ++nl;
+    launch(B, nl, "gemm_wi_geglu", fl * 2 * B.I * d, 0, [&] { launch_gemm<EPI_GEGLU>(B.tm_x, l.tm_wi, gi, nsm, st); });
+    GemmArgs g2 = gemm_args(T, d, B.I, h, d);
+    launch(B, nl, "gemm_wo2_resid", fl * B.I * d, 0,
+           [&] { launch_gemm<EPI_RESID>(B.tm_act_i, l.tm_wo2, g2, nsm, st); });
   }
 
   // final_norm, + type embedding, head layer 0's norm1
-  final_to_head_kernel<D><<<(T + 7) / 8, 256, 0, st>>>(h, T, B.final_norm, B.eps, d_hidden, trow, dm.qtype,
-                                                       B.type_emb, B.head[0].n1w, B.head[0].n1b, h2, x);
-  CK(cudaGetLastError());
-  ++nl;
+  launch(B, nl, "final_to_head", 0, Td * (4 + 4 + 2 + (d_hidden ? 4 : 0)), [&] {
+    final_to_head_kernel<D><<<(T + 7) / 8, 256, 0, st>>>(h, T, B.final_norm, B.eps, d_hidden, trow, dm.qtype,
+                                                         B.type_emb, B.head[0].n1w, B.head[0].n1b, h2, x);
+  });
 
   // full head layers (all but the last)
   for (int j = 0; j + 1 < B.n_head; ++j) {
     const HeadLayer& hl = B.head[j];
     GemmArgs g = gemm_args(T, 3 * d, d, qkv, 3 * d);
     g.bias = hl.in_b;
-    launch_gemm<EPI_STORE>(B.tm_x, hl.tm_in, g, nsm, st); ++nl;
-    attn(qkv, qkv + d, qkv + 2 * d, att, 3 * d, 3 * d, 3 * d, d, dm.items_full, (int)m.items_full.size(), -1);
+    launch(B, nl, "head_gemm_in", fl * 3 * d * d, 0, [&] { launch_gemm<EPI_STORE>(B.tm_x, hl.tm_in, g, nsm, st); });
+    attn("head_attn", qkv, qkv + d, qkv + 2 * d, att, 3 * d, 3 * d, 3 * d, d, dm.items_full,
+         (int)m.items_full.size(), -1, m.pairs_global);
     GemmArgs go = gemm_args(T, d, d, h2, d);
     go.bias = hl.out_b;
-    launch_gemm<EPI_RESID>(B.tm_att, hl.tm_out, go, nsm, st); ++nl;
-    launch_ln<D>(h2, nullptr, T, hl.n2w, hl.n2b, 1e-5f, x, st); ++nl;
+    launch(B, nl, "head_gemm_out", fl * d * d, 0, [&] { launch_gemm<EPI_RESID>(B.tm_att, hl.tm_out, go, nsm, st); });
+    ln("head_ln", h2, nullptr, T, hl.n2w, hl.n2b, 1e-5f, x);
     GemmArgs g1 = gemm_args(T, B.F, d, act, B.F);
     g1.bias = hl.l1_b;
     g1.act = ACT_RELU;
-    launch_gemm<EPI_STORE>(B.tm_x, hl.tm_l1, g1, nsm, st); ++nl;
+    launch(B, nl, "head_gemm_l1", fl * B.F * d, 0, [&] { launch_gemm<EPI_STORE>(B.tm_x, hl.tm_l1, g1, nsm, st); });
     GemmArgs g2 = gemm_args(T, d, B.F, h2, d);
     g2.bias = hl.l2_b;
-    launch_gemm<EPI_RESID>(B.tm_act_f, hl.tm_l2, g2, nsm, st); ++nl;
+    launch(B, nl, "head_gemm_l2", fl * B.F * d, 0,
+           [&] { launch_gemm<EPI_RESID>(B.tm_act_f, hl.tm_l2, g2, nsm, st); });
     const HeadLayer& nx = B.head[j + 1];
-    launch_ln<D>(h2, nullptr, T, nx.n1w, nx.n1b, 1e-5f, x, st); ++nl;
+    ln("head_ln", h2, nullptr, T, nx.n1w, nx.n1b, 1e-5f, x);
   }
 
   // last head layer, pruned to the scorer's rows: keys/values from every token, the rest at
@@ -711,48 +782,57 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
   {
     const HeadLayer& hl = B.head[B.n_head - 1];
     const int R = m.R;
+    const double flr = 2.0 * R;
     bf16* kv = qkv;  // [T, 2d]
     GemmArgs gkv = gemm_args(T, 2 * d, d, kv, 2 * d);
     gkv.bias = hl.in_b + d;
-    launch_gemm<EPI_STORE>(B.tm_x, hl.tm_in_kv, gkv, nsm, st); ++nl;
-    gather_rows_bf16_kernel<<<R, 128, 0, st>>>(x, dm.srows, R, d, B.xs.as<bf16>()); ++nl;
-    gather_rows_f32_kernel<<<R, 256, 0, st>>>(h2, dm.srows, R, d, B.hs.as<float>()); ++nl;
-    CK(cudaGetLastError());
+    launch(B, nl, "head_gemm_kv", fl * 2 * d * d, 0,
+           [&] { launch_gemm<EPI_STORE>(B.tm_x, hl.tm_in_kv, gkv, nsm, st); });
+    launch(B, nl, "gather_rows", 0, (double)R * d * 4, [&] {
+      gather_rows_bf16_kernel<<<R, 128, 0, st>>>(x, dm.srows, R, d, B.xs.as<bf16>());
+    });
+    launch(B, nl, "gather_rows", 0, (double)R * d * 8, [&] {
+      gather_rows_f32_kernel<<<R, 256, 0, st>>>(h2, dm.srows, R, d, B.hs.as<float>());
+    });
     GemmArgs gq = gemm_args(R, d, d, B.qs.p, d);
     gq.bias = hl.in_b;
-    launch_gemm<EPI_STORE>(B.tm_xs, hl.tm_in_q, gq, nsm, st); ++nl;
-    attn(B.qs.as<bf16>(), kv, kv + d, B.atts.as<bf16>(), d, 2 * d, 2 * d, d, dm.items_rows,
-         (int)m.items_rows.size(), -1);
+    launch(B, nl, "head_rows_gemm", flr * d * d, 0, [&] { launch_gemm<EPI_STORE>(B.tm_xs, hl.tm_in_q, gq, nsm, st); });
+    attn("head_rows_attn", B.qs.as<bf16>(), kv, kv + d, B.atts.as<bf16>(), d, 2 * d, 2 * d, d, dm.items_rows,
+         (int)m.items_rows.size(), -1, m.pairs_rows);
     GemmArgs go = gemm_args(R, d, d, B.hs.p, d);
     go.bias = hl.out_b;
-    launch_gemm<EPI_RESID>(B.tm_atts, hl.tm_out, go, nsm, st); ++nl;
-    launch_ln<D>(B.hs.as<float>(), nullptr, R, hl.n2w, hl.n2b, 1e-5f, B.xs.as<bf16>(), st); ++nl;
+    launch(B, nl, "head_rows_gemm", flr * d * d, 0,
+           [&] { launch_gemm<EPI_RESID>(B.tm_atts, hl.tm_out, go, nsm, st); });
+    ln("head_ln", B.hs.as<float>(), nullptr, R, hl.n2w, hl.n2b, 1e-5f, B.xs.as<bf16>());
     GemmArgs g1 = gemm_args(R, B.F, d, B.fs.p, B.F);
     g1.bias = hl.l1_b;
     g1.act = ACT_RELU;
-    launch_gemm<EPI_STORE>(B.tm_xs, hl.tm_l1, g1, nsm, st); ++nl;
+    launch(B, nl, "head_rows_gemm", flr * B.F * d, 0,
+           [&] { launch_gemm<EPI_STORE>(B.tm_xs, hl.tm_l1, g1, nsm, st); });
     GemmArgs g2 = gemm_args(R, d, B.F, B.hs.p, d);
     g2.bias = hl.l2_b;
-    launch_gemm<EPI_RESID>(B.tm_fs, hl.tm_l2, g2, nsm, st); ++nl;
+    launch(B, nl, "head_rows_gemm", flr * B.F * d, 0,
+           [&] { launch_gemm<EPI_RESID>(B.tm_fs, hl.tm_l2, g2, nsm, st); });
   }
 
   // scorer at the marker slots, pooled at position 0
   if (m.M > 0) {
-    launch_ln<D>(B.hs.as<float>(), dm.mrows, m.M, B.sc_nw, B.sc_nb, 1e-5f, B.xm.as<bf16>(), st); ++nl;
+    ln("scorer_ln", B.hs.as<float>(), dm.mrows, m.M, B.sc_nw, B.sc_nb, 1e-5f, B.xm.as<bf16>());
     GemmArgs gs = gemm_args(m.M, B.S, d, B.sh.p, B.S);
     gs.bias = B.sc_b1;
     gs.act = ACT_GELU;
     gs.out_f32 = 1;
-    launch_gemm<EPI_STORE>(B.tm_xm, B.tm_sc1, gs, nsm, st); ++nl;
-    scorer_logits_kernel<<<(m.M + 7) / 8, 256, 0, st>>>(B.sh.as<float>(), m.M, B.S, B.sc_w3, B.sc_b3, dm.mcount,
-                                                        m.kmax, d_logits);
-    CK(cudaGetLastError());
-    ++nl;
+    launch(B, nl, "scorer_gemm", 2.0 * m.M * B.S * d, 0,
+           [&] { launch_gemm<EPI_STORE>(B.tm_xm, B.tm_sc1, gs, nsm, st); });
+    launch(B, nl, "scorer_logits", 2.0 * m.M * B.S, 0, [&] {
+      scorer_logits_kernel<<<(m.M + 7) / 8, 256, 0, st>>>(B.sh.as<float>(), m.M, B.S, B.sc_w3, B.sc_b3, dm.mcount,
+                                                          m.kmax, d_logits);
+    });
   }
   if (m.n > 0) {
-    gather_rows_f32_kernel<<<m.n, 256, 0, st>>>(B.hs.as<float>(), dm.prows, m.n, d, d_pooled);
-    CK(cudaGetLastError());
-    ++nl;
+    launch(B, nl, "gather_rows", 0, (double)m.n * d * 8, [&] {
+      gather_rows_f32_kernel<<<m.n, 256, 0, st>>>(B.hs.as<float>(), dm.prows, m.n, d, d_pooled);
+    });
   }
   B.launches = nl;
 }
@@ -770,6 +850,7 @@ void forward_enqueue(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const
 void check_status(s1c_backend& B) {
   CK(cudaMemcpyAsync(B.h_status, B.d_status, sizeof(int), cudaMemcpyDeviceToHost, B.stream));
   CK(cudaStreamSynchronize(B.stream));
+  if (!B.prof_pending.empty()) prof_collect(B);
   if (*B.h_status != 0) {
     const int code = *B.h_status;
     CK(cudaMemsetAsync(B.d_status, 0, sizeof(int), B.stream));
@@ -786,7 +867,7 @@ void forward_host(s1c_backend& B, const s1c_varlen& in, float* logits, float* po
   const int T = in.cu_seqlens[in.n];
   for (int t = 0; t < T; ++t)
     if (in.ids[t] >= (uint32_t)B.V) throw S1cError(S1C_ERR_ARG, "token " + std::to_string(t) + ": id outside the vocabulary");
-  HostMeta m = make_meta(in);
+  HostMeta m = make_meta(in, B.window);
   ensure_capacity(B, m.T, m.R);
   const size_t nl = (size_t)m.M, np = (size_t)m.n * B.d, nh = hidden ? (size_t)m.T * B.d : 0;
   B.out_stage.ensure((nl + np + nh + 64) * 4);
@@ -896,7 +977,8 @@ s1c_status s1c_create(const s1c_model_desc* desc, const s1c_tensor* tensors, int
       throw S1cError(S1C_ERR_UNSUPPORTED, std::string("the kernels are built for sm_100a; device is ") + prop.name);
     b->device = device;
     b->num_sms = prop.multiProcessorCount;
-    CK(cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking));
+    CK(cudaStreamCreateWithFlags(&b->own_stream, cudaStreamNonBlocking));
+    b->stream = b->own_stream;
     set_all_gemm_smem();
     build(*b, *desc, tensors, n_tensors);
     CK(cudaDeviceSynchronize());
@@ -923,6 +1005,39 @@ const char* s1c_name(const s1c_backend* b) { return b ? b->name.c_str() : ""; }
 const char* s1c_active_kernels(const s1c_backend* b) { return b ? b->kernels.c_str() : ""; }
 size_t s1c_padded_len(const s1c_backend*, size_t len, size_t) { return len; }
 int64_t s1c_last_launch_count(const s1c_backend* b) { return b ? b->launches : 0; }
+
+s1c_status s1c_set_stream(s1c_backend* b, void* stream) {
+  return guarded(b, [&] {
+    CK(cudaStreamSynchronize(b->stream));
+    b->stream = stream ? static_cast<cudaStream_t>(stream) : b->own_stream;
+  });
+}
+
+s1c_status s1c_profile(s1c_backend* b, int32_t on) {
+  return guarded(b, [&] {
+    b->prof_on = on != 0;
+    b->prof_stats.clear();
+    b->prof_pending.clear();
+    b->ev_used = 0;
+  });
+}
+
+size_t s1c_profile_report(const s1c_backend* b, char* buf, size_t cap) {
+  if (!b) return 0;
+  std::string out;
+  char line[256];
+  for (const auto& kv : b->prof_stats) {
+    std::snprintf(line, sizeof line, "%s %lld %.6f %.6e %.6e\n", kv.first.c_str(), (long long)kv.second.launches,
+                  kv.second.ms, kv.second.flops, kv.second.bytes);
+    out += line;
+  }
+  if (buf && cap) {
+    const size_t n = std::min(cap - 1, out.size());
+    std::memcpy(buf, out.data(), n);
+    buf[n] = 0;
+  }
+  return out.size() + 1;
+}
 
 s1c_status s1c_warmup(s1c_backend* b) {
   return guarded(b, [&] {
@@ -979,7 +1094,7 @@ s1c_status s1c_forward_device(s1c_backend* b, const s1c_varlen* in, const uint32
       throw S1cError(S1C_ERR_ARG, "null argument");
     validate_varlen(*b, *in);
     if (in->n == 0) return;
-    HostMeta m = make_meta(*in);
+    HostMeta m = make_meta(*in, b->window);
     ensure_capacity(*b, m.T, m.R);
     DevMeta dm = upload_meta(*b, m, nullptr);
     forward_enqueue(*b, m, dm, d_ids, d_logits, d_pooled, d_hidden);
