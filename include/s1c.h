@@ -133,6 +133,15 @@ S1C_API s1c_status s1c_forward_varlen(s1c_backend* b, const s1c_varlen* in, floa
 S1C_API s1c_status s1c_forward_device(s1c_backend* b, const s1c_varlen* in, const uint32_t* d_ids, float* d_logits,
                               float* d_pooled, float* d_hidden);
 
+/* As s1c_forward_device, but returns once the work is enqueued on the handle's stream: several
+ * forwards can be in flight, and the host prepares the next batch while the GPU runs. Inputs and
+ * outputs must stay valid until s1c_synchronize returns; the outputs of consecutive calls must not
+ * alias unless the caller orders them. Device-side errors surface at s1c_synchronize. */
+S1C_API s1c_status s1c_forward_device_async(s1c_backend* b, const s1c_varlen* in, const uint32_t* d_ids,
+                                            float* d_logits, float* d_pooled, float* d_hidden);
+/* Wait for every forward enqueued on this handle and report any device-side error. */
+S1C_API s1c_status s1c_synchronize(s1c_backend* b);
+
 /* `Backend::encoder_hidden` (backend.rs:128-132; lib.rs:1869-1878): [n*len*hidden] f32 in the
  * padded layout. Real positions hold the encoder's final hidden state; padding positions are
  * never computed by the varlen path and are written as 0. */
@@ -148,10 +157,12 @@ S1C_API s1c_status s1c_gemm(int32_t epi, const void* d_A, const void* d_B, void*
                     int32_t rope_cols, int32_t out_cols, void* stream);
 
 /* Isolated varlen attention on device pointers (head_dim 64): q/k/v/o with row pitches, host
- * cu_seqlens [n+1]; window < 0 = global. Blocks until done. */
+ * cu_seqlens [n+1]; window < 0 = global. impl 0 = tcgen05 kernel (v must lie in k's rows: same
+ * pitch, 64-aligned column offset), 1 = mma.sync kernel. Blocks until done. */
 S1C_API s1c_status s1c_attention(const void* d_q, const void* d_k, const void* d_v, void* d_o, int32_t q_stride,
-                         int32_t k_stride, int32_t v_stride, int32_t o_stride, int32_t heads,
-                         const int32_t* cu_seqlens, int32_t n, int32_t window, float scale, void* stream);
+                                 int32_t k_stride, int32_t v_stride, int32_t o_stride, int32_t heads,
+                                 const int32_t* cu_seqlens, int32_t n, int32_t window, float scale, int32_t impl,
+                                 void* stream);
 
 /* Run this handle's forwards on `stream` (a cudaStream_t of the handle's device); NULL returns
  * to the handle's own stream. Lets a caller order forwards with its own work and time them with

@@ -92,9 +92,11 @@ def lib() -> C.CDLL:
         "s1c_forward_padded": (I32, [P, C.POINTER(CBatch), P, P]),
         "s1c_forward_varlen": (I32, [P, C.POINTER(CVarlen), P, P, P]),
         "s1c_forward_device": (I32, [P, C.POINTER(CVarlen), P, P, P, P]),
+        "s1c_forward_device_async": (I32, [P, C.POINTER(CVarlen), P, P, P, P]),
+        "s1c_synchronize": (I32, [P]),
         "s1c_encoder_hidden": (I32, [P, C.POINTER(CBatch), P]),
         "s1c_gemm": (I32, [I32, P, P, P, I32, I32, I32, P, I32, I32, P, F32, I32, I32, P]),
-        "s1c_attention": (I32, [P, P, P, P, I32, I32, I32, I32, I32, P, I32, I32, F32, P]),
+        "s1c_attention": (I32, [P, P, P, P, I32, I32, I32, I32, I32, P, I32, I32, F32, I32, P]),
         "s1c_last_launch_count": (I64, [P]),
         "s1c_set_stream": (I32, [P, P]),
         "s1c_profile": (I32, [P, I32]),
@@ -245,6 +247,15 @@ class CudaBackend:
         cv, keep = self._cvarlen(v)
         self._check(lib().s1c_forward_device(self._h, C.byref(cv), d_ids, d_logits, d_pooled, d_hidden or None))
 
+    def forward_device_async(self, v: Varlen, d_ids: int, d_logits: int, d_pooled: int, d_hidden: int = 0) -> None:
+        """Enqueue a forward without waiting; ``synchronize()`` waits and reports device errors."""
+        cv, keep = self._cvarlen(v)
+        self._check(lib().s1c_forward_device_async(self._h, C.byref(cv), d_ids, d_logits, d_pooled,
+                                                   d_hidden or None))
+
+    def synchronize(self) -> None:
+        self._check(lib().s1c_synchronize(self._h))
+
     def last_launch_count(self) -> int:
         return int(lib().s1c_last_launch_count(self._h))
 
@@ -302,11 +313,13 @@ def gemm(epi: int, a_ptr: int, b_ptr: int, out_ptr: int, M: int, N: int, K: int,
 
 
 def attention(q_ptr: int, k_ptr: int, v_ptr: int, o_ptr: int, q_stride: int, k_stride: int, v_stride: int,
-              o_stride: int, heads: int, cu_seqlens: np.ndarray, window: int, scale: float, stream: int = 0) -> None:
+              o_stride: int, heads: int, cu_seqlens: np.ndarray, window: int, scale: float, impl: int = 0,
+              stream: int = 0) -> None:
+    """impl 0: tcgen05 kernel; 1: mma.sync kernel."""
     L = lib()
     cu = np.ascontiguousarray(cu_seqlens, dtype=np.int32)
     rc = L.s1c_attention(q_ptr, k_ptr, v_ptr, o_ptr, q_stride, k_stride, v_stride, o_stride, heads, _ptr(cu),
-                         len(cu) - 1, window, scale, stream or None)
+                         len(cu) - 1, window, scale, impl, stream or None)
     if rc != S1C_OK:
         _raise(rc, L.s1c_create_error().decode())
 

@@ -104,6 +104,33 @@ S1C_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code, vo
   }
 }
 
+// Warp-collective bounded wait: every lane polls, the warp leaves together.
+S1C_DEV bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int* status, int code, volatile int* abort) {
+  const uint32_t a = smem_u32(bar);
+  const int lane = threadIdx.x & 31;
+  uint64_t t0 = 0;
+  for (uint32_t it = 0;; ++it) {
+    const bool done = mbar_try_wait(a, parity);
+    if (__all_sync(0xffffffffu, done)) return true;
+    if ((it & 63u) == 63u) {
+      int give_up = 0;
+      if (lane == 0) {
+        const uint64_t now = globaltimer();
+        if (t0 == 0) t0 = now;
+        if ((abort && *abort) || now - t0 > S1C_WAIT_BUDGET_NS) give_up = 1;
+      }
+      give_up = __shfl_sync(0xffffffffu, give_up, 0);
+      if (give_up) {
+        if (lane == 0) {
+          if (!(abort && *abort)) report(status, code);
+          if (abort) *abort = 1;
+        }
+        return false;
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------------------
 // TMA: 2D tiled bulk tensor load into this CTA's shared memory, completing on an mbarrier.
 // (No cluster or multi-destination forms are used anywhere in this library.)

@@ -40,7 +40,7 @@ struct GemmArgs {
   int act;                // EPI_STORE activation
   int out_f32;            // EPI_STORE: fp32 output
   const int* pos;         // EPI_ROPE: position of each row inside its sequence
-  const float2* rope_cs;  // EPI_ROPE: [max_pos][32] (cos, sin) of the layer's theta
+  const float* inv_freq;  // EPI_ROPE: [32] inverse frequencies of the layer's theta
   int rope_cols;          // EPI_ROPE: columns [0, rope_cols) hold q and k heads
   int out_cols;           // EPI_GEGLU: output width I
   int* status;
@@ -70,37 +70,45 @@ S1C_DEV void store_bf16x32(__nv_bfloat16* dst, const float (&v)[32]) {
   }
 }
 
-// Warp-collective bounded wait: every lane polls, the warp leaves together.
-S1C_DEV bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int* status, int code, volatile int* abort) {
-  const uint32_t a = smem_u32(bar);
-  const int lane = threadIdx.x & 31;
-  uint64_t t0 = 0;
-  for (uint32_t it = 0;; ++it) {
-    const bool done = mbar_try_wait(a, parity);
-    if (__all_sync(0xffffffffu, done)) return true;
-    if ((it & 63u) == 63u) {
-      int give_up = 0;
-      if (lane == 0) {
-        const uint64_t now = globaltimer();
-        if (t0 == 0) t0 = now;
-        if ((abort && *abort) || now - t0 > S1C_WAIT_BUDGET_NS) give_up = 1;
-      }
-      give_up = __shfl_sync(0xffffffffu, give_up, 0);
-      if (give_up) {
-        if (lane == 0) {
-          if (!(abort && *abort)) report(status, code);
-          if (abort) *abort = 1;
-        }
-        return false;
-      }
-    }
-  }
-}
-
 template <int BN, int EPI>
 __device__ __forceinline__ void gemm_epilogue_tile(const GemmArgs& args, uint32_t t, int row, int m_ok, int n0,
                                                    int n_block) {
-  if constexpr (EPI == EPI_STORE || EPI == EPI_RESID) {
+  if constexpr (EPI == EPI_RESID) {
+    // fp32 residual read-modify-write, two 32-column chunks at a time: the residual loads of a
+    // pair are issued before the accumulator loads so their latency overlaps (the rows were
+    // prefetched into L2 while the mainloop ran).
+    float* rbase = static_cast<float*>(args.out) + (size_t)row * args.ldo + n0;
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; c += 2) {
+      const int col = n0 + c * 32;
+      const bool ok = m_ok && col < args.N;
+      float4 r[16];
+      if (ok) {
+        const float4* p = reinterpret_cast<const float4*>(rbase + c * 32);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) r[i] = p[i];
+      }
+      float v[64];
+      tmem_ld32(t + c * 32, *reinterpret_cast<float(*)[32]>(v));
+      tmem_ld32(t + c * 32 + 32, *reinterpret_cast<float(*)[32]>(v + 32));
+      if (!ok) continue;
+      if (args.bias) {
+        const float4* b4 = reinterpret_cast<const float4*>(args.bias + col);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float4 b = __ldg(b4 + i);
+          v[4 * i] += b.x; v[4 * i + 1] += b.y; v[4 * i + 2] += b.z; v[4 * i + 3] += b.w;
+        }
+      }
+      float4* p = reinterpret_cast<float4*>(rbase + c * 32);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        float4 x = r[i];
+        x.x += v[4 * i]; x.y += v[4 * i + 1]; x.z += v[4 * i + 2]; x.w += v[4 * i + 3];
+        p[i] = x;
+      }
+    }
+  } else if constexpr (EPI == EPI_STORE) {
 #pragma unroll 1
     for (int c = 0; c < BN / 32; ++c) {
       float v[32];
@@ -115,34 +123,32 @@ __device__ __forceinline__ void gemm_epilogue_tile(const GemmArgs& args, uint32_
           v[4 * i] += b.x; v[4 * i + 1] += b.y; v[4 * i + 2] += b.z; v[4 * i + 3] += b.w;
         }
       }
-      if constexpr (EPI == EPI_RESID) {
+      if (args.act == ACT_RELU) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.0f);
+      } else if (args.act == ACT_GELU) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
+      }
+      if (args.out_f32) {
         float4* p = reinterpret_cast<float4*>(static_cast<float*>(args.out) + (size_t)row * args.ldo + col);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          float4 r = p[i];
-          r.x += v[4 * i]; r.y += v[4 * i + 1]; r.z += v[4 * i + 2]; r.w += v[4 * i + 3];
-          p[i] = r;
-        }
+        for (int i = 0; i < 8; ++i) p[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
       } else {
-        if (args.act == ACT_RELU) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.0f);
-        } else if (args.act == ACT_GELU) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
-        }
-        if (args.out_f32) {
-          float4* p = reinterpret_cast<float4*>(static_cast<float*>(args.out) + (size_t)row * args.ldo + col);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) p[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-        } else {
-          store_bf16x32(static_cast<__nv_bfloat16*>(args.out) + (size_t)row * args.ldo + col, v);
-        }
+        store_bf16x32(static_cast<__nv_bfloat16*>(args.out) + (size_t)row * args.ldo + col, v);
       }
     }
   } else if constexpr (EPI == EPI_ROPE) {
-    const int p = m_ok ? __ldg(args.pos + row) : 0;
-    const float2* cs = args.rope_cs + (size_t)p * 32;
+    // Rotate-half RoPE of every 64-wide q/k head in the tile at this row's position: the angle is
+    // p * inv_freq[j] in fp32 (split_rope.metal:46-76) and its cos/sin are computed once per row
+    // and shared by the tile's heads.
+    const bool rope = n0 < args.rope_cols;  // uniform: q/k tiles never straddle the v columns
+    float cs[32], sn[32];
+    if (rope) {
+      const float p = m_ok ? (float)__ldg(args.pos + row) : 0.0f;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) sincosf(p * __ldg(args.inv_freq + j), &sn[j], &cs[j]);
+    }
 #pragma unroll 1
     for (int hh = 0; hh < BN / 64; ++hh) {
       float x1[32], x2[32];
@@ -150,13 +156,12 @@ __device__ __forceinline__ void gemm_epilogue_tile(const GemmArgs& args, uint32_
       tmem_ld32(t + hh * 64 + 32, x2);
       const int col = n0 + hh * 64;
       if (!m_ok || col >= args.N) continue;
-      if (col < args.rope_cols) {
+      if (rope) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
-          const float2 c = __ldg(cs + j);
           const float a = x1[j], b = x2[j];
-          x1[j] = a * c.x - b * c.y;
-          x2[j] = a * c.y + b * c.x;
+          x1[j] = a * cs[j] - b * sn[j];
+          x2[j] = a * sn[j] + b * cs[j];
         }
       }
       __nv_bfloat16* o = static_cast<__nv_bfloat16*>(args.out) + (size_t)row * args.ldo + col;
@@ -308,10 +313,19 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     int acc = 0;
     uint32_t aph = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      if (!mbar_wait_warp(&tfull[acc], aph, args.status, DEV_TIMEOUT_EPILOGUE, abort_flag)) break;
-      tc_fence_after();
       const int m0 = (tile / num_n) * BM, n_block = tile % num_n;
       const int row = m0 + quad * 32 + lane;
+      if constexpr (EPI == EPI_RESID) {
+        // Pull this row's residual span into L2 while the tile's MMAs run.
+        if (row < args.M) {
+          const char* rp = reinterpret_cast<const char*>(static_cast<const float*>(args.out) +
+                                                         (size_t)row * args.ldo + n_block * BN);
+          const int span = min(BN, args.N - n_block * BN) * 4;
+          for (int off = 0; off < span; off += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(rp + off));
+        }
+      }
+      if (!mbar_wait_warp(&tfull[acc], aph, args.status, DEV_TIMEOUT_EPILOGUE, abort_flag)) break;
+      tc_fence_after();
       const uint32_t t = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
       gemm_epilogue_tile<BN, EPI>(args, t, row, row < args.M, n_block * BN, n_block);
       tc_fence_before();

@@ -14,6 +14,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <memory>
@@ -24,6 +25,7 @@
 
 #include "../../include/s1c.h"
 #include "attention.cuh"
+#include "attention_tc.cuh"
 #include "gemm_sm100.cuh"
 #include "rowwise.cuh"
 
@@ -256,19 +258,31 @@ struct s1c_backend {
   float *sc_nw = nullptr, *sc_nb = nullptr, *sc_b1 = nullptr, *sc_w3 = nullptr, *sc_b3 = nullptr;
   bf16* sc_w1 = nullptr;
   CUtensorMap tm_sc1;
-  float2* rope_cs[2] = {nullptr, nullptr};  // 0 global theta, 1 local theta
+  float* inv_freq[2] = {nullptr, nullptr};  // 0 global theta, 1 local theta
 
   // activations (capacity in rows, multiples of 128)
+  bool attn_tc = true;  // tcgen05 attention (attention_tc.cuh); false: mma.sync (attention.cuh)
   int cap_T = 0, cap_R = 0;
   DevBuf h, x, qkv, att, act;          // [cap_T, ...]
   DevBuf h2;                           // head residual stream [cap_T, d] fp32
   DevBuf xs, qs, atts, hs, fs, xm, sh; // scorer rows [cap_R, ...]
   CUtensorMap tm_x, tm_att, tm_act_i, tm_act_f, tm_xs, tm_atts, tm_fs, tm_xm;
+  CUtensorMap tm_qkv_att, tm_kv_att, tm_qs_att;  // 128-row boxes for the tcgen05 attention
 
   // metadata
-  DevBuf meta;        // device arena
-  void* meta_host = nullptr;  // pinned staging
-  size_t meta_host_bytes = 0;
+  // Metadata staging ring: a forward's small host arrays go to a pinned slot and one H2D copy
+  // into that slot's device arena. A slot's host side is reused only after its copy has
+  // completed (event), so forwards can be enqueued back to back without a host sync.
+  struct MetaSlot {
+    void* host = nullptr;
+    size_t host_bytes = 0;
+    DevBuf dev;
+    cudaEvent_t copied = nullptr;
+    bool pending = false;
+  };
+  static constexpr int META_SLOTS = 4;
+  MetaSlot meta[META_SLOTS];
+  int meta_next = 0;
   DevBuf tok;         // pos [cap_T] + token_row [cap_T] int32
   int* d_status = nullptr;
   int* h_status = nullptr;
@@ -283,7 +297,10 @@ struct s1c_backend {
     for (void* p : allocs) cudaFree(p);
     if (d_status) cudaFree(d_status);
     if (h_status) cudaFreeHost(h_status);
-    if (meta_host) cudaFreeHost(meta_host);
+    for (auto& sl : meta) {
+      if (sl.host) cudaFreeHost(sl.host);
+      if (sl.copied) cudaEventDestroy(sl.copied);
+    }
     if (h_out) cudaFreeHost(h_out);
     if (own_stream) cudaStreamDestroy(own_stream);
   }
@@ -343,30 +360,24 @@ float* upload_vector(s1c_backend& B, const s1c_tensor& t, int64_t n, int64_t off
   return d;
 }
 
-// RoPE (cos, sin) table: inverse frequency exp2(-(i / 32) * log2(theta)) and angle p * inv_freq
-// in fp32 as the reference kernel computes them (split_rope.metal:46-76); cos/sin of that fp32
-// angle evaluated in double and rounded once. Returns a fresh device allocation.
-float2* make_rope_table_raw(float theta, int max_pos) {
-  std::vector<float2> t((size_t)max_pos * 32);
+// RoPE inverse frequencies exp2(-(i / 32) * log2(theta)), i = 0..31, in fp32 as the reference
+// kernel computes them (split_rope.metal:46-76). The GEMM epilogue forms the angle p * inv_freq
+// in fp32 and takes its cos/sin. Returns a fresh device allocation of 32 floats.
+float* make_inv_freq_raw(float theta) {
+  float t[32];
   const float lbase = std::log2(theta);
-  for (int i = 0; i < 32; ++i) {
-    const float inv = std::exp2(-((float)i / 32.0f) * lbase);
-    for (int p = 0; p < max_pos; ++p) {
-      const float ang = (float)p * inv;
-      t[(size_t)p * 32 + i] = make_float2((float)std::cos((double)ang), (float)std::sin((double)ang));
-    }
-  }
-  float2* d = nullptr;
-  CK(cudaMalloc(&d, t.size() * sizeof(float2)));
-  cudaError_t e = cudaMemcpy(d, t.data(), t.size() * sizeof(float2), cudaMemcpyHostToDevice);
+  for (int i = 0; i < 32; ++i) t[i] = std::exp2(-((float)i / 32.0f) * lbase);
+  float* d = nullptr;
+  CK(cudaMalloc(&d, sizeof t));
+  cudaError_t e = cudaMemcpy(d, t, sizeof t, cudaMemcpyHostToDevice);
   if (e != cudaSuccess) {
     cudaFree(d);
-    throw S1cError(S1C_ERR_CUDA, std::string("rope table upload: ") + cudaGetErrorString(e));
+    throw S1cError(S1C_ERR_CUDA, std::string("inv_freq upload: ") + cudaGetErrorString(e));
   }
   return d;
 }
-float2* make_rope_table(s1c_backend& B, float theta, int max_pos) {
-  float2* d = make_rope_table_raw(theta, max_pos);
+float* make_inv_freq(s1c_backend& B, float theta) {
+  float* d = make_inv_freq_raw(theta);
   B.allocs.push_back(d);
   return d;
 }
@@ -386,7 +397,14 @@ void ensure_capacity(s1c_backend& B, int T, int R) {
     B.act.ensure((size_t)cap * wide * 2);
     B.tok.ensure((size_t)cap * 2 * 4);
     B.cap_T = cap;
+    // Rows past a forward's token count are read (and discarded) by full tiles: keep them finite.
+    CK(cudaMemsetAsync(B.qkv.p, 0, B.qkv.bytes, B.stream));
+    CK(cudaMemsetAsync(B.x.p, 0, B.x.bytes, B.stream));
+    CK(cudaMemsetAsync(B.att.p, 0, B.att.bytes, B.stream));
+    CK(cudaMemsetAsync(B.act.p, 0, B.act.bytes, B.stream));
     B.tm_x = make_tmap(B.x.p, cap, B.d, B.d, GEMM_BM);
+    B.tm_qkv_att = make_tmap(B.qkv.p, cap, 3 * B.d, 3 * B.d, ATTC_BQ);
+    B.tm_kv_att = make_tmap(B.qkv.p, cap, 2 * B.d, 2 * B.d, ATTC_BK);
     B.tm_att = make_tmap(B.att.p, cap, B.d, B.d, GEMM_BM);
     B.tm_act_i = make_tmap(B.act.p, cap, B.I, B.I, GEMM_BM);
     B.tm_act_f = make_tmap(B.act.p, cap, B.F, B.F, GEMM_BM);
@@ -402,7 +420,10 @@ void ensure_capacity(s1c_backend& B, int T, int R) {
     B.xm.ensure((size_t)cap * B.d * 2);
     B.sh.ensure((size_t)cap * B.S * 4);
     B.cap_R = cap;
+    CK(cudaMemsetAsync(B.qs.p, 0, B.qs.bytes, B.stream));
+    CK(cudaMemsetAsync(B.xs.p, 0, B.xs.bytes, B.stream));
     B.tm_xs = make_tmap(B.xs.p, cap, B.d, B.d, GEMM_BM);
+    B.tm_qs_att = make_tmap(B.qs.p, cap, B.d, B.d, ATTC_BQ);
     B.tm_atts = make_tmap(B.atts.p, cap, B.d, B.d, GEMM_BM);
     B.tm_fs = make_tmap(B.fs.p, cap, B.F, B.F, GEMM_BM);
     B.tm_xm = make_tmap(B.xm.p, cap, B.d, B.d, GEMM_BM);
@@ -504,8 +525,8 @@ void build(s1c_backend& B, const s1c_model_desc& D, const s1c_tensor* tensors, i
   B.sc_b3 = upload_vector(B, tt.get("scorer.3.bias", {1}), 1);
   B.tm_sc1 = make_tmap(B.sc_w1, (B.S + 255) / 256 * 256, d, d, GEMM_BN);
 
-  B.rope_cs[0] = make_rope_table(B, D.global_rope_theta, B.max_pos);
-  B.rope_cs[1] = make_rope_table(B, D.local_rope_theta, B.max_pos);
+  B.inv_freq[0] = make_inv_freq(B, D.global_rope_theta);
+  B.inv_freq[1] = make_inv_freq(B, D.local_rope_theta);
   CK(cudaMalloc(&B.d_status, sizeof(int)));
   CK(cudaMemset(B.d_status, 0, sizeof(int)));
   CK(cudaMallocHost(&B.h_status, sizeof(int)));
@@ -544,7 +565,7 @@ void validate_varlen(const s1c_backend& B, const s1c_varlen& in) {
   }
 }
 
-HostMeta make_meta(const s1c_varlen& in, int window) {
+HostMeta make_meta(const s1c_varlen& in, int window, int qtile) {
   HostMeta m;
   m.n = in.n;
   m.kmax = in.kmax;
@@ -569,10 +590,10 @@ HostMeta make_meta(const s1c_varlen& in, int window) {
     m.pairs_global += (double)len * len;
     m.pairs_rows += (double)(1 + in.kmax) * len;
     for (int i = 0; i < len; ++i) m.pairs_local += std::min(i, window) + std::min(len - 1 - i, window) + 1;
-    for (int q = 0; q < len; q += ATT_BQ) m.items_full.push_back(make_int4(r, base + q, std::min(ATT_BQ, len - q), 0));
+    for (int q = 0; q < len; q += qtile) m.items_full.push_back(make_int4(r, base + q, std::min(qtile, len - q), 0));
     const int rows = 1 + in.kmax;
-    for (int q = 0; q < rows; q += ATT_BQ)
-      m.items_rows.push_back(make_int4(r, r * rows + q, std::min(ATT_BQ, rows - q), 1));
+    for (int q = 0; q < rows; q += qtile)
+      m.items_rows.push_back(make_int4(r, r * rows + q, std::min(qtile, rows - q), 1));
   }
   return m;
 }
@@ -613,22 +634,29 @@ DevMeta upload_meta(s1c_backend& B, const HostMeta& m, const uint32_t* host_ids)
     total += (parts[i].bytes + 255) / 256 * 256;
   }
   total = std::max<size_t>(total, 256);
-  if (total > B.meta_host_bytes) {
-    CK(cudaStreamSynchronize(B.stream));
-    if (B.meta_host) cudaFreeHost(B.meta_host);
-    B.meta_host = nullptr;
-    B.meta_host_bytes = 0;
-    CK(cudaMallocHost(&B.meta_host, total * 2));
-    B.meta_host_bytes = total * 2;
+  s1c_backend::MetaSlot& sl = B.meta[B.meta_next];
+  B.meta_next = (B.meta_next + 1) % s1c_backend::META_SLOTS;
+  if (!sl.copied) CK(cudaEventCreateWithFlags(&sl.copied, cudaEventDisableTiming));
+  if (sl.pending) CK(cudaEventSynchronize(sl.copied));  // the slot's previous copy has left the host buffer
+  sl.pending = false;
+  if (total > sl.host_bytes) {
+    if (sl.host) cudaFreeHost(sl.host);
+    sl.host = nullptr;
+    sl.host_bytes = 0;
+    CK(cudaMallocHost(&sl.host, total * 2));
+    sl.host_bytes = total * 2;
   }
-  // The staging buffer may still feed a copy of the previous forward.
-  CK(cudaStreamSynchronize(B.stream));
-  B.meta.ensure(B.meta_host_bytes);
-  char* hs = static_cast<char*>(B.meta_host);
+  if (total > sl.dev.bytes) {
+    CK(cudaStreamSynchronize(B.stream));  // kernels of earlier forwards may still read the arena
+    sl.dev.ensure(sl.host_bytes);
+  }
+  char* hs = static_cast<char*>(sl.host);
   for (size_t i = 0; i < parts.size(); ++i)
     if (parts[i].bytes) std::memcpy(hs + off[i], parts[i].src, parts[i].bytes);
-  CK(cudaMemcpyAsync(B.meta.p, B.meta_host, total, cudaMemcpyHostToDevice, B.stream));
-  char* dv = B.meta.as<char>();
+  CK(cudaMemcpyAsync(sl.dev.p, sl.host, total, cudaMemcpyHostToDevice, B.stream));
+  CK(cudaEventRecord(sl.copied, B.stream));
+  sl.pending = true;
+  char* dv = sl.dev.as<char>();
   DevMeta dm;
   dm.ids = reinterpret_cast<const uint32_t*>(dv + off[0]);
   dm.cu = reinterpret_cast<const int*>(dv + off[1]);
@@ -707,13 +735,25 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
     embed_ln_kernel<D><<<(T + 7) / 8, 256, 0, st>>>(d_ids, T, B.tok_emb, B.V, B.emb_norm, B.eps, h, x, B.d_status);
   });
 
-  auto attn = [&](const char* name, const bf16* q, const bf16* k, const bf16* v, bf16* o, int qs, int ks, int vs,
-                  int os, const int4* items, int n_items, int window, double pairs) {
+  // Attention over the items' query tiles: the tcgen05 kernel reads Q/K/V through TMA maps
+  // (tq with q at column q_col0, tkv with k at k_col0 and v at v_col0); the mma.sync kernel
+  // through the raw pointers and row pitches.
+  auto attn = [&](const char* name, const CUtensorMap& tq, const CUtensorMap& tkv, int q_col0, int k_col0,
+                  int v_col0, const bf16* q, const bf16* k, const bf16* v, bf16* o, int qs, int ks, int vs, int os,
+                  const int4* items, int n_items, int window, double pairs) {
     if (n_items == 0) return;
-    AttnArgs a{q, k, v, o, qs, ks, vs, os, dm.cu, items, window, scale_log2};
-    launch(B, nl, name, 4.0 * d * pairs, 0, [&] {
-      attention_varlen_kernel<<<dim3(n_items, d / 64), ATT_THREADS, 0, st>>>(a);
-    });
+    if (B.attn_tc) {
+      AttnTcArgs a{dm.cu, items, o, os, q_col0, k_col0, v_col0, d / 64, window, scale_log2, B.d_status};
+      launch(B, nl, name, 4.0 * d * pairs, 0, [&] {
+        attention_tc_kernel<<<dim3(n_items, (d / 64 + ATTC_HEADS - 1) / ATTC_HEADS), ATTC_THREADS, ATTC_SMEM, st>>>(
+            tq, tkv, a);
+      });
+    } else {
+      AttnArgs a{q, k, v, o, qs, ks, vs, os, dm.cu, items, window, scale_log2};
+      launch(B, nl, name, 4.0 * d * pairs, 0, [&] {
+        attention_varlen_kernel<<<dim3(n_items, d / 64), ATT_THREADS, 0, st>>>(a);
+      });
+    }
   };
   auto gemm_args = [&](int M, int N, int K, void* out, int ldo) {
     GemmArgs a{};
@@ -731,11 +771,12 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
     if (i > 0) ln("ln_attn", h, nullptr, T, l.attn_norm, nullptr, B.eps, x);
     GemmArgs g = gemm_args(T, 3 * d, d, qkv, 3 * d);
     g.pos = pos;
-    g.rope_cs = B.rope_cs[l.local ? 1 : 0];
+    g.inv_freq = B.inv_freq[l.local ? 1 : 0];
     g.rope_cols = 2 * d;
     launch(B, nl, "gemm_qkv_rope", fl * 3 * d * d, 0, [&] { launch_gemm<EPI_ROPE>(B.tm_x, l.tm_wqkv, g, nsm, st); });
-    attn(l.local ? "attn_local" : "attn_global", qkv, qkv + d, qkv + 2 * d, att, 3 * d, 3 * d, 3 * d, d,
-         dm.items_full, (int)m.items_full.size(), l.local ? B.window : -1, l.local ? m.pairs_local : m.pairs_global);
+    attn(l.local ? "attn_local" : "attn_global", B.tm_qkv_att, B.tm_qkv_att, 0, d, 2 * d, qkv, qkv + d,
+         qkv + 2 * d, att, 3 * d, 3 * d, 3 * d, d, dm.items_full, (int)m.items_full.size(), l.local ? B.window : -1,
+         l.local ? m.pairs_local : m.pairs_global);
     GemmArgs go = gemm_args(T, d, d, h, d);
     launch(B, nl, "gemm_wo_resid", fl * d * d, 0, [&] { launch_gemm<EPI_RESID>(B.tm_att, l.tm_wo, go, nsm, st); });
     ln("ln_mlp", h, nullptr, T, l.mlp_norm, nullptr, B.eps, x);
@@ -759,8 +800,8 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
     GemmArgs g = gemm_args(T, 3 * d, d, qkv, 3 * d);
     g.bias = hl.in_b;
     launch(B, nl, "head_gemm_in", fl * 3 * d * d, 0, [&] { launch_gemm<EPI_STORE>(B.tm_x, hl.tm_in, g, nsm, st); });
-    attn("head_attn", qkv, qkv + d, qkv + 2 * d, att, 3 * d, 3 * d, 3 * d, d, dm.items_full,
-         (int)m.items_full.size(), -1, m.pairs_global);
+    attn("head_attn", B.tm_qkv_att, B.tm_qkv_att, 0, d, 2 * d, qkv, qkv + d, qkv + 2 * d, att, 3 * d, 3 * d,
+         3 * d, d, dm.items_full, (int)m.items_full.size(), -1, m.pairs_global);
     GemmArgs go = gemm_args(T, d, d, h2, d);
     go.bias = hl.out_b;
     launch(B, nl, "head_gemm_out", fl * d * d, 0, [&] { launch_gemm<EPI_RESID>(B.tm_att, hl.tm_out, go, nsm, st); });
@@ -797,8 +838,8 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
     GemmArgs gq = gemm_args(R, d, d, B.qs.p, d);
     gq.bias = hl.in_b;
     launch(B, nl, "head_rows_gemm", flr * d * d, 0, [&] { launch_gemm<EPI_STORE>(B.tm_xs, hl.tm_in_q, gq, nsm, st); });
-    attn("head_rows_attn", B.qs.as<bf16>(), kv, kv + d, B.atts.as<bf16>(), d, 2 * d, 2 * d, d, dm.items_rows,
-         (int)m.items_rows.size(), -1, m.pairs_rows);
+    attn("head_rows_attn", B.tm_qs_att, B.tm_kv_att, 0, 0, d, B.qs.as<bf16>(), kv, kv + d, B.atts.as<bf16>(), d,
+         2 * d, 2 * d, d, dm.items_rows, (int)m.items_rows.size(), -1, m.pairs_rows);
     GemmArgs go = gemm_args(R, d, d, B.hs.p, d);
     go.bias = hl.out_b;
     launch(B, nl, "head_rows_gemm", flr * d * d, 0,
@@ -867,7 +908,7 @@ void forward_host(s1c_backend& B, const s1c_varlen& in, float* logits, float* po
   const int T = in.cu_seqlens[in.n];
   for (int t = 0; t < T; ++t)
     if (in.ids[t] >= (uint32_t)B.V) throw S1cError(S1C_ERR_ARG, "token " + std::to_string(t) + ": id outside the vocabulary");
-  HostMeta m = make_meta(in, B.window);
+  HostMeta m = make_meta(in, B.window, B.attn_tc ? ATTC_BQ : ATT_BQ);
   ensure_capacity(B, m.T, m.R);
   const size_t nl = (size_t)m.M, np = (size_t)m.n * B.d, nh = hidden ? (size_t)m.T * B.d : 0;
   B.out_stage.ensure((nl + np + nh + 64) * 4);
@@ -931,6 +972,30 @@ void pack_batch(const s1c_batch& b, PackedBatch& p) {
   p.v.qtype = p.qtype.data();
 }
 
+// Backend settings, a strict comma list like the reference's `Knobs` (laya-mlx/src/lib.rs:155-259):
+// an unknown key or value is an error naming it. Keys: attn=tc|mma.
+void apply_settings(s1c_backend& B, const char* spec) {
+  if (!spec) return;
+  std::string s(spec);
+  size_t i = 0;
+  while (i <= s.size()) {
+    size_t j = s.find(',', i);
+    if (j == std::string::npos) j = s.size();
+    const std::string kv = s.substr(i, j - i);
+    i = j + 1;
+    if (kv.empty()) continue;
+    const size_t eq = kv.find('=');
+    const std::string k = kv.substr(0, eq), v = eq == std::string::npos ? "" : kv.substr(eq + 1);
+    if (k == "attn") {
+      if (v == "tc") B.attn_tc = true;
+      else if (v == "mma") B.attn_tc = false;
+      else throw S1cError(S1C_ERR_CONFIG, "settings: `" + kv + "`: `" + v + "` is not one of tc, mma");
+    } else {
+      throw S1cError(S1C_ERR_CONFIG, "settings: unknown setting `" + k + "`");
+    }
+  }
+}
+
 template <class F>
 s1c_status guarded(s1c_backend* b, F&& f) {
   if (!b) return S1C_ERR_ARG;
@@ -980,6 +1045,8 @@ s1c_status s1c_create(const s1c_model_desc* desc, const s1c_tensor* tensors, int
     CK(cudaStreamCreateWithFlags(&b->own_stream, cudaStreamNonBlocking));
     b->stream = b->own_stream;
     set_all_gemm_smem();
+    CK(cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATTC_SMEM));
+    apply_settings(*b, std::getenv("S1C_SETTINGS"));
     build(*b, *desc, tensors, n_tensors);
     CK(cudaDeviceSynchronize());
   } catch (const S1cError& e) {
@@ -1087,6 +1154,24 @@ s1c_status s1c_encoder_hidden(s1c_backend* b, const s1c_batch* batch, float* out
   });
 }
 
+s1c_status s1c_forward_device_async(s1c_backend* b, const s1c_varlen* in, const uint32_t* d_ids, float* d_logits,
+                                    float* d_pooled, float* d_hidden) {
+  return guarded(b, [&] {
+    if (!in || !d_ids || !d_pooled || (in->n > 0 && in->kmax > 0 && !d_logits))
+      throw S1cError(S1C_ERR_ARG, "null argument");
+    validate_varlen(*b, *in);
+    if (in->n == 0) return;
+    HostMeta m = make_meta(*in, b->window, b->attn_tc ? ATTC_BQ : ATT_BQ);
+    ensure_capacity(*b, m.T, m.R);
+    DevMeta dm = upload_meta(*b, m, nullptr);
+    forward_enqueue(*b, m, dm, d_ids, d_logits, d_pooled, d_hidden);
+  });
+}
+
+s1c_status s1c_synchronize(s1c_backend* b) {
+  return guarded(b, [&] { check_status(*b); });
+}
+
 s1c_status s1c_forward_device(s1c_backend* b, const s1c_varlen* in, const uint32_t* d_ids, float* d_logits,
                               float* d_pooled, float* d_hidden) {
   return guarded(b, [&] {
@@ -1094,7 +1179,7 @@ s1c_status s1c_forward_device(s1c_backend* b, const s1c_varlen* in, const uint32
       throw S1cError(S1C_ERR_ARG, "null argument");
     validate_varlen(*b, *in);
     if (in->n == 0) return;
-    HostMeta m = make_meta(*in, b->window);
+    HostMeta m = make_meta(*in, b->window, b->attn_tc ? ATTC_BQ : ATT_BQ);
     ensure_capacity(*b, m.T, m.R);
     DevMeta dm = upload_meta(*b, m, nullptr);
     forward_enqueue(*b, m, dm, d_ids, d_logits, d_pooled, d_hidden);
@@ -1106,7 +1191,7 @@ s1c_status s1c_gemm(int32_t epi, const void* d_A, const void* d_B, void* d_out, 
                     const float* d_bias, int32_t act, int32_t out_f32, const int32_t* d_pos, float rope_theta,
                     int32_t rope_cols, int32_t out_cols, void* stream) {
   static std::mutex mu;
-  static std::map<std::pair<int, float>, float2*> tables;  // (device, theta) -> RoPE table
+  static std::map<std::pair<int, float>, float*> tables;  // (device, theta) -> inverse frequencies
   static int* d_status_dummy[64] = {nullptr};
   try {
     if (!d_A || !d_B || !d_out || M <= 0 || N <= 0 || K <= 0 || K % 8 || N % 32)
@@ -1130,8 +1215,8 @@ s1c_status s1c_gemm(int32_t epi, const void* d_A, const void* d_B, void* d_out, 
       a.status = d_status_dummy[dev];
       if (epi == EPI_ROPE) {
         auto key = std::make_pair(dev, rope_theta);
-        if (!tables.count(key)) tables[key] = make_rope_table_raw(rope_theta, 8192);
-        a.rope_cs = tables[key];
+        if (!tables.count(key)) tables[key] = make_inv_freq_raw(rope_theta);
+        a.inv_freq = tables[key];
         if (!d_pos) throw S1cError(S1C_ERR_ARG, "RoPE needs positions");
       }
     }
@@ -1158,34 +1243,69 @@ s1c_status s1c_gemm(int32_t epi, const void* d_A, const void* d_B, void* d_out, 
 
 s1c_status s1c_attention(const void* d_q, const void* d_k, const void* d_v, void* d_o, int32_t q_stride,
                          int32_t k_stride, int32_t v_stride, int32_t o_stride, int32_t heads,
-                         const int32_t* cu_seqlens, int32_t n, int32_t window, float scale, void* stream) {
+                         const int32_t* cu_seqlens, int32_t n, int32_t window, float scale, int32_t impl,
+                         void* stream) {
+  int* d_cu = nullptr;
+  int4* d_items = nullptr;
   try {
-    if (!d_q || !d_k || !d_v || !d_o || !cu_seqlens || n <= 0 || heads <= 0)
+    if (!d_q || !d_k || !d_v || !d_o || !cu_seqlens || n <= 0 || heads <= 0 || (impl != 0 && impl != 1))
       throw S1cError(S1C_ERR_ARG, "bad attention arguments");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int qtile = impl == 0 ? ATTC_BQ : ATT_BQ;
     std::vector<int4> items;
     for (int r = 0; r < n; ++r) {
       const int base = cu_seqlens[r], len = cu_seqlens[r + 1] - base;
-      for (int q = 0; q < len; q += ATT_BQ) items.push_back(make_int4(r, base + q, std::min(ATT_BQ, len - q), 0));
+      for (int q = 0; q < len; q += qtile) items.push_back(make_int4(r, base + q, std::min(qtile, len - q), 0));
     }
-    int* d_cu = nullptr;
-    int4* d_items = nullptr;
+    const int T = cu_seqlens[n];
     CK(cudaMalloc(&d_cu, (n + 1) * 4));
     CK(cudaMalloc(&d_items, items.size() * 16));
     CK(cudaMemcpy(d_cu, cu_seqlens, (n + 1) * 4, cudaMemcpyHostToDevice));
     CK(cudaMemcpy(d_items, items.data(), items.size() * 16, cudaMemcpyHostToDevice));
-    AttnArgs a{static_cast<const bf16*>(d_q), static_cast<const bf16*>(d_k), static_cast<const bf16*>(d_v),
-               static_cast<bf16*>(d_o), q_stride, k_stride, v_stride, o_stride, d_cu, d_items, window,
-               scale * 1.4426950408889634f};
-    attention_varlen_kernel<<<dim3((unsigned)items.size(), heads), ATT_THREADS, 0, st>>>(a);
-    cudaError_t e = cudaGetLastError();
-    cudaError_t e2 = cudaStreamSynchronize(st);
+    const float scale_log2 = scale * 1.4426950408889634f;
+    if (impl == 0) {
+      // one map for Q, one for K and V together: V must sit in K's rows at a 64-aligned column
+      const ptrdiff_t dv = static_cast<const bf16*>(d_v) - static_cast<const bf16*>(d_k);
+      if (v_stride != k_stride || dv < 0 || dv % 64 || dv + heads * 64 > k_stride)
+        throw S1cError(S1C_ERR_ARG, "tcgen05 attention needs v in the rows of k (same pitch, 64-aligned column)");
+      static bool attr_set[64] = {false};
+      int dev = 0;
+      CK(cudaGetDevice(&dev));
+      if (!attr_set[dev]) {
+        CK(cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATTC_SMEM));
+        attr_set[dev] = true;
+      }
+      int* d_status = nullptr;
+      CK(cudaMalloc(&d_status, sizeof(int)));
+      CK(cudaMemset(d_status, 0, sizeof(int)));
+      const CUtensorMap tq = make_tmap(d_q, T, heads * 64, q_stride, ATTC_BQ);
+      const CUtensorMap tkv = make_tmap(d_k, T, dv + heads * 64, k_stride, ATTC_BK);
+      AttnTcArgs a{d_cu, d_items, static_cast<bf16*>(d_o), o_stride, 0, 0, (int)dv, heads, window, scale_log2, d_status};
+      attention_tc_kernel<<<dim3((unsigned)items.size(), (heads + ATTC_HEADS - 1) / ATTC_HEADS), ATTC_THREADS,
+                            ATTC_SMEM, st>>>(tq, tkv, a);
+      cudaError_t e = cudaGetLastError();
+      cudaError_t e2 = cudaStreamSynchronize(st);
+      int hs = 0;
+      if (e2 == cudaSuccess) cudaMemcpy(&hs, d_status, sizeof(int), cudaMemcpyDeviceToHost);
+      cudaFree(d_status);
+      if (e != cudaSuccess) throw S1cError(S1C_ERR_CUDA, cudaGetErrorString(e));
+      if (e2 != cudaSuccess) throw S1cError(S1C_ERR_CUDA, cudaGetErrorString(e2));
+      if (hs) throw S1cError(S1C_ERR_DEVICE_TIMEOUT, "device-side wait ran out (code " + std::to_string(hs) + ")");
+    } else {
+      AttnArgs a{static_cast<const bf16*>(d_q), static_cast<const bf16*>(d_k), static_cast<const bf16*>(d_v),
+                 static_cast<bf16*>(d_o), q_stride, k_stride, v_stride, o_stride, d_cu, d_items, window, scale_log2};
+      attention_varlen_kernel<<<dim3((unsigned)items.size(), heads), ATT_THREADS, 0, st>>>(a);
+      cudaError_t e = cudaGetLastError();
+      cudaError_t e2 = cudaStreamSynchronize(st);
+      if (e != cudaSuccess) throw S1cError(S1C_ERR_CUDA, cudaGetErrorString(e));
+      if (e2 != cudaSuccess) throw S1cError(S1C_ERR_CUDA, cudaGetErrorString(e2));
+    }
     cudaFree(d_cu);
     cudaFree(d_items);
-    if (e != cudaSuccess) throw S1cError(S1C_ERR_CUDA, cudaGetErrorString(e));
-    if (e2 != cudaSuccess) throw S1cError(S1C_ERR_CUDA, cudaGetErrorString(e2));
     return S1C_OK;
   } catch (const S1cError& e) {
+    if (d_cu) cudaFree(d_cu);
+    if (d_items) cudaFree(d_items);
     g_create_error = e.what();
     return e.code;
   }

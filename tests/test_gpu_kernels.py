@@ -120,8 +120,9 @@ def _attn_ref(q, k, v, cu, window, scale, heads):
     return out
 
 
+@pytest.mark.parametrize("impl", [1, 0])
 @pytest.mark.parametrize("window", [-1, 64, 3])
-def test_attention_varlen_matches_torch(cuda_lib, window):
+def test_attention_varlen_matches_torch(cuda_lib, window, impl):
     from sys1rust_b200.backend import attention
     heads, d = 16, 1024
     lens = [1, 2, 63, 64, 65, 129, 300, 1024]
@@ -130,6 +131,6 @@ def test_attention_varlen_matches_torch(cuda_lib, window):
     qkv = _rand((T, 3 * d), 13)
     o = torch.empty(T, d, dtype=torch.bfloat16, device="cuda")
     attention(qkv.data_ptr(), qkv[:, d:].data_ptr(), qkv[:, 2 * d:].data_ptr(), o.data_ptr(), 3 * d, 3 * d, 3 * d, d,
-              heads, cu, window, 0.125)
+              heads, cu, window, 0.125, impl=impl)
     ref = _attn_ref(qkv[:, :d], qkv[:, d:2 * d], qkv[:, 2 * d:], cu, window, 0.125, heads)
     assert _rel_err(o, ref) < 1e-2
