@@ -10,9 +10,12 @@
 //   warp 1      allocates 2*BN TMEM columns and issues tcgen05.mma (M=128, N=BN, K=16 per
 //               instruction, fp32 accumulation in TMEM); tcgen05.commit releases a stage when
 //               the MMAs reading it are done and hands a finished accumulator to the epilogue.
-//   warps 2..5  epilogue: tcgen05.ld of the accumulator (one row per thread), the fused
-//               epilogue math, stores to global memory. Two accumulators alternate, so the
-//               epilogue of tile i overlaps the MMAs of tile i+1.
+//   warps 2..5  epilogue: tcgen05.ld of the accumulator (one row per thread), the fused math,
+//               then each warp writes its 32-row slice of a 128-byte-wide column block into a
+//               swizzled shared-memory staging buffer and one lane hands it to TMA: a tensor
+//               store for bf16 / fp32 outputs, a tensor reduce-add for the fp32 residual stream.
+//               Global traffic is therefore fully coalesced whatever the row layout. Two
+//               accumulators alternate, so the epilogue of tile i overlaps the MMAs of tile i+1.
 // Tiles are walked n-fastest (tile = m_block * n_blocks + n_block) so CTAs running together
 // share their A rows and stream the whole weight from L2.
 //
@@ -22,7 +25,8 @@
 //              (split_rope.metal:46-76), v copied; stored bf16 [M, 3d] (q | k | v, head-major).
 //   EPI_GEGLU  the encoder's Wi with its rows interleaved per 128 (input 128 | gate 128 per
 //              256-wide tile): out = gelu_erf(input) * gate (lib.rs:367-368, :494-510), bf16 [M, I].
-//   EPI_RESID  fp32 residual stream update in place: out += acc (+ bias)  (lib.rs:1375-1390).
+//   EPI_RESID  fp32 residual stream update: out += acc (+ bias) (lib.rs:1375-1390), one fp32 add per
+//              element performed by the TMA reduction.
 #pragma once
 #include <cuda.h>
 #include "common.cuh"
@@ -34,11 +38,9 @@ enum Act : int { ACT_NONE = 0, ACT_RELU = 1, ACT_GELU = 2 };
 
 struct GemmArgs {
   int M, N, K;
-  void* out;
-  int ldo;                // row pitch of `out`, elements
   const float* bias;      // [N] or null (EPI_STORE, EPI_RESID)
   int act;                // EPI_STORE activation
-  int out_f32;            // EPI_STORE: fp32 output
+  int out_f32;            // EPI_STORE: fp32 output (the output map is fp32, 32-column boxes)
   const int* pos;         // EPI_ROPE: position of each row inside its sequence
   const float* inv_freq;  // EPI_ROPE: [32] inverse frequencies of the layer's theta
   int rope_cols;          // EPI_ROPE: columns [0, rope_cols) hold q and k heads
@@ -50,98 +52,140 @@ constexpr int GEMM_BM = 128;
 constexpr int GEMM_BK = 64;
 constexpr int GEMM_STAGES = 4;
 constexpr int GEMM_THREADS = 192;
+constexpr uint32_t GEMM_STG_BYTES = 4096;  // one staging buffer: 32 rows x 128 bytes
 
 __host__ __device__ constexpr size_t gemm_smem_bytes(int BN) {
-  return (size_t)GEMM_STAGES * (GEMM_BM * GEMM_BK * 2 + BN * GEMM_BK * 2) + 1024 /*align*/ + 256 /*barriers*/;
+  return (size_t)GEMM_STAGES * (GEMM_BM * GEMM_BK * 2 + BN * GEMM_BK * 2) + 8 * GEMM_STG_BYTES + 1024 /*align*/ +
+         256 /*barriers*/;
 }
 
 S1C_DEV float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
 
-S1C_DEV void store_bf16x32(__nv_bfloat16* dst, const float (&v)[32]) {
-  uint4* d = reinterpret_cast<uint4*>(dst);
+// TMA tensor store / reduce-add of a staged box, and the bulk-group bookkeeping.
+S1C_DEV void tma_store_2d(const void* tmap, const void* src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(tmap),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+S1C_DEV void tma_reduce_add_2d(const void* tmap, const void* src, int x, int y) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];" ::"l"(tmap),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+S1C_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+S1C_DEV void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+S1C_DEV void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Per-warp staging of 32 rows x 128 bytes with the 128-byte swizzle the output tensor map uses:
+// row r, 16-byte chunk c lives at r*128 + ((c ^ (r & 7)) * 16). Double buffered per warp.
+struct Stager {
+  uint8_t* base;   // this warp's two buffers
+  uint32_t count;  // units issued so far
+  int lane;
+
+  // Wait until the buffer about to be written is no longer read by an older store.
+  S1C_DEV uint8_t* acquire() {
+    if (count >= 2) {
+      if (lane == 0) bulk_wait_read1();
+      __syncwarp();
+    }
+    return base + (count & 1) * GEMM_STG_BYTES;
+  }
+  S1C_DEV void put_f32x32(uint8_t* buf, const float (&v)[32]) {
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    uint4 u;
-    u.x = pack_bf16x2(v[8 * i + 0], v[8 * i + 1]);
-    u.y = pack_bf16x2(v[8 * i + 2], v[8 * i + 3]);
-    u.z = pack_bf16x2(v[8 * i + 4], v[8 * i + 5]);
-    u.w = pack_bf16x2(v[8 * i + 6], v[8 * i + 7]);
-    d[i] = u;
+    for (int c = 0; c < 8; ++c)
+      *reinterpret_cast<float4*>(buf + lane * 128 + ((c ^ (lane & 7)) << 4)) =
+          make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+  }
+  S1C_DEV void put_bf16x64(uint8_t* buf, const float* v) {
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+      *reinterpret_cast<uint4*>(buf + lane * 128 + ((c ^ (lane & 7)) << 4)) =
+          make_uint4(pack_bf16x2(v[8 * c], v[8 * c + 1]), pack_bf16x2(v[8 * c + 2], v[8 * c + 3]),
+                     pack_bf16x2(v[8 * c + 4], v[8 * c + 5]), pack_bf16x2(v[8 * c + 6], v[8 * c + 7]));
+  }
+  // Hand the staged box at (x, y) to TMA.
+  S1C_DEV void issue(const void* tmap, const uint8_t* buf, int x, int y, bool reduce) {
+    fence_proxy_async();
+    __syncwarp();
+    if (lane == 0) {
+      if (reduce) tma_reduce_add_2d(tmap, buf, x, y);
+      else tma_store_2d(tmap, buf, x, y);
+      bulk_commit();
+    }
+    ++count;
+  }
+};
+
+S1C_DEV void add_bias32(float* v, const float* bias, int col) {
+  const float4* b4 = reinterpret_cast<const float4*>(bias + col);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float4 b = __ldg(b4 + i);
+    v[4 * i] += b.x; v[4 * i + 1] += b.y; v[4 * i + 2] += b.z; v[4 * i + 3] += b.w;
   }
 }
 
 template <int BN, int EPI>
-__device__ __forceinline__ void gemm_epilogue_tile(const GemmArgs& args, uint32_t t, int row, int m_ok, int n0,
-                                                   int n_block) {
-  if constexpr (EPI == EPI_RESID) {
-    // fp32 residual read-modify-write, two 32-column chunks at a time: the residual loads of a
-    // pair are issued before the accumulator loads so their latency overlaps (the rows were
-    // prefetched into L2 while the mainloop ran).
-    float* rbase = static_cast<float*>(args.out) + (size_t)row * args.ldo + n0;
+__device__ __forceinline__ void gemm_epilogue_tile(const GemmArgs& args, const CUtensorMap* tmC, Stager& sg,
+                                                   uint32_t t, int row, bool m_ok, int y0, int n0, int n_block) {
+  if constexpr (EPI == EPI_RESID || EPI == EPI_STORE) {
+    const bool f32 = (EPI == EPI_RESID) || args.out_f32;
+    if (f32) {
+      // fp32 output: 32-column units. Rows past M add (or store) zeros.
 #pragma unroll 1
-    for (int c = 0; c < BN / 32; c += 2) {
-      const int col = n0 + c * 32;
-      const bool ok = m_ok && col < args.N;
-      float4 r[16];
-      if (ok) {
-        const float4* p = reinterpret_cast<const float4*>(rbase + c * 32);
+      for (int c = 0; c < BN / 32; ++c) {
+        float v[32];
+        tmem_ld32(t + c * 32, v);
+        const int col = n0 + c * 32;
+        if (col >= args.N) continue;  // warp-uniform
+        if (args.bias) add_bias32(v, args.bias, col);
+        if constexpr (EPI == EPI_STORE) {
+          if (args.act == ACT_RELU) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) r[i] = p[i];
-      }
-      float v[64];
-      tmem_ld32(t + c * 32, *reinterpret_cast<float(*)[32]>(v));
-      tmem_ld32(t + c * 32 + 32, *reinterpret_cast<float(*)[32]>(v + 32));
-      if (!ok) continue;
-      if (args.bias) {
-        const float4* b4 = reinterpret_cast<const float4*>(args.bias + col);
+            for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.0f);
+          } else if (args.act == ACT_GELU) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float4 b = __ldg(b4 + i);
-          v[4 * i] += b.x; v[4 * i + 1] += b.y; v[4 * i + 2] += b.z; v[4 * i + 3] += b.w;
+            for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
+          }
         }
-      }
-      float4* p = reinterpret_cast<float4*>(rbase + c * 32);
+        if (!m_ok) {
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        float4 x = r[i];
-        x.x += v[4 * i]; x.y += v[4 * i + 1]; x.z += v[4 * i + 2]; x.w += v[4 * i + 3];
-        p[i] = x;
+          for (int j = 0; j < 32; ++j) v[j] = 0.f;
+        }
+        uint8_t* buf = sg.acquire();
+        sg.put_f32x32(buf, v);
+        sg.issue(tmC, buf, col, y0, EPI == EPI_RESID);
       }
-    }
-  } else if constexpr (EPI == EPI_STORE) {
+    } else {
+      // bf16 output: 64-column units.
 #pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
-      float v[32];
-      tmem_ld32(t + c * 32, v);
-      const int col = n0 + c * 32;
-      if (!m_ok || col >= args.N) continue;
-      if (args.bias) {
-        const float4* b4 = reinterpret_cast<const float4*>(args.bias + col);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float4 b = __ldg(b4 + i);
-          v[4 * i] += b.x; v[4 * i + 1] += b.y; v[4 * i + 2] += b.z; v[4 * i + 3] += b.w;
+      for (int c = 0; c < BN / 64; ++c) {
+        float v[64];
+        tmem_ld32(t + c * 64, *reinterpret_cast<float(*)[32]>(v));
+        tmem_ld32(t + c * 64 + 32, *reinterpret_cast<float(*)[32]>(v + 32));
+        const int col = n0 + c * 64;
+        if (col >= args.N) continue;
+        if (args.bias) {
+          add_bias32(v, args.bias, col);
+          if (col + 32 < args.N) add_bias32(v + 32, args.bias, col + 32);
         }
-      }
-      if (args.act == ACT_RELU) {
+        if (args.act == ACT_RELU) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.0f);
-      } else if (args.act == ACT_GELU) {
+          for (int j = 0; j < 64; ++j) v[j] = fmaxf(v[j], 0.0f);
+        } else if (args.act == ACT_GELU) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
-      }
-      if (args.out_f32) {
-        float4* p = reinterpret_cast<float4*>(static_cast<float*>(args.out) + (size_t)row * args.ldo + col);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) p[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-      } else {
-        store_bf16x32(static_cast<__nv_bfloat16*>(args.out) + (size_t)row * args.ldo + col, v);
+          for (int j = 0; j < 64; ++j) v[j] = gelu_erf(v[j]);
+        }
+        uint8_t* buf = sg.acquire();
+        sg.put_bf16x64(buf, v);
+        sg.issue(tmC, buf, col, y0, false);
       }
     }
   } else if constexpr (EPI == EPI_ROPE) {
     // Rotate-half RoPE of every 64-wide q/k head in the tile at this row's position: the angle is
-    // p * inv_freq[j] in fp32 (split_rope.metal:46-76) and its cos/sin are computed once per row
-    // and shared by the tile's heads.
+    // p * inv_freq[j] in fp32 (split_rope.metal:46-76); its cos/sin are computed once per row and
+    // shared by the tile's heads.
     const bool rope = n0 < args.rope_cols;  // uniform: q/k tiles never straddle the v columns
     float cs[32], sn[32];
     if (rope) {
@@ -151,35 +195,41 @@ __device__ __forceinline__ void gemm_epilogue_tile(const GemmArgs& args, uint32_
     }
 #pragma unroll 1
     for (int hh = 0; hh < BN / 64; ++hh) {
-      float x1[32], x2[32];
-      tmem_ld32(t + hh * 64, x1);
-      tmem_ld32(t + hh * 64 + 32, x2);
+      float x[64];
+      tmem_ld32(t + hh * 64, *reinterpret_cast<float(*)[32]>(x));
+      tmem_ld32(t + hh * 64 + 32, *reinterpret_cast<float(*)[32]>(x + 32));
       const int col = n0 + hh * 64;
-      if (!m_ok || col >= args.N) continue;
+      if (col >= args.N) continue;
       if (rope) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
-          const float a = x1[j], b = x2[j];
-          x1[j] = a * cs[j] - b * sn[j];
-          x2[j] = a * sn[j] + b * cs[j];
+          const float a = x[j], b = x[j + 32];
+          x[j] = a * cs[j] - b * sn[j];
+          x[j + 32] = a * sn[j] + b * cs[j];
         }
       }
-      __nv_bfloat16* o = static_cast<__nv_bfloat16*>(args.out) + (size_t)row * args.ldo + col;
-      store_bf16x32(o, x1);
-      store_bf16x32(o + 32, x2);
+      uint8_t* buf = sg.acquire();
+      sg.put_bf16x64(buf, x);
+      sg.issue(tmC, buf, col, y0, false);
     }
   } else {  // EPI_GEGLU, BN == 256: columns [0,128) input, [128,256) gate
     static_assert(EPI != EPI_GEGLU || BN == 256, "GeGLU tiles are 128 input + 128 gate columns");
 #pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
-      float a[32], g[32];
-      tmem_ld32(t + c * 32, a);
-      tmem_ld32(t + 128 + c * 32, g);
-      const int ocol = n_block * 128 + c * 32;
-      if (!m_ok || ocol >= args.out_cols) continue;
+    for (int u = 0; u < 2; ++u) {
+      const int ocol = n_block * 128 + u * 64;
+      float a[64];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) a[j] = gelu_erf(a[j]) * g[j];
-      store_bf16x32(static_cast<__nv_bfloat16*>(args.out) + (size_t)row * args.ldo + ocol, a);
+      for (int h = 0; h < 2; ++h) {
+        float g[32];
+        tmem_ld32(t + u * 64 + h * 32, *reinterpret_cast<float(*)[32]>(a + h * 32));
+        tmem_ld32(t + 128 + u * 64 + h * 32, g);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) a[h * 32 + j] = gelu_erf(a[h * 32 + j]) * g[j];
+      }
+      if (ocol >= args.out_cols) continue;
+      uint8_t* buf = sg.acquire();
+      sg.put_bf16x64(buf, a);
+      sg.issue(tmC, buf, ocol, y0, false);
     }
   }
 }
@@ -187,20 +237,21 @@ __device__ __forceinline__ void gemm_epilogue_tile(const GemmArgs& args, uint32_
 template <int BN, int EPI>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_bf16_sm100(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    const GemmArgs args) {
+                    const __grid_constant__ CUtensorMap tmC, const GemmArgs args) {
   constexpr int BM = GEMM_BM, BK = GEMM_BK, STAGES = GEMM_STAGES;
   constexpr uint32_t A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2, STAGE_BYTES = A_BYTES + B_BYTES;
   constexpr uint32_t TMEM_COLS = 2 * BN;
   static_assert(TMEM_COLS == 32 || TMEM_COLS == 64 || TMEM_COLS == 128 || TMEM_COLS == 256 || TMEM_COLS == 512,
                 "TMEM allocations are powers of two from 32 to 512 columns");
-  static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "tcgen05 M=128 needs N % 16 == 0, 16..256");
+  static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "tcgen05 M=128 needs N % 16 == 0, 16..256");
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_u = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_u + 1023u) & ~1023u) - raw_u);
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint8_t* sStg = sB + STAGES * B_BYTES;  // 4 warps x 2 buffers x 4 KB, 1024-aligned
+  uint64_t* full = reinterpret_cast<uint64_t*>(sStg + 8 * GEMM_STG_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -310,29 +361,26 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
   } else {
     const int quad = warp & 3;  // TMEM lanes this warp may read: [32*quad, 32*quad + 32)
+    Stager sg{sStg + (warp - 2) * 2 * GEMM_STG_BYTES, 0u, lane};
+    if (lane == 0) prefetch_tmap(&tmC);
     int acc = 0;
     uint32_t aph = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       const int m0 = (tile / num_n) * BM, n_block = tile % num_n;
-      const int row = m0 + quad * 32 + lane;
-      if constexpr (EPI == EPI_RESID) {
-        // Pull this row's residual span into L2 while the tile's MMAs run.
-        if (row < args.M) {
-          const char* rp = reinterpret_cast<const char*>(static_cast<const float*>(args.out) +
-                                                         (size_t)row * args.ldo + n_block * BN);
-          const int span = min(BN, args.N - n_block * BN) * 4;
-          for (int off = 0; off < span; off += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(rp + off));
-        }
-      }
+      const int y0 = m0 + quad * 32;
+      const int row = y0 + lane;
       if (!mbar_wait_warp(&tfull[acc], aph, args.status, DEV_TIMEOUT_EPILOGUE, abort_flag)) break;
       tc_fence_after();
       const uint32_t t = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
-      gemm_epilogue_tile<BN, EPI>(args, t, row, row < args.M, n_block * BN, n_block);
+      gemm_epilogue_tile<BN, EPI>(args, &tmC, sg, t, row, row < args.M, y0, n_block * BN, n_block);
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
       acc ^= 1;
       if (acc == 0) aph ^= 1u;
     }
+    // Stores in flight finish (and stop reading shared memory) before the CTA exits.
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
   }
   __syncthreads();
   if (warp == 1) {

@@ -118,20 +118,31 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   return fn;
 }
 
-// K-major bf16 matrix [rows, k] with row pitch `ld` elements, tiles of box_rows x 64, 128-byte swizzle.
-CUtensorMap make_tmap(const void* ptr, uint64_t rows, uint64_t k, uint64_t ld, uint32_t box_rows) {
-  if ((reinterpret_cast<uintptr_t>(ptr) & 15) || (ld * 2) % 16)
+// 2D row-major matrix [rows, cols] (row pitch `ld` elements) tiled in boxes of box_rows x 128 bytes
+// with the 128-byte swizzle: bf16 boxes are 64 elements wide, fp32 boxes 32.
+CUtensorMap make_tmap_t(const void* ptr, bool f32, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows) {
+  const uint64_t es = f32 ? 4 : 2;
+  if ((reinterpret_cast<uintptr_t>(ptr) & 15) || (ld * es) % 16)
     throw S1cError(S1C_ERR_ARG, "TMA operand must be 16-byte aligned with a 16-byte multiple row pitch");
   CUtensorMap m;
-  cuuint64_t dims[2] = {k, rows};
-  cuuint64_t strides[1] = {ld * 2};
-  cuuint32_t box[2] = {64, box_rows};
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld * es};
+  cuuint32_t box[2] = {(cuuint32_t)(128 / es), box_rows};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = get_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box,
-                               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = get_encode_fn()(&m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                               const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) throw S1cError(S1C_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
   return m;
+}
+// K-major bf16 GEMM / attention operand [rows, k], boxes of box_rows x 64 elements.
+CUtensorMap make_tmap(const void* ptr, uint64_t rows, uint64_t k, uint64_t ld, uint32_t box_rows) {
+  return make_tmap_t(ptr, false, rows, k, ld, box_rows);
+}
+// GEMM output map: boxes of 32 rows x 128 bytes (one epilogue warp's slice).
+CUtensorMap make_out_tmap(const void* ptr, bool f32, uint64_t rows, uint64_t cols, uint64_t ld) {
+  return make_tmap_t(ptr, f32, rows, cols, ld, 32);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -152,11 +163,12 @@ void set_all_gemm_smem() {
 }
 
 template <int EPI>
-void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int num_sms, cudaStream_t st) {
+void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmArgs& a, int num_sms,
+                 cudaStream_t st) {
   if (a.M <= 0) return;
   const int tiles = ((a.M + GEMM_BM - 1) / GEMM_BM) * ((a.N + GEMM_BN - 1) / GEMM_BN);
   const int grid = std::min(tiles, num_sms);
-  gemm_bf16_sm100<GEMM_BN, EPI><<<grid, GEMM_THREADS, gemm_smem_bytes(GEMM_BN), st>>>(ta, tb, a);
+  gemm_bf16_sm100<GEMM_BN, EPI><<<grid, GEMM_THREADS, gemm_smem_bytes(GEMM_BN), st>>>(ta, tb, tc, a);
   CK(cudaGetLastError());
 }
 
@@ -261,13 +273,16 @@ struct s1c_backend {
   float* inv_freq[2] = {nullptr, nullptr};  // 0 global theta, 1 local theta
 
   // activations (capacity in rows, multiples of 128)
-  bool attn_tc = true;  // tcgen05 attention (attention_tc.cuh); false: mma.sync (attention.cuh)
+  bool attn_tc = false;  // true: tcgen05 attention (attention_tc.cuh, `attn=tc`); false: mma.sync (attention.cuh)
   int cap_T = 0, cap_R = 0;
   DevBuf h, x, qkv, att, act;          // [cap_T, ...]
   DevBuf h2;                           // head residual stream [cap_T, d] fp32
   DevBuf xs, qs, atts, hs, fs, xm, sh; // scorer rows [cap_R, ...]
   CUtensorMap tm_x, tm_att, tm_act_i, tm_act_f, tm_xs, tm_atts, tm_fs, tm_xm;
   CUtensorMap tm_qkv_att, tm_kv_att, tm_qs_att;  // 128-row boxes for the tcgen05 attention
+  // GEMM output maps (32-row boxes): bf16 qkv as [T,3d] and [T,2d], act as [T,I] and [T,F];
+  // fp32 residual streams h, h2; scorer-row buffers.
+  CUtensorMap to_qkv3, to_kv2, to_act_i, to_act_f, to_h, to_h2, to_qs, to_hs, to_fs, to_sh;
 
   // metadata
   // Metadata staging ring: a forward's small host arrays go to a pinned slot and one H2D copy
@@ -405,6 +420,12 @@ void ensure_capacity(s1c_backend& B, int T, int R) {
     B.tm_x = make_tmap(B.x.p, cap, B.d, B.d, GEMM_BM);
     B.tm_qkv_att = make_tmap(B.qkv.p, cap, 3 * B.d, 3 * B.d, ATTC_BQ);
     B.tm_kv_att = make_tmap(B.qkv.p, cap, 2 * B.d, 2 * B.d, ATTC_BK);
+    B.to_qkv3 = make_out_tmap(B.qkv.p, false, cap, 3 * B.d, 3 * B.d);
+    B.to_kv2 = make_out_tmap(B.qkv.p, false, cap, 2 * B.d, 2 * B.d);
+    B.to_act_i = make_out_tmap(B.act.p, false, cap, B.I, B.I);
+    B.to_act_f = make_out_tmap(B.act.p, false, cap, B.F, B.F);
+    B.to_h = make_out_tmap(B.h.p, true, cap, B.d, B.d);
+    B.to_h2 = make_out_tmap(B.h2.p, true, cap, B.d, B.d);
     B.tm_att = make_tmap(B.att.p, cap, B.d, B.d, GEMM_BM);
     B.tm_act_i = make_tmap(B.act.p, cap, B.I, B.I, GEMM_BM);
     B.tm_act_f = make_tmap(B.act.p, cap, B.F, B.F, GEMM_BM);
@@ -424,6 +445,10 @@ void ensure_capacity(s1c_backend& B, int T, int R) {
     CK(cudaMemsetAsync(B.xs.p, 0, B.xs.bytes, B.stream));
     B.tm_xs = make_tmap(B.xs.p, cap, B.d, B.d, GEMM_BM);
     B.tm_qs_att = make_tmap(B.qs.p, cap, B.d, B.d, ATTC_BQ);
+    B.to_qs = make_out_tmap(B.qs.p, false, cap, B.d, B.d);
+    B.to_hs = make_out_tmap(B.hs.p, true, cap, B.d, B.d);
+    B.to_fs = make_out_tmap(B.fs.p, false, cap, B.F, B.F);
+    B.to_sh = make_out_tmap(B.sh.p, true, cap, B.S, B.S);
     B.tm_atts = make_tmap(B.atts.p, cap, B.d, B.d, GEMM_BM);
     B.tm_fs = make_tmap(B.fs.p, cap, B.F, B.F, GEMM_BM);
     B.tm_xm = make_tmap(B.xm.p, cap, B.d, B.d, GEMM_BM);
@@ -755,9 +780,9 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
       });
     }
   };
-  auto gemm_args = [&](int M, int N, int K, void* out, int ldo) {
+  auto gemm_args = [&](int M, int N, int K) {
     GemmArgs a{};
-    a.M = M; a.N = N; a.K = K; a.out = out; a.ldo = ldo; a.status = B.d_status;
+    a.M = M; a.N = N; a.K = K; a.status = B.d_status;
     return a;
   };
   auto ln = [&](const char* name, const float* in, const int* gather, int rows, const float* w, const float* b,
@@ -769,23 +794,23 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
   for (int i = 0; i < B.L; ++i) {
     const EncLayer& l = B.layers[i];
     if (i > 0) ln("ln_attn", h, nullptr, T, l.attn_norm, nullptr, B.eps, x);
-    GemmArgs g = gemm_args(T, 3 * d, d, qkv, 3 * d);
+    GemmArgs g = gemm_args(T, 3 * d, d);
     g.pos = pos;
     g.inv_freq = B.inv_freq[l.local ? 1 : 0];
     g.rope_cols = 2 * d;
-    launch(B, nl, "gemm_qkv_rope", fl * 3 * d * d, 0, [&] { launch_gemm<EPI_ROPE>(B.tm_x, l.tm_wqkv, g, nsm, st); });
+    launch(B, nl, "gemm_qkv_rope", fl * 3 * d * d, 0, [&] { launch_gemm<EPI_ROPE>(B.tm_x, l.tm_wqkv, B.to_qkv3, g, nsm, st); });
     attn(l.local ? "attn_local" : "attn_global", B.tm_qkv_att, B.tm_qkv_att, 0, d, 2 * d, qkv, qkv + d,
          qkv + 2 * d, att, 3 * d, 3 * d, 3 * d, d, dm.items_full, (int)m.items_full.size(), l.local ? B.window : -1,
          l.local ? m.pairs_local : m.pairs_global);
-    GemmArgs go = gemm_args(T, d, d, h, d);
-    launch(B, nl, "gemm_wo_resid", fl * d * d, 0, [&] { launch_gemm<EPI_RESID>(B.tm_att, l.tm_wo, go, nsm, st); });
+    GemmArgs go = gemm_args(T, d, d);
+    launch(B, nl, "gemm_wo_resid", fl * d * d, 0, [&] { launch_gemm<EPI_RESID>(B.tm_att, l.tm_wo, B.to_h, go, nsm, st); });
     ln("ln_mlp", h, nullptr, T, l.mlp_norm, nullptr, B.eps, x);
-    GemmArgs gi = gemm_args(T, B.Ipad, d, act, B.I);
+    GemmArgs gi = gemm_args(T, B.Ipad, d);
     gi.out_cols = B.I;
-    launch(B, nl, "gemm_wi_geglu", fl * 2 * B.I * d, 0, [&] { launch_gemm<EPI_GEGLU>(B.tm_x, l.tm_wi, gi, nsm, st); });
-    GemmArgs g2 = gemm_args(T, d, B.I, h, d);
+    launch(B, nl, "gemm_wi_geglu", fl * 2 * B.I * d, 0, [&] { launch_gemm<EPI_GEGLU>(B.tm_x, l.tm_wi, B.to_act_i, gi, nsm, st); });
+    GemmArgs g2 = gemm_args(T, d, B.I);
     launch(B, nl, "gemm_wo2_resid", fl * B.I * d, 0,
-           [&] { launch_gemm<EPI_RESID>(B.tm_act_i, l.tm_wo2, g2, nsm, st); });
+           [&] { launch_gemm<EPI_RESID>(B.tm_act_i, l.tm_wo2, B.to_h, g2, nsm, st); });
   }
 
   // final_norm, + type embedding, head layer 0's norm1
@@ -797,23 +822,23 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
   // full head layers (all but the last)
   for (int j = 0; j + 1 < B.n_head; ++j) {
     const HeadLayer& hl = B.head[j];
-    GemmArgs g = gemm_args(T, 3 * d, d, qkv, 3 * d);
+    GemmArgs g = gemm_args(T, 3 * d, d);
     g.bias = hl.in_b;
-    launch(B, nl, "head_gemm_in", fl * 3 * d * d, 0, [&] { launch_gemm<EPI_STORE>(B.tm_x, hl.tm_in, g, nsm, st); });
+    launch(B, nl, "head_gemm_in", fl * 3 * d * d, 0, [&] { launch_gemm<EPI_STORE>(B.tm_x, hl.tm_in, B.to_qkv3, g, nsm, st); });
     attn("head_attn", B.tm_qkv_att, B.tm_qkv_att, 0, d, 2 * d, qkv, qkv + d, qkv + 2 * d, att, 3 * d, 3 * d,
          3 * d, d, dm.items_full, (int)m.items_full.size(), -1, m.pairs_global);
-    GemmArgs go = gemm_args(T, d, d, h2, d);
+    GemmArgs go = gemm_args(T, d, d);
     go.bias = hl.out_b;
-    launch(B, nl, "head_gemm_out", fl * d * d, 0, [&] { launch_gemm<EPI_RESID>(B.tm_att, hl.tm_out, go, nsm, st); });
+    launch(B, nl, "head_gemm_out", fl * d * d, 0, [&] { launch_gemm<EPI_RESID>(B.tm_att, hl.tm_out, B.to_h2, go, nsm, st); });
     ln("head_ln", h2, nullptr, T, hl.n2w, hl.n2b, 1e-5f, x);
-    GemmArgs g1 = gemm_args(T, B.F, d, act, B.F);
+    GemmArgs g1 = gemm_args(T, B.F, d);
     g1.bias = hl.l1_b;
     g1.act = ACT_RELU;
-    launch(B, nl, "head_gemm_l1", fl * B.F * d, 0, [&] { launch_gemm<EPI_STORE>(B.tm_x, hl.tm_l1, g1, nsm, st); });
-    GemmArgs g2 = gemm_args(T, d, B.F, h2, d);
+    launch(B, nl, "head_gemm_l1", fl * B.F * d, 0, [&] { launch_gemm<EPI_STORE>(B.tm_x, hl.tm_l1, B.to_act_f, g1, nsm, st); });
+    GemmArgs g2 = gemm_args(T, d, B.F);
     g2.bias = hl.l2_b;
     launch(B, nl, "head_gemm_l2", fl * B.F * d, 0,
-           [&] { launch_gemm<EPI_RESID>(B.tm_act_f, hl.tm_l2, g2, nsm, st); });
+           [&] { launch_gemm<EPI_RESID>(B.tm_act_f, hl.tm_l2, B.to_h2, g2, nsm, st); });
     const HeadLayer& nx = B.head[j + 1];
     ln("head_ln", h2, nullptr, T, nx.n1w, nx.n1b, 1e-5f, x);
   }
@@ -825,46 +850,46 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
     const int R = m.R;
     const double flr = 2.0 * R;
     bf16* kv = qkv;  // [T, 2d]
-    GemmArgs gkv = gemm_args(T, 2 * d, d, kv, 2 * d);
+    GemmArgs gkv = gemm_args(T, 2 * d, d);
     gkv.bias = hl.in_b + d;
     launch(B, nl, "head_gemm_kv", fl * 2 * d * d, 0,
-           [&] { launch_gemm<EPI_STORE>(B.tm_x, hl.tm_in_kv, gkv, nsm, st); });
+           [&] { launch_gemm<EPI_STORE>(B.tm_x, hl.tm_in_kv, B.to_kv2, gkv, nsm, st); });
     launch(B, nl, "gather_rows", 0, (double)R * d * 4, [&] {
       gather_rows_bf16_kernel<<<R, 128, 0, st>>>(x, dm.srows, R, d, B.xs.as<bf16>());
     });
     launch(B, nl, "gather_rows", 0, (double)R * d * 8, [&] {
       gather_rows_f32_kernel<<<R, 256, 0, st>>>(h2, dm.srows, R, d, B.hs.as<float>());
     });
-    GemmArgs gq = gemm_args(R, d, d, B.qs.p, d);
+    GemmArgs gq = gemm_args(R, d, d);
     gq.bias = hl.in_b;
-    launch(B, nl, "head_rows_gemm", flr * d * d, 0, [&] { launch_gemm<EPI_STORE>(B.tm_xs, hl.tm_in_q, gq, nsm, st); });
+    launch(B, nl, "head_rows_gemm", flr * d * d, 0, [&] { launch_gemm<EPI_STORE>(B.tm_xs, hl.tm_in_q, B.to_qs, gq, nsm, st); });
     attn("head_rows_attn", B.tm_qs_att, B.tm_kv_att, 0, 0, d, B.qs.as<bf16>(), kv, kv + d, B.atts.as<bf16>(), d,
          2 * d, 2 * d, d, dm.items_rows, (int)m.items_rows.size(), -1, m.pairs_rows);
-    GemmArgs go = gemm_args(R, d, d, B.hs.p, d);
+    GemmArgs go = gemm_args(R, d, d);
     go.bias = hl.out_b;
     launch(B, nl, "head_rows_gemm", flr * d * d, 0,
-           [&] { launch_gemm<EPI_RESID>(B.tm_atts, hl.tm_out, go, nsm, st); });
+           [&] { launch_gemm<EPI_RESID>(B.tm_atts, hl.tm_out, B.to_hs, go, nsm, st); });
     ln("head_ln", B.hs.as<float>(), nullptr, R, hl.n2w, hl.n2b, 1e-5f, B.xs.as<bf16>());
-    GemmArgs g1 = gemm_args(R, B.F, d, B.fs.p, B.F);
+    GemmArgs g1 = gemm_args(R, B.F, d);
     g1.bias = hl.l1_b;
     g1.act = ACT_RELU;
     launch(B, nl, "head_rows_gemm", flr * B.F * d, 0,
-           [&] { launch_gemm<EPI_STORE>(B.tm_xs, hl.tm_l1, g1, nsm, st); });
-    GemmArgs g2 = gemm_args(R, d, B.F, B.hs.p, d);
+           [&] { launch_gemm<EPI_STORE>(B.tm_xs, hl.tm_l1, B.to_fs, g1, nsm, st); });
+    GemmArgs g2 = gemm_args(R, d, B.F);
     g2.bias = hl.l2_b;
     launch(B, nl, "head_rows_gemm", flr * B.F * d, 0,
-           [&] { launch_gemm<EPI_RESID>(B.tm_fs, hl.tm_l2, g2, nsm, st); });
+           [&] { launch_gemm<EPI_RESID>(B.tm_fs, hl.tm_l2, B.to_hs, g2, nsm, st); });
   }
 
   // scorer at the marker slots, pooled at position 0
   if (m.M > 0) {
     ln("scorer_ln", B.hs.as<float>(), dm.mrows, m.M, B.sc_nw, B.sc_nb, 1e-5f, B.xm.as<bf16>());
-    GemmArgs gs = gemm_args(m.M, B.S, d, B.sh.p, B.S);
+    GemmArgs gs = gemm_args(m.M, B.S, d);
     gs.bias = B.sc_b1;
     gs.act = ACT_GELU;
     gs.out_f32 = 1;
     launch(B, nl, "scorer_gemm", 2.0 * m.M * B.S * d, 0,
-           [&] { launch_gemm<EPI_STORE>(B.tm_xm, B.tm_sc1, gs, nsm, st); });
+           [&] { launch_gemm<EPI_STORE>(B.tm_xm, B.tm_sc1, B.to_sh, gs, nsm, st); });
     launch(B, nl, "scorer_logits", 2.0 * m.M * B.S, 0, [&] {
       scorer_logits_kernel<<<(m.M + 7) / 8, 256, 0, st>>>(B.sh.as<float>(), m.M, B.S, B.sc_w3, B.sc_b3, dm.mcount,
                                                           m.kmax, d_logits);
@@ -1202,7 +1227,7 @@ s1c_status s1c_gemm(int32_t epi, const void* d_A, const void* d_B, void* d_out, 
     CK(cudaGetDeviceProperties(&prop, dev));
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     GemmArgs a{};
-    a.M = M; a.N = N; a.K = K; a.out = d_out; a.bias = d_bias; a.act = act; a.out_f32 = out_f32;
+    a.M = M; a.N = N; a.K = K; a.bias = d_bias; a.act = act; a.out_f32 = out_f32;
     a.pos = d_pos; a.rope_cols = rope_cols; a.out_cols = out_cols;
     {
       std::lock_guard<std::mutex> g(mu);
@@ -1220,15 +1245,16 @@ s1c_status s1c_gemm(int32_t epi, const void* d_A, const void* d_B, void* d_out, 
         if (!d_pos) throw S1cError(S1C_ERR_ARG, "RoPE needs positions");
       }
     }
-    const int ldo = (epi == EPI_GEGLU) ? out_cols : N;
-    a.ldo = ldo;
+    const bool f32 = epi == EPI_RESID || (epi == EPI_STORE && out_f32);
+    const int out_w = (epi == EPI_GEGLU) ? out_cols : N;
     const CUtensorMap ta = make_tmap(d_A, (uint64_t)M, K, K, GEMM_BM);
     const CUtensorMap tb = make_tmap(d_B, N, K, K, GEMM_BN);
+    const CUtensorMap tc = make_out_tmap(d_out, f32, (uint64_t)M, out_w, out_w);
     switch (epi) {
-      case EPI_STORE: launch_gemm<EPI_STORE>(ta, tb, a, prop.multiProcessorCount, st); break;
-      case EPI_ROPE: launch_gemm<EPI_ROPE>(ta, tb, a, prop.multiProcessorCount, st); break;
-      case EPI_GEGLU: launch_gemm<EPI_GEGLU>(ta, tb, a, prop.multiProcessorCount, st); break;
-      case EPI_RESID: launch_gemm<EPI_RESID>(ta, tb, a, prop.multiProcessorCount, st); break;
+      case EPI_STORE: launch_gemm<EPI_STORE>(ta, tb, tc, a, prop.multiProcessorCount, st); break;
+      case EPI_ROPE: launch_gemm<EPI_ROPE>(ta, tb, tc, a, prop.multiProcessorCount, st); break;
+      case EPI_GEGLU: launch_gemm<EPI_GEGLU>(ta, tb, tc, a, prop.multiProcessorCount, st); break;
+      case EPI_RESID: launch_gemm<EPI_RESID>(ta, tb, tc, a, prop.multiProcessorCount, st); break;
       default: throw S1cError(S1C_ERR_ARG, "unknown epilogue");
     }
     return S1C_OK;
