@@ -63,6 +63,13 @@ S1C_DEV void mma_bf16_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// 2^x on the special-function unit (inputs of -inf give +0).
+S1C_DEV float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // Byte offset of 16-byte chunk `c` of row `r` in a [64][64] bf16 tile with XOR swizzle.
 S1C_DEV uint32_t swz(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
 
@@ -81,7 +88,7 @@ S1C_DEV void load_tile_async(uint32_t tile, const __nv_bfloat16* base, int strid
   }
 }
 
-__global__ void __launch_bounds__(ATT_THREADS) attention_varlen_kernel(const AttnArgs args) {
+__global__ void __launch_bounds__(ATT_THREADS, 4) attention_varlen_kernel(const AttnArgs args) {
   __shared__ __align__(128) __nv_bfloat16 sQ[ATT_BQ * ATT_D];
   __shared__ __align__(128) __nv_bfloat16 sK[2][ATT_BK * ATT_D];
   __shared__ __align__(128) __nv_bfloat16 sV[2][ATT_BK * ATT_D];
@@ -114,6 +121,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_varlen_kernel(const Att
   cp_async_commit();
 
   const int g = lane >> 2, t4 = lane & 3;
+  const bool local = args.window >= 0 && mode == 0;
   // Query positions of this thread's two rows (mode 0 only; used by the window test).
   const int qrow0 = warp * 16 + g;
   const int qpos0 = q_first - s_begin + qrow0, qpos1 = qpos0 + 8;
@@ -163,25 +171,33 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_varlen_kernel(const Att
       }
     }
 
-    // Mask keys outside [k_lo, k_hi) and, for local layers, outside the window.
+    // Keys this thread's two rows may see, as column offsets [lo, hi) inside the tile: the
+    // sequence's [k_lo, k_hi), narrowed to |i - j| <= window on local layers. Masking runs only
+    // when some row of the warp does not see the whole tile (edge tiles).
     const int kt0 = k_lo + it * ATT_BK;
+    int lo0 = 0, hi0 = k_hi - kt0, lo1 = 0, hi1 = k_hi - kt0;
+    if (local) {
+      lo0 = max(lo0, s_begin + qpos0 - args.window - kt0);
+      hi0 = min(hi0, s_begin + qpos0 + args.window + 1 - kt0);
+      lo1 = max(lo1, s_begin + qpos1 - args.window - kt0);
+      hi1 = min(hi1, s_begin + qpos1 + args.window + 1 - kt0);
+    }
+    const bool whole = lo0 <= 0 && hi0 >= ATT_BK && lo1 <= 0 && hi1 >= ATT_BK;
+    if (!__all_sync(0xffffffffu, whole)) {
+      const int b = 2 * t4;  // column of element (j, e) = j * 8 + b + (e & 1)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < 8; ++j) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int key = kt0 + j * 8 + 2 * t4 + (e & 1);
-        bool ok = key < k_hi;
-        if (args.window >= 0 && mode == 0) {
-          const int kp = key - s_begin;
-          const int qp = (e < 2) ? qpos0 : qpos1;
-          ok = ok && abs(qp - kp) <= args.window;
+        for (int e = 0; e < 4; ++e) {
+          const int c = j * 8 + (e & 1) + b;
+          const bool ok = (e < 2) ? (c >= lo0 && c < hi0) : (c >= lo1 && c < hi1);
+          s[j][e] = ok ? s[j][e] : -INFINITY;
         }
-        s[j][e] = ok ? s[j][e] * args.scale_log2 : -INFINITY;
       }
     }
 
-    // Online softmax (base 2), rows g and g + 8 of this warp.
-    float mx0 = m0, mx1 = m1;
+    // Online softmax (base 2) on raw scores: max first, then p = 2^(s * scale - max * scale).
+    float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       mx0 = fmaxf(mx0, fmaxf(s[j][0], s[j][1]));
@@ -191,17 +207,20 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_varlen_kernel(const Att
     mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
     mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
     mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    mx0 = fmaxf(m0, mx0 * args.scale_log2);
+    mx1 = fmaxf(m1, mx1 * args.scale_log2);
     const float base0 = (mx0 == -INFINITY) ? 0.f : mx0;
     const float base1 = (mx1 == -INFINITY) ? 0.f : mx1;
-    const float corr0 = exp2f(m0 - base0), corr1 = exp2f(m1 - base1);
+    const float corr0 = ex2_approx(m0 - base0), corr1 = ex2_approx(m1 - base1);
     m0 = mx0;
     m1 = mx1;
     float rs0 = 0.f, rs1 = 0.f;
     uint32_t pa[8][2];
+    const float sc = args.scale_log2;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const float p0 = exp2f(s[j][0] - base0), p1 = exp2f(s[j][1] - base0);
-      const float p2 = exp2f(s[j][2] - base1), p3 = exp2f(s[j][3] - base1);
+      const float p0 = ex2_approx(fmaf(s[j][0], sc, -base0)), p1 = ex2_approx(fmaf(s[j][1], sc, -base0));
+      const float p2 = ex2_approx(fmaf(s[j][2], sc, -base1)), p3 = ex2_approx(fmaf(s[j][3], sc, -base1));
       rs0 += p0 + p1;
       rs1 += p2 + p3;
       pa[j][0] = pack_bf16x2(p0, p1);
