@@ -95,7 +95,7 @@ def lib() -> C.CDLL:
         "s1c_forward_device_async": (I32, [P, C.POINTER(CVarlen), P, P, P, P]),
         "s1c_synchronize": (I32, [P]),
         "s1c_encoder_hidden": (I32, [P, C.POINTER(CBatch), P]),
-        "s1c_gemm": (I32, [I32, P, P, P, I32, I32, I32, P, I32, I32, P, F32, I32, I32, P]),
+        "s1c_gemm": (I32, [I32, P, P, P, I32, I32, I32, P, I32, I32, P, F32, I32, I32, I32, P]),
         "s1c_attention": (I32, [P, P, P, P, I32, I32, I32, I32, I32, P, I32, I32, F32, I32, P]),
         "s1c_last_launch_count": (I64, [P]),
         "s1c_set_stream": (I32, [P, P]),
@@ -304,10 +304,11 @@ EPI_STORE, EPI_ROPE, EPI_GEGLU, EPI_RESID = 0, 1, 2, 3
 
 def gemm(epi: int, a_ptr: int, b_ptr: int, out_ptr: int, M: int, N: int, K: int, bias_ptr: int = 0, act: int = 0,
          out_f32: int = 0, pos_ptr: int = 0, rope_theta: float = 10000.0, rope_cols: int = 0, out_cols: int = 0,
-         stream: int = 0) -> None:
+         variant: int = 0, stream: int = 0) -> None:
+    """variant 0: by shape; 1: one-CTA 128x256 tiles; 2: two-CTA 256x256 tiles."""
     L = lib()
     rc = L.s1c_gemm(epi, a_ptr, b_ptr, out_ptr, M, N, K, bias_ptr or None, act, out_f32, pos_ptr or None,
-                    rope_theta, rope_cols, out_cols, stream or None)
+                    rope_theta, rope_cols, out_cols, variant, stream or None)
     if rc != S1C_OK:
         _raise(rc, L.s1c_create_error().decode())
 

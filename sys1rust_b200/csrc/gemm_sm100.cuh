@@ -380,8 +380,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
     // Stores in flight finish (and stop reading shared memory) before the CTA exits.
     if (lane == 0) bulk_wait_all();
-    __syncwarp();
   }
+  __syncwarp();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();

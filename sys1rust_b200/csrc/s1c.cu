@@ -27,6 +27,7 @@
 #include "attention.cuh"
 #include "attention_tc.cuh"
 #include "gemm_sm100.cuh"
+#include "gemm_sm100_2cta.cuh"
 #include "rowwise.cuh"
 
 using namespace s1c;
@@ -140,6 +141,14 @@ CUtensorMap make_tmap_t(const void* ptr, bool f32, uint64_t rows, uint64_t cols,
 CUtensorMap make_tmap(const void* ptr, uint64_t rows, uint64_t k, uint64_t ld, uint32_t box_rows) {
   return make_tmap_t(ptr, false, rows, k, ld, box_rows);
 }
+// A weight (B operand) with its two TMA maps: 256-row boxes for the one-CTA kernel, 128-row
+// boxes for the two-CTA kernel (each CTA of a pair loads half of the 256-row tile).
+struct WeightMap {
+  CUtensorMap full, half;
+};
+WeightMap make_wmap(const void* ptr, uint64_t rows, uint64_t k, uint64_t ld) {
+  return WeightMap{make_tmap(ptr, rows, k, ld, 256), make_tmap(ptr, rows, k, ld, 128)};
+}
 // GEMM output map: boxes of 32 rows x 128 bytes (one epilogue warp's slice).
 CUtensorMap make_out_tmap(const void* ptr, bool f32, uint64_t rows, uint64_t cols, uint64_t ld) {
   return make_tmap_t(ptr, f32, rows, cols, ld, 32);
@@ -154,6 +163,8 @@ template <int EPI>
 void set_gemm_smem() {
   CK(cudaFuncSetAttribute(gemm_bf16_sm100<GEMM_BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                           (int)gemm_smem_bytes(GEMM_BN)));
+  CK(cudaFuncSetAttribute(gemm2_bf16_sm100<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                          (int)gemm2_smem_bytes()));
 }
 void set_all_gemm_smem() {
   set_gemm_smem<EPI_STORE>();
@@ -162,13 +173,21 @@ void set_all_gemm_smem() {
   set_gemm_smem<EPI_RESID>();
 }
 
+// GEMM variant: 0 = by shape (two-CTA when there are at least 256 rows), 1 = one-CTA, 2 = two-CTA.
 template <int EPI>
-void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmArgs& a, int num_sms,
-                 cudaStream_t st) {
+void launch_gemm(const CUtensorMap& ta, const WeightMap& tb, const CUtensorMap& tc, const GemmArgs& a, int num_sms,
+                 cudaStream_t st, int variant = 0) {
   if (a.M <= 0) return;
-  const int tiles = ((a.M + GEMM_BM - 1) / GEMM_BM) * ((a.N + GEMM_BN - 1) / GEMM_BN);
-  const int grid = std::min(tiles, num_sms);
-  gemm_bf16_sm100<GEMM_BN, EPI><<<grid, GEMM_THREADS, gemm_smem_bytes(GEMM_BN), st>>>(ta, tb, tc, a);
+  const bool two = variant == 2 || (variant == 0 && a.M >= 256);
+  if (two) {
+    const int tiles = ((a.M + 255) / 256) * ((a.N + GEMM_BN - 1) / GEMM_BN);
+    const int clusters = std::min(tiles, num_sms / 2);
+    gemm2_bf16_sm100<EPI><<<2 * clusters, GEMM_THREADS, gemm2_smem_bytes(), st>>>(ta, tb.half, tc, a);
+  } else {
+    const int tiles = ((a.M + GEMM_BM - 1) / GEMM_BM) * ((a.N + GEMM_BN - 1) / GEMM_BN);
+    const int grid = std::min(tiles, num_sms);
+    gemm_bf16_sm100<GEMM_BN, EPI><<<grid, GEMM_THREADS, gemm_smem_bytes(GEMM_BN), st>>>(ta, tb.full, tc, a);
+  }
   CK(cudaGetLastError());
 }
 
@@ -225,14 +244,14 @@ struct EncLayer {
   bf16 *wqkv = nullptr, *wo = nullptr, *wi = nullptr, *wo2 = nullptr;
   float *attn_norm = nullptr, *mlp_norm = nullptr;
   bool local = false;
-  CUtensorMap tm_wqkv, tm_wo, tm_wi, tm_wo2;
+  WeightMap tm_wqkv, tm_wo, tm_wi, tm_wo2;
 };
 
 struct HeadLayer {
   bf16 *in_w = nullptr, *out_w = nullptr, *l1_w = nullptr, *l2_w = nullptr;
   float *in_b = nullptr, *out_b = nullptr, *l1_b = nullptr, *l2_b = nullptr;
   float *n1w = nullptr, *n1b = nullptr, *n2w = nullptr, *n2b = nullptr;
-  CUtensorMap tm_in, tm_in_q, tm_in_kv, tm_out, tm_l1, tm_l2;
+  WeightMap tm_in, tm_in_q, tm_in_kv, tm_out, tm_l1, tm_l2;
 };
 
 }  // namespace
@@ -269,10 +288,11 @@ struct s1c_backend {
   std::vector<HeadLayer> head;
   float *sc_nw = nullptr, *sc_nb = nullptr, *sc_b1 = nullptr, *sc_w3 = nullptr, *sc_b3 = nullptr;
   bf16* sc_w1 = nullptr;
-  CUtensorMap tm_sc1;
+  WeightMap tm_sc1;
   float* inv_freq[2] = {nullptr, nullptr};  // 0 global theta, 1 local theta
 
   // activations (capacity in rows, multiples of 128)
+  int gemm_variant = 0;   // `gemm=auto|1cta|2cta`
   bool attn_tc = false;  // true: tcgen05 attention (attention_tc.cuh, `attn=tc`); false: mma.sync (attention.cuh)
   int cap_T = 0, cap_R = 0;
   DevBuf h, x, qkv, att, act;          // [cap_T, ...]
@@ -506,10 +526,10 @@ void build(s1c_backend& B, const s1c_model_desc& D, const s1c_tensor* tensors, i
     l.wo = upload_matrix(B, tt.get(p + ".attn.Wo.weight", {d, d}), d, d);
     l.wi = upload_matrix(B, tt.get(p + ".mlp.Wi.weight", {2 * I, d}), 2 * I, d, wi_map.data(), B.Ipad);
     l.wo2 = upload_matrix(B, tt.get(p + ".mlp.Wo.weight", {d, I}), d, I);
-    l.tm_wqkv = make_tmap(l.wqkv, 3 * d, d, d, GEMM_BN);
-    l.tm_wo = make_tmap(l.wo, (d + 255) / 256 * 256, d, d, GEMM_BN);
-    l.tm_wi = make_tmap(l.wi, B.Ipad, d, d, GEMM_BN);
-    l.tm_wo2 = make_tmap(l.wo2, (d + 255) / 256 * 256, I, I, GEMM_BN);
+    l.tm_wqkv = make_wmap(l.wqkv, 3 * d, d, d);
+    l.tm_wo = make_wmap(l.wo, (d + 255) / 256 * 256, d, d);
+    l.tm_wi = make_wmap(l.wi, B.Ipad, d, d);
+    l.tm_wo2 = make_wmap(l.wo2, (d + 255) / 256 * 256, I, I);
   }
   const std::string h0 = "head.layers.0.linear1.weight";
   if (!tt.has(h0)) throw S1cError(S1C_ERR_WEIGHTS, h0 + ": missing tensor");
@@ -532,12 +552,12 @@ void build(s1c_backend& B, const s1c_model_desc& D, const s1c_tensor* tensors, i
     hl.n1b = upload_vector(B, tt.get(p + ".norm1.bias", {d}), d);
     hl.n2w = upload_vector(B, tt.get(p + ".norm2.weight", {d}), d);
     hl.n2b = upload_vector(B, tt.get(p + ".norm2.bias", {d}), d);
-    hl.tm_in = make_tmap(hl.in_w, 3 * d, d, d, GEMM_BN);
-    hl.tm_in_q = make_tmap(hl.in_w, d, d, d, GEMM_BN);
-    hl.tm_in_kv = make_tmap(hl.in_w + d * d, 2 * d, d, d, GEMM_BN);
-    hl.tm_out = make_tmap(hl.out_w, (d + 255) / 256 * 256, d, d, GEMM_BN);
-    hl.tm_l1 = make_tmap(hl.l1_w, B.F, d, d, GEMM_BN);
-    hl.tm_l2 = make_tmap(hl.l2_w, (d + 255) / 256 * 256, B.F, B.F, GEMM_BN);
+    hl.tm_in = make_wmap(hl.in_w, 3 * d, d, d);
+    hl.tm_in_q = make_wmap(hl.in_w, d, d, d);
+    hl.tm_in_kv = make_wmap(hl.in_w + d * d, 2 * d, d, d);
+    hl.tm_out = make_wmap(hl.out_w, (d + 255) / 256 * 256, d, d);
+    hl.tm_l1 = make_wmap(hl.l1_w, B.F, d, d);
+    hl.tm_l2 = make_wmap(hl.l2_w, (d + 255) / 256 * 256, B.F, B.F);
   }
   if (!tt.has("scorer.1.weight")) throw S1cError(S1C_ERR_WEIGHTS, "scorer.1.weight: missing tensor");
   B.S = (int)tt.by_name["scorer.1.weight"]->shape[0];
@@ -548,7 +568,7 @@ void build(s1c_backend& B, const s1c_model_desc& D, const s1c_tensor* tensors, i
   B.sc_b1 = upload_vector(B, tt.get("scorer.1.bias", {B.S}), B.S);
   B.sc_w3 = upload_vector(B, tt.get("scorer.3.weight", {1, B.S}), B.S);
   B.sc_b3 = upload_vector(B, tt.get("scorer.3.bias", {1}), 1);
-  B.tm_sc1 = make_tmap(B.sc_w1, (B.S + 255) / 256 * 256, d, d, GEMM_BN);
+  B.tm_sc1 = make_wmap(B.sc_w1, (B.S + 255) / 256 * 256, d, d);
 
   B.inv_freq[0] = make_inv_freq(B, D.global_rope_theta);
   B.inv_freq[1] = make_inv_freq(B, D.local_rope_theta);
@@ -798,19 +818,19 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
     g.pos = pos;
     g.inv_freq = B.inv_freq[l.local ? 1 : 0];
     g.rope_cols = 2 * d;
-    launch(B, nl, "gemm_qkv_rope", fl * 3 * d * d, 0, [&] { launch_gemm<EPI_ROPE>(B.tm_x, l.tm_wqkv, B.to_qkv3, g, nsm, st); });
+    launch(B, nl, "gemm_qkv_rope", fl * 3 * d * d, 0, [&] { launch_gemm<EPI_ROPE>(B.tm_x, l.tm_wqkv, B.to_qkv3, g, nsm, st, B.gemm_variant); });
     attn(l.local ? "attn_local" : "attn_global", B.tm_qkv_att, B.tm_qkv_att, 0, d, 2 * d, qkv, qkv + d,
          qkv + 2 * d, att, 3 * d, 3 * d, 3 * d, d, dm.items_full, (int)m.items_full.size(), l.local ? B.window : -1,
          l.local ? m.pairs_local : m.pairs_global);
     GemmArgs go = gemm_args(T, d, d);
-    launch(B, nl, "gemm_wo_resid", fl * d * d, 0, [&] { launch_gemm<EPI_RESID>(B.tm_att, l.tm_wo, B.to_h, go, nsm, st); });
+    launch(B, nl, "gemm_wo_resid", fl * d * d, 0, [&] { launch_gemm<EPI_RESID>(B.tm_att, l.tm_wo, B.to_h, go, nsm, st, B.gemm_variant); });
     ln("ln_mlp", h, nullptr, T, l.mlp_norm, nullptr, B.eps, x);
     GemmArgs gi = gemm_args(T, B.Ipad, d);
     gi.out_cols = B.I;
-    launch(B, nl, "gemm_wi_geglu", fl * 2 * B.I * d, 0, [&] { launch_gemm<EPI_GEGLU>(B.tm_x, l.tm_wi, B.to_act_i, gi, nsm, st); });
+    launch(B, nl, "gemm_wi_geglu", fl * 2 * B.I * d, 0, [&] { launch_gemm<EPI_GEGLU>(B.tm_x, l.tm_wi, B.to_act_i, gi, nsm, st, B.gemm_variant); });
     GemmArgs g2 = gemm_args(T, d, B.I);
     launch(B, nl, "gemm_wo2_resid", fl * B.I * d, 0,
-           [&] { launch_gemm<EPI_RESID>(B.tm_act_i, l.tm_wo2, B.to_h, g2, nsm, st); });
+           [&] { launch_gemm<EPI_RESID>(B.tm_act_i, l.tm_wo2, B.to_h, g2, nsm, st, B.gemm_variant); });
   }
 
   // final_norm, + type embedding, head layer 0's norm1
@@ -824,21 +844,21 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
     const HeadLayer& hl = B.head[j];
     GemmArgs g = gemm_args(T, 3 * d, d);
     g.bias = hl.in_b;
-    launch(B, nl, "head_gemm_in", fl * 3 * d * d, 0, [&] { launch_gemm<EPI_STORE>(B.tm_x, hl.tm_in, B.to_qkv3, g, nsm, st); });
+    launch(B, nl, "head_gemm_in", fl * 3 * d * d, 0, [&] { launch_gemm<EPI_STORE>(B.tm_x, hl.tm_in, B.to_qkv3, g, nsm, st, B.gemm_variant); });
     attn("head_attn", B.tm_qkv_att, B.tm_qkv_att, 0, d, 2 * d, qkv, qkv + d, qkv + 2 * d, att, 3 * d, 3 * d,
          3 * d, d, dm.items_full, (int)m.items_full.size(), -1, m.pairs_global);
     GemmArgs go = gemm_args(T, d, d);
     go.bias = hl.out_b;
-    launch(B, nl, "head_gemm_out", fl * d * d, 0, [&] { launch_gemm<EPI_RESID>(B.tm_att, hl.tm_out, B.to_h2, go, nsm, st); });
+    launch(B, nl, "head_gemm_out", fl * d * d, 0, [&] { launch_gemm<EPI_RESID>(B.tm_att, hl.tm_out, B.to_h2, go, nsm, st, B.gemm_variant); });
     ln("head_ln", h2, nullptr, T, hl.n2w, hl.n2b, 1e-5f, x);
     GemmArgs g1 = gemm_args(T, B.F, d);
     g1.bias = hl.l1_b;
     g1.act = ACT_RELU;
-    launch(B, nl, "head_gemm_l1", fl * B.F * d, 0, [&] { launch_gemm<EPI_STORE>(B.tm_x, hl.tm_l1, B.to_act_f, g1, nsm, st); });
+    launch(B, nl, "head_gemm_l1", fl * B.F * d, 0, [&] { launch_gemm<EPI_STORE>(B.tm_x, hl.tm_l1, B.to_act_f, g1, nsm, st, B.gemm_variant); });
     GemmArgs g2 = gemm_args(T, d, B.F);
     g2.bias = hl.l2_b;
     launch(B, nl, "head_gemm_l2", fl * B.F * d, 0,
-           [&] { launch_gemm<EPI_RESID>(B.tm_act_f, hl.tm_l2, B.to_h2, g2, nsm, st); });
+           [&] { launch_gemm<EPI_RESID>(B.tm_act_f, hl.tm_l2, B.to_h2, g2, nsm, st, B.gemm_variant); });
     const HeadLayer& nx = B.head[j + 1];
     ln("head_ln", h2, nullptr, T, nx.n1w, nx.n1b, 1e-5f, x);
   }
@@ -853,7 +873,7 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
     GemmArgs gkv = gemm_args(T, 2 * d, d);
     gkv.bias = hl.in_b + d;
     launch(B, nl, "head_gemm_kv", fl * 2 * d * d, 0,
-           [&] { launch_gemm<EPI_STORE>(B.tm_x, hl.tm_in_kv, B.to_kv2, gkv, nsm, st); });
+           [&] { launch_gemm<EPI_STORE>(B.tm_x, hl.tm_in_kv, B.to_kv2, gkv, nsm, st, B.gemm_variant); });
     launch(B, nl, "gather_rows", 0, (double)R * d * 4, [&] {
       gather_rows_bf16_kernel<<<R, 128, 0, st>>>(x, dm.srows, R, d, B.xs.as<bf16>());
     });
@@ -862,23 +882,23 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
     });
     GemmArgs gq = gemm_args(R, d, d);
     gq.bias = hl.in_b;
-    launch(B, nl, "head_rows_gemm", flr * d * d, 0, [&] { launch_gemm<EPI_STORE>(B.tm_xs, hl.tm_in_q, B.to_qs, gq, nsm, st); });
+    launch(B, nl, "head_rows_gemm", flr * d * d, 0, [&] { launch_gemm<EPI_STORE>(B.tm_xs, hl.tm_in_q, B.to_qs, gq, nsm, st, B.gemm_variant); });
     attn("head_rows_attn", B.tm_qs_att, B.tm_kv_att, 0, 0, d, B.qs.as<bf16>(), kv, kv + d, B.atts.as<bf16>(), d,
          2 * d, 2 * d, d, dm.items_rows, (int)m.items_rows.size(), -1, m.pairs_rows);
     GemmArgs go = gemm_args(R, d, d);
     go.bias = hl.out_b;
     launch(B, nl, "head_rows_gemm", flr * d * d, 0,
-           [&] { launch_gemm<EPI_RESID>(B.tm_atts, hl.tm_out, B.to_hs, go, nsm, st); });
+           [&] { launch_gemm<EPI_RESID>(B.tm_atts, hl.tm_out, B.to_hs, go, nsm, st, B.gemm_variant); });
     ln("head_ln", B.hs.as<float>(), nullptr, R, hl.n2w, hl.n2b, 1e-5f, B.xs.as<bf16>());
     GemmArgs g1 = gemm_args(R, B.F, d);
     g1.bias = hl.l1_b;
     g1.act = ACT_RELU;
     launch(B, nl, "head_rows_gemm", flr * B.F * d, 0,
-           [&] { launch_gemm<EPI_STORE>(B.tm_xs, hl.tm_l1, B.to_fs, g1, nsm, st); });
+           [&] { launch_gemm<EPI_STORE>(B.tm_xs, hl.tm_l1, B.to_fs, g1, nsm, st, B.gemm_variant); });
     GemmArgs g2 = gemm_args(R, d, B.F);
     g2.bias = hl.l2_b;
     launch(B, nl, "head_rows_gemm", flr * B.F * d, 0,
-           [&] { launch_gemm<EPI_RESID>(B.tm_fs, hl.tm_l2, B.to_hs, g2, nsm, st); });
+           [&] { launch_gemm<EPI_RESID>(B.tm_fs, hl.tm_l2, B.to_hs, g2, nsm, st, B.gemm_variant); });
   }
 
   // scorer at the marker slots, pooled at position 0
@@ -889,7 +909,7 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
     gs.act = ACT_GELU;
     gs.out_f32 = 1;
     launch(B, nl, "scorer_gemm", 2.0 * m.M * B.S * d, 0,
-           [&] { launch_gemm<EPI_STORE>(B.tm_xm, B.tm_sc1, B.to_sh, gs, nsm, st); });
+           [&] { launch_gemm<EPI_STORE>(B.tm_xm, B.tm_sc1, B.to_sh, gs, nsm, st, B.gemm_variant); });
     launch(B, nl, "scorer_logits", 2.0 * m.M * B.S, 0, [&] {
       scorer_logits_kernel<<<(m.M + 7) / 8, 256, 0, st>>>(B.sh.as<float>(), m.M, B.S, B.sc_w3, B.sc_b3, dm.mcount,
                                                           m.kmax, d_logits);
@@ -998,7 +1018,7 @@ void pack_batch(const s1c_batch& b, PackedBatch& p) {
 }
 
 // Backend settings, a strict comma list like the reference's `Knobs` (laya-mlx/src/lib.rs:155-259):
-// an unknown key or value is an error naming it. Keys: attn=tc|mma.
+// an unknown key or value is an error naming it. Keys: attn=tc|mma, gemm=auto|1cta|2cta.
 void apply_settings(s1c_backend& B, const char* spec) {
   if (!spec) return;
   std::string s(spec);
@@ -1011,7 +1031,12 @@ void apply_settings(s1c_backend& B, const char* spec) {
     if (kv.empty()) continue;
     const size_t eq = kv.find('=');
     const std::string k = kv.substr(0, eq), v = eq == std::string::npos ? "" : kv.substr(eq + 1);
-    if (k == "attn") {
+    if (k == "gemm") {
+      if (v == "auto") B.gemm_variant = 0;
+      else if (v == "1cta") B.gemm_variant = 1;
+      else if (v == "2cta") B.gemm_variant = 2;
+      else throw S1cError(S1C_ERR_CONFIG, "settings: `" + kv + "`: `" + v + "` is not one of auto, 1cta, 2cta");
+    } else if (k == "attn") {
       if (v == "tc") B.attn_tc = true;
       else if (v == "mma") B.attn_tc = false;
       else throw S1cError(S1C_ERR_CONFIG, "settings: `" + kv + "`: `" + v + "` is not one of tc, mma");
@@ -1214,7 +1239,7 @@ s1c_status s1c_forward_device(s1c_backend* b, const s1c_varlen* in, const uint32
 
 s1c_status s1c_gemm(int32_t epi, const void* d_A, const void* d_B, void* d_out, int32_t M, int32_t N, int32_t K,
                     const float* d_bias, int32_t act, int32_t out_f32, const int32_t* d_pos, float rope_theta,
-                    int32_t rope_cols, int32_t out_cols, void* stream) {
+                    int32_t rope_cols, int32_t out_cols, int32_t variant, void* stream) {
   static std::mutex mu;
   static std::map<std::pair<int, float>, float*> tables;  // (device, theta) -> inverse frequencies
   static int* d_status_dummy[64] = {nullptr};
@@ -1248,13 +1273,14 @@ s1c_status s1c_gemm(int32_t epi, const void* d_A, const void* d_B, void* d_out, 
     const bool f32 = epi == EPI_RESID || (epi == EPI_STORE && out_f32);
     const int out_w = (epi == EPI_GEGLU) ? out_cols : N;
     const CUtensorMap ta = make_tmap(d_A, (uint64_t)M, K, K, GEMM_BM);
-    const CUtensorMap tb = make_tmap(d_B, N, K, K, GEMM_BN);
+    if (variant < 0 || variant > 2) throw S1cError(S1C_ERR_ARG, "variant must be 0, 1 or 2");
+    const WeightMap tb = make_wmap(d_B, N, K, K);
     const CUtensorMap tc = make_out_tmap(d_out, f32, (uint64_t)M, out_w, out_w);
     switch (epi) {
-      case EPI_STORE: launch_gemm<EPI_STORE>(ta, tb, tc, a, prop.multiProcessorCount, st); break;
-      case EPI_ROPE: launch_gemm<EPI_ROPE>(ta, tb, tc, a, prop.multiProcessorCount, st); break;
-      case EPI_GEGLU: launch_gemm<EPI_GEGLU>(ta, tb, tc, a, prop.multiProcessorCount, st); break;
-      case EPI_RESID: launch_gemm<EPI_RESID>(ta, tb, tc, a, prop.multiProcessorCount, st); break;
+      case EPI_STORE: launch_gemm<EPI_STORE>(ta, tb, tc, a, prop.multiProcessorCount, st, variant); break;
+      case EPI_ROPE: launch_gemm<EPI_ROPE>(ta, tb, tc, a, prop.multiProcessorCount, st, variant); break;
+      case EPI_GEGLU: launch_gemm<EPI_GEGLU>(ta, tb, tc, a, prop.multiProcessorCount, st, variant); break;
+      case EPI_RESID: launch_gemm<EPI_RESID>(ta, tb, tc, a, prop.multiProcessorCount, st, variant); break;
       default: throw S1cError(S1C_ERR_ARG, "unknown epilogue");
     }
     return S1C_OK;

@@ -23,39 +23,46 @@ def _rand(shape, seed, scale=1.0):
     return (torch.randn(*shape, generator=g) * scale).to(torch.bfloat16).cuda()
 
 
+VARIANTS = [1, 2]  # one-CTA 128x256 tiles, two-CTA 256x256 tiles
+
+
+@pytest.mark.parametrize("variant", VARIANTS)
 @pytest.mark.parametrize("M,N,K", [(128, 256, 64), (300, 768, 1024), (1024, 3072, 1024), (77, 1024, 2624),
                                    (513, 256, 4096)])
-def test_gemm_store_matches_torch(cuda_lib, M, N, K):
+def test_gemm_store_matches_torch(cuda_lib, M, N, K, variant):
     from sys1rust_b200.backend import EPI_STORE, gemm
     a, b = _rand((M, K), 1), _rand((N, K), 2)
     out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
-    gemm(EPI_STORE, a.data_ptr(), b.data_ptr(), out.data_ptr(), M, N, K)
+    gemm(EPI_STORE, a.data_ptr(), b.data_ptr(), out.data_ptr(), M, N, K, variant=variant)
     torch.cuda.synchronize()
     ref = a.float() @ b.float().t()
     assert _rel_err(out, ref) < 1e-2
 
 
+@pytest.mark.parametrize("variant", VARIANTS)
 @pytest.mark.parametrize("act", [0, 1, 2])
-def test_gemm_bias_activation_fp32_out(cuda_lib, act):
+def test_gemm_bias_activation_fp32_out(cuda_lib, act, variant):
     from sys1rust_b200.backend import EPI_STORE, gemm
     M, N, K = 200, 512, 1024
     a, b = _rand((M, K), 3), _rand((N, K), 4)
     bias = torch.randn(N, generator=torch.Generator().manual_seed(5)).float().cuda()
     out = torch.empty(M, N, dtype=torch.float32, device="cuda")
-    gemm(EPI_STORE, a.data_ptr(), b.data_ptr(), out.data_ptr(), M, N, K, bias_ptr=bias.data_ptr(), act=act, out_f32=1)
+    gemm(EPI_STORE, a.data_ptr(), b.data_ptr(), out.data_ptr(), M, N, K, bias_ptr=bias.data_ptr(), act=act, out_f32=1,
+         variant=variant)
     torch.cuda.synchronize()
     ref = a.float() @ b.float().t() + bias
     ref = [ref, torch.relu(ref), torch.nn.functional.gelu(ref)][act]
     assert _rel_err(out, ref) < 1e-4
 
 
-def test_gemm_residual_in_place(cuda_lib):
+@pytest.mark.parametrize("variant", VARIANTS)
+def test_gemm_residual_in_place(cuda_lib, variant):
     from sys1rust_b200.backend import EPI_RESID, gemm
     M, N, K = 333, 1024, 2624
     a, b = _rand((M, K), 6), _rand((N, K), 7)
     h = torch.randn(M, N, generator=torch.Generator().manual_seed(8)).float().cuda()
     ref = h + a.float() @ b.float().t()
-    gemm(EPI_RESID, a.data_ptr(), b.data_ptr(), h.data_ptr(), M, N, K)
+    gemm(EPI_RESID, a.data_ptr(), b.data_ptr(), h.data_ptr(), M, N, K, variant=variant)
     torch.cuda.synchronize()
     assert _rel_err(h, ref) < 1e-4
 
@@ -73,8 +80,9 @@ def _rope_ref(x, pos, theta):
     return torch.cat([x1 * c[:, None] - x2 * s[:, None], x1 * s[:, None] + x2 * c[:, None]], -1).view(M, Cc)
 
 
+@pytest.mark.parametrize("variant", VARIANTS)
 @pytest.mark.parametrize("theta", [160000.0, 10000.0])
-def test_gemm_rope_epilogue(cuda_lib, theta):
+def test_gemm_rope_epilogue(cuda_lib, theta, variant):
     from sys1rust_b200.backend import EPI_ROPE, gemm
     d = 1024
     M, N, K = 700, 3 * d, d
@@ -82,22 +90,23 @@ def test_gemm_rope_epilogue(cuda_lib, theta):
     pos = torch.from_numpy(np.concatenate([np.arange(500), np.arange(200)]).astype(np.int32)).cuda()
     out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
     gemm(EPI_ROPE, a.data_ptr(), b.data_ptr(), out.data_ptr(), M, N, K, pos_ptr=pos.data_ptr(), rope_theta=theta,
-         rope_cols=2 * d)
+         rope_cols=2 * d, variant=variant)
     torch.cuda.synchronize()
     acc = a.float() @ b.float().t()
     ref = torch.cat([_rope_ref(acc[:, :2 * d], pos, theta), acc[:, 2 * d:]], 1)
     assert _rel_err(out, ref) < 1e-2
 
 
+@pytest.mark.parametrize("variant", VARIANTS)
 @pytest.mark.parametrize("I", [2624, 384])
-def test_gemm_geglu_epilogue(cuda_lib, I):
+def test_gemm_geglu_epilogue(cuda_lib, I, variant):
     from sys1rust_b200.backend import EPI_GEGLU, gemm, interleave_wi
     M, K = 260, 1024
     a = _rand((M, K), 11)
     wi = _rand((2 * I, K), 12)
     wil = torch.from_numpy(interleave_wi(wi.cpu().view(torch.int16).numpy(), I)).view(torch.bfloat16).cuda()
     out = torch.empty(M, I, dtype=torch.bfloat16, device="cuda")
-    gemm(EPI_GEGLU, a.data_ptr(), wil.data_ptr(), out.data_ptr(), M, wil.shape[0], K, out_cols=I)
+    gemm(EPI_GEGLU, a.data_ptr(), wil.data_ptr(), out.data_ptr(), M, wil.shape[0], K, out_cols=I, variant=variant)
     torch.cuda.synchronize()
     y = a.float() @ wi.float().t()
     ref = torch.nn.functional.gelu(y[:, :I]) * y[:, I:]
