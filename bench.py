@@ -188,7 +188,9 @@ def main():
     w = SyntheticWeights(cfg, seed=0)
     be = CudaBackend.from_synthetic(cfg, w.tensors, device=local, max_tokens=BATCH_TOKENS)
     log(f"[rank {rank}] model ready in {time.time() - t0:.1f}s: {be.name()}")
-    stream = torch.cuda.current_stream()
+    # A dedicated (non-default) stream: the backend captures per-shape CUDA graphs on it.
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
     be.set_stream(stream.cuda_stream)
 
     all_reqs, mine = workload(world, rank)
@@ -250,8 +252,9 @@ def main():
     prof_ms = p0.elapsed_time(p1)
     prof = be.profile_report()
     be.profile(False)
+    kernel_ms = sum(v["ms"] for v in prof.values()) / args.steps
     # ---- e2e: host buffers through the C ABI, copies inside the timed region --------------
-    be.set_stream(0)
+    be.set_stream(0)  # the backend's own stream
     for b in batches[:2]:
         be.forward_varlen(b)
     barrier()
@@ -372,6 +375,7 @@ def main():
             "clocks": clk.summary(),
             "gpu_launches": int(launches),
             "profiled_pass_ms_per_step": prof_ms / args.steps,
+            "kernel_ms_per_step": kernel_ms,
             "kernels": kernels,
         }
         print(json.dumps(line), flush=True)

@@ -304,26 +304,43 @@ struct s1c_backend {
   // fp32 residual streams h, h2; scorer-row buffers.
   CUtensorMap to_qkv3, to_kv2, to_act_i, to_act_f, to_h, to_h2, to_qs, to_hs, to_fs, to_sh;
 
-  // metadata
-  // Metadata staging ring: a forward's small host arrays go to a pinned slot and one H2D copy
-  // into that slot's device arena. A slot's host side is reused only after its copy has
+  // Metadata: a forward's small host arrays (and the token ids when they come from the host) are
+  // staged in a pinned host slot and copied in one transfer into `meta_dev`, a device arena whose
+  // address only changes when it grows. Host slots form a ring; a slot is reused once its copy has
   // completed (event), so forwards can be enqueued back to back without a host sync.
   struct MetaSlot {
     void* host = nullptr;
     size_t host_bytes = 0;
-    DevBuf dev;
     cudaEvent_t copied = nullptr;
     bool pending = false;
   };
   static constexpr int META_SLOTS = 4;
   MetaSlot meta[META_SLOTS];
   int meta_next = 0;
+  DevBuf meta_dev;
   DevBuf tok;         // pos [cap_T] + token_row [cap_T] int32
   int* d_status = nullptr;
   int* h_status = nullptr;
-  DevBuf out_stage;   // device outputs for the host-buffer entry points
+  DevBuf out_stage;   // logits and pooled of the current forward (copied out by the entry points)
   float* h_out = nullptr;  // pinned host outputs
   size_t h_out_bytes = 0;
+
+  // CUDA graphs of whole forwards, keyed by the shape that fixes every launch configuration and
+  // every buffer offset: (tokens, rows, kmax, attention items, pruned-row items). Kernel arguments
+  // point only at the backend's own buffers, so a graph replays any batch of that shape. A shape
+  // is captured the second time it is seen; all graphs are dropped when a buffer moves.
+  bool use_graphs = true;
+  struct Graph {
+    cudaGraphExec_t exec = nullptr;
+    int64_t launches = 0;
+  };
+  std::map<std::vector<int>, Graph> graphs;
+  std::map<std::vector<int>, int> seen;
+  void drop_graphs() {
+    for (auto& kv : graphs) cudaGraphExecDestroy(kv.second.exec);
+    graphs.clear();
+    seen.clear();
+  }
 
   ~s1c_backend() {
     if (stream) cudaStreamSynchronize(stream);
@@ -336,6 +353,7 @@ struct s1c_backend {
       if (sl.host) cudaFreeHost(sl.host);
       if (sl.copied) cudaEventDestroy(sl.copied);
     }
+    drop_graphs();
     if (h_out) cudaFreeHost(h_out);
     if (own_stream) cudaStreamDestroy(own_stream);
   }
@@ -423,6 +441,7 @@ void ensure_capacity(s1c_backend& B, int T, int R) {
   if (want_T > B.cap_T) {
     const int cap = std::max(want_T, B.cap_T + B.cap_T / 2 / 128 * 128);
     CK(cudaStreamSynchronize(B.stream));
+    B.drop_graphs();
     const size_t wide = (size_t)std::max(B.Ipad / 2, B.F);
     B.h.ensure((size_t)cap * B.d * 4);
     B.h2.ensure((size_t)cap * B.d * 4);
@@ -453,6 +472,7 @@ void ensure_capacity(s1c_backend& B, int T, int R) {
   if (want_R > B.cap_R) {
     const int cap = std::max(want_R, B.cap_R + B.cap_R / 2 / 128 * 128);
     CK(cudaStreamSynchronize(B.stream));
+    B.drop_graphs();
     B.xs.ensure((size_t)cap * B.d * 2);
     B.qs.ensure((size_t)cap * B.d * 2);
     B.atts.ensure((size_t)cap * B.d * 2);
@@ -661,8 +681,9 @@ DevMeta upload_meta(s1c_backend& B, const HostMeta& m, const uint32_t* host_ids)
     const void* src;
     size_t bytes;
   };
+  // The ids region is always reserved (ids that are already on the device are copied into it).
   std::vector<Part> parts = {
-      {host_ids, host_ids ? (size_t)m.T * 4 : 0},
+      {host_ids, (size_t)m.T * 4},
       {m.cu.data(), m.cu.size() * 4},
       {m.srows.data(), m.srows.size() * 4},
       {m.mrows.data(), m.mrows.size() * 4},
@@ -691,17 +712,20 @@ DevMeta upload_meta(s1c_backend& B, const HostMeta& m, const uint32_t* host_ids)
     CK(cudaMallocHost(&sl.host, total * 2));
     sl.host_bytes = total * 2;
   }
-  if (total > sl.dev.bytes) {
+  if (total > B.meta_dev.bytes) {
     CK(cudaStreamSynchronize(B.stream));  // kernels of earlier forwards may still read the arena
-    sl.dev.ensure(sl.host_bytes);
+    B.drop_graphs();
+    B.meta_dev.ensure(total * 2);
   }
+  // Only the metadata proper is copied when the ids come from the device.
+  const size_t skip = host_ids ? 0 : off[1];
   char* hs = static_cast<char*>(sl.host);
   for (size_t i = 0; i < parts.size(); ++i)
-    if (parts[i].bytes) std::memcpy(hs + off[i], parts[i].src, parts[i].bytes);
-  CK(cudaMemcpyAsync(sl.dev.p, sl.host, total, cudaMemcpyHostToDevice, B.stream));
+    if (parts[i].bytes && parts[i].src) std::memcpy(hs + off[i], parts[i].src, parts[i].bytes);
+  CK(cudaMemcpyAsync(B.meta_dev.as<char>() + skip, hs + skip, total - skip, cudaMemcpyHostToDevice, B.stream));
   CK(cudaEventRecord(sl.copied, B.stream));
   sl.pending = true;
-  char* dv = sl.dev.as<char>();
+  char* dv = B.meta_dev.as<char>();
   DevMeta dm;
   dm.ids = reinterpret_cast<const uint32_t*>(dv + off[0]);
   dm.cu = reinterpret_cast<const int*>(dv + off[1]);
@@ -946,6 +970,66 @@ void check_status(s1c_backend& B) {
   }
 }
 
+// Enqueue one forward. Token ids come from the host (`host_ids`, staged with the metadata) or
+// from device memory (`dev_ids`, copied into the arena); logits and pooled land in `out_stage`;
+// `d_hidden` (nullable) receives the encoder's final hidden state directly. With graphs on, a
+// shape seen before replays its captured graph instead of launching kernel by kernel.
+struct StageOut {
+  float* logits;
+  float* pooled;
+  size_t n_logits, n_pooled;
+};
+StageOut enqueue_forward(s1c_backend& B, const s1c_varlen& in, const uint32_t* host_ids, const uint32_t* dev_ids,
+                         float* d_hidden) {
+  HostMeta m = make_meta(in, B.window, B.attn_tc ? ATTC_BQ : ATT_BQ);
+  ensure_capacity(B, m.T, m.R);
+  const size_t nl = (size_t)m.M, np = (size_t)m.n * B.d;
+  const size_t need = ((nl + 63) / 64 * 64 + np) * 4;
+  if (need > B.out_stage.bytes) {
+    CK(cudaStreamSynchronize(B.stream));
+    B.drop_graphs();
+    B.out_stage.ensure(need * 2);
+  }
+  StageOut so{B.out_stage.as<float>(), B.out_stage.as<float>() + (nl + 63) / 64 * 64, nl, np};
+  DevMeta dm = upload_meta(B, m, host_ids);
+  if (dev_ids)
+    CK(cudaMemcpyAsync(const_cast<uint32_t*>(dm.ids), dev_ids, (size_t)m.T * 4, cudaMemcpyDeviceToDevice, B.stream));
+  const bool graphable = B.use_graphs && !d_hidden && !B.prof_on && B.stream != nullptr &&
+                         B.stream != cudaStreamLegacy && B.stream != cudaStreamPerThread;
+  if (!graphable) {
+    forward_enqueue(B, m, dm, dm.ids, so.logits, so.pooled, d_hidden);
+    return so;
+  }
+  const std::vector<int> key = {m.T, m.n, m.kmax, (int)m.items_full.size(), (int)m.items_rows.size()};
+  auto it = B.graphs.find(key);
+  if (it == B.graphs.end()) {
+    if (B.seen[key]++ < 1) {  // first sighting: launch directly
+      forward_enqueue(B, m, dm, dm.ids, so.logits, so.pooled, nullptr);
+      return so;
+    }
+    if (B.graphs.size() >= 64) B.drop_graphs();
+    cudaGraph_t g = nullptr;
+    CK(cudaStreamBeginCapture(B.stream, cudaStreamCaptureModeThreadLocal));
+    try {
+      forward_enqueue(B, m, dm, dm.ids, so.logits, so.pooled, nullptr);
+    } catch (...) {
+      cudaStreamEndCapture(B.stream, &g);
+      if (g) cudaGraphDestroy(g);
+      throw;
+    }
+    CK(cudaStreamEndCapture(B.stream, &g));
+    s1c_backend::Graph gr;
+    const cudaError_t e = cudaGraphInstantiate(&gr.exec, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) throw S1cError(S1C_ERR_CUDA, std::string("cudaGraphInstantiate: ") + cudaGetErrorString(e));
+    gr.launches = B.launches;
+    it = B.graphs.emplace(key, gr).first;
+  }
+  CK(cudaGraphLaunch(it->second.exec, B.stream));
+  B.launches = it->second.launches;
+  return so;
+}
+
 // Host-buffer forward: ids and metadata copied in, logits / pooled / hidden copied out.
 void forward_host(s1c_backend& B, const s1c_varlen& in, float* logits, float* pooled, float* hidden) {
   validate_varlen(B, in);
@@ -953,17 +1037,13 @@ void forward_host(s1c_backend& B, const s1c_varlen& in, float* logits, float* po
   const int T = in.cu_seqlens[in.n];
   for (int t = 0; t < T; ++t)
     if (in.ids[t] >= (uint32_t)B.V) throw S1cError(S1C_ERR_ARG, "token " + std::to_string(t) + ": id outside the vocabulary");
-  HostMeta m = make_meta(in, B.window, B.attn_tc ? ATTC_BQ : ATT_BQ);
-  ensure_capacity(B, m.T, m.R);
-  const size_t nl = (size_t)m.M, np = (size_t)m.n * B.d, nh = hidden ? (size_t)m.T * B.d : 0;
-  B.out_stage.ensure((nl + np + nh + 64) * 4);
-  float* d_logits = B.out_stage.as<float>();
-  float* d_pooled = d_logits + (nl + 15) / 16 * 16;
-  float* d_hidden = hidden ? d_pooled + (np + 15) / 16 * 16 : nullptr;
-  DevMeta dm = upload_meta(B, m, in.ids);
-  forward_enqueue(B, m, dm, dm.ids, d_logits, d_pooled, d_hidden);
-  const size_t out_bytes = (nl + np + nh) * 4;
+  const size_t nh = hidden ? (size_t)T * B.d : 0;
+  DevBuf hid_dev;
+  if (nh) hid_dev.ensure(nh * 4);
+  const StageOut so = enqueue_forward(B, in, in.ids, nullptr, nh ? hid_dev.as<float>() : nullptr);
+  const size_t out_bytes = (so.n_logits + so.n_pooled + nh) * 4;
   if (out_bytes > B.h_out_bytes) {
+    CK(cudaStreamSynchronize(B.stream));
     if (B.h_out) cudaFreeHost(B.h_out);
     B.h_out = nullptr;
     B.h_out_bytes = 0;
@@ -971,13 +1051,24 @@ void forward_host(s1c_backend& B, const s1c_varlen& in, float* logits, float* po
     B.h_out_bytes = out_bytes * 2 + 64;
   }
   float* ho = B.h_out;
-  if (nl) CK(cudaMemcpyAsync(ho, d_logits, nl * 4, cudaMemcpyDeviceToHost, B.stream));
-  CK(cudaMemcpyAsync(ho + nl, d_pooled, np * 4, cudaMemcpyDeviceToHost, B.stream));
-  if (nh) CK(cudaMemcpyAsync(ho + nl + np, d_hidden, nh * 4, cudaMemcpyDeviceToHost, B.stream));
+  if (so.n_logits) CK(cudaMemcpyAsync(ho, so.logits, so.n_logits * 4, cudaMemcpyDeviceToHost, B.stream));
+  CK(cudaMemcpyAsync(ho + so.n_logits, so.pooled, so.n_pooled * 4, cudaMemcpyDeviceToHost, B.stream));
+  if (nh) CK(cudaMemcpyAsync(ho + so.n_logits + so.n_pooled, hid_dev.p, nh * 4, cudaMemcpyDeviceToHost, B.stream));
   check_status(B);
-  if (nl) std::memcpy(logits, ho, nl * 4);
-  std::memcpy(pooled, ho + nl, np * 4);
-  if (nh) std::memcpy(hidden, ho + nl + np, nh * 4);
+  if (so.n_logits) std::memcpy(logits, ho, so.n_logits * 4);
+  std::memcpy(pooled, ho + so.n_logits, so.n_pooled * 4);
+  if (nh) std::memcpy(hidden, ho + so.n_logits + so.n_pooled, nh * 4);
+}
+
+// Device-buffer forward: ids already on the device, outputs copied device to device.
+void forward_device(s1c_backend& B, const s1c_varlen& in, const uint32_t* d_ids, float* d_logits, float* d_pooled,
+                    float* d_hidden) {
+  validate_varlen(B, in);
+  if (in.n == 0) return;
+  const StageOut so = enqueue_forward(B, in, nullptr, d_ids, d_hidden);
+  if (so.n_logits)
+    CK(cudaMemcpyAsync(d_logits, so.logits, so.n_logits * 4, cudaMemcpyDeviceToDevice, B.stream));
+  CK(cudaMemcpyAsync(d_pooled, so.pooled, so.n_pooled * 4, cudaMemcpyDeviceToDevice, B.stream));
 }
 
 // Padded Batch -> varlen (Packing::new, lib.rs:906-930): real tokens row-major; positions are
@@ -1018,7 +1109,7 @@ void pack_batch(const s1c_batch& b, PackedBatch& p) {
 }
 
 // Backend settings, a strict comma list like the reference's `Knobs` (laya-mlx/src/lib.rs:155-259):
-// an unknown key or value is an error naming it. Keys: attn=tc|mma, gemm=auto|1cta|2cta.
+// an unknown key or value is an error naming it. Keys: attn=tc|mma, gemm=auto|1cta|2cta, graphs=0|1.
 void apply_settings(s1c_backend& B, const char* spec) {
   if (!spec) return;
   std::string s(spec);
@@ -1031,7 +1122,11 @@ void apply_settings(s1c_backend& B, const char* spec) {
     if (kv.empty()) continue;
     const size_t eq = kv.find('=');
     const std::string k = kv.substr(0, eq), v = eq == std::string::npos ? "" : kv.substr(eq + 1);
-    if (k == "gemm") {
+    if (k == "graphs") {
+      if (v == "1") B.use_graphs = true;
+      else if (v == "0") B.use_graphs = false;
+      else throw S1cError(S1C_ERR_CONFIG, "settings: `" + kv + "`: `" + v + "` is not 0 or 1");
+    } else if (k == "gemm") {
       if (v == "auto") B.gemm_variant = 0;
       else if (v == "1cta") B.gemm_variant = 1;
       else if (v == "2cta") B.gemm_variant = 2;
@@ -1209,12 +1304,7 @@ s1c_status s1c_forward_device_async(s1c_backend* b, const s1c_varlen* in, const 
   return guarded(b, [&] {
     if (!in || !d_ids || !d_pooled || (in->n > 0 && in->kmax > 0 && !d_logits))
       throw S1cError(S1C_ERR_ARG, "null argument");
-    validate_varlen(*b, *in);
-    if (in->n == 0) return;
-    HostMeta m = make_meta(*in, b->window, b->attn_tc ? ATTC_BQ : ATT_BQ);
-    ensure_capacity(*b, m.T, m.R);
-    DevMeta dm = upload_meta(*b, m, nullptr);
-    forward_enqueue(*b, m, dm, d_ids, d_logits, d_pooled, d_hidden);
+    forward_device(*b, *in, d_ids, d_logits, d_pooled, d_hidden);
   });
 }
 
@@ -1227,12 +1317,7 @@ s1c_status s1c_forward_device(s1c_backend* b, const s1c_varlen* in, const uint32
   return guarded(b, [&] {
     if (!in || !d_ids || !d_pooled || (in->n > 0 && in->kmax > 0 && !d_logits))
       throw S1cError(S1C_ERR_ARG, "null argument");
-    validate_varlen(*b, *in);
-    if (in->n == 0) return;
-    HostMeta m = make_meta(*in, b->window, b->attn_tc ? ATTC_BQ : ATT_BQ);
-    ensure_capacity(*b, m.T, m.R);
-    DevMeta dm = upload_meta(*b, m, nullptr);
-    forward_enqueue(*b, m, dm, d_ids, d_logits, d_pooled, d_hidden);
+    forward_device(*b, *in, d_ids, d_logits, d_pooled, d_hidden);
     check_status(*b);
   });
 }
@@ -1246,10 +1331,9 @@ s1c_status s1c_gemm(int32_t epi, const void* d_A, const void* d_B, void* d_out, 
   try {
     if (!d_A || !d_B || !d_out || M <= 0 || N <= 0 || K <= 0 || K % 8 || N % 32)
       throw S1cError(S1C_ERR_ARG, "bad GEMM arguments (K must be a multiple of 8, N of 32)");
-    int dev = 0;
+    int dev = 0, n_sms = 0;
     CK(cudaGetDevice(&dev));
-    cudaDeviceProp prop;
-    CK(cudaGetDeviceProperties(&prop, dev));
+    CK(cudaDeviceGetAttribute(&n_sms, cudaDevAttrMultiProcessorCount, dev));
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     GemmArgs a{};
     a.M = M; a.N = N; a.K = K; a.bias = d_bias; a.act = act; a.out_f32 = out_f32;
@@ -1277,10 +1361,10 @@ s1c_status s1c_gemm(int32_t epi, const void* d_A, const void* d_B, void* d_out, 
     const WeightMap tb = make_wmap(d_B, N, K, K);
     const CUtensorMap tc = make_out_tmap(d_out, f32, (uint64_t)M, out_w, out_w);
     switch (epi) {
-      case EPI_STORE: launch_gemm<EPI_STORE>(ta, tb, tc, a, prop.multiProcessorCount, st, variant); break;
-      case EPI_ROPE: launch_gemm<EPI_ROPE>(ta, tb, tc, a, prop.multiProcessorCount, st, variant); break;
-      case EPI_GEGLU: launch_gemm<EPI_GEGLU>(ta, tb, tc, a, prop.multiProcessorCount, st, variant); break;
-      case EPI_RESID: launch_gemm<EPI_RESID>(ta, tb, tc, a, prop.multiProcessorCount, st, variant); break;
+      case EPI_STORE: launch_gemm<EPI_STORE>(ta, tb, tc, a, n_sms, st, variant); break;
+      case EPI_ROPE: launch_gemm<EPI_ROPE>(ta, tb, tc, a, n_sms, st, variant); break;
+      case EPI_GEGLU: launch_gemm<EPI_GEGLU>(ta, tb, tc, a, n_sms, st, variant); break;
+      case EPI_RESID: launch_gemm<EPI_RESID>(ta, tb, tc, a, n_sms, st, variant); break;
       default: throw S1cError(S1C_ERR_ARG, "unknown epilogue");
     }
     return S1C_OK;
