@@ -45,6 +45,9 @@ struct GemmArgs {
   const float* inv_freq;  // EPI_ROPE: [32] inverse frequencies of the layer's theta
   int rope_cols;          // EPI_ROPE: columns [0, rope_cols) hold q and k heads
   int out_cols;           // EPI_GEGLU: output width I
+  int k_splits;           // > 1: split-K; each split reduce-adds its fp32 partial sums into the output
+                          // map (the fp32 residual for EPI_RESID, else a zeroed workspace that
+                          // splitk_finalize turns into the epilogue's output)
   int* status;
 };
 
@@ -123,6 +126,28 @@ S1C_DEV void add_bias32(float* v, const float* bias, int col) {
   for (int i = 0; i < 8; ++i) {
     const float4 b = __ldg(b4 + i);
     v[4 * i] += b.x; v[4 * i + 1] += b.y; v[4 * i + 2] += b.z; v[4 * i + 3] += b.w;
+  }
+}
+
+// Split-K partial sums: raw fp32 accumulators (bias only on split 0 of a residual GEMM) reduce-added
+// into the output map in 32-column units.
+template <int BN>
+__device__ __forceinline__ void gemm_epilogue_partial(const GemmArgs& args, const CUtensorMap* tmC, Stager& sg,
+                                                      uint32_t t, bool m_ok, int y0, int n0, const float* bias) {
+#pragma unroll 1
+  for (int c = 0; c < BN / 32; ++c) {
+    float v[32];
+    tmem_ld32(t + c * 32, v);
+    const int col = n0 + c * 32;
+    if (col >= args.N) continue;
+    if (bias) add_bias32(v, bias, col);
+    if (!m_ok) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = 0.f;
+    }
+    uint8_t* buf = sg.acquire();
+    sg.put_f32x32(buf, v);
+    sg.issue(tmC, buf, col, y0, true);
   }
 }
 
@@ -261,8 +286,17 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_m = (args.M + BM - 1) / BM, num_n = (args.N + BN - 1) / BN;
-  const int num_tiles = num_m * num_n;
+  const int ksp = args.k_splits > 1 ? args.k_splits : 1;  // host keeps ksp <= nk
+  const int num_tiles = num_m * num_n * ksp;
   const int nk = (args.K + BK - 1) / BK;
+  // tile -> (m block, n block, k split); the split covers k blocks [kb0, kb1)
+  auto decode = [&](int tile, int& m_block, int& n_block, int& kb0, int& kb1) {
+    const int mn = tile / ksp, ks = tile % ksp;
+    m_block = mn / num_n;
+    n_block = mn % num_n;
+    kb0 = ks * nk / ksp;
+    kb1 = (ks + 1) * nk / ksp;
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -294,8 +328,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       uint32_t ph = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
-        const int m0 = (tile / num_n) * BM, n0 = (tile % num_n) * BN;
-        for (int kb = 0; kb < nk; ++kb) {
+        int mb, nb, kb0, kb1;
+        decode(tile, mb, nb, kb0, kb1);
+        const int m0 = mb * BM, n0 = nb * BN;
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[s], ph ^ 1u, args.status, DEV_TIMEOUT_PRODUCER, abort_flag)) {
             ok = false;
             break;
@@ -333,7 +369,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         if (!mbar_wait(&tempty[acc], aph ^ 1u, args.status, DEV_TIMEOUT_MMA_TEMPTY, abort_flag)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + (uint32_t)(acc * BN);
-        for (int kb = 0; kb < nk; ++kb) {
+        int mb, nb, kb0, kb1;
+        decode(tile, mb, nb, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[s], ph, args.status, DEV_TIMEOUT_MMA_FULL, abort_flag)) {
             ok = false;
             break;
@@ -343,7 +381,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k)
             umma_bf16(d, sdesc_kmajor_sw128(a0 + k * 32), sdesc_kmajor_sw128(b0 + k * 32), idesc,
-                      (kb | k) != 0 ? 1u : 0u);
+                      (kb != kb0 || k != 0) ? 1u : 0u);
           umma_commit(&empty[s]);
           if (++s == STAGES) {
             s = 0;
@@ -366,13 +404,19 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     int acc = 0;
     uint32_t aph = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      const int m0 = (tile / num_n) * BM, n_block = tile % num_n;
+      int mb, n_block, kb0, kb1;
+      decode(tile, mb, n_block, kb0, kb1);
+      const int m0 = mb * BM;
       const int y0 = m0 + quad * 32;
       const int row = y0 + lane;
       if (!mbar_wait_warp(&tfull[acc], aph, args.status, DEV_TIMEOUT_EPILOGUE, abort_flag)) break;
       tc_fence_after();
       const uint32_t t = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
-      gemm_epilogue_tile<BN, EPI>(args, &tmC, sg, t, row, row < args.M, y0, n_block * BN, n_block);
+      if (ksp > 1)
+        gemm_epilogue_partial<BN>(args, &tmC, sg, t, row < args.M, y0, n_block * BN,
+                                  (EPI == EPI_RESID && kb0 == 0) ? args.bias : nullptr);
+      else
+        gemm_epilogue_tile<BN, EPI>(args, &tmC, sg, t, row, row < args.M, y0, n_block * BN, n_block);
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
       acc ^= 1;

@@ -28,6 +28,7 @@
 #include "attention_tc.cuh"
 #include "gemm_sm100.cuh"
 #include "gemm_sm100_2cta.cuh"
+#include "splitk.cuh"
 #include "rowwise.cuh"
 
 using namespace s1c;
@@ -173,12 +174,63 @@ void set_all_gemm_smem() {
   set_gemm_smem<EPI_RESID>();
 }
 
-// GEMM variant: 0 = by shape (two-CTA when there are at least 256 rows), 1 = one-CTA, 2 = two-CTA.
+// Where a GEMM's output goes, for the split-K path: the output buffer and its row pitch, and the
+// fp32 workspace the splits reduce into (nullptr for residual GEMMs, which reduce straight into the
+// fp32 stream). The workspace is all zeros between GEMMs.
+struct SplitCtx {
+  float* ws;
+  size_t ws_bytes;
+  void* out;
+  int ldo;
+};
+
+// Split-K factor for a GEMM with few output tiles: enough splits to cover the SMs, at least one
+// 64-wide K block per split. 1 = no split.
+int pick_k_splits(int M, int N, int K, int num_sms) {
+  const int tiles = ((M + GEMM_BM - 1) / GEMM_BM) * ((N + GEMM_BN - 1) / GEMM_BN);
+  const int nk = (K + GEMM_BK - 1) / GEMM_BK;
+  if (tiles * 2 > num_sms) return 1;
+  return std::max(1, std::min({num_sms / tiles, nk, 32}));
+}
+
+// GEMM variant: 0 = by shape (split-K when there are few tiles and a split context is given,
+// two-CTA when there are at least 256 rows), 1 = one-CTA, 2 = two-CTA, 3 = one-CTA split-K.
 template <int EPI>
-void launch_gemm(const CUtensorMap& ta, const WeightMap& tb, const CUtensorMap& tc, const GemmArgs& a, int num_sms,
-                 cudaStream_t st, int variant = 0) {
-  if (a.M <= 0) return;
-  const bool two = variant == 2 || (variant == 0 && a.M >= 256);
+void launch_gemm(const CUtensorMap& ta, const WeightMap& tb, const CUtensorMap& tc, const GemmArgs& a0, int num_sms,
+                 cudaStream_t st, int variant = 0, const SplitCtx* sk = nullptr, int64_t* extra_launches = nullptr) {
+  if (a0.M <= 0) return;
+  GemmArgs a = a0;
+  a.k_splits = 1;
+  int ksp = 1;
+  if (sk && (variant == 0 || variant == 3)) {
+    ksp = pick_k_splits(a.M, a.N, a.K, num_sms);
+    if (variant == 3) ksp = std::max(ksp, std::min(2, (a.K + GEMM_BK - 1) / GEMM_BK));
+    const size_t ws_need = (size_t)((a.M + GEMM_BM - 1) / GEMM_BM) * GEMM_BM * a.N * 4;
+    if (EPI != EPI_RESID && (!sk->ws || ws_need > sk->ws_bytes)) ksp = 1;
+  }
+  if (ksp > 1) {
+    a.k_splits = ksp;
+    const int tiles = ((a.M + GEMM_BM - 1) / GEMM_BM) * ((a.N + GEMM_BN - 1) / GEMM_BN) * ksp;
+    const int grid = std::min(tiles, num_sms);
+    if (EPI == EPI_RESID) {
+      gemm_bf16_sm100<GEMM_BN, EPI><<<grid, GEMM_THREADS, gemm_smem_bytes(GEMM_BN), st>>>(ta, tb.full, tc, a);
+      CK(cudaGetLastError());
+      return;
+    }
+    const int rows = (a.M + GEMM_BM - 1) / GEMM_BM * GEMM_BM;
+    const CUtensorMap tw = make_out_tmap(sk->ws, true, rows, a.N, a.N);
+    gemm_bf16_sm100<GEMM_BN, EPI><<<grid, GEMM_THREADS, gemm_smem_bytes(GEMM_BN), st>>>(ta, tb.full, tw, a);
+    CK(cudaGetLastError());
+    SplitKFinal f{sk->ws, a.M, a.N, sk->out, sk->ldo, a.bias, a.act, a.out_f32, a.pos, a.inv_freq, a.rope_cols,
+                  a.out_cols};
+    const long work = (long)a.M * ((EPI == EPI_GEGLU ? a.out_cols : a.N) / 8);
+    splitk_finalize_kernel<EPI><<<(unsigned)((work + 255) / 256), 256, 0, st>>>(f);
+    CK(cudaGetLastError());
+    if (extra_launches) ++*extra_launches;
+    return;
+  }
+  // By shape the one-CTA kernel runs: on the encoder shapes the two-CTA kernel measured the same.
+  const bool two = variant == 2;
   if (two) {
     const int tiles = ((a.M + 255) / 256) * ((a.N + GEMM_BN - 1) / GEMM_BN);
     const int clusters = std::min(tiles, num_sms / 2);
@@ -322,6 +374,7 @@ struct s1c_backend {
   int* d_status = nullptr;
   int* h_status = nullptr;
   DevBuf out_stage;   // logits and pooled of the current forward (copied out by the entry points)
+  DevBuf splitk_ws;   // split-K fp32 partial sums (all zeros between GEMMs)
   float* h_out = nullptr;  // pinned host outputs
   size_t h_out_bytes = 0;
 
@@ -594,6 +647,8 @@ void build(s1c_backend& B, const s1c_model_desc& D, const s1c_tensor* tensors, i
   B.inv_freq[1] = make_inv_freq(B, D.local_rope_theta);
   CK(cudaMalloc(&B.d_status, sizeof(int)));
   CK(cudaMemset(B.d_status, 0, sizeof(int)));
+  B.splitk_ws.ensure((size_t)16 << 20);
+  CK(cudaMemset(B.splitk_ws.p, 0, B.splitk_ws.bytes));
   CK(cudaMallocHost(&B.h_status, sizeof(int)));
   ensure_capacity(B, std::max(D.max_tokens, 128), 128);
 }
@@ -834,6 +889,10 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
     launch(B, nl, name, 0, (double)rows * d * 6.0, [&] { launch_ln<D>(in, gather, rows, w, b, eps, out, st); });
   };
   const double fl = 2.0 * T;  // GEMM FLOPs per (output column x reduction element)
+  // Split-K contexts: output buffer + pitch for the finalize step; residual GEMMs need no workspace.
+  auto sk = [&](void* out, int ldo) { return SplitCtx{B.splitk_ws.as<float>(), B.splitk_ws.bytes, out, ldo}; };
+  const SplitCtx skr{nullptr, 0, nullptr, 0};
+  SplitCtx sk_tmp{};
 
   for (int i = 0; i < B.L; ++i) {
     const EncLayer& l = B.layers[i];
@@ -842,19 +901,19 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
     g.pos = pos;
     g.inv_freq = B.inv_freq[l.local ? 1 : 0];
     g.rope_cols = 2 * d;
-    launch(B, nl, "gemm_qkv_rope", fl * 3 * d * d, 0, [&] { launch_gemm<EPI_ROPE>(B.tm_x, l.tm_wqkv, B.to_qkv3, g, nsm, st, B.gemm_variant); });
+    launch(B, nl, "gemm_qkv_rope", fl * 3 * d * d, 0, [&] { launch_gemm<EPI_ROPE>(B.tm_x, l.tm_wqkv, B.to_qkv3, g, nsm, st, B.gemm_variant, &(sk_tmp = sk(qkv, 3 * d)), &nl); });
     attn(l.local ? "attn_local" : "attn_global", B.tm_qkv_att, B.tm_qkv_att, 0, d, 2 * d, qkv, qkv + d,
          qkv + 2 * d, att, 3 * d, 3 * d, 3 * d, d, dm.items_full, (int)m.items_full.size(), l.local ? B.window : -1,
          l.local ? m.pairs_local : m.pairs_global);
     GemmArgs go = gemm_args(T, d, d);
-    launch(B, nl, "gemm_wo_resid", fl * d * d, 0, [&] { launch_gemm<EPI_RESID>(B.tm_att, l.tm_wo, B.to_h, go, nsm, st, B.gemm_variant); });
+    launch(B, nl, "gemm_wo_resid", fl * d * d, 0, [&] { launch_gemm<EPI_RESID>(B.tm_att, l.tm_wo, B.to_h, go, nsm, st, B.gemm_variant, &skr, &nl); });
     ln("ln_mlp", h, nullptr, T, l.mlp_norm, nullptr, B.eps, x);
     GemmArgs gi = gemm_args(T, B.Ipad, d);
     gi.out_cols = B.I;
-    launch(B, nl, "gemm_wi_geglu", fl * 2 * B.I * d, 0, [&] { launch_gemm<EPI_GEGLU>(B.tm_x, l.tm_wi, B.to_act_i, gi, nsm, st, B.gemm_variant); });
+    launch(B, nl, "gemm_wi_geglu", fl * 2 * B.I * d, 0, [&] { launch_gemm<EPI_GEGLU>(B.tm_x, l.tm_wi, B.to_act_i, gi, nsm, st, B.gemm_variant, &(sk_tmp = sk(act, B.I)), &nl); });
     GemmArgs g2 = gemm_args(T, d, B.I);
     launch(B, nl, "gemm_wo2_resid", fl * B.I * d, 0,
-           [&] { launch_gemm<EPI_RESID>(B.tm_act_i, l.tm_wo2, B.to_h, g2, nsm, st, B.gemm_variant); });
+           [&] { launch_gemm<EPI_RESID>(B.tm_act_i, l.tm_wo2, B.to_h, g2, nsm, st, B.gemm_variant, &skr, &nl); });
   }
 
   // final_norm, + type embedding, head layer 0's norm1
@@ -868,21 +927,21 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
     const HeadLayer& hl = B.head[j];
     GemmArgs g = gemm_args(T, 3 * d, d);
     g.bias = hl.in_b;
-    launch(B, nl, "head_gemm_in", fl * 3 * d * d, 0, [&] { launch_gemm<EPI_STORE>(B.tm_x, hl.tm_in, B.to_qkv3, g, nsm, st, B.gemm_variant); });
+    launch(B, nl, "head_gemm_in", fl * 3 * d * d, 0, [&] { launch_gemm<EPI_STORE>(B.tm_x, hl.tm_in, B.to_qkv3, g, nsm, st, B.gemm_variant, &(sk_tmp = sk(qkv, 3 * d)), &nl); });
     attn("head_attn", B.tm_qkv_att, B.tm_qkv_att, 0, d, 2 * d, qkv, qkv + d, qkv + 2 * d, att, 3 * d, 3 * d,
          3 * d, d, dm.items_full, (int)m.items_full.size(), -1, m.pairs_global);
     GemmArgs go = gemm_args(T, d, d);
     go.bias = hl.out_b;
-    launch(B, nl, "head_gemm_out", fl * d * d, 0, [&] { launch_gemm<EPI_RESID>(B.tm_att, hl.tm_out, B.to_h2, go, nsm, st, B.gemm_variant); });
+    launch(B, nl, "head_gemm_out", fl * d * d, 0, [&] { launch_gemm<EPI_RESID>(B.tm_att, hl.tm_out, B.to_h2, go, nsm, st, B.gemm_variant, &skr, &nl); });
     ln("head_ln", h2, nullptr, T, hl.n2w, hl.n2b, 1e-5f, x);
     GemmArgs g1 = gemm_args(T, B.F, d);
     g1.bias = hl.l1_b;
     g1.act = ACT_RELU;
-    launch(B, nl, "head_gemm_l1", fl * B.F * d, 0, [&] { launch_gemm<EPI_STORE>(B.tm_x, hl.tm_l1, B.to_act_f, g1, nsm, st, B.gemm_variant); });
+    launch(B, nl, "head_gemm_l1", fl * B.F * d, 0, [&] { launch_gemm<EPI_STORE>(B.tm_x, hl.tm_l1, B.to_act_f, g1, nsm, st, B.gemm_variant, &(sk_tmp = sk(act, B.F)), &nl); });
     GemmArgs g2 = gemm_args(T, d, B.F);
     g2.bias = hl.l2_b;
     launch(B, nl, "head_gemm_l2", fl * B.F * d, 0,
-           [&] { launch_gemm<EPI_RESID>(B.tm_act_f, hl.tm_l2, B.to_h2, g2, nsm, st, B.gemm_variant); });
+           [&] { launch_gemm<EPI_RESID>(B.tm_act_f, hl.tm_l2, B.to_h2, g2, nsm, st, B.gemm_variant, &skr, &nl); });
     const HeadLayer& nx = B.head[j + 1];
     ln("head_ln", h2, nullptr, T, nx.n1w, nx.n1b, 1e-5f, x);
   }
@@ -897,7 +956,7 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
     GemmArgs gkv = gemm_args(T, 2 * d, d);
     gkv.bias = hl.in_b + d;
     launch(B, nl, "head_gemm_kv", fl * 2 * d * d, 0,
-           [&] { launch_gemm<EPI_STORE>(B.tm_x, hl.tm_in_kv, B.to_kv2, gkv, nsm, st, B.gemm_variant); });
+           [&] { launch_gemm<EPI_STORE>(B.tm_x, hl.tm_in_kv, B.to_kv2, gkv, nsm, st, B.gemm_variant, &(sk_tmp = sk(qkv, 2 * d)), &nl); });
     launch(B, nl, "gather_rows", 0, (double)R * d * 4, [&] {
       gather_rows_bf16_kernel<<<R, 128, 0, st>>>(x, dm.srows, R, d, B.xs.as<bf16>());
     });
@@ -906,23 +965,23 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
     });
     GemmArgs gq = gemm_args(R, d, d);
     gq.bias = hl.in_b;
-    launch(B, nl, "head_rows_gemm", flr * d * d, 0, [&] { launch_gemm<EPI_STORE>(B.tm_xs, hl.tm_in_q, B.to_qs, gq, nsm, st, B.gemm_variant); });
+    launch(B, nl, "head_rows_gemm", flr * d * d, 0, [&] { launch_gemm<EPI_STORE>(B.tm_xs, hl.tm_in_q, B.to_qs, gq, nsm, st, B.gemm_variant, &(sk_tmp = sk(B.qs.p, d)), &nl); });
     attn("head_rows_attn", B.tm_qs_att, B.tm_kv_att, 0, 0, d, B.qs.as<bf16>(), kv, kv + d, B.atts.as<bf16>(), d,
          2 * d, 2 * d, d, dm.items_rows, (int)m.items_rows.size(), -1, m.pairs_rows);
     GemmArgs go = gemm_args(R, d, d);
     go.bias = hl.out_b;
     launch(B, nl, "head_rows_gemm", flr * d * d, 0,
-           [&] { launch_gemm<EPI_RESID>(B.tm_atts, hl.tm_out, B.to_hs, go, nsm, st, B.gemm_variant); });
+           [&] { launch_gemm<EPI_RESID>(B.tm_atts, hl.tm_out, B.to_hs, go, nsm, st, B.gemm_variant, &skr, &nl); });
     ln("head_ln", B.hs.as<float>(), nullptr, R, hl.n2w, hl.n2b, 1e-5f, B.xs.as<bf16>());
     GemmArgs g1 = gemm_args(R, B.F, d);
     g1.bias = hl.l1_b;
     g1.act = ACT_RELU;
     launch(B, nl, "head_rows_gemm", flr * B.F * d, 0,
-           [&] { launch_gemm<EPI_STORE>(B.tm_xs, hl.tm_l1, B.to_fs, g1, nsm, st, B.gemm_variant); });
+           [&] { launch_gemm<EPI_STORE>(B.tm_xs, hl.tm_l1, B.to_fs, g1, nsm, st, B.gemm_variant, &(sk_tmp = sk(B.fs.p, B.F)), &nl); });
     GemmArgs g2 = gemm_args(R, d, B.F);
     g2.bias = hl.l2_b;
     launch(B, nl, "head_rows_gemm", flr * B.F * d, 0,
-           [&] { launch_gemm<EPI_RESID>(B.tm_fs, hl.tm_l2, B.to_hs, g2, nsm, st, B.gemm_variant); });
+           [&] { launch_gemm<EPI_RESID>(B.tm_fs, hl.tm_l2, B.to_hs, g2, nsm, st, B.gemm_variant, &skr, &nl); });
   }
 
   // scorer at the marker slots, pooled at position 0
@@ -933,7 +992,7 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
     gs.act = ACT_GELU;
     gs.out_f32 = 1;
     launch(B, nl, "scorer_gemm", 2.0 * m.M * B.S * d, 0,
-           [&] { launch_gemm<EPI_STORE>(B.tm_xm, B.tm_sc1, B.to_sh, gs, nsm, st, B.gemm_variant); });
+           [&] { launch_gemm<EPI_STORE>(B.tm_xm, B.tm_sc1, B.to_sh, gs, nsm, st, B.gemm_variant, &(sk_tmp = sk(B.sh.p, B.S)), &nl); });
     launch(B, nl, "scorer_logits", 2.0 * m.M * B.S, 0, [&] {
       scorer_logits_kernel<<<(m.M + 7) / 8, 256, 0, st>>>(B.sh.as<float>(), m.M, B.S, B.sc_w3, B.sc_b3, dm.mcount,
                                                           m.kmax, d_logits);
@@ -1357,14 +1416,24 @@ s1c_status s1c_gemm(int32_t epi, const void* d_A, const void* d_B, void* d_out, 
     const bool f32 = epi == EPI_RESID || (epi == EPI_STORE && out_f32);
     const int out_w = (epi == EPI_GEGLU) ? out_cols : N;
     const CUtensorMap ta = make_tmap(d_A, (uint64_t)M, K, K, GEMM_BM);
-    if (variant < 0 || variant > 2) throw S1cError(S1C_ERR_ARG, "variant must be 0, 1 or 2");
+    if (variant < 0 || variant > 3) throw S1cError(S1C_ERR_ARG, "variant must be 0, 1, 2 or 3");
     const WeightMap tb = make_wmap(d_B, N, K, K);
     const CUtensorMap tc = make_out_tmap(d_out, f32, (uint64_t)M, out_w, out_w);
+    // Split-K workspace of this entry point: one 16 MB zeroed buffer per device, kept for the process.
+    static float* ws_dev[64] = {nullptr};
+    {
+      std::lock_guard<std::mutex> g(mu);
+      if (!ws_dev[dev]) {
+        CK(cudaMalloc(&ws_dev[dev], (size_t)16 << 20));
+        CK(cudaMemset(ws_dev[dev], 0, (size_t)16 << 20));
+      }
+    }
+    const SplitCtx sk{ws_dev[dev], (size_t)16 << 20, d_out, out_w};
     switch (epi) {
-      case EPI_STORE: launch_gemm<EPI_STORE>(ta, tb, tc, a, n_sms, st, variant); break;
-      case EPI_ROPE: launch_gemm<EPI_ROPE>(ta, tb, tc, a, n_sms, st, variant); break;
-      case EPI_GEGLU: launch_gemm<EPI_GEGLU>(ta, tb, tc, a, n_sms, st, variant); break;
-      case EPI_RESID: launch_gemm<EPI_RESID>(ta, tb, tc, a, n_sms, st, variant); break;
+      case EPI_STORE: launch_gemm<EPI_STORE>(ta, tb, tc, a, n_sms, st, variant, &sk); break;
+      case EPI_ROPE: launch_gemm<EPI_ROPE>(ta, tb, tc, a, n_sms, st, variant, &sk); break;
+      case EPI_GEGLU: launch_gemm<EPI_GEGLU>(ta, tb, tc, a, n_sms, st, variant, &sk); break;
+      case EPI_RESID: launch_gemm<EPI_RESID>(ta, tb, tc, a, n_sms, st, variant, &sk); break;
       default: throw S1cError(S1C_ERR_ARG, "unknown epilogue");
     }
     return S1C_OK;

@@ -23,7 +23,7 @@ def _rand(shape, seed, scale=1.0):
     return (torch.randn(*shape, generator=g) * scale).to(torch.bfloat16).cuda()
 
 
-VARIANTS = [1, 2]  # one-CTA 128x256 tiles, two-CTA 256x256 tiles
+VARIANTS = [1, 2, 3]  # one-CTA 128x256 tiles, two-CTA 256x256 tiles, one-CTA split-K
 
 
 @pytest.mark.parametrize("variant", VARIANTS)
