@@ -45,9 +45,10 @@ struct GemmArgs {
   const float* inv_freq;  // EPI_ROPE: [32] inverse frequencies of the layer's theta
   int rope_cols;          // EPI_ROPE: columns [0, rope_cols) hold q and k heads
   int out_cols;           // EPI_GEGLU: output width I
-  int k_splits;           // > 1: split-K; each split reduce-adds its fp32 partial sums into the output
-                          // map (the fp32 residual for EPI_RESID, else a zeroed workspace that
-                          // splitk_finalize turns into the epilogue's output)
+  int k_splits;           // > 1: split-K; split s stores its fp32 partial sums into rows
+                          // [s * split_rows, ...) of the workspace the output map then describes;
+                          // splitk_finalize sums the slices in order and applies the epilogue
+  int split_rows;         // rows of one workspace slice (M rounded up to the tile height)
   int* status;
 };
 
@@ -129,25 +130,20 @@ S1C_DEV void add_bias32(float* v, const float* bias, int col) {
   }
 }
 
-// Split-K partial sums: raw fp32 accumulators (bias only on split 0 of a residual GEMM) reduce-added
-// into the output map in 32-column units.
+// Split-K partial sums: the raw fp32 accumulators of one split, stored (32-column units) into that
+// split's slice of the workspace. Each element of a slice is written by exactly one tile.
 template <int BN>
 __device__ __forceinline__ void gemm_epilogue_partial(const GemmArgs& args, const CUtensorMap* tmC, Stager& sg,
-                                                      uint32_t t, bool m_ok, int y0, int n0, const float* bias) {
+                                                      uint32_t t, int y0, int n0) {
 #pragma unroll 1
   for (int c = 0; c < BN / 32; ++c) {
     float v[32];
     tmem_ld32(t + c * 32, v);
     const int col = n0 + c * 32;
     if (col >= args.N) continue;
-    if (bias) add_bias32(v, bias, col);
-    if (!m_ok) {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = 0.f;
-    }
     uint8_t* buf = sg.acquire();
     sg.put_f32x32(buf, v);
-    sg.issue(tmC, buf, col, y0, true);
+    sg.issue(tmC, buf, col, y0, false);
   }
 }
 
@@ -413,8 +409,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       tc_fence_after();
       const uint32_t t = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
       if (ksp > 1)
-        gemm_epilogue_partial<BN>(args, &tmC, sg, t, row < args.M, y0, n_block * BN,
-                                  (EPI == EPI_RESID && kb0 == 0) ? args.bias : nullptr);
+        gemm_epilogue_partial<BN>(args, &tmC, sg, t, (tile % ksp) * args.split_rows + y0, n_block * BN);
       else
         gemm_epilogue_tile<BN, EPI>(args, &tmC, sg, t, row, row < args.M, y0, n_block * BN, n_block);
       tc_fence_before();

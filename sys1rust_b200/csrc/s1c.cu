@@ -174,9 +174,9 @@ void set_all_gemm_smem() {
   set_gemm_smem<EPI_RESID>();
 }
 
-// Where a GEMM's output goes, for the split-K path: the output buffer and its row pitch, and the
-// fp32 workspace the splits reduce into (nullptr for residual GEMMs, which reduce straight into the
-// fp32 stream). The workspace is all zeros between GEMMs.
+// Where a GEMM's output goes, for the split-K path: the output buffer and its row pitch (the fp32
+// residual stream for residual GEMMs), and the fp32 workspace that holds one slice of partial sums
+// per split.
 struct SplitCtx {
   float* ws;
   size_t ws_bytes;
@@ -185,16 +185,19 @@ struct SplitCtx {
 };
 
 // Split-K factor for a GEMM with few output tiles: enough splits to cover the SMs, at least one
-// 64-wide K block per split. 1 = no split.
-int pick_k_splits(int M, int N, int K, int num_sms) {
+// 64-wide K block per split, at most 16 splits, slices within the workspace. 1 = no split.
+int pick_k_splits(int M, int N, int K, int num_sms, size_t ws_bytes) {
   const int tiles = ((M + GEMM_BM - 1) / GEMM_BM) * ((N + GEMM_BN - 1) / GEMM_BN);
   const int nk = (K + GEMM_BK - 1) / GEMM_BK;
   if (tiles * 2 > num_sms) return 1;
-  return std::max(1, std::min({num_sms / tiles, nk, 32}));
+  int ksp = std::max(1, std::min({num_sms / tiles, nk, 16}));
+  const size_t slice = (size_t)((M + GEMM_BM - 1) / GEMM_BM) * GEMM_BM * N * 4;
+  while (ksp > 1 && (size_t)ksp * slice > ws_bytes) --ksp;
+  return ksp;
 }
 
 // GEMM variant: 0 = by shape (split-K when there are few tiles and a split context is given,
-// two-CTA when there are at least 256 rows), 1 = one-CTA, 2 = two-CTA, 3 = one-CTA split-K.
+// else the one-CTA kernel), 1 = one-CTA, 2 = two-CTA, 3 = one-CTA split-K (at least 2 splits).
 template <int EPI>
 void launch_gemm(const CUtensorMap& ta, const WeightMap& tb, const CUtensorMap& tc, const GemmArgs& a0, int num_sms,
                  cudaStream_t st, int variant = 0, const SplitCtx* sk = nullptr, int64_t* extra_launches = nullptr) {
@@ -202,27 +205,22 @@ void launch_gemm(const CUtensorMap& ta, const WeightMap& tb, const CUtensorMap& 
   GemmArgs a = a0;
   a.k_splits = 1;
   int ksp = 1;
-  if (sk && (variant == 0 || variant == 3)) {
-    ksp = pick_k_splits(a.M, a.N, a.K, num_sms);
-    if (variant == 3) ksp = std::max(ksp, std::min(2, (a.K + GEMM_BK - 1) / GEMM_BK));
-    const size_t ws_need = (size_t)((a.M + GEMM_BM - 1) / GEMM_BM) * GEMM_BM * a.N * 4;
-    if (EPI != EPI_RESID && (!sk->ws || ws_need > sk->ws_bytes)) ksp = 1;
+  const int rows = (a.M + GEMM_BM - 1) / GEMM_BM * GEMM_BM;
+  if (sk && sk->ws && (variant == 0 || variant == 3)) {
+    ksp = pick_k_splits(a.M, a.N, a.K, num_sms, sk->ws_bytes);
+    if (variant == 3 && ksp < 2 && (a.K + GEMM_BK - 1) / GEMM_BK >= 2 && 2 * (size_t)rows * a.N * 4 <= sk->ws_bytes)
+      ksp = 2;
   }
   if (ksp > 1) {
     a.k_splits = ksp;
-    const int tiles = ((a.M + GEMM_BM - 1) / GEMM_BM) * ((a.N + GEMM_BN - 1) / GEMM_BN) * ksp;
+    a.split_rows = rows;
+    const int tiles = (rows / GEMM_BM) * ((a.N + GEMM_BN - 1) / GEMM_BN) * ksp;
     const int grid = std::min(tiles, num_sms);
-    if (EPI == EPI_RESID) {
-      gemm_bf16_sm100<GEMM_BN, EPI><<<grid, GEMM_THREADS, gemm_smem_bytes(GEMM_BN), st>>>(ta, tb.full, tc, a);
-      CK(cudaGetLastError());
-      return;
-    }
-    const int rows = (a.M + GEMM_BM - 1) / GEMM_BM * GEMM_BM;
-    const CUtensorMap tw = make_out_tmap(sk->ws, true, rows, a.N, a.N);
+    const CUtensorMap tw = make_out_tmap(sk->ws, true, (uint64_t)ksp * rows, a.N, a.N);
     gemm_bf16_sm100<GEMM_BN, EPI><<<grid, GEMM_THREADS, gemm_smem_bytes(GEMM_BN), st>>>(ta, tb.full, tw, a);
     CK(cudaGetLastError());
-    SplitKFinal f{sk->ws, a.M, a.N, sk->out, sk->ldo, a.bias, a.act, a.out_f32, a.pos, a.inv_freq, a.rope_cols,
-                  a.out_cols};
+    SplitKFinal f{sk->ws, ksp, rows, a.M, a.N, sk->out, sk->ldo, a.bias, a.act, a.out_f32, a.pos, a.inv_freq,
+                  a.rope_cols, a.out_cols};
     const long work = (long)a.M * ((EPI == EPI_GEGLU ? a.out_cols : a.N) / 8);
     splitk_finalize_kernel<EPI><<<(unsigned)((work + 255) / 256), 256, 0, st>>>(f);
     CK(cudaGetLastError());
@@ -374,7 +372,7 @@ struct s1c_backend {
   int* d_status = nullptr;
   int* h_status = nullptr;
   DevBuf out_stage;   // logits and pooled of the current forward (copied out by the entry points)
-  DevBuf splitk_ws;   // split-K fp32 partial sums (all zeros between GEMMs)
+  DevBuf splitk_ws;   // split-K fp32 partial sums, one slice per split
   float* h_out = nullptr;  // pinned host outputs
   size_t h_out_bytes = 0;
 
@@ -647,8 +645,7 @@ void build(s1c_backend& B, const s1c_model_desc& D, const s1c_tensor* tensors, i
   B.inv_freq[1] = make_inv_freq(B, D.local_rope_theta);
   CK(cudaMalloc(&B.d_status, sizeof(int)));
   CK(cudaMemset(B.d_status, 0, sizeof(int)));
-  B.splitk_ws.ensure((size_t)16 << 20);
-  CK(cudaMemset(B.splitk_ws.p, 0, B.splitk_ws.bytes));
+  B.splitk_ws.ensure((size_t)32 << 20);
   CK(cudaMallocHost(&B.h_status, sizeof(int)));
   ensure_capacity(B, std::max(D.max_tokens, 128), 128);
 }
@@ -889,9 +886,9 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
     launch(B, nl, name, 0, (double)rows * d * 6.0, [&] { launch_ln<D>(in, gather, rows, w, b, eps, out, st); });
   };
   const double fl = 2.0 * T;  // GEMM FLOPs per (output column x reduction element)
-  // Split-K contexts: output buffer + pitch for the finalize step; residual GEMMs need no workspace.
+  // Split-K contexts: the output buffer and pitch the finalize step writes (for residual GEMMs the
+  // fp32 stream it adds to).
   auto sk = [&](void* out, int ldo) { return SplitCtx{B.splitk_ws.as<float>(), B.splitk_ws.bytes, out, ldo}; };
-  const SplitCtx skr{nullptr, 0, nullptr, 0};
   SplitCtx sk_tmp{};
 
   for (int i = 0; i < B.L; ++i) {
@@ -906,14 +903,14 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
          qkv + 2 * d, att, 3 * d, 3 * d, 3 * d, d, dm.items_full, (int)m.items_full.size(), l.local ? B.window : -1,
          l.local ? m.pairs_local : m.pairs_global);
     GemmArgs go = gemm_args(T, d, d);
-    launch(B, nl, "gemm_wo_resid", fl * d * d, 0, [&] { launch_gemm<EPI_RESID>(B.tm_att, l.tm_wo, B.to_h, go, nsm, st, B.gemm_variant, &skr, &nl); });
+    launch(B, nl, "gemm_wo_resid", fl * d * d, 0, [&] { launch_gemm<EPI_RESID>(B.tm_att, l.tm_wo, B.to_h, go, nsm, st, B.gemm_variant, &(sk_tmp = sk(h, d)), &nl); });
     ln("ln_mlp", h, nullptr, T, l.mlp_norm, nullptr, B.eps, x);
     GemmArgs gi = gemm_args(T, B.Ipad, d);
     gi.out_cols = B.I;
     launch(B, nl, "gemm_wi_geglu", fl * 2 * B.I * d, 0, [&] { launch_gemm<EPI_GEGLU>(B.tm_x, l.tm_wi, B.to_act_i, gi, nsm, st, B.gemm_variant, &(sk_tmp = sk(act, B.I)), &nl); });
     GemmArgs g2 = gemm_args(T, d, B.I);
     launch(B, nl, "gemm_wo2_resid", fl * B.I * d, 0,
-           [&] { launch_gemm<EPI_RESID>(B.tm_act_i, l.tm_wo2, B.to_h, g2, nsm, st, B.gemm_variant, &skr, &nl); });
+           [&] { launch_gemm<EPI_RESID>(B.tm_act_i, l.tm_wo2, B.to_h, g2, nsm, st, B.gemm_variant, &(sk_tmp = sk(h, d)), &nl); });
   }
 
   // final_norm, + type embedding, head layer 0's norm1
@@ -932,7 +929,7 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
          3 * d, d, dm.items_full, (int)m.items_full.size(), -1, m.pairs_global);
     GemmArgs go = gemm_args(T, d, d);
     go.bias = hl.out_b;
-    launch(B, nl, "head_gemm_out", fl * d * d, 0, [&] { launch_gemm<EPI_RESID>(B.tm_att, hl.tm_out, B.to_h2, go, nsm, st, B.gemm_variant, &skr, &nl); });
+    launch(B, nl, "head_gemm_out", fl * d * d, 0, [&] { launch_gemm<EPI_RESID>(B.tm_att, hl.tm_out, B.to_h2, go, nsm, st, B.gemm_variant, &(sk_tmp = sk(h2, d)), &nl); });
     ln("head_ln", h2, nullptr, T, hl.n2w, hl.n2b, 1e-5f, x);
     GemmArgs g1 = gemm_args(T, B.F, d);
     g1.bias = hl.l1_b;
@@ -941,7 +938,7 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
     GemmArgs g2 = gemm_args(T, d, B.F);
     g2.bias = hl.l2_b;
     launch(B, nl, "head_gemm_l2", fl * B.F * d, 0,
-           [&] { launch_gemm<EPI_RESID>(B.tm_act_f, hl.tm_l2, B.to_h2, g2, nsm, st, B.gemm_variant, &skr, &nl); });
+           [&] { launch_gemm<EPI_RESID>(B.tm_act_f, hl.tm_l2, B.to_h2, g2, nsm, st, B.gemm_variant, &(sk_tmp = sk(h2, d)), &nl); });
     const HeadLayer& nx = B.head[j + 1];
     ln("head_ln", h2, nullptr, T, nx.n1w, nx.n1b, 1e-5f, x);
   }
@@ -971,7 +968,7 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
     GemmArgs go = gemm_args(R, d, d);
     go.bias = hl.out_b;
     launch(B, nl, "head_rows_gemm", flr * d * d, 0,
-           [&] { launch_gemm<EPI_RESID>(B.tm_atts, hl.tm_out, B.to_hs, go, nsm, st, B.gemm_variant, &skr, &nl); });
+           [&] { launch_gemm<EPI_RESID>(B.tm_atts, hl.tm_out, B.to_hs, go, nsm, st, B.gemm_variant, &(sk_tmp = sk(B.hs.p, d)), &nl); });
     ln("head_ln", B.hs.as<float>(), nullptr, R, hl.n2w, hl.n2b, 1e-5f, B.xs.as<bf16>());
     GemmArgs g1 = gemm_args(R, B.F, d);
     g1.bias = hl.l1_b;
@@ -981,7 +978,7 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
     GemmArgs g2 = gemm_args(R, d, B.F);
     g2.bias = hl.l2_b;
     launch(B, nl, "head_rows_gemm", flr * B.F * d, 0,
-           [&] { launch_gemm<EPI_RESID>(B.tm_fs, hl.tm_l2, B.to_hs, g2, nsm, st, B.gemm_variant, &skr, &nl); });
+           [&] { launch_gemm<EPI_RESID>(B.tm_fs, hl.tm_l2, B.to_hs, g2, nsm, st, B.gemm_variant, &(sk_tmp = sk(B.hs.p, d)), &nl); });
   }
 
   // scorer at the marker slots, pooled at position 0
@@ -1419,16 +1416,13 @@ s1c_status s1c_gemm(int32_t epi, const void* d_A, const void* d_B, void* d_out, 
     if (variant < 0 || variant > 3) throw S1cError(S1C_ERR_ARG, "variant must be 0, 1, 2 or 3");
     const WeightMap tb = make_wmap(d_B, N, K, K);
     const CUtensorMap tc = make_out_tmap(d_out, f32, (uint64_t)M, out_w, out_w);
-    // Split-K workspace of this entry point: one 16 MB zeroed buffer per device, kept for the process.
+    // Split-K workspace of this entry point: one 32 MB buffer per device, kept for the process.
     static float* ws_dev[64] = {nullptr};
     {
       std::lock_guard<std::mutex> g(mu);
-      if (!ws_dev[dev]) {
-        CK(cudaMalloc(&ws_dev[dev], (size_t)16 << 20));
-        CK(cudaMemset(ws_dev[dev], 0, (size_t)16 << 20));
-      }
+      if (!ws_dev[dev]) CK(cudaMalloc(&ws_dev[dev], (size_t)32 << 20));
     }
-    const SplitCtx sk{ws_dev[dev], (size_t)16 << 20, d_out, out_w};
+    const SplitCtx sk{ws_dev[dev], (size_t)32 << 20, d_out, out_w};
     switch (epi) {
       case EPI_STORE: launch_gemm<EPI_STORE>(ta, tb, tc, a, n_sms, st, variant, &sk); break;
       case EPI_ROPE: launch_gemm<EPI_ROPE>(ta, tb, tc, a, n_sms, st, variant, &sk); break;
