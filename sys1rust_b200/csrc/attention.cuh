@@ -89,6 +89,8 @@ S1C_DEV void load_tile_async(uint32_t tile, const __nv_bfloat16* base, int strid
 }
 
 __global__ void __launch_bounds__(ATT_THREADS, 4) attention_varlen_kernel(const AttnArgs args) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ __align__(128) __nv_bfloat16 sQ[ATT_BQ * ATT_D];
   __shared__ __align__(128) __nv_bfloat16 sK[2][ATT_BK * ATT_D];
   __shared__ __align__(128) __nv_bfloat16 sV[2][ATT_BK * ATT_D];

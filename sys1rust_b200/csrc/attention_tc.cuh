@@ -123,6 +123,8 @@ __global__ void __launch_bounds__(ATTC_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_trigger();
+  pdl_wait();
 
   if (warp == 0) {
     if (lane == 0 && nsteps > 0) {

@@ -42,6 +42,14 @@ S1C_DEV void report(int* status, int code) {
   if (status) atomicCAS(status, 0, code);
 }
 
+// Programmatic dependent launch: a kernel launched with programmatic stream serialisation may start
+// while its predecessor on the stream finishes. `pdl_trigger` lets this kernel's own successor be
+// scheduled early; `pdl_wait` blocks until every predecessor has completed and its memory is
+// visible. Each kernel calls `pdl_wait` before its first access to global memory that an earlier
+// kernel of the forward reads or writes. Both are no-ops for a kernel launched without the attribute.
+S1C_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+S1C_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 S1C_DEV uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

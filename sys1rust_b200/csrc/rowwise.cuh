@@ -108,6 +108,8 @@ template <int D>
 __global__ void embed_ln_kernel(const uint32_t* __restrict__ ids, int T, const __nv_bfloat16* __restrict__ tok_emb,
                                 int vocab, const float* __restrict__ w, float eps, float* __restrict__ h,
                                 __nv_bfloat16* __restrict__ x, int* status) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= T) return;
@@ -127,6 +129,8 @@ template <int D>
 __global__ void layernorm_kernel(const float* __restrict__ in, const int* __restrict__ gather, int rows,
                                  const float* __restrict__ w, const float* __restrict__ b, float eps,
                                  __nv_bfloat16* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -143,6 +147,8 @@ __global__ void final_to_head_kernel(const float* __restrict__ h, int T, const f
                                      const uint32_t* __restrict__ qtype, const float* __restrict__ type_emb,
                                      const float* __restrict__ n1w, const float* __restrict__ n1b,
                                      float* __restrict__ h2, __nv_bfloat16* __restrict__ x) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= T) return;
@@ -162,6 +168,8 @@ __global__ void final_to_head_kernel(const float* __restrict__ h, int T, const f
 
 __global__ void gather_rows_f32_kernel(const float* __restrict__ in, const int* __restrict__ idx, int rows, int d,
                                        float* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x;
   if (row >= rows) return;
   const float4* s = reinterpret_cast<const float4*>(in + (size_t)idx[row] * d);
@@ -171,6 +179,8 @@ __global__ void gather_rows_f32_kernel(const float* __restrict__ in, const int* 
 
 __global__ void gather_rows_bf16_kernel(const __nv_bfloat16* __restrict__ in, const int* __restrict__ idx, int rows,
                                         int d, __nv_bfloat16* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x;
   if (row >= rows) return;
   const uint4* s = reinterpret_cast<const uint4*>(in + (size_t)idx[row] * d);
@@ -182,6 +192,8 @@ __global__ void gather_rows_bf16_kernel(const __nv_bfloat16* __restrict__ in, co
 __global__ void scorer_logits_kernel(const float* __restrict__ hid, int R, int S, const float* __restrict__ w3,
                                      const float* __restrict__ b3, const int* __restrict__ marker_count, int kmax,
                                      float* __restrict__ logits) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= R) return;

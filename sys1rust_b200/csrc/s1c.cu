@@ -158,6 +158,25 @@ CUtensorMap make_out_tmap(const void* ptr, bool f32, uint64_t rows, uint64_t col
 // ---------------------------------------------------------------------------------------------
 // kernel launch helpers
 
+// Launch with programmatic stream serialisation when `t_pdl` is set (see pdl_trigger / pdl_wait in
+// common.cuh): the kernel may start while its predecessor drains, and waits on the device before
+// touching the predecessor's data.
+thread_local bool t_pdl = true;
+template <typename... P, typename... A>
+void launch_k(void (*kernel)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, A&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = t_pdl ? 1 : 0;
+  CK(cudaLaunchKernelEx(&cfg, kernel, std::forward<A>(args)...));
+}
+
 constexpr int GEMM_BN = 256;
 
 template <int EPI>
@@ -217,12 +236,12 @@ void launch_gemm(const CUtensorMap& ta, const WeightMap& tb, const CUtensorMap& 
     const int tiles = (rows / GEMM_BM) * ((a.N + GEMM_BN - 1) / GEMM_BN) * ksp;
     const int grid = std::min(tiles, num_sms);
     const CUtensorMap tw = make_out_tmap(sk->ws, true, (uint64_t)ksp * rows, a.N, a.N);
-    gemm_bf16_sm100<GEMM_BN, EPI><<<grid, GEMM_THREADS, gemm_smem_bytes(GEMM_BN), st>>>(ta, tb.full, tw, a);
+    launch_k(gemm_bf16_sm100<GEMM_BN, EPI>, dim3(grid), dim3(GEMM_THREADS), gemm_smem_bytes(GEMM_BN), st, ta, tb.full, tw, a);
     CK(cudaGetLastError());
     SplitKFinal f{sk->ws, ksp, rows, a.M, a.N, sk->out, sk->ldo, a.bias, a.act, a.out_f32, a.pos, a.inv_freq,
                   a.rope_cols, a.out_cols};
     const long work = (long)a.M * ((EPI == EPI_GEGLU ? a.out_cols : a.N) / 8);
-    splitk_finalize_kernel<EPI><<<(unsigned)((work + 255) / 256), 256, 0, st>>>(f);
+    launch_k(splitk_finalize_kernel<EPI>, dim3((unsigned)((work + 255) / 256)), dim3(256), 0, st, f);
     CK(cudaGetLastError());
     if (extra_launches) ++*extra_launches;
     return;
@@ -232,11 +251,11 @@ void launch_gemm(const CUtensorMap& ta, const WeightMap& tb, const CUtensorMap& 
   if (two) {
     const int tiles = ((a.M + 255) / 256) * ((a.N + GEMM_BN - 1) / GEMM_BN);
     const int clusters = std::min(tiles, num_sms / 2);
-    gemm2_bf16_sm100<EPI><<<2 * clusters, GEMM_THREADS, gemm2_smem_bytes(), st>>>(ta, tb.half, tc, a);
+    launch_k(gemm2_bf16_sm100<EPI>, dim3(2 * clusters), dim3(GEMM_THREADS), gemm2_smem_bytes(), st, ta, tb.half, tc, a);
   } else {
     const int tiles = ((a.M + GEMM_BM - 1) / GEMM_BM) * ((a.N + GEMM_BN - 1) / GEMM_BN);
     const int grid = std::min(tiles, num_sms);
-    gemm_bf16_sm100<GEMM_BN, EPI><<<grid, GEMM_THREADS, gemm_smem_bytes(GEMM_BN), st>>>(ta, tb.full, tc, a);
+    launch_k(gemm_bf16_sm100<GEMM_BN, EPI>, dim3(grid), dim3(GEMM_THREADS), gemm_smem_bytes(GEMM_BN), st, ta, tb.full, tc, a);
   }
   CK(cudaGetLastError());
 }
@@ -245,12 +264,14 @@ template <int D>
 void launch_ln(const float* in, const int* gather, int rows, const float* w, const float* b, float eps, bf16* out,
                cudaStream_t st) {
   if (rows <= 0) return;
-  layernorm_kernel<D><<<(rows + 7) / 8, 256, 0, st>>>(in, gather, rows, w, b, eps, out);
+  launch_k(layernorm_kernel<D>, dim3((rows + 7) / 8), dim3(256), 0, st, in, gather, rows, w, b, eps, out);
   CK(cudaGetLastError());
 }
 
 __global__ void prep_tokens_kernel(const int* __restrict__ cu, int n, int T, int* __restrict__ pos,
                                    int* __restrict__ row) {
+  pdl_trigger();
+  pdl_wait();
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= T) return;
   int lo = 0, hi = n - 1;  // largest r with cu[r] <= t
@@ -343,6 +364,7 @@ struct s1c_backend {
 
   // activations (capacity in rows, multiples of 128)
   int gemm_variant = 0;   // `gemm=auto|1cta|2cta`
+  bool pdl = true;        // `pdl=0|1`: programmatic dependent launch between the forward's kernels
   bool attn_tc = false;  // true: tcgen05 attention (attention_tc.cuh, `attn=tc`); false: mma.sync (attention.cuh)
   int cap_T = 0, cap_R = 0;
   DevBuf h, x, qkv, att, act;          // [cap_T, ...]
@@ -850,10 +872,10 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
   const float scale_log2 = (1.0f / 8.0f) * 1.4426950408889634f;  // 1/sqrt(64) * log2(e)
 
   launch(B, nl, "prep_tokens", 0, 8.0 * T, [&] {
-    prep_tokens_kernel<<<(T + 255) / 256, 256, 0, st>>>(dm.cu, m.n, T, pos, trow);
+    launch_k(prep_tokens_kernel, dim3((T + 255) / 256), dim3(256), 0, st, dm.cu, m.n, T, pos, trow);
   });
   launch(B, nl, "embed_ln", 0, 8.0 * Td, [&] {
-    embed_ln_kernel<D><<<(T + 7) / 8, 256, 0, st>>>(d_ids, T, B.tok_emb, B.V, B.emb_norm, B.eps, h, x, B.d_status);
+    launch_k(embed_ln_kernel<D>, dim3((T + 7) / 8), dim3(256), 0, st, d_ids, T, B.tok_emb, B.V, B.emb_norm, B.eps, h, x, B.d_status);
   });
 
   // Attention over the items' query tiles: the tcgen05 kernel reads Q/K/V through TMA maps
@@ -866,13 +888,13 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
     if (B.attn_tc) {
       AttnTcArgs a{dm.cu, items, o, os, q_col0, k_col0, v_col0, d / 64, window, scale_log2, B.d_status};
       launch(B, nl, name, 4.0 * d * pairs, 0, [&] {
-        attention_tc_kernel<<<dim3(n_items, (d / 64 + ATTC_HEADS - 1) / ATTC_HEADS), ATTC_THREADS, ATTC_SMEM, st>>>(
+        launch_k(attention_tc_kernel, dim3(dim3(n_items, (d / 64 + ATTC_HEADS - 1) / ATTC_HEADS)), dim3(ATTC_THREADS), ATTC_SMEM, st, 
             tq, tkv, a);
       });
     } else {
       AttnArgs a{q, k, v, o, qs, ks, vs, os, dm.cu, items, window, scale_log2};
       launch(B, nl, name, 4.0 * d * pairs, 0, [&] {
-        attention_varlen_kernel<<<dim3(n_items, d / 64), ATT_THREADS, 0, st>>>(a);
+        launch_k(attention_varlen_kernel, dim3(dim3(n_items, d / 64)), dim3(ATT_THREADS), 0, st, a);
       });
     }
   };
@@ -915,7 +937,7 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
 
   // final_norm, + type embedding, head layer 0's norm1
   launch(B, nl, "final_to_head", 0, Td * (4 + 4 + 2 + (d_hidden ? 4 : 0)), [&] {
-    final_to_head_kernel<D><<<(T + 7) / 8, 256, 0, st>>>(h, T, B.final_norm, B.eps, d_hidden, trow, dm.qtype,
+    launch_k(final_to_head_kernel<D>, dim3((T + 7) / 8), dim3(256), 0, st, h, T, B.final_norm, B.eps, d_hidden, trow, dm.qtype,
                                                          B.type_emb, B.head[0].n1w, B.head[0].n1b, h2, x);
   });
 
@@ -955,10 +977,10 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
     launch(B, nl, "head_gemm_kv", fl * 2 * d * d, 0,
            [&] { launch_gemm<EPI_STORE>(B.tm_x, hl.tm_in_kv, B.to_kv2, gkv, nsm, st, B.gemm_variant, &(sk_tmp = sk(qkv, 2 * d)), &nl); });
     launch(B, nl, "gather_rows", 0, (double)R * d * 4, [&] {
-      gather_rows_bf16_kernel<<<R, 128, 0, st>>>(x, dm.srows, R, d, B.xs.as<bf16>());
+      launch_k(gather_rows_bf16_kernel, dim3(R), dim3(128), 0, st, x, dm.srows, R, d, B.xs.as<bf16>());
     });
     launch(B, nl, "gather_rows", 0, (double)R * d * 8, [&] {
-      gather_rows_f32_kernel<<<R, 256, 0, st>>>(h2, dm.srows, R, d, B.hs.as<float>());
+      launch_k(gather_rows_f32_kernel, dim3(R), dim3(256), 0, st, h2, dm.srows, R, d, B.hs.as<float>());
     });
     GemmArgs gq = gemm_args(R, d, d);
     gq.bias = hl.in_b;
@@ -991,13 +1013,13 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
     launch(B, nl, "scorer_gemm", 2.0 * m.M * B.S * d, 0,
            [&] { launch_gemm<EPI_STORE>(B.tm_xm, B.tm_sc1, B.to_sh, gs, nsm, st, B.gemm_variant, &(sk_tmp = sk(B.sh.p, B.S)), &nl); });
     launch(B, nl, "scorer_logits", 2.0 * m.M * B.S, 0, [&] {
-      scorer_logits_kernel<<<(m.M + 7) / 8, 256, 0, st>>>(B.sh.as<float>(), m.M, B.S, B.sc_w3, B.sc_b3, dm.mcount,
+      launch_k(scorer_logits_kernel, dim3((m.M + 7) / 8), dim3(256), 0, st, B.sh.as<float>(), m.M, B.S, B.sc_w3, B.sc_b3, dm.mcount,
                                                           m.kmax, d_logits);
     });
   }
   if (m.n > 0) {
     launch(B, nl, "gather_rows", 0, (double)m.n * d * 8, [&] {
-      gather_rows_f32_kernel<<<m.n, 256, 0, st>>>(B.hs.as<float>(), dm.prows, m.n, d, d_pooled);
+      launch_k(gather_rows_f32_kernel, dim3(m.n), dim3(256), 0, st, B.hs.as<float>(), dm.prows, m.n, d, d_pooled);
     });
   }
   B.launches = nl;
@@ -1005,6 +1027,7 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
 
 void forward_enqueue(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uint32_t* d_ids, float* d_logits,
                      float* d_pooled, float* d_hidden) {
+  t_pdl = B.pdl;
   switch (B.d) {
     case 256: run_forward<256>(B, m, dm, d_ids, d_logits, d_pooled, d_hidden); break;
     case 768: run_forward<768>(B, m, dm, d_ids, d_logits, d_pooled, d_hidden); break;
@@ -1165,7 +1188,8 @@ void pack_batch(const s1c_batch& b, PackedBatch& p) {
 }
 
 // Backend settings, a strict comma list like the reference's `Knobs` (laya-mlx/src/lib.rs:155-259):
-// an unknown key or value is an error naming it. Keys: attn=tc|mma, gemm=auto|1cta|2cta, graphs=0|1.
+// an unknown key or value is an error naming it. Keys: attn=tc|mma, gemm=auto|1cta|2cta, graphs=0|1,
+// pdl=0|1.
 void apply_settings(s1c_backend& B, const char* spec) {
   if (!spec) return;
   std::string s(spec);
@@ -1178,7 +1202,11 @@ void apply_settings(s1c_backend& B, const char* spec) {
     if (kv.empty()) continue;
     const size_t eq = kv.find('=');
     const std::string k = kv.substr(0, eq), v = eq == std::string::npos ? "" : kv.substr(eq + 1);
-    if (k == "graphs") {
+    if (k == "pdl") {
+      if (v == "1") B.pdl = true;
+      else if (v == "0") B.pdl = false;
+      else throw S1cError(S1C_ERR_CONFIG, "settings: `" + kv + "`: `" + v + "` is not 0 or 1");
+    } else if (k == "graphs") {
       if (v == "1") B.use_graphs = true;
       else if (v == "0") B.use_graphs = false;
       else throw S1cError(S1C_ERR_CONFIG, "settings: `" + kv + "`: `" + v + "` is not 0 or 1");
@@ -1480,8 +1508,7 @@ s1c_status s1c_attention(const void* d_q, const void* d_k, const void* d_v, void
       const CUtensorMap tq = make_tmap(d_q, T, heads * 64, q_stride, ATTC_BQ);
       const CUtensorMap tkv = make_tmap(d_k, T, dv + heads * 64, k_stride, ATTC_BK);
       AttnTcArgs a{d_cu, d_items, static_cast<bf16*>(d_o), o_stride, 0, 0, (int)dv, heads, window, scale_log2, d_status};
-      attention_tc_kernel<<<dim3((unsigned)items.size(), (heads + ATTC_HEADS - 1) / ATTC_HEADS), ATTC_THREADS,
-                            ATTC_SMEM, st>>>(tq, tkv, a);
+      launch_k(attention_tc_kernel, dim3(dim3((unsigned)items.size(), (heads + ATTC_HEADS - 1) / ATTC_HEADS)), dim3(ATTC_THREADS), ATTC_SMEM, st, tq, tkv, a);
       cudaError_t e = cudaGetLastError();
       cudaError_t e2 = cudaStreamSynchronize(st);
       int hs = 0;
@@ -1493,7 +1520,7 @@ s1c_status s1c_attention(const void* d_q, const void* d_k, const void* d_v, void
     } else {
       AttnArgs a{static_cast<const bf16*>(d_q), static_cast<const bf16*>(d_k), static_cast<const bf16*>(d_v),
                  static_cast<bf16*>(d_o), q_stride, k_stride, v_stride, o_stride, d_cu, d_items, window, scale_log2};
-      attention_varlen_kernel<<<dim3((unsigned)items.size(), heads), ATT_THREADS, 0, st>>>(a);
+      launch_k(attention_varlen_kernel, dim3(dim3((unsigned)items.size(), heads)), dim3(ATT_THREADS), 0, st, a);
       cudaError_t e = cudaGetLastError();
       cudaError_t e2 = cudaStreamSynchronize(st);
       if (e != cudaSuccess) throw S1cError(S1C_ERR_CUDA, cudaGetErrorString(e));

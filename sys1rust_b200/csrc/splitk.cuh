@@ -36,6 +36,8 @@ S1C_DEV void slice_sum8(const SplitKFinal& f, int r, int c, float (&v)[8]) {
 // One thread per (row, 8 consecutive output columns).
 template <int EPI>
 __global__ void splitk_finalize_kernel(const SplitKFinal f) {
+  pdl_trigger();
+  pdl_wait();
   const int groups = (EPI == EPI_GEGLU ? f.out_cols : f.N) / 8;
   const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (long)f.M * groups) return;
