@@ -204,13 +204,17 @@ struct SplitCtx {
 };
 
 // Split-K factor for a GEMM with few output tiles: enough splits to cover the SMs, at least one
-// 64-wide K block per split, at most 16 splits, slices within the workspace. 1 = no split.
+// 64-wide K block per split, at most 16 splits, partial-sum traffic bounded by the weight traffic,
+// slices within the workspace. 1 = no split.
 int pick_k_splits(int M, int N, int K, int num_sms, size_t ws_bytes) {
   const int tiles = ((M + GEMM_BM - 1) / GEMM_BM) * ((N + GEMM_BN - 1) / GEMM_BN);
   const int nk = (K + GEMM_BK - 1) / GEMM_BK;
   if (tiles * 2 > num_sms) return 1;
-  int ksp = std::max(1, std::min({num_sms / tiles, nk, 16}));
-  const size_t slice = (size_t)((M + GEMM_BM - 1) / GEMM_BM) * GEMM_BM * N * 4;
+  const int rows = (M + GEMM_BM - 1) / GEMM_BM * GEMM_BM;
+  // Partial sums of all splits (splits x rows x N fp32) stay within twice the weight bytes (N x K
+  // bf16): at most K / rows splits.
+  int ksp = std::max(1, std::min({num_sms / tiles, nk, 16, K / rows}));
+  const size_t slice = (size_t)rows * N * 4;
   while (ksp > 1 && (size_t)ksp * slice > ws_bytes) --ksp;
   return ksp;
 }
