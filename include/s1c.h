@@ -178,6 +178,21 @@ S1C_API s1c_status s1c_profile(s1c_backend* b, int32_t on);
  * bytes are algorithmic). Returns the size needed including the terminating 0. */
 S1C_API size_t s1c_profile_report(const s1c_backend* b, char* buf, size_t cap);
 
+/* Split-K GEMM that allocates nothing (no counterpart in the reference). Same arguments and result
+ * as s1c_gemm with variant 3, for callers that cannot allocate device memory: a serving loop that
+ * must not stall in cudaMalloc / cudaFree (both can synchronise the whole device), or a host whose
+ * framework owns all device memory through its own pool. The fp32 partial sums go to a fixed
+ * 4 MiB array compiled into this library (held by every GPU that loads it until the process
+ * exits), so at least two split slices must fit: 2 * ceil(M / 128) * 128 * N * 4 bytes <= 4 MiB,
+ * else the call returns S1C_ERR_ARG with the limit in s1c_create_error(). The first call on a
+ * device looks up that device's array addresses (make it before any stream capture). All calls
+ * share the array and the last call's partial sums stay in it; calls whose work overlaps on the
+ * GPU race on it. The call does not synchronise. */
+S1C_API s1c_status s1c_gemm_splitk_noalloc(int32_t epi, const void* d_A, const void* d_B, void* d_out, int32_t M,
+                                           int32_t N, int32_t K, const float* d_bias, int32_t act, int32_t out_f32,
+                                           const int32_t* d_pos, float rope_theta, int32_t rope_cols,
+                                           int32_t out_cols, void* stream);
+
 /* Number of this library's kernel launches the last forward on this handle enqueued. */
 S1C_API int64_t s1c_last_launch_count(const s1c_backend* b);
 

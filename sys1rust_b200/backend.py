@@ -101,6 +101,7 @@ def lib() -> C.CDLL:
         "s1c_set_stream": (I32, [P, P]),
         "s1c_profile": (I32, [P, I32]),
         "s1c_profile_report": (SZ, [P, C.c_char_p, SZ]),
+        "s1c_gemm_splitk_noalloc": (I32, [I32, P, P, P, I32, I32, I32, P, I32, I32, P, F32, I32, I32, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -309,6 +310,18 @@ def gemm(epi: int, a_ptr: int, b_ptr: int, out_ptr: int, M: int, N: int, K: int,
     L = lib()
     rc = L.s1c_gemm(epi, a_ptr, b_ptr, out_ptr, M, N, K, bias_ptr or None, act, out_f32, pos_ptr or None,
                     rope_theta, rope_cols, out_cols, variant, stream or None)
+    if rc != S1C_OK:
+        _raise(rc, L.s1c_create_error().decode())
+
+
+def gemm_splitk_noalloc(epi: int, a_ptr: int, b_ptr: int, out_ptr: int, M: int, N: int, K: int, bias_ptr: int = 0,
+                        act: int = 0, out_f32: int = 0, pos_ptr: int = 0, rope_theta: float = 10000.0,
+                        rope_cols: int = 0, out_cols: int = 0, stream: int = 0) -> None:
+    """Split-K GEMM whose partial sums live in the library's fixed 4 MiB device array: no device
+    allocation on any call (``s1c_gemm_splitk_noalloc``)."""
+    L = lib()
+    rc = L.s1c_gemm_splitk_noalloc(epi, a_ptr, b_ptr, out_ptr, M, N, K, bias_ptr or None, act, out_f32,
+                                   pos_ptr or None, rope_theta, rope_cols, out_cols, stream or None)
     if rc != S1C_OK:
         _raise(rc, L.s1c_create_error().decode())
 

@@ -1251,6 +1251,51 @@ s1c_status guarded(s1c_backend* b, F&& f) {
 }  // namespace
 
 // =============================================================================================
+// Allocation-free split-K GEMM (s1c_gemm_splitk_noalloc)
+//
+// For callers that must not allocate device memory: the split-K partial sums, the RoPE inverse
+// frequencies and the device status word live in file-scope __device__ arrays of fixed size, held
+// by every GPU that loads this library until the process exits. Host code cannot use these names
+// as device addresses; `noalloc_device` looks the addresses up once per device (cudaGetSymbolAddress,
+// with that device current) on the entry point's first call there. All calls share the arrays:
+// each call overwrites them, and calls whose work overlaps on the GPU race on them.
+
+constexpr size_t NOALLOC_SCRATCH_FLOATS = (size_t)1 << 20;  // 4 MiB of fp32 partial sums
+
+static __device__ __align__(256) float s1c_noalloc_scratch[NOALLOC_SCRATCH_FLOATS];
+static __device__ __align__(256) float s1c_noalloc_inv_freq[32];
+static __device__ __align__(256) int s1c_noalloc_status;
+
+namespace {
+
+struct NoAllocDevice {
+  bool ready = false;
+  float* scratch = nullptr;
+  float* inv_freq = nullptr;
+  int* status = nullptr;
+  int n_sms = 0;
+};
+
+NoAllocDevice& noalloc_device(int dev) {
+  static NoAllocDevice devs[64];
+  static std::mutex mu;
+  if (dev < 0 || dev >= 64) throw S1cError(S1C_ERR_ARG, "device ordinal out of range");
+  std::lock_guard<std::mutex> g(mu);
+  NoAllocDevice& d = devs[dev];
+  if (!d.ready) {
+    CK(cudaGetSymbolAddress(reinterpret_cast<void**>(&d.scratch), s1c_noalloc_scratch));
+    CK(cudaGetSymbolAddress(reinterpret_cast<void**>(&d.inv_freq), s1c_noalloc_inv_freq));
+    CK(cudaGetSymbolAddress(reinterpret_cast<void**>(&d.status), s1c_noalloc_status));
+    CK(cudaDeviceGetAttribute(&d.n_sms, cudaDevAttrMultiProcessorCount, dev));
+    set_all_gemm_smem();
+    d.ready = true;
+  }
+  return d;
+}
+
+}  // namespace
+
+// =============================================================================================
 // C ABI
 
 extern "C" {
@@ -1538,6 +1583,58 @@ s1c_status s1c_attention(const void* d_q, const void* d_k, const void* d_v, void
     if (d_items) cudaFree(d_items);
     g_create_error = e.what();
     return e.code;
+  }
+}
+
+s1c_status s1c_gemm_splitk_noalloc(int32_t epi, const void* d_A, const void* d_B, void* d_out, int32_t M, int32_t N,
+                                   int32_t K, const float* d_bias, int32_t act, int32_t out_f32, const int32_t* d_pos,
+                                   float rope_theta, int32_t rope_cols, int32_t out_cols, void* stream) {
+  try {
+    if (!d_A || !d_B || !d_out || M <= 0 || N <= 0 || K <= 0 || K % 8 || N % 32 || epi < EPI_STORE || epi > EPI_RESID)
+      throw S1cError(S1C_ERR_ARG, "bad GEMM arguments (K must be a multiple of 8, N of 32)");
+    if (epi == EPI_ROPE && !d_pos) throw S1cError(S1C_ERR_ARG, "RoPE needs positions");
+    if ((K + GEMM_BK - 1) / GEMM_BK < 2) throw S1cError(S1C_ERR_ARG, "split-K needs K > 64");
+    const size_t rows = (size_t)(M + GEMM_BM - 1) / GEMM_BM * GEMM_BM;
+    const size_t scratch_bytes = NOALLOC_SCRATCH_FLOATS * sizeof(float);
+    if (2 * rows * (size_t)N * 4 > scratch_bytes)
+      throw S1cError(S1C_ERR_ARG, "s1c_gemm_splitk_noalloc: two split slices of " + std::to_string(rows) + " x " +
+                                      std::to_string(N) + " fp32 exceed the " + std::to_string(scratch_bytes >> 20) +
+                                      " MiB static scratch (rows rounded up to 128; need 2 * rows * N * 4 bytes)");
+    int dev = 0;
+    CK(cudaGetDevice(&dev));
+    NoAllocDevice& nd = noalloc_device(dev);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    CK(cudaMemsetAsync(nd.status, 0, sizeof(int), st));
+    GemmArgs a{};
+    a.M = M; a.N = N; a.K = K; a.bias = d_bias; a.act = act; a.out_f32 = out_f32;
+    a.pos = d_pos; a.rope_cols = rope_cols; a.out_cols = out_cols; a.status = nd.status;
+    if (epi == EPI_ROPE) {
+      float inv[32];
+      const float lbase = std::log2(rope_theta);
+      for (int i = 0; i < 32; ++i) inv[i] = std::exp2(-((float)i / 32.0f) * lbase);
+      CK(cudaMemcpyAsync(nd.inv_freq, inv, sizeof inv, cudaMemcpyHostToDevice, st));
+      a.inv_freq = nd.inv_freq;
+    }
+    const bool f32 = epi == EPI_RESID || (epi == EPI_STORE && out_f32);
+    const int out_w = (epi == EPI_GEGLU) ? out_cols : N;
+    const CUtensorMap ta = make_tmap(d_A, (uint64_t)M, K, K, GEMM_BM);
+    const WeightMap tb = make_wmap(d_B, N, K, K);
+    const CUtensorMap tc = make_out_tmap(d_out, f32, (uint64_t)M, out_w, out_w);
+    const SplitCtx sk{nd.scratch, scratch_bytes, d_out, out_w};
+    t_pdl = false;
+    switch (epi) {
+      case EPI_STORE: launch_gemm<EPI_STORE>(ta, tb, tc, a, nd.n_sms, st, 3, &sk); break;
+      case EPI_ROPE: launch_gemm<EPI_ROPE>(ta, tb, tc, a, nd.n_sms, st, 3, &sk); break;
+      case EPI_GEGLU: launch_gemm<EPI_GEGLU>(ta, tb, tc, a, nd.n_sms, st, 3, &sk); break;
+      case EPI_RESID: launch_gemm<EPI_RESID>(ta, tb, tc, a, nd.n_sms, st, 3, &sk); break;
+    }
+    return S1C_OK;
+  } catch (const S1cError& e) {
+    g_create_error = e.what();
+    return e.code;
+  } catch (const std::exception& e) {
+    g_create_error = e.what();
+    return S1C_ERR_ARG;
   }
 }
 
