@@ -6,16 +6,18 @@
 // with |i - j| <= window (local layers); softmax in fp32, output bf16.
 //
 // One CTA = one tile of up to 128 query rows x ATTC_HEADS heads, processed head after head so
-// the TMA/MMA pipeline never drains between heads. 192 threads:
+// the TMA/MMA pipeline never drains between heads; two CTAs share an SM (96 KB of shared memory
+// and 256 TMEM columns each). 192 threads:
 //   warp 0      TMA producer: Q tile [128 x 64] per head (double buffered), K and V tiles
-//               [128 keys x 64] per key step (double buffered), 128-byte swizzle.
+//               [64 keys x 64] per key step (3-stage ring), 128-byte swizzle.
 //   warp 1      TMEM owner and MMA issuer:
-//                 S = Q K^T        M=128 N=128 K=64   (K-major A and B)         -> TMEM cols [0,128)
-//                 O_j = P_j V_j    M=128 N=64  K=128  (P K-major from smem, V MN-major) -> TMEM
-//                                  cols [128,192) / [192,256) alternating
+//                 S = Q K^T        M=128 N=64 K=64   (K-major A and B)          -> TMEM cols [0,64)
+//                 O_j = P_j V_j    M=128 N=64 K=64   (P K-major from smem, V MN-major) -> TMEM
+//                                  cols [64,128) / [128,192) alternating
 //               S of the next key step is issued as soon as the softmax has read the current S.
-//   warps 2..5  softmax, one query row per thread (TMEM lane = row): masks, online max / sum in
-//               fp32 (base-2 exponent), P rounded to bf16 into shared memory in the swizzled
+//   warps 2..5  softmax, one query row per thread (TMEM lane = row): masks only on tiles that
+//               cross a row's key range, online max / sum in fp32 with p = 2^(s*scale - m) (one
+//               FFMA and one ex2 per score), P rounded to bf16 into shared memory in the swizzled
 //               K-major layout the MMA reads, O_j folded into a register accumulator with the
 //               running correction, final O / l stored bf16.
 #pragma once
@@ -24,11 +26,12 @@
 
 namespace s1c {
 
-constexpr int ATTC_BQ = 128, ATTC_BK = 128, ATTC_THREADS = 192, ATTC_HEADS = 4;
+constexpr int ATTC_BQ = 128, ATTC_BK = 64, ATTC_THREADS = 192, ATTC_HEADS = 4, ATTC_KV_STAGES = 3;
 constexpr uint32_t ATTC_Q_BYTES = ATTC_BQ * 64 * 2;       // 16 KB
-constexpr uint32_t ATTC_KV_BYTES = ATTC_BK * 64 * 2;      // 16 KB each for K and V
-constexpr uint32_t ATTC_P_BYTES = ATTC_BQ * ATTC_BK * 2;  // 32 KB: two [128 x 64] swizzled halves
-constexpr size_t ATTC_SMEM = 2 * ATTC_Q_BYTES + 2 * 2 * ATTC_KV_BYTES + ATTC_P_BYTES + 1024 + 256;
+constexpr uint32_t ATTC_KV_BYTES = ATTC_BK * 64 * 2;      // 8 KB each for K and V
+constexpr uint32_t ATTC_P_BYTES = ATTC_BQ * ATTC_BK * 2;  // 16 KB: one swizzled [128 x 64] block
+constexpr size_t ATTC_SMEM =
+    2 * ATTC_Q_BYTES + ATTC_KV_STAGES * 2 * ATTC_KV_BYTES + ATTC_P_BYTES + 1024 + 256;
 
 struct AttnTcArgs {
   const int* cu_seqlens;
@@ -47,7 +50,7 @@ struct AttnTcArgs {
 S1C_DEV uint64_t sdesc_mnmajor_sw128(uint32_t saddr) {
   uint64_t d = 0;
   d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
-  d |= (uint64_t)(16384u >> 4) << 16;  // leading byte offset: next 64-wide N block (unused, N = 64)
+  d |= (uint64_t)(8192u >> 4) << 16;   // leading byte offset: next 64-wide N block (unused, N = 64)
   d |= (uint64_t)(1024u >> 4) << 32;   // stride byte offset: next 8-key group
   d |= (uint64_t)1u << 46;
   d |= (uint64_t)2u << 61;
@@ -59,29 +62,36 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32_bmn(int M, int N) {
   return idesc_bf16_f32(M, N) | (1u << 16);
 }
 
-__global__ void __launch_bounds__(ATTC_THREADS, 1)
+S1C_DEV float ex2f_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__global__ void __launch_bounds__(ATTC_THREADS, 2)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
                         const AttnTcArgs args) {
+  constexpr int NS = ATTC_KV_STAGES;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_u = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_u + 1023u) & ~1023u) - raw_u);
   uint8_t* sQ = smem;                              // [2][16 KB]
-  uint8_t* sK = sQ + 2 * ATTC_Q_BYTES;             // [2][16 KB]
-  uint8_t* sV = sK + 2 * ATTC_KV_BYTES;            // [2][16 KB]
-  uint8_t* sP = sV + 2 * ATTC_KV_BYTES;            // 32 KB
+  uint8_t* sK = sQ + 2 * ATTC_Q_BYTES;             // [NS][8 KB]
+  uint8_t* sV = sK + NS * ATTC_KV_BYTES;           // [NS][8 KB]
+  uint8_t* sP = sV + NS * ATTC_KV_BYTES;           // 16 KB
   uint64_t* bars = reinterpret_cast<uint64_t*>(sP + ATTC_P_BYTES);
   uint64_t* q_full = bars + 0;    // [2]
   uint64_t* q_empty = bars + 2;   // [2]
-  uint64_t* kv_full = bars + 4;   // [2]
-  uint64_t* kv_empty = bars + 6;  // [2]
-  uint64_t* s_full = bars + 8;
-  uint64_t* s_free = bars + 9;
-  uint64_t* p_full = bars + 10;
-  uint64_t* p_free = bars + 11;
-  uint64_t* o_full = bars + 12;   // [2]
-  uint64_t* o_free = bars + 14;   // [2]
-  uint64_t* drain = bars + 16;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
+  uint64_t* kv_full = bars + 4;   // [NS]
+  uint64_t* kv_empty = bars + 4 + NS;
+  uint64_t* s_full = bars + 4 + 2 * NS;
+  uint64_t* s_free = s_full + 1;
+  uint64_t* p_full = s_full + 2;
+  uint64_t* p_free = s_full + 3;
+  uint64_t* o_full = s_full + 4;  // [2]
+  uint64_t* o_free = s_full + 6;  // [2]
+  uint64_t* drain = s_full + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -90,8 +100,9 @@ __global__ void __launch_bounds__(ATTC_THREADS, 1)
   const int s_begin = args.cu_seqlens[seq], s_end = args.cu_seqlens[seq + 1];
   const int h0 = blockIdx.y * ATTC_HEADS;
   const int nh = min(ATTC_HEADS, args.heads - h0);
+  const bool local = args.window >= 0 && mode == 0;
   int k_lo = s_begin, k_hi = s_end;
-  if (args.window >= 0 && mode == 0) {
+  if (local) {
     k_lo = max(s_begin, q_first - args.window);
     k_hi = min(s_end, q_first + q_count + args.window);
   }
@@ -102,10 +113,12 @@ __global__ void __launch_bounds__(ATTC_THREADS, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&q_full[i], 1);
       mbar_init(&q_empty[i], 1);
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
       mbar_init(&o_full[i], 1);
       mbar_init(&o_free[i], 128);
+    }
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
     }
     mbar_init(s_full, 1);
     mbar_init(s_free, 128);
@@ -139,8 +152,8 @@ __global__ void __launch_bounds__(ATTC_THREADS, 1)
         tma_load_2d(sQ + qb * ATTC_Q_BYTES, &tmQ, &q_full[qb], args.q_col0 + h * 64, q_first);
         ++issued_q;
         for (int j = 0; j < nt; ++j) {
-          const int step = hi * nt + j, s = step & 1;
-          if (!mbar_wait(&kv_empty[s], ((step >> 1) & 1) ^ 1u, args.status, DEV_TIMEOUT_PRODUCER, abort_flag)) {
+          const int step = hi * nt + j, s = step % NS;
+          if (!mbar_wait(&kv_empty[s], ((step / NS) & 1) ^ 1u, args.status, DEV_TIMEOUT_PRODUCER, abort_flag)) {
             ok = false;
             break;
           }
@@ -150,24 +163,24 @@ __global__ void __launch_bounds__(ATTC_THREADS, 1)
           ++issued_kv;
         }
       }
-      // Loads still in flight land before the CTA exits (at most the last two of each ring).
+      // Loads still in flight land before the CTA exits.
       for (int i = max(0, issued_q - 2); i < issued_q; ++i)
         mbar_wait(&q_full[i & 1], (i >> 1) & 1, args.status, DEV_TIMEOUT_DRAIN, nullptr);
-      for (int i = max(0, issued_kv - 2); i < issued_kv; ++i)
-        mbar_wait(&kv_full[i & 1], (i >> 1) & 1, args.status, DEV_TIMEOUT_DRAIN, nullptr);
+      for (int i = max(0, issued_kv - NS); i < issued_kv; ++i)
+        mbar_wait(&kv_full[i % NS], (i / NS) & 1, args.status, DEV_TIMEOUT_DRAIN, nullptr);
     }
   } else if (warp == 1) {
     if (lane == 0 && nsteps > 0) {
       constexpr uint32_t idS = idesc_bf16_f32(128, ATTC_BK);
       constexpr uint32_t idO = idesc_bf16_f32_bmn(128, 64);
-      const uint32_t tS = tmem, tO = tmem + 128;
+      const uint32_t tS = tmem, tO = tmem + 64;
       bool ok = true;
       // S for step `st`: needs Q of its head and K of its stage.
       auto issue_s = [&](int st) -> bool {
-        const int hi = st / nt, j = st % nt, s = st & 1, qb = hi & 1;
+        const int hi = st / nt, j = st % nt, s = st % NS, qb = hi & 1;
         if (j == 0 && !mbar_wait(&q_full[qb], (hi >> 1) & 1, args.status, DEV_TIMEOUT_MMA_FULL, abort_flag))
           return false;
-        if (!mbar_wait(&kv_full[s], (st >> 1) & 1, args.status, DEV_TIMEOUT_MMA_FULL, abort_flag)) return false;
+        if (!mbar_wait(&kv_full[s], (st / NS) & 1, args.status, DEV_TIMEOUT_MMA_FULL, abort_flag)) return false;
         if (st > 0 && !mbar_wait(s_free, (st - 1) & 1, args.status, DEV_TIMEOUT_MMA_TEMPTY, abort_flag)) return false;
         tc_fence_after();
         const uint32_t qa = smem_u32(sQ + qb * ATTC_Q_BYTES), ka = smem_u32(sK + s * ATTC_KV_BYTES);
@@ -181,7 +194,7 @@ __global__ void __launch_bounds__(ATTC_THREADS, 1)
       ok = issue_s(0);
       for (int st = 0; ok && st < nsteps; ++st) {
         if (st + 1 < nsteps && !issue_s(st + 1)) break;
-        const int s = st & 1, ob = st & 1;
+        const int s = st % NS, ob = st & 1;
         if (!mbar_wait(p_full, st & 1, args.status, DEV_TIMEOUT_MMA_FULL, abort_flag)) break;
         if (st >= 2 && !mbar_wait(&o_free[ob], ((st >> 1) - 1) & 1, args.status, DEV_TIMEOUT_MMA_TEMPTY, abort_flag))
           break;
@@ -189,8 +202,8 @@ __global__ void __launch_bounds__(ATTC_THREADS, 1)
         const uint32_t pa = smem_u32(sP), va = smem_u32(sV + s * ATTC_KV_BYTES);
 #pragma unroll
         for (int k = 0; k < ATTC_BK / 16; ++k)
-          umma_bf16(tO + ob * 64, sdesc_kmajor_sw128(pa + (k >> 2) * 16384 + (k & 3) * 32),
-                    sdesc_mnmajor_sw128(va + k * 2048), idO, k ? 1u : 0u);
+          umma_bf16(tO + ob * 64, sdesc_kmajor_sw128(pa + k * 32), sdesc_mnmajor_sw128(va + k * 2048), idO,
+                    k ? 1u : 0u);
         umma_commit(&o_full[ob]);
         umma_commit(&kv_empty[s]);
         umma_commit(p_free);
@@ -202,13 +215,12 @@ __global__ void __launch_bounds__(ATTC_THREADS, 1)
     const int quad = warp & 3;
     const int r = quad * 32 + lane;  // query row of this thread
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-    const uint32_t tS = tmem + lane_off, tO = tmem + lane_off + 128;
-    const int qpos = q_first - s_begin + r;
-    const bool local = args.window >= 0 && mode == 0;
+    const uint32_t tS = tmem + lane_off, tO = tmem + lane_off + 64;
+    const int qtok = q_first + r;  // query token (mode 0)
+    const float sc = args.scale_log2;
     float o[64];
     float m = -INFINITY, l = 0.f, corr_prev = 0.f;
-    bool ok = true;
-    for (int st = 0; ok && st < nsteps; ++st) {
+    for (int st = 0; st < nsteps; ++st) {
       const int hi = st / nt, j = st % nt;
       if (j == 0) {
 #pragma unroll
@@ -218,56 +230,61 @@ __global__ void __launch_bounds__(ATTC_THREADS, 1)
       }
       if (!mbar_wait_warp(s_full, st & 1, args.status, DEV_TIMEOUT_EPILOGUE, abort_flag)) break;
       tc_fence_after();
-      float s[128];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, *reinterpret_cast<float(*)[32]>(s + c * 32));
+      float s[64];
+      tmem_ld32(tS, *reinterpret_cast<float(*)[32]>(s));
+      tmem_ld32(tS + 32, *reinterpret_cast<float(*)[32]>(s + 32));
       tc_fence_before();
       mbar_arrive(s_free);
-      // mask + scale, row max
+      // Keys this row may see, as column offsets [lo, hi) inside the tile.
       const int kt0 = k_lo + j * ATTC_BK;
-      const int kp0 = kt0 - s_begin;
-      float mx = m;
-#pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        bool valid = kt0 + c < k_hi;
-        if (local) valid = valid && abs(qpos - (kp0 + c)) <= args.window;
-        s[c] = valid ? s[c] * args.scale_log2 : -INFINITY;
-        mx = fmaxf(mx, s[c]);
+      int lo = 0, hi_c = k_hi - kt0;
+      if (local) {
+        lo = max(lo, qtok - args.window - kt0);
+        hi_c = min(hi_c, qtok + args.window + 1 - kt0);
       }
-      const float base = (mx == -INFINITY) ? 0.f : mx;
-      const float corr = exp2f(m - base);
-      m = mx;
-      float rs = 0.f;
-      uint32_t pk[64];
+      if (!__all_sync(0xffffffffu, lo <= 0 && hi_c >= ATTC_BK)) {
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const float p0 = exp2f(s[2 * c] - base), p1 = exp2f(s[2 * c + 1] - base);
-        rs += p0 + p1;
-        pk[c] = pack_bf16x2(p0, p1);
+        for (int c = 0; c < 64; ++c) s[c] = (c >= lo && c < hi_c) ? s[c] : -INFINITY;
+      }
+      float mx = s[0];
+#pragma unroll
+      for (int c = 1; c < 64; ++c) mx = fmaxf(mx, s[c]);
+      mx = fmaxf(m, mx * sc);
+      const float base = (mx == -INFINITY) ? 0.f : mx;
+      const float corr = ex2f_approx(m - base);
+      m = mx;
+      // P row -> shared memory (one swizzled [128 x 64] block), once the previous PV has read P.
+      if (st > 0 && !mbar_wait_warp(p_free, (st - 1) & 1, args.status, DEV_TIMEOUT_EPILOGUE, abort_flag)) break;
+      float rs = 0.f;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        float p[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          p[i] = ex2f_approx(fmaf(s[8 * q + i], sc, -base));
+          rs += p[i];
+        }
+        *reinterpret_cast<uint4*>(sP + r * 128 + ((q ^ (r & 7)) << 4)) =
+            make_uint4(pack_bf16x2(p[0], p[1]), pack_bf16x2(p[2], p[3]), pack_bf16x2(p[4], p[5]),
+                       pack_bf16x2(p[6], p[7]));
       }
       l = l * corr + rs;
-      // P row -> shared memory (two swizzled [128 x 64] halves), once the previous PV has read P.
-      if (st > 0 && !mbar_wait_warp(p_free, (st - 1) & 1, args.status, DEV_TIMEOUT_EPILOGUE, abort_flag)) break;
-#pragma unroll
-      for (int q = 0; q < 16; ++q) {
-        const int half = q >> 3, chunk = q & 7;
-        uint4 v = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-        *reinterpret_cast<uint4*>(sP + half * 16384 + r * 128 + ((chunk ^ (r & 7)) << 4)) = v;
-      }
       fence_proxy_async();
       mbar_arrive(p_full);
-      // Fold the previous step's O (same head) into the register accumulator.
+      // Fold a finished O_j (same head) into the register accumulator, 32 columns at a time.
       auto fold = [&](int sj, float cr) -> bool {
         const int ob = sj & 1;
         if (!mbar_wait_warp(&o_full[ob], (sj >> 1) & 1, args.status, DEV_TIMEOUT_EPILOGUE, abort_flag)) return false;
         tc_fence_after();
-        float t[64];
-        tmem_ld32(tO + ob * 64, *reinterpret_cast<float(*)[32]>(t));
-        tmem_ld32(tO + ob * 64 + 32, *reinterpret_cast<float(*)[32]>(t + 32));
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          float t[32];
+          tmem_ld32(tO + ob * 64 + half * 32, t);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[half * 32 + i] = o[half * 32 + i] * cr + t[i];
+        }
         tc_fence_before();
         mbar_arrive(&o_free[ob]);
-#pragma unroll
-        for (int i = 0; i < 64; ++i) o[i] = o[i] * cr + t[i];
         return true;
       };
       if (j > 0 && !fold(st - 1, corr_prev)) break;
@@ -288,6 +305,7 @@ __global__ void __launch_bounds__(ATTC_THREADS, 1)
       }
     }
   }
+  __syncwarp();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();

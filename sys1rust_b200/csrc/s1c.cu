@@ -375,7 +375,8 @@ struct s1c_backend {
   DevBuf h2;                           // head residual stream [cap_T, d] fp32
   DevBuf xs, qs, atts, hs, fs, xm, sh; // scorer rows [cap_R, ...]
   CUtensorMap tm_x, tm_att, tm_act_i, tm_act_f, tm_xs, tm_atts, tm_fs, tm_xm;
-  CUtensorMap tm_qkv_att, tm_kv_att, tm_qs_att;  // 128-row boxes for the tcgen05 attention
+  // tcgen05 attention maps: Q boxes of ATTC_BQ rows, K/V boxes of ATTC_BK rows
+  CUtensorMap tm_qkv_att, tm_qkv_kv, tm_kv_att, tm_qs_att;
   // GEMM output maps (32-row boxes): bf16 qkv as [T,3d] and [T,2d], act as [T,I] and [T,F];
   // fp32 residual streams h, h2; scorer-row buffers.
   CUtensorMap to_qkv3, to_kv2, to_act_i, to_act_f, to_h, to_h2, to_qs, to_hs, to_fs, to_sh;
@@ -535,6 +536,7 @@ void ensure_capacity(s1c_backend& B, int T, int R) {
     CK(cudaMemsetAsync(B.act.p, 0, B.act.bytes, B.stream));
     B.tm_x = make_tmap(B.x.p, cap, B.d, B.d, GEMM_BM);
     B.tm_qkv_att = make_tmap(B.qkv.p, cap, 3 * B.d, 3 * B.d, ATTC_BQ);
+    B.tm_qkv_kv = make_tmap(B.qkv.p, cap, 3 * B.d, 3 * B.d, ATTC_BK);
     B.tm_kv_att = make_tmap(B.qkv.p, cap, 2 * B.d, 2 * B.d, ATTC_BK);
     B.to_qkv3 = make_out_tmap(B.qkv.p, false, cap, 3 * B.d, 3 * B.d);
     B.to_kv2 = make_out_tmap(B.qkv.p, false, cap, 2 * B.d, 2 * B.d);
@@ -925,7 +927,7 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
     g.inv_freq = B.inv_freq[l.local ? 1 : 0];
     g.rope_cols = 2 * d;
     launch(B, nl, "gemm_qkv_rope", fl * 3 * d * d, 0, [&] { launch_gemm<EPI_ROPE>(B.tm_x, l.tm_wqkv, B.to_qkv3, g, nsm, st, B.gemm_variant, &(sk_tmp = sk(qkv, 3 * d)), &nl); });
-    attn(l.local ? "attn_local" : "attn_global", B.tm_qkv_att, B.tm_qkv_att, 0, d, 2 * d, qkv, qkv + d,
+    attn(l.local ? "attn_local" : "attn_global", B.tm_qkv_att, B.tm_qkv_kv, 0, d, 2 * d, qkv, qkv + d,
          qkv + 2 * d, att, 3 * d, 3 * d, 3 * d, d, dm.items_full, (int)m.items_full.size(), l.local ? B.window : -1,
          l.local ? m.pairs_local : m.pairs_global);
     GemmArgs go = gemm_args(T, d, d);
@@ -951,7 +953,7 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
     GemmArgs g = gemm_args(T, 3 * d, d);
     g.bias = hl.in_b;
     launch(B, nl, "head_gemm_in", fl * 3 * d * d, 0, [&] { launch_gemm<EPI_STORE>(B.tm_x, hl.tm_in, B.to_qkv3, g, nsm, st, B.gemm_variant, &(sk_tmp = sk(qkv, 3 * d)), &nl); });
-    attn("head_attn", B.tm_qkv_att, B.tm_qkv_att, 0, d, 2 * d, qkv, qkv + d, qkv + 2 * d, att, 3 * d, 3 * d,
+    attn("head_attn", B.tm_qkv_att, B.tm_qkv_kv, 0, d, 2 * d, qkv, qkv + d, qkv + 2 * d, att, 3 * d, 3 * d,
          3 * d, d, dm.items_full, (int)m.items_full.size(), -1, m.pairs_global);
     GemmArgs go = gemm_args(T, d, d);
     go.bias = hl.out_b;
