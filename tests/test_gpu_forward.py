@@ -192,7 +192,7 @@ def test_graph_replay_matches_direct_launches(cuda_lib):
     from conftest import get_backend
     cfg, w, be = get_backend("small:3")
     old = os.environ.get("S1C_SETTINGS")
-    os.environ["S1C_SETTINGS"] = "graphs=0"
+    os.environ["S1C_SETTINGS"] = (old + "," if old else "") + "graphs=0"
     try:
         direct = CudaBackend.from_synthetic(cfg, w.tensors)
     finally:
