@@ -9,7 +9,7 @@
 // the TMA/MMA pipeline never drains between heads; two CTAs share an SM (96 KB of shared memory
 // and 256 TMEM columns each). 192 threads:
 //   warp 0      TMA producer: Q tile [128 x 64] per head (double buffered), K and V tiles
-//               [64 keys x 64] per key step (3-stage ring), 128-byte swizzle.
+//               [64 keys x 64] per key step (2-stage ring), 128-byte swizzle.
 //   warp 1      TMEM owner and MMA issuer:
 //                 S = Q K^T        M=128 N=64 K=64   (K-major A and B)          -> TMEM cols [0,64)
 //                 O_j = P_j V_j    M=128 N=64 K=64   (P K-major from smem, V MN-major) -> TMEM
@@ -17,21 +17,21 @@
 //               S of the next key step is issued as soon as the softmax has read the current S.
 //   warps 2..5  softmax, one query row per thread (TMEM lane = row): masks only on tiles that
 //               cross a row's key range, online max / sum in fp32 with p = 2^(s*scale - m) (one
-//               FFMA and one ex2 per score), P rounded to bf16 into shared memory in the swizzled
-//               K-major layout the MMA reads, O_j folded into a register accumulator with the
-//               running correction, final O / l stored bf16.
+//               FFMA and one ex2 per score), P rounded to bf16 into one of two shared-memory
+//               buffers in the swizzled K-major layout the MMA reads, O_j folded into a register
+//               accumulator with the running correction, final O / l stored bf16.
 #pragma once
 #include <cuda.h>
 #include "common.cuh"
 
 namespace s1c {
 
-constexpr int ATTC_BQ = 128, ATTC_BK = 64, ATTC_THREADS = 192, ATTC_HEADS = 4, ATTC_KV_STAGES = 3;
+constexpr int ATTC_BQ = 128, ATTC_BK = 64, ATTC_THREADS = 192, ATTC_HEADS = 4, ATTC_KV_STAGES = 2;
 constexpr uint32_t ATTC_Q_BYTES = ATTC_BQ * 64 * 2;       // 16 KB
 constexpr uint32_t ATTC_KV_BYTES = ATTC_BK * 64 * 2;      // 8 KB each for K and V
-constexpr uint32_t ATTC_P_BYTES = ATTC_BQ * ATTC_BK * 2;  // 16 KB: one swizzled [128 x 64] block
+constexpr uint32_t ATTC_P_BYTES = ATTC_BQ * ATTC_BK * 2;  // 16 KB: one swizzled [128 x 64] block (x2)
 constexpr size_t ATTC_SMEM =
-    2 * ATTC_Q_BYTES + ATTC_KV_STAGES * 2 * ATTC_KV_BYTES + ATTC_P_BYTES + 1024 + 256;
+    2 * ATTC_Q_BYTES + ATTC_KV_STAGES * 2 * ATTC_KV_BYTES + 2 * ATTC_P_BYTES + 1024 + 256;
 
 struct AttnTcArgs {
   const int* cu_seqlens;
@@ -78,19 +78,19 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
   uint8_t* sQ = smem;                              // [2][16 KB]
   uint8_t* sK = sQ + 2 * ATTC_Q_BYTES;             // [NS][8 KB]
   uint8_t* sV = sK + NS * ATTC_KV_BYTES;           // [NS][8 KB]
-  uint8_t* sP = sV + NS * ATTC_KV_BYTES;           // 16 KB
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + ATTC_P_BYTES);
+  uint8_t* sP = sV + NS * ATTC_KV_BYTES;           // [2][16 KB]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * ATTC_P_BYTES);
   uint64_t* q_full = bars + 0;    // [2]
   uint64_t* q_empty = bars + 2;   // [2]
   uint64_t* kv_full = bars + 4;   // [NS]
   uint64_t* kv_empty = bars + 4 + NS;
   uint64_t* s_full = bars + 4 + 2 * NS;
   uint64_t* s_free = s_full + 1;
-  uint64_t* p_full = s_full + 2;
-  uint64_t* p_free = s_full + 3;
-  uint64_t* o_full = s_full + 4;  // [2]
-  uint64_t* o_free = s_full + 6;  // [2]
-  uint64_t* drain = s_full + 8;
+  uint64_t* p_full = s_full + 2;  // [2]
+  uint64_t* p_free = s_full + 4;  // [2]
+  uint64_t* o_full = s_full + 6;  // [2]
+  uint64_t* o_free = s_full + 8;  // [2]
+  uint64_t* drain = s_full + 10;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -115,6 +115,8 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
       mbar_init(&q_empty[i], 1);
       mbar_init(&o_full[i], 1);
       mbar_init(&o_free[i], 128);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&p_free[i], 1);
     }
     for (int i = 0; i < NS; ++i) {
       mbar_init(&kv_full[i], 1);
@@ -122,8 +124,6 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
     }
     mbar_init(s_full, 1);
     mbar_init(s_free, 128);
-    mbar_init(p_full, 128);
-    mbar_init(p_free, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -195,18 +195,18 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
       for (int st = 0; ok && st < nsteps; ++st) {
         if (st + 1 < nsteps && !issue_s(st + 1)) break;
         const int s = st % NS, ob = st & 1;
-        if (!mbar_wait(p_full, st & 1, args.status, DEV_TIMEOUT_MMA_FULL, abort_flag)) break;
+        if (!mbar_wait(&p_full[ob], (st >> 1) & 1, args.status, DEV_TIMEOUT_MMA_FULL, abort_flag)) break;
         if (st >= 2 && !mbar_wait(&o_free[ob], ((st >> 1) - 1) & 1, args.status, DEV_TIMEOUT_MMA_TEMPTY, abort_flag))
           break;
         tc_fence_after();
-        const uint32_t pa = smem_u32(sP), va = smem_u32(sV + s * ATTC_KV_BYTES);
+        const uint32_t pa = smem_u32(sP + ob * ATTC_P_BYTES), va = smem_u32(sV + s * ATTC_KV_BYTES);
 #pragma unroll
         for (int k = 0; k < ATTC_BK / 16; ++k)
           umma_bf16(tO + ob * 64, sdesc_kmajor_sw128(pa + k * 32), sdesc_mnmajor_sw128(va + k * 2048), idO,
                     k ? 1u : 0u);
         umma_commit(&o_full[ob]);
         umma_commit(&kv_empty[s]);
-        umma_commit(p_free);
+        umma_commit(&p_free[ob]);
       }
       umma_commit(drain);
       mbar_wait(drain, 0, args.status, DEV_TIMEOUT_DRAIN, nullptr);
@@ -246,31 +246,40 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
 #pragma unroll
         for (int c = 0; c < 64; ++c) s[c] = (c >= lo && c < hi_c) ? s[c] : -INFINITY;
       }
-      float mx = s[0];
+      float pm[8];  // 8 independent partial maxima, then a tree
 #pragma unroll
-      for (int c = 1; c < 64; ++c) mx = fmaxf(mx, s[c]);
+      for (int i = 0; i < 8; ++i) pm[i] = s[i];
+#pragma unroll
+      for (int c = 8; c < 64; ++c) pm[c & 7] = fmaxf(pm[c & 7], s[c]);
+      float mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])), fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
       mx = fmaxf(m, mx * sc);
       const float base = (mx == -INFINITY) ? 0.f : mx;
       const float corr = ex2f_approx(m - base);
       m = mx;
-      // P row -> shared memory (one swizzled [128 x 64] block), once the previous PV has read P.
-      if (st > 0 && !mbar_wait_warp(p_free, (st - 1) & 1, args.status, DEV_TIMEOUT_EPILOGUE, abort_flag)) break;
-      float rs = 0.f;
+      // P row -> shared memory buffer st & 1 (one swizzled [128 x 64] block), once the PV MMA of
+      // step st - 2 has read that buffer.
+      const int pb = st & 1;
+      if (st >= 2 &&
+          !mbar_wait_warp(&p_free[pb], ((st >> 1) - 1) & 1, args.status, DEV_TIMEOUT_EPILOGUE, abort_flag))
+        break;
+      uint8_t* prow = sP + pb * ATTC_P_BYTES + r * 128;
+      float rsum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
         float p[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           p[i] = ex2f_approx(fmaf(s[8 * q + i], sc, -base));
-          rs += p[i];
+          rsum[i] += p[i];
         }
-        *reinterpret_cast<uint4*>(sP + r * 128 + ((q ^ (r & 7)) << 4)) =
+        *reinterpret_cast<uint4*>(prow + ((q ^ (r & 7)) << 4)) =
             make_uint4(pack_bf16x2(p[0], p[1]), pack_bf16x2(p[2], p[3]), pack_bf16x2(p[4], p[5]),
                        pack_bf16x2(p[6], p[7]));
       }
+      const float rs = ((rsum[0] + rsum[1]) + (rsum[2] + rsum[3])) + ((rsum[4] + rsum[5]) + (rsum[6] + rsum[7]));
       l = l * corr + rs;
       fence_proxy_async();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[pb]);
       // Fold a finished O_j (same head) into the register accumulator, 32 columns at a time.
       auto fold = [&](int sj, float cr) -> bool {
         const int ob = sj & 1;
