@@ -152,7 +152,9 @@ S1C_API s1c_status s1c_encoder_hidden(s1c_backend* b, const s1c_batch* batch, fl
  * nullable, out_f32), 1 RoPE (q,k heads in columns [0, rope_cols), positions d_pos, theta),
  * 2 GeGLU (B interleaved per 128 rows, out [M, out_cols] bf16), 3 fp32 residual add in place.
  * variant: 0 by shape, 1 one-CTA 128x256 tiles, 2 two-CTA 256x256 tiles (cta_group::2), 3 one-CTA with
- * the K dimension split across CTAs (fp32 partial sums reduced in a workspace, then the epilogue).
+ * the K dimension split across CTAs (fp32 partial sums reduced in a workspace, then the epilogue),
+ * 4 cluster split-K (the CTAs of a thread-block cluster split K and reduce their partial tiles
+ * through distributed shared memory in one launch; what variant 0 picks for few output tiles).
  * `stream` is a cudaStream_t (NULL = legacy default stream); the call does not synchronise. */
 S1C_API s1c_status s1c_gemm(int32_t epi, const void* d_A, const void* d_B, void* d_out, int32_t M, int32_t N, int32_t K,
                             const float* d_bias, int32_t act, int32_t out_f32, const int32_t* d_pos, float rope_theta,

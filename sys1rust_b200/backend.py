@@ -306,7 +306,8 @@ EPI_STORE, EPI_ROPE, EPI_GEGLU, EPI_RESID = 0, 1, 2, 3
 def gemm(epi: int, a_ptr: int, b_ptr: int, out_ptr: int, M: int, N: int, K: int, bias_ptr: int = 0, act: int = 0,
          out_f32: int = 0, pos_ptr: int = 0, rope_theta: float = 10000.0, rope_cols: int = 0, out_cols: int = 0,
          variant: int = 0, stream: int = 0) -> None:
-    """variant 0: by shape; 1: one-CTA 128x256 tiles; 2: two-CTA 256x256 tiles; 3: one-CTA split-K."""
+    """variant 0: by shape; 1: one-CTA 128x256 tiles; 2: two-CTA 256x256 tiles; 3: one-CTA split-K through
+    a workspace; 4: cluster split-K (partials reduced in distributed shared memory)."""
     L = lib()
     rc = L.s1c_gemm(epi, a_ptr, b_ptr, out_ptr, M, N, K, bias_ptr or None, act, out_f32, pos_ptr or None,
                     rope_theta, rope_cols, out_cols, variant, stream or None)

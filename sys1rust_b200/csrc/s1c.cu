@@ -28,6 +28,7 @@
 #include "attention_tc.cuh"
 #include "gemm_sm100.cuh"
 #include "gemm_sm100_2cta.cuh"
+#include "gemm_sm100_csk.cuh"
 #include "splitk.cuh"
 #include "rowwise.cuh"
 
@@ -142,13 +143,14 @@ CUtensorMap make_tmap_t(const void* ptr, bool f32, uint64_t rows, uint64_t cols,
 CUtensorMap make_tmap(const void* ptr, uint64_t rows, uint64_t k, uint64_t ld, uint32_t box_rows) {
   return make_tmap_t(ptr, false, rows, k, ld, box_rows);
 }
-// A weight (B operand) with its two TMA maps: 256-row boxes for the one-CTA kernel, 128-row
-// boxes for the two-CTA kernel (each CTA of a pair loads half of the 256-row tile).
+// A weight (B operand) with its TMA maps: 256-row boxes for the one-CTA kernel, 128-row boxes
+// for the two-CTA kernel (each CTA of a pair loads half of the 256-row tile) and the 128-wide
+// cluster split-K tiles, 64-row boxes for the 64-wide cluster split-K tiles and the GeGLU halves.
 struct WeightMap {
-  CUtensorMap full, half;
+  CUtensorMap full, half, quarter;
 };
 WeightMap make_wmap(const void* ptr, uint64_t rows, uint64_t k, uint64_t ld) {
-  return WeightMap{make_tmap(ptr, rows, k, ld, 256), make_tmap(ptr, rows, k, ld, 128)};
+  return WeightMap{make_tmap(ptr, rows, k, ld, 256), make_tmap(ptr, rows, k, ld, 128), make_tmap(ptr, rows, k, ld, 64)};
 }
 // GEMM output map: boxes of 32 rows x 128 bytes (one epilogue warp's slice).
 CUtensorMap make_out_tmap(const void* ptr, bool f32, uint64_t rows, uint64_t cols, uint64_t ld) {
@@ -186,7 +188,19 @@ void set_gemm_smem() {
   CK(cudaFuncSetAttribute(gemm2_bf16_sm100<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                           (int)gemm2_smem_bytes()));
 }
+template <int BN, int EPI>
+void set_csk_smem() {
+  CK(cudaFuncSetAttribute(gemm_csk_sm100<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                          (int)csk_smem_bytes<BN>()));
+}
 void set_all_gemm_smem() {
+  set_csk_smem<128, EPI_STORE>();
+  set_csk_smem<128, EPI_ROPE>();
+  set_csk_smem<128, EPI_GEGLU>();
+  set_csk_smem<128, EPI_RESID>();
+  set_csk_smem<64, EPI_STORE>();
+  set_csk_smem<64, EPI_ROPE>();
+  set_csk_smem<64, EPI_RESID>();
   set_gemm_smem<EPI_STORE>();
   set_gemm_smem<EPI_ROPE>();
   set_gemm_smem<EPI_GEGLU>();
@@ -219,17 +233,81 @@ int pick_k_splits(int M, int N, int K, int num_sms, size_t ws_bytes) {
   return ksp;
 }
 
-// GEMM variant: 0 = by shape (split-K when there are few tiles and a split context is given,
-// else the one-CTA kernel), 1 = one-CTA, 2 = two-CTA, 3 = one-CTA split-K (at least 2 splits).
+// Cluster split-K plan (gemm_sm100_csk.cuh) for a GEMM with few output tiles: the tile width
+// (128, or 64 when that puts more SMs on the weights; GeGLU tiles are always 128 wide) and the
+// cluster size C (1, 2, 4 or 8 CTAs, each a K split of at least one 64-wide block), as many CTAs
+// as fit on the SMs in one wave.
+struct CskPlan {
+  int bn = 128, C = 1, tiles = 0;
+};
+CskPlan plan_csk(int M, int N, int K, int num_sms, bool geglu) {
+  CskPlan best;
+  const int nk = (K + GEMM_BK - 1) / GEMM_BK;
+  for (int bn : {128, 64}) {
+    if (geglu && bn != 128) continue;
+    const int tiles = ((M + GEMM_BM - 1) / GEMM_BM) * ((N + bn - 1) / bn);
+    int C = CSK_MAX_C;
+    while (C > 1 && (C > nk || tiles * C > num_sms)) C >>= 1;
+    if (best.tiles == 0 || tiles * C > best.tiles * best.C) best = CskPlan{bn, C, tiles};
+  }
+  return best;
+}
+
+template <int BN, int EPI>
+void launch_csk_bn(const CUtensorMap& ta, const CUtensorMap& tb, const CskArgs& a, int tiles, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(tiles * a.C));
+  cfg.blockDim = dim3(GEMM_THREADS);
+  cfg.dynamicSmemBytes = csk_smem_bytes<BN>();
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)a.C;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = t_pdl ? 2 : 1;
+  CK(cudaLaunchKernelEx(&cfg, gemm_csk_sm100<BN, EPI>, ta, tb, a));
+}
+
+template <int EPI>
+void launch_csk(const CUtensorMap& ta, const WeightMap& tb, const GemmArgs& g, const SplitCtx& sk, int num_sms,
+                cudaStream_t st) {
+  const CskPlan p = plan_csk(g.M, g.N, g.K, num_sms, EPI == EPI_GEGLU);
+  CskArgs a{};
+  a.M = g.M; a.N = g.N; a.K = g.K; a.C = p.C;
+  a.out = sk.out; a.ldo = sk.ldo;
+  a.bias = g.bias; a.act = g.act; a.out_f32 = g.out_f32;
+  a.pos = g.pos; a.inv_freq = g.inv_freq; a.rope_cols = g.rope_cols; a.out_cols = g.out_cols;
+  a.status = g.status;
+  if constexpr (EPI == EPI_GEGLU) {
+    launch_csk_bn<128, EPI>(ta, tb.quarter, a, p.tiles, st);
+  } else {
+    if (p.bn == 128) launch_csk_bn<128, EPI>(ta, tb.half, a, p.tiles, st);
+    else launch_csk_bn<64, EPI>(ta, tb.quarter, a, p.tiles, st);
+  }
+}
+
+// GEMM variant: 0 = by shape (cluster split-K when there are few tiles and an output context is
+// given, else the one-CTA kernel), 1 = one-CTA, 2 = two-CTA, 3 = one-CTA split-K through the fp32
+// workspace and a finalize kernel (at least 2 splits), 4 = cluster split-K.
 template <int EPI>
 void launch_gemm(const CUtensorMap& ta, const WeightMap& tb, const CUtensorMap& tc, const GemmArgs& a0, int num_sms,
                  cudaStream_t st, int variant = 0, const SplitCtx* sk = nullptr, int64_t* extra_launches = nullptr) {
   if (a0.M <= 0) return;
   GemmArgs a = a0;
   a.k_splits = 1;
+  // Few output tiles (small token counts): the cluster split-K kernel, one launch per GEMM.
+  if (sk && (variant == 4 || (variant == 0 && ((a.M + GEMM_BM - 1) / GEMM_BM) * ((a.N + GEMM_BN - 1) / GEMM_BN) * 2 <= num_sms))) {
+    launch_csk<EPI>(ta, tb, a, *sk, num_sms, st);
+    CK(cudaGetLastError());
+    return;
+  }
   int ksp = 1;
   const int rows = (a.M + GEMM_BM - 1) / GEMM_BM * GEMM_BM;
-  if (sk && sk->ws && (variant == 0 || variant == 3)) {
+  if (sk && sk->ws && variant == 3) {
     ksp = pick_k_splits(a.M, a.N, a.K, num_sms, sk->ws_bytes);
     if (variant == 3 && ksp < 2 && (a.K + GEMM_BK - 1) / GEMM_BK >= 2 && 2 * (size_t)rows * a.N * 4 <= sk->ws_bytes)
       ksp = 2;
@@ -367,7 +445,7 @@ struct s1c_backend {
   float* inv_freq[2] = {nullptr, nullptr};  // 0 global theta, 1 local theta
 
   // activations (capacity in rows, multiples of 128)
-  int gemm_variant = 0;   // `gemm=auto|1cta|2cta`
+  int gemm_variant = 0;   // `gemm=auto|1cta|2cta|splitk|csk`
   bool pdl = true;        // `pdl=0|1`: programmatic dependent launch between the forward's kernels
   bool attn_tc = false;  // true: tcgen05 attention (attention_tc.cuh, `attn=tc`); false: mma.sync (attention.cuh)
   int cap_T = 0, cap_R = 0;
@@ -1220,7 +1298,9 @@ void apply_settings(s1c_backend& B, const char* spec) {
       if (v == "auto") B.gemm_variant = 0;
       else if (v == "1cta") B.gemm_variant = 1;
       else if (v == "2cta") B.gemm_variant = 2;
-      else throw S1cError(S1C_ERR_CONFIG, "settings: `" + kv + "`: `" + v + "` is not one of auto, 1cta, 2cta");
+      else if (v == "splitk") B.gemm_variant = 3;
+      else if (v == "csk") B.gemm_variant = 4;
+      else throw S1cError(S1C_ERR_CONFIG, "settings: `" + kv + "`: `" + v + "` is not one of auto, 1cta, 2cta, splitk, csk");
     } else if (k == "attn") {
       if (v == "tc") B.attn_tc = true;
       else if (v == "mma") B.attn_tc = false;
@@ -1492,7 +1572,7 @@ s1c_status s1c_gemm(int32_t epi, const void* d_A, const void* d_B, void* d_out, 
     const bool f32 = epi == EPI_RESID || (epi == EPI_STORE && out_f32);
     const int out_w = (epi == EPI_GEGLU) ? out_cols : N;
     const CUtensorMap ta = make_tmap(d_A, (uint64_t)M, K, K, GEMM_BM);
-    if (variant < 0 || variant > 3) throw S1cError(S1C_ERR_ARG, "variant must be 0, 1, 2 or 3");
+    if (variant < 0 || variant > 4) throw S1cError(S1C_ERR_ARG, "variant must be 0, 1, 2, 3 or 4");
     const WeightMap tb = make_wmap(d_B, N, K, K);
     const CUtensorMap tc = make_out_tmap(d_out, f32, (uint64_t)M, out_w, out_w);
     // Split-K workspace of this entry point: one 32 MB buffer per device, kept for the process.

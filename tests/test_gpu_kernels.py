@@ -23,7 +23,7 @@ def _rand(shape, seed, scale=1.0):
     return (torch.randn(*shape, generator=g) * scale).to(torch.bfloat16).cuda()
 
 
-VARIANTS = [1, 2, 3]  # one-CTA 128x256 tiles, two-CTA 256x256 tiles, one-CTA split-K
+VARIANTS = [1, 2, 3, 4]  # one-CTA 128x256 tiles, two-CTA 256x256 tiles, workspace split-K, cluster split-K
 
 
 @pytest.mark.parametrize("variant", VARIANTS)
@@ -65,6 +65,28 @@ def test_gemm_residual_in_place(cuda_lib, variant):
     gemm(EPI_RESID, a.data_ptr(), b.data_ptr(), h.data_ptr(), M, N, K, variant=variant)
     torch.cuda.synchronize()
     assert _rel_err(h, ref) < 1e-4
+
+
+@pytest.mark.parametrize("M", [1, 17, 128, 200, 256])
+@pytest.mark.parametrize("N,K", [(1024, 64), (1024, 128), (1024, 1024), (3072, 1024), (1024, 2624), (256, 4096)])
+def test_cluster_split_k_shapes(cuda_lib, M, N, K):
+    """Cluster split-K over cluster sizes 1..8 (K of 1, 2, 16, 41 and 64 blocks) and both tile
+    widths; the result is bit-identical from one call to the next (partials summed in rank order)."""
+    from sys1rust_b200.backend import EPI_RESID, EPI_STORE, gemm
+    a, b = _rand((M, K), 31), _rand((N, K), 32)
+    out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    gemm(EPI_STORE, a.data_ptr(), b.data_ptr(), out.data_ptr(), M, N, K, variant=4)
+    torch.cuda.synchronize()
+    assert _rel_err(out, a.float() @ b.float().t()) < 1e-2
+    h0 = torch.randn(M, N, generator=torch.Generator().manual_seed(33)).float().cuda()
+    outs = []
+    for _ in range(2):
+        h = h0.clone()
+        gemm(EPI_RESID, a.data_ptr(), b.data_ptr(), h.data_ptr(), M, N, K, variant=4)
+        torch.cuda.synchronize()
+        outs.append(h)
+    assert _rel_err(outs[0], h0 + a.float() @ b.float().t()) < 1e-4
+    assert torch.equal(outs[0], outs[1])
 
 
 def _rope_ref(x, pos, theta):
