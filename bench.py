@@ -40,16 +40,16 @@ def log(*a):
 
 
 def dist_env():
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    return rank, world, local
+    from sys1rust_b200.dist import env_rank
+    r = env_rank()
+    return r.rank, r.world, r.local
 
 
 def workload(world: int, rank: int):
-    from sys1rust_b200.workloads import cfg5_requests, shard_lpt
+    from sys1rust_b200.dist import shard_for_rank
+    from sys1rust_b200.workloads import cfg5_requests
     reqs = cfg5_requests(n=REQ_PER_GPU * world, seed=1)
-    return reqs, shard_lpt(reqs, world)[rank]
+    return reqs, shard_for_rank(reqs, world, rank)
 
 
 def cpu_oracle_sample(cfg, weights, items, budget_s: float):
@@ -169,13 +169,10 @@ def main():
     args.warmup = max(args.warmup, 3)
 
     import torch
+    from sys1rust_b200 import dist
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
-    if world > 1:
-        import datetime
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
+    dist.init(world, backend="nccl", timeout_s=120, device=torch.device("cuda", local))
 
     from sys1rust_b200.backend import CudaBackend
     from sys1rust_b200.config import large_model
@@ -211,16 +208,11 @@ def main():
 
     def barrier():
         torch.cuda.synchronize()
-        if world > 1:
-            torch.distributed.barrier()
+        dist.barrier(world)
         torch.cuda.synchronize()
 
     def max_over_ranks(x: float) -> float:
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device="cuda")
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        return float(t.item())
+        return dist.max_over_ranks(x, world, device="cuda")
 
     for _ in range(args.warmup):
         step()
@@ -347,8 +339,7 @@ def main():
                "sample": f"{info['requests']} requests / {info['tokens']} tokens of this workload, one row per "
                          f"forward, {info['seconds']:.1f} s, torch fp32 oracle"}
 
-    if world > 1:
-        torch.distributed.barrier()
+    dist.barrier(world)
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "value_per_gpu": value / world,
@@ -380,8 +371,7 @@ def main():
         }
         print(json.dumps(line), flush=True)
     be.close()
-    if world > 1:
-        torch.distributed.destroy_process_group()
+    dist.shutdown(world)
 
 
 if __name__ == "__main__":
