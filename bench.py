@@ -31,6 +31,10 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "encoder tokens/sec/GPU (packed varlen) at 1/2/4/8 B200; p50 ms per 128-tok request"
+# DRAM bytes (read + write) per algorithmic FLOP of a kernel, from one ncu capture
+# (profiles/gemm_wi_geglu_M16384.md: 84.49 MB for 176.09 GFLOP at M = 16384); a launch's traffic is
+# this times its FLOPs.
+DRAM_BYTES_PER_FLOP = {"gemm_wi_geglu": 84.49e6 / 176.09e9}
 REQ_PER_GPU = 1024
 BATCH_TOKENS = 16384
 
@@ -303,13 +307,8 @@ def main():
     dom_name, dom = max(prof.items(), key=lambda kv: kv[1]["ms"])
     per_launch_ms = dom["ms"] / dom["launches"]
     traffic = None
-    try:
-        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
-            tr = json.load(f).get(dom_name)
-        if tr:
-            traffic = tr["dram_bytes_per_flop"] * dom["flops"] / dom["launches"]
-    except (OSError, ValueError, KeyError):
-        pass
+    if dom_name in DRAM_BYTES_PER_FLOP and dom["flops"] > 0:
+        traffic = DRAM_BYTES_PER_FLOP[dom_name] * dom["flops"] / dom["launches"]
     if dom["flops"] > 0:
         achieved = dom["flops"] / dom["launches"] / (per_launch_ms / 1e3) / 1e12
         peak = peaks.get("bf16_tflops_sustained")

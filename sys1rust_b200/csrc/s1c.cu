@@ -1603,12 +1603,25 @@ s1c_status s1c_attention(const void* d_q, const void* d_k, const void* d_v, void
                          int32_t k_stride, int32_t v_stride, int32_t o_stride, int32_t heads,
                          const int32_t* cu_seqlens, int32_t n, int32_t window, float scale, int32_t impl,
                          void* stream) {
-  int* d_cu = nullptr;
-  int4* d_items = nullptr;
+  // Metadata buffers of this entry point: one per device, grown on demand and kept for the
+  // process (calls are serialised by the lock; each call waits for its kernel before returning).
+  struct AttnScratch {
+    int* d_cu = nullptr;
+    int4* d_items = nullptr;
+    int* d_status = nullptr;
+    size_t cu_cap = 0, items_cap = 0;
+  };
+  static std::mutex mu;
+  static AttnScratch scratch[64];
+  std::lock_guard<std::mutex> guard(mu);
   try {
     if (!d_q || !d_k || !d_v || !d_o || !cu_seqlens || n <= 0 || heads <= 0 || (impl != 0 && impl != 1))
       throw S1cError(S1C_ERR_ARG, "bad attention arguments");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    int dev = 0;
+    CK(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) throw S1cError(S1C_ERR_ARG, "device index out of range");
+    AttnScratch& sc = scratch[dev];
     const int qtile = impl == 0 ? ATTC_BQ : ATT_BQ;
     std::vector<int4> items;
     for (int r = 0; r < n; ++r) {
@@ -1616,10 +1629,25 @@ s1c_status s1c_attention(const void* d_q, const void* d_k, const void* d_v, void
       for (int q = 0; q < len; q += qtile) items.push_back(make_int4(r, base + q, std::min(qtile, len - q), 0));
     }
     const int T = cu_seqlens[n];
-    CK(cudaMalloc(&d_cu, (n + 1) * 4));
-    CK(cudaMalloc(&d_items, items.size() * 16));
-    CK(cudaMemcpy(d_cu, cu_seqlens, (n + 1) * 4, cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(d_items, items.data(), items.size() * 16, cudaMemcpyHostToDevice));
+    if (sc.cu_cap < (size_t)n + 1) {
+      if (sc.d_cu) CK(cudaFree(sc.d_cu));
+      sc.d_cu = nullptr;
+      sc.cu_cap = 0;
+      CK(cudaMalloc(&sc.d_cu, ((size_t)n + 1) * 4));
+      sc.cu_cap = (size_t)n + 1;
+    }
+    if (sc.items_cap < items.size()) {
+      if (sc.d_items) CK(cudaFree(sc.d_items));
+      sc.d_items = nullptr;
+      sc.items_cap = 0;
+      CK(cudaMalloc(&sc.d_items, items.size() * 16));
+      sc.items_cap = items.size();
+    }
+    if (!sc.d_status) CK(cudaMalloc(&sc.d_status, sizeof(int)));
+    int* d_cu = sc.d_cu;
+    int4* d_items = sc.d_items;
+    CK(cudaMemcpyAsync(d_cu, cu_seqlens, ((size_t)n + 1) * 4, cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(d_items, items.data(), items.size() * 16, cudaMemcpyHostToDevice, st));
     const float scale_log2 = scale * 1.4426950408889634f;
     if (impl == 0) {
       // one map for Q, one for K and V together: V must sit in K's rows at a 64-aligned column
@@ -1627,15 +1655,12 @@ s1c_status s1c_attention(const void* d_q, const void* d_k, const void* d_v, void
       if (v_stride != k_stride || dv < 0 || dv % 64 || dv + heads * 64 > k_stride)
         throw S1cError(S1C_ERR_ARG, "tcgen05 attention needs v in the rows of k (same pitch, 64-aligned column)");
       static bool attr_set[64] = {false};
-      int dev = 0;
-      CK(cudaGetDevice(&dev));
       if (!attr_set[dev]) {
         CK(cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATTC_SMEM));
         attr_set[dev] = true;
       }
-      int* d_status = nullptr;
-      CK(cudaMalloc(&d_status, sizeof(int)));
-      CK(cudaMemset(d_status, 0, sizeof(int)));
+      int* d_status = sc.d_status;
+      CK(cudaMemsetAsync(d_status, 0, sizeof(int), st));
       const CUtensorMap tq = make_tmap(d_q, T, heads * 64, q_stride, ATTC_BQ);
       const CUtensorMap tkv = make_tmap(d_k, T, dv + heads * 64, k_stride, ATTC_BK);
       AttnTcArgs a{d_cu, d_items, static_cast<bf16*>(d_o), o_stride, 0, 0, (int)dv, heads, window, scale_log2, d_status};
@@ -1644,7 +1669,6 @@ s1c_status s1c_attention(const void* d_q, const void* d_k, const void* d_v, void
       cudaError_t e2 = cudaStreamSynchronize(st);
       int hs = 0;
       if (e2 == cudaSuccess) cudaMemcpy(&hs, d_status, sizeof(int), cudaMemcpyDeviceToHost);
-      cudaFree(d_status);
       if (e != cudaSuccess) throw S1cError(S1C_ERR_CUDA, cudaGetErrorString(e));
       if (e2 != cudaSuccess) throw S1cError(S1C_ERR_CUDA, cudaGetErrorString(e2));
       if (hs) throw S1cError(S1C_ERR_DEVICE_TIMEOUT, "device-side wait ran out (code " + std::to_string(hs) + ")");
@@ -1657,12 +1681,8 @@ s1c_status s1c_attention(const void* d_q, const void* d_k, const void* d_v, void
       if (e != cudaSuccess) throw S1cError(S1C_ERR_CUDA, cudaGetErrorString(e));
       if (e2 != cudaSuccess) throw S1cError(S1C_ERR_CUDA, cudaGetErrorString(e2));
     }
-    cudaFree(d_cu);
-    cudaFree(d_items);
     return S1C_OK;
   } catch (const S1cError& e) {
-    if (d_cu) cudaFree(d_cu);
-    if (d_items) cudaFree(d_items);
     g_create_error = e.what();
     return e.code;
   }

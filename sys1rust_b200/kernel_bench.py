@@ -1,0 +1,128 @@
+"""Single-kernel timing through the C ABI, for profiling one kernel on one shape.
+
+    python -m sys1rust_b200.kernel_bench gemm --shape wi_geglu --m 16384 [--variant 1] [--reps 20]
+    python -m sys1rust_b200.kernel_bench attention --window 64 --tokens 16384 [--impl 1] [--reps 20]
+
+``gemm`` runs one encoder GEMM with its fused epilogue (shapes as in ``gemm_sweep``); ``attention``
+runs the varlen attention over a packed batch of cfg5-distributed sequence lengths (lognormal,
+median 200, clipped to [32, 1024]) filling ``--tokens`` tokens, 16 heads of 64, ``--window`` -1 for
+global layers. Prints one JSON line: mean time per launch from CUDA events over ``--reps`` launches
+after 3 warm-up launches, and the algorithmic TFLOP/s (attention: 4 * 64 per valid (query, key)
+pair and head, the key set of the reference's masks). ``s1c_attention`` uploads its work list and
+waits for the kernel on every call, so the attention figures are per call and include that upload
+(a lower bound on the kernel's rate; the forward's per-launch profile times the kernel alone).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+
+import numpy as np
+import torch
+
+from .backend import attention, gemm, interleave_wi
+from .gemm_sweep import SHAPES
+
+
+def _time(fn, reps: int) -> float:
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def bench_gemm(shape: str, M: int, variant: int, reps: int, seed: int = 0) -> dict:
+    from .backend import EPI_GEGLU, EPI_RESID
+    name, K, N, epi = next(s for s in SHAPES if s[0] == shape)
+    g = torch.Generator().manual_seed(seed)
+    a = torch.randn(M, K, generator=g).to(torch.bfloat16).cuda()
+    if epi == EPI_GEGLU:
+        w = torch.randn(N, K, generator=g).to(torch.bfloat16)
+        b = torch.from_numpy(interleave_wi(w.view(torch.int16).numpy(), N // 2)).view(torch.bfloat16).cuda()
+        o = torch.empty(M, N // 2, dtype=torch.bfloat16, device="cuda")
+    else:
+        b = torch.randn(N, K, generator=g).to(torch.bfloat16).cuda()
+        o = torch.zeros(M, N, dtype=torch.float32 if epi == EPI_RESID else torch.bfloat16, device="cuda")
+    pos = torch.from_numpy((np.arange(M) % 512).astype(np.int32)).cuda()
+
+    def launch():
+        gemm(epi, a.data_ptr(), b.data_ptr(), o.data_ptr(), M, b.shape[0], K, pos_ptr=pos.data_ptr(),
+             rope_theta=10000.0, rope_cols=2048, out_cols=N // 2, variant=variant,
+             stream=torch.cuda.current_stream().cuda_stream)
+
+    ms = _time(launch, reps)
+    return {"kernel": "gemm", "shape": name, "M": M, "N": N, "K": K, "variant": variant, "ms": ms,
+            "tflops": 2.0 * M * N * K / (ms / 1e3) / 1e12}
+
+
+def cfg5_lengths(tokens: int, seed: int = 1) -> list:
+    rng = np.random.default_rng(seed)
+    out, tot = [], 0
+    while True:
+        L = int(np.clip(np.round(np.exp(np.log(200.0) + 0.6 * rng.standard_normal())), 32, 1024))
+        if tot + L > tokens:
+            break
+        out.append(L)
+        tot += L
+    return out
+
+
+def valid_pairs(lens, window: int) -> int:
+    tot = 0
+    for L in lens:
+        if window < 0:
+            tot += L * L
+        else:
+            i = np.arange(L)
+            tot += int((np.minimum(i, window) + np.minimum(L - 1 - i, window) + 1).sum())
+    return tot
+
+
+def bench_attention(tokens: int, window: int, impl: int, reps: int, heads: int = 16, seed: int = 0) -> dict:
+    lens = cfg5_lengths(tokens)
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    T, d = int(cu[-1]), heads * 64
+    g = torch.Generator().manual_seed(seed)
+    qkv = torch.randn(T, 3 * d, generator=g).to(torch.bfloat16).cuda()
+    o = torch.empty(T, d, dtype=torch.bfloat16, device="cuda")
+    q, k, v = qkv[:, :d], qkv[:, d:2 * d], qkv[:, 2 * d:]
+
+    def launch():
+        attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), 3 * d, 3 * d, 3 * d, d, heads, cu, window,
+                  0.125, impl=impl, stream=torch.cuda.current_stream().cuda_stream)
+
+    ms = _time(launch, reps)
+    flops = 4.0 * 64 * heads * valid_pairs(lens, window)
+    return {"kernel": "attention", "impl": impl, "window": window, "tokens": T, "sequences": len(lens),
+            "ms_per_call": ms, "tflops_per_call": flops / (ms / 1e3) / 1e12, "flops": flops}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    sub = ap.add_subparsers(dest="kernel", required=True)
+    g = sub.add_parser("gemm")
+    g.add_argument("--shape", default="wi_geglu", choices=[s[0] for s in SHAPES])
+    g.add_argument("--m", type=int, default=16384)
+    g.add_argument("--variant", type=int, default=0)
+    g.add_argument("--reps", type=int, default=20)
+    a = sub.add_parser("attention")
+    a.add_argument("--tokens", type=int, default=16384)
+    a.add_argument("--window", type=int, default=64)
+    a.add_argument("--impl", type=int, default=1)
+    a.add_argument("--reps", type=int, default=20)
+    args = ap.parse_args()
+    if args.kernel == "gemm":
+        r = bench_gemm(args.shape, args.m, args.variant, args.reps)
+    else:
+        r = bench_attention(args.tokens, args.window, args.impl, args.reps)
+    print(json.dumps(r))
+
+
+if __name__ == "__main__":
+    main()
