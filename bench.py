@@ -266,6 +266,26 @@ def main():
     e2e_s = max_over_ranks(e2e_s)
     e2e_value = tokens_total * e2e_steps / e2e_s
 
+    # ---- serving: this rank's requests submitted one by one to the serving queue ------------
+    # (sys1rust_b200.server: cross-request packing into <= BATCH_TOKENS varlen batches on a native
+    # worker thread; host buffers in and out, so copies are inside the timed region)
+    from sys1rust_b200.server import Server
+    with Server([be], max_concurrent=len(mine) + 1, max_batch_tokens=BATCH_TOKENS, linger_us=1000) as srv:
+        def serve_all():
+            tk = [srv.submit(it) for it in mine]
+            for it, t in zip(mine, tk):
+                srv.wait(t, len(it.markers))
+        serve_all()  # warm-up pass
+        barrier()
+        t_srv = time.perf_counter()
+        serve_all()
+        srv_s = max_over_ranks(time.perf_counter() - t_srv)
+        srv_stats = srv.stats()
+    server = {"value": tokens_total / srv_s, "unit": "tokens/s", "requests_per_gpu": len(mine),
+              "batches_per_gpu": int(srv_stats["batches"]) // 2,
+              "path": "sys1rust_b200.server.Server over s1c_server_*: requests submitted one by one, packed "
+                      "across requests by the native worker, results collected per request"}
+
     # ---- latency of one 128-token request (cfg1), host API ---------------------------------
     lat = None
     one = Varlen.from_rows(cfg1())
@@ -361,6 +381,7 @@ def main():
             "encoder_gemm_tflops": enc_tflops,
             "cpu_baseline": cpu,
             "latency_cfg1": lat,
+            "server": server,
             "cfg3_tokens_per_s": cfg3_tps,
             "clocks": clk.summary(),
             "gpu_launches": int(launches),

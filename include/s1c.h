@@ -39,11 +39,15 @@ typedef int32_t s1c_status;
 #define S1C_ERR_CONFIG (-4)         /* config the kernels do not support (Error::Config) */
 #define S1C_ERR_DEVICE_TIMEOUT (-5) /* a bounded device-side wait ran out; the context stays usable */
 #define S1C_ERR_UNSUPPORTED (-6)    /* no sm_100 device */
+#define S1C_ERR_BUSY (-7)           /* serving: admission cap reached, "server busy, try again later" (503, Retry-After: 1) */
+#define S1C_ERR_DEAD (-8)           /* serving: no inference worker, "inference worker is not running" (503) */
+#define S1C_ERR_TIMEOUT (-9)        /* serving: result not ready within the wait's timeout; the ticket stays valid */
 
 /* Tensor element types accepted at load (the conversions of laya-core/src/weights.rs:82-115). */
 #define S1C_DT_F32 0
 #define S1C_DT_F16 1
 #define S1C_DT_BF16 2
+#define S1C_DT_F64 3
 
 /* Encoder + head configuration: the normalised `EncoderConfig` (laya-core/src/config.rs:64-202)
  * plus the head layer count of `AgentConfig` (config.rs:9-30). */
@@ -107,7 +111,8 @@ S1C_API s1c_status s1c_create(const s1c_model_desc* desc, const s1c_tensor* tens
                       s1c_backend** out);
 S1C_API void s1c_destroy(s1c_backend* b);
 S1C_API const char* s1c_last_error(const s1c_backend* b);
-/* Error text of the last s1c_create that failed on the calling thread. */
+/* Error text of the last call without a backend handle that failed on the calling thread
+ * (s1c_create, s1c_weights_*, s1c_server_*, s1c_gemm, s1c_attention). */
 S1C_API const char* s1c_create_error(void);
 
 /* `Backend::name` (backend.rs:111), e.g. "cuda(sm_100a,bf16)". */
@@ -197,6 +202,93 @@ S1C_API s1c_status s1c_gemm_splitk_noalloc(int32_t epi, const void* d_A, const v
 
 /* Number of this library's kernel launches the last forward on this handle enqueued. */
 S1C_API int64_t s1c_last_launch_count(const s1c_backend* b);
+
+/* ---- Checkpoint files (laya_core::Weights, runtime/crates/laya-core/src/weights.rs:10-77) ----
+ * A memory-mapped `model.safetensors`, validated when opened: an interrupted download fails at
+ * open with the file's path and length, never inside a later call. Tensor views point into the
+ * mapping and stay valid until s1c_weights_close. Errors are S1C_ERR_WEIGHTS with the text in
+ * s1c_create_error(), worded as the reference's Error::Weights messages. */
+typedef struct s1c_weights s1c_weights;
+
+/* Weights::open (weights.rs:23-43): maps <model_dir>/model.safetensors. Errors:
+ *   "'model.safetensors' not found in <model_dir>"
+ *   "<model_dir>/model.safetensors (<bytes> bytes) is truncated or not a safetensors file: <why>" */
+S1C_API s1c_status s1c_weights_open(const char* model_dir, s1c_weights** out);
+S1C_API void s1c_weights_close(s1c_weights* w);
+/* Weights::names (weights.rs:50-57): the tensor count; names in header order via s1c_weights_tensor. */
+S1C_API int32_t s1c_weights_count(const s1c_weights* w);
+/* Index of the tensor called `name`, or -1. */
+S1C_API int32_t s1c_weights_find(const s1c_weights* w, const char* name);
+/* View of tensor i (name, dtype, shape, data in the mapping). Float dtypes only, as to_f32
+ * converts (weights.rs:82-105): F32, F16, BF16, F64; others are "unsupported dtype <X>". */
+S1C_API s1c_status s1c_weights_tensor(const s1c_weights* w, int32_t i, s1c_tensor* out);
+/* Weights::verify (weights.rs:66-77): the encoder., type_emb., scorer. and act_head. families are
+ * present; else "checkpoint is missing '<prefix>' parameters; expected an RL Agent decision model". */
+S1C_API s1c_status s1c_weights_verify(const s1c_weights* w);
+/* s1c_create over every float tensor of an open checkpoint (F16 / F32 / F64 converted at load). */
+S1C_API s1c_status s1c_create_from_weights(const s1c_model_desc* desc, const s1c_weights* w, int32_t device,
+                                           s1c_backend** out);
+
+/* ---- Serving: cross-request batching over GPU workers --------------------------------------
+ * Replaces the reference server's single inference thread (runtime/crates/sys1rust/src/worker.rs)
+ * with one worker per backend that packs queued requests from many clients into varlen batches,
+ * keeping its admission contract (http.rs:168-230): submit never blocks; over the concurrency cap it
+ * returns S1C_ERR_BUSY at once. A request is the tokenised row of one `Agent::predict` call. The
+ * permit is held from submit until the result is collected (s1c_server_wait) or the ticket is
+ * cancelled; a cancelled request still queued is dropped unrun (worker.rs:202-205). A failed forward
+ * fails the requests of its batch only. Error texts: s1c_create_error(). */
+typedef struct s1c_server s1c_server;
+
+/* The forward a worker runs on one packed batch: outputs as s1c_forward_varlen (logits [n*kmax],
+ * pooled [n*hidden]); on failure return a negative status and optionally point *error at a
+ * message valid until the next call with the same ctx. */
+typedef s1c_status (*s1c_server_forward_fn)(void* ctx, const s1c_varlen* batch, float* logits, float* pooled,
+                                            const char** error);
+
+typedef struct s1c_server_opts {
+  int32_t max_concurrent;   /* admission cap; <= 0: 16, the reference's DEFAULT_MAX_CONCURRENT (config.rs:14) */
+  int32_t max_batch_tokens; /* packed tokens per batch; <= 0: 16384 (a longer request runs alone) */
+  int32_t max_batch_rows;   /* rows per batch; <= 0: 1024 */
+  int32_t linger_us;        /* wait up to this long for more requests when under half a batch is queued */
+} s1c_server_opts;
+
+/* One request: token ids of the row (`collate_to`'s row layout, sequence.rs:44-104), marker
+ * positions inside the row, question type (0 choice, 1 score, 2 noul). Copied at submit. */
+typedef struct s1c_request {
+  const uint32_t* ids;
+  int32_t len;
+  const uint32_t* marker_pos;
+  int32_t n_markers;
+  uint32_t qtype;
+} s1c_request;
+
+typedef struct s1c_server_stats {
+  uint64_t batches, rows, tokens, failed_batches, busy_rejections, cancelled_skipped;
+  int32_t in_flight, queued, workers_alive;
+} s1c_server_stats;
+
+/* One worker per backend (each handle then belongs to the server until s1c_server_destroy). */
+S1C_API s1c_status s1c_server_create(s1c_backend* const* backends, int32_t n_backends, const s1c_server_opts* opts,
+                                     s1c_server** out);
+/* Workers running `fn` with ctx[i] (tests, other engines); `hidden` sizes the pooled rows. */
+S1C_API s1c_status s1c_server_create_with(s1c_server_forward_fn fn, void* const* ctx, int32_t n_workers,
+                                          int32_t hidden, const s1c_server_opts* opts, s1c_server** out);
+/* Queue a request. S1C_ERR_BUSY over the cap, S1C_ERR_DEAD once stopped, S1C_ERR_ARG for a
+ * malformed row (empty, or a marker outside the row). */
+S1C_API s1c_status s1c_server_submit(s1c_server* s, const s1c_request* req, uint64_t* ticket);
+/* Wait for a result (timeout_ms < 0: no limit) and collect it, releasing the permit: logits
+ * [n_markers], pooled [hidden], infer_ms (nullable) = the batch's forward time. S1C_ERR_TIMEOUT
+ * leaves the ticket pending. Any other status ends the ticket. */
+S1C_API s1c_status s1c_server_wait(s1c_server* s, uint64_t ticket, int32_t timeout_ms, float* logits, float* pooled,
+                                   float* infer_ms);
+/* The client went away: drop the ticket (unrun if still queued) and release its permit. */
+S1C_API s1c_status s1c_server_cancel(s1c_server* s, uint64_t ticket);
+S1C_API s1c_status s1c_server_get_stats(s1c_server* s, s1c_server_stats* out);
+/* Stop accepting, fail the queued requests with S1C_ERR_DEAD, let running batches finish and
+ * join the workers. Collect or cancel outstanding tickets afterwards. */
+S1C_API void s1c_server_stop(s1c_server* s);
+/* Stop (if needed) and free. No other call on `s` may be running or follow. */
+S1C_API void s1c_server_destroy(s1c_server* s);
 
 #ifdef __cplusplus
 }

@@ -27,6 +27,7 @@ HEADER = os.path.join(os.path.dirname(HERE), "include", "s1c.h")
 
 S1C_OK, S1C_ERR_ARG, S1C_ERR_CUDA, S1C_ERR_WEIGHTS, S1C_ERR_CONFIG, S1C_ERR_DEVICE_TIMEOUT, S1C_ERR_UNSUPPORTED = \
     0, -1, -2, -3, -4, -5, -6
+S1C_ERR_BUSY, S1C_ERR_DEAD, S1C_ERR_TIMEOUT = -7, -8, -9
 DT_F32, DT_F16, DT_BF16 = 0, 1, 2
 
 
@@ -68,6 +69,28 @@ class CVarlen(C.Structure):
                 ("marker_pos", C.c_void_p), ("marker_count", C.c_void_p), ("qtype", C.c_void_p)]
 
 
+class ServerOpts(C.Structure):
+    _fields_ = [("max_concurrent", C.c_int32), ("max_batch_tokens", C.c_int32), ("max_batch_rows", C.c_int32),
+                ("linger_us", C.c_int32)]
+
+
+class CRequest(C.Structure):
+    _fields_ = [("ids", C.c_void_p), ("len", C.c_int32), ("marker_pos", C.c_void_p), ("n_markers", C.c_int32),
+                ("qtype", C.c_uint32)]
+
+
+class ServerStats(C.Structure):
+    _fields_ = [("batches", C.c_uint64), ("rows", C.c_uint64), ("tokens", C.c_uint64),
+                ("failed_batches", C.c_uint64), ("busy_rejections", C.c_uint64),
+                ("cancelled_skipped", C.c_uint64), ("in_flight", C.c_int32), ("queued", C.c_int32),
+                ("workers_alive", C.c_int32)]
+
+
+# s1c_server_forward_fn
+SERVER_FORWARD_FN = C.CFUNCTYPE(C.c_int32, C.c_void_p, C.POINTER(CVarlen), C.POINTER(C.c_float),
+                                C.POINTER(C.c_float), C.POINTER(C.c_char_p))
+
+
 _lib = None
 
 
@@ -102,6 +125,22 @@ def lib() -> C.CDLL:
         "s1c_profile": (I32, [P, I32]),
         "s1c_profile_report": (SZ, [P, C.c_char_p, SZ]),
         "s1c_gemm_splitk_noalloc": (I32, [I32, P, P, P, I32, I32, I32, P, I32, I32, P, F32, I32, I32, P]),
+        "s1c_weights_open": (I32, [C.c_char_p, C.POINTER(P)]),
+        "s1c_weights_close": (None, [P]),
+        "s1c_weights_count": (I32, [P]),
+        "s1c_weights_find": (I32, [P, C.c_char_p]),
+        "s1c_weights_tensor": (I32, [P, I32, C.POINTER(Tensor)]),
+        "s1c_weights_verify": (I32, [P]),
+        "s1c_create_from_weights": (I32, [C.POINTER(ModelDesc), P, I32, C.POINTER(P)]),
+        "s1c_server_create": (I32, [C.POINTER(P), I32, C.POINTER(ServerOpts), C.POINTER(P)]),
+        "s1c_server_create_with": (I32, [SERVER_FORWARD_FN, C.POINTER(P), I32, I32, C.POINTER(ServerOpts),
+                                         C.POINTER(P)]),
+        "s1c_server_submit": (I32, [P, C.POINTER(CRequest), C.POINTER(C.c_uint64)]),
+        "s1c_server_wait": (I32, [P, C.c_uint64, I32, P, P, C.POINTER(F32)]),
+        "s1c_server_cancel": (I32, [P, C.c_uint64]),
+        "s1c_server_get_stats": (I32, [P, C.POINTER(ServerStats)]),
+        "s1c_server_stop": (None, [P]),
+        "s1c_server_destroy": (None, [P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -115,6 +154,7 @@ def header_functions() -> List[str]:
     """Every function ``include/s1c.h`` declares."""
     with open(HEADER) as f:
         text = re.sub(r"/\*.*?\*/", "", f.read(), flags=re.S)
+    text = re.sub(r"typedef\s+\w+\s*\(\s*\*\s*\w+\s*\)\s*\([^;]*\);", "", text)  # function-pointer types
     return sorted(set(re.findall(r"\b(s1c_[a-z_]+)\s*\(", text)))
 
 
@@ -142,20 +182,108 @@ class BackendOutput:
     hidden: Optional[np.ndarray] = None
 
 
+_DT_NAME = {DT_F32: "F32", DT_F16: "F16", DT_BF16: "BF16", 3: "F64"}
+_DT_NP = {"F32": np.float32, "F16": np.uint16, "BF16": np.uint16, "F64": np.float64}
+
+
+class WeightsFile:
+    """A memory-mapped ``model.safetensors`` read by the library (``laya_core::Weights``,
+    ``weights.rs:10-77``): validated at open, so a missing or truncated file raises ``WeightsError``
+    with the reference's wording; tensors are views into the mapping until ``close``."""
+
+    def __init__(self, model_dir: str):
+        L = lib()
+        h = C.c_void_p()
+        rc = L.s1c_weights_open(os.fsencode(model_dir), C.byref(h))
+        if rc != S1C_OK:
+            _raise(rc, L.s1c_create_error().decode())
+        self._h = h
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib().s1c_weights_close(self._h)
+            self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _tensor(self, i: int) -> Tensor:
+        t = Tensor()
+        rc = lib().s1c_weights_tensor(self._h, i, C.byref(t))
+        if rc != S1C_OK:
+            _raise(rc, lib().s1c_create_error().decode())
+        return t
+
+    def names(self) -> List[str]:
+        """Names of the tensors (every dtype), in header order."""
+        out = []
+        for i in range(lib().s1c_weights_count(self._h)):
+            t = Tensor()
+            if lib().s1c_weights_tensor(self._h, i, C.byref(t)) == S1C_OK:
+                out.append(t.name.decode())
+            else:
+                out.append(None)
+        return out
+
+    def shape(self, name: str) -> Tuple[int, ...]:
+        i = lib().s1c_weights_find(self._h, name.encode())
+        if i < 0:
+            raise WeightsError(S1C_ERR_WEIGHTS, f"{name}: tensor not found")
+        t = self._tensor(i)
+        return tuple(int(t.shape[d]) for d in range(t.ndim))
+
+    def tensor(self, name: str) -> Tuple[str, Tuple[int, ...], np.ndarray]:
+        """``(dtype, shape, raw array)`` of a float tensor (a copy of the mapped bytes)."""
+        i = lib().s1c_weights_find(self._h, name.encode())
+        if i < 0:
+            raise WeightsError(S1C_ERR_WEIGHTS, f"{name}: tensor not found")
+        t = self._tensor(i)
+        dt = _DT_NAME[t.dtype]
+        shape = tuple(int(t.shape[d]) for d in range(t.ndim))
+        n = int(np.prod(shape)) if shape else 1
+        buf = (C.c_char * (n * np.dtype(_DT_NP[dt]).itemsize)).from_address(t.data)
+        return dt, shape, np.frombuffer(bytes(buf), dtype=_DT_NP[dt]).reshape(shape)
+
+    def verify(self) -> None:
+        rc = lib().s1c_weights_verify(self._h)
+        if rc != S1C_OK:
+            _raise(rc, lib().s1c_create_error().decode())
+
+
 class CudaBackend:
     """One model on one GPU. Calls on one instance must be serialised."""
 
-    def __init__(self, cfg: ModelConfig, tensors: Dict[str, Tuple[str, Tuple[int, ...], np.ndarray]],
-                 device: int = 0, max_tokens: int = 16384):
-        L = lib()
+    def _desc(self, cfg: ModelConfig, max_tokens: int) -> ModelDesc:
         e = cfg.encoder
         self.cfg = cfg
         self.hidden = e.hidden_size
         self._local = np.array([1 if x else 0 for x in e.layer_is_local], dtype=np.uint8)
-        desc = ModelDesc(e.vocab_size, e.hidden_size, e.num_hidden_layers, e.num_attention_heads,
+        return ModelDesc(e.vocab_size, e.hidden_size, e.num_hidden_layers, e.num_attention_heads,
                          e.intermediate_size, e.norm_eps, e.local_attention, e.global_rope_theta,
                          e.local_rope_theta, self._local.ctypes.data_as(C.POINTER(C.c_uint8)),
                          cfg.head_layers, e.max_position_embeddings, max_tokens)
+
+    def __init__(self, cfg: ModelConfig, tensors: Optional[Dict[str, Tuple[str, Tuple[int, ...], np.ndarray]]],
+                 device: int = 0, max_tokens: int = 16384, weights_file: Optional[WeightsFile] = None):
+        L = lib()
+        desc = self._desc(cfg, max_tokens)
+        if weights_file is not None:
+            h = C.c_void_p()
+            rc = L.s1c_create_from_weights(C.byref(desc), weights_file._h, device, C.byref(h))
+            if rc != S1C_OK:
+                _raise(rc, L.s1c_create_error().decode())
+            self._h = h
+            self.device = device
+            return
         keep = []
         arr = (Tensor * len(tensors))()
         for i, (name, (dt, shape, data)) in enumerate(tensors.items()):
@@ -163,7 +291,7 @@ class CudaBackend:
             keep.append(data)
             nb = name.encode()
             keep.append(nb)
-            code = {"F32": DT_F32, "F16": DT_F16, "BF16": DT_BF16}[dt]
+            code = {"F32": DT_F32, "F16": DT_F16, "BF16": DT_BF16, "F64": 3}[dt]
             sh = (C.c_int64 * 4)(*(list(shape) + [0] * (4 - len(shape))))
             arr[i] = Tensor(nb, code, len(shape), sh, data.ctypes.data)
         h = C.c_void_p()
@@ -180,13 +308,14 @@ class CudaBackend:
 
     @staticmethod
     def from_dir(model_dir: str, device: int = 0, max_tokens: int = 16384) -> "CudaBackend":
-        """Load ``model.safetensors`` + configs from a checkpoint directory (``Agent::load``)."""
-        from .weights import load_safetensors_bits
+        """Load a checkpoint directory (``Agent::load``): ``encoder/config.json`` and
+        ``rl_agent_config.json`` here, ``model.safetensors`` mapped and converted by the library."""
         cfg = ModelConfig.load(model_dir)
-        t = load_safetensors_bits(os.path.join(model_dir, "model.safetensors"))
-        cfg.head_ffn = t["head.layers.0.linear1.weight"][1][0]
-        cfg.scorer_hidden = t["scorer.1.weight"][1][0]
-        return CudaBackend(cfg, t, device=device, max_tokens=max_tokens)
+        with WeightsFile(model_dir) as wf:
+            wf.verify()
+            cfg.head_ffn = wf.shape("head.layers.0.linear1.weight")[0]
+            cfg.scorer_hidden = wf.shape("scorer.1.weight")[0]
+            return CudaBackend(cfg, None, device=device, max_tokens=max_tokens, weights_file=wf)
 
     def close(self) -> None:
         if getattr(self, "_h", None):

@@ -31,6 +31,8 @@
 #include "gemm_sm100_csk.cuh"
 #include "splitk.cuh"
 #include "rowwise.cuh"
+#include "safetensors.h"
+#include "server.h"
 
 using namespace s1c;
 typedef __nv_bfloat16 bf16;
@@ -100,6 +102,7 @@ float elem_f32(const s1c_tensor& t, size_t i) {
     case S1C_DT_F32: return static_cast<const float*>(t.data)[i];
     case S1C_DT_F16: return f16_bits_to_f32(static_cast<const uint16_t*>(t.data)[i]);
     case S1C_DT_BF16: return bf16_bits_to_f32(static_cast<const uint16_t*>(t.data)[i]);
+    case S1C_DT_F64: return (float)static_cast<const double*>(t.data)[i];
   }
   throw S1cError(S1C_ERR_WEIGHTS, std::string(t.name) + ": unsupported dtype");
 }
@@ -1738,6 +1741,337 @@ s1c_status s1c_gemm_splitk_noalloc(int32_t epi, const void* d_A, const void* d_B
     g_create_error = e.what();
     return S1C_ERR_ARG;
   }
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------------------------
+// Checkpoint files
+
+struct s1c_weights {
+  s1c::st::File file;
+  std::string dir;
+};
+
+extern "C" {
+
+s1c_status s1c_weights_open(const char* model_dir, s1c_weights** out) {
+  g_create_error.clear();
+  if (!model_dir || !out) {
+    g_create_error = "null argument";
+    return S1C_ERR_ARG;
+  }
+  *out = nullptr;
+  const std::string dir(model_dir);
+  const std::string path = dir + ((dir.empty() || dir.back() == '/') ? "" : "/") + "model.safetensors";
+  struct stat sb;
+  if (stat(path.c_str(), &sb) != 0 || !S_ISREG(sb.st_mode)) {
+    g_create_error = "'model.safetensors' not found in " + dir;
+    return S1C_ERR_WEIGHTS;
+  }
+  std::unique_ptr<s1c_weights> w(new s1c_weights());
+  w->dir = dir;
+  try {
+    w->file.open(path);
+  } catch (const std::exception& e) {
+    g_create_error = path + " (" + std::to_string((unsigned long long)sb.st_size) +
+                     " bytes) is truncated or not a safetensors file: " + e.what();
+    return S1C_ERR_WEIGHTS;
+  }
+  *out = w.release();
+  return S1C_OK;
+}
+
+void s1c_weights_close(s1c_weights* w) { delete w; }
+
+int32_t s1c_weights_count(const s1c_weights* w) { return w ? (int32_t)w->file.tensors().size() : 0; }
+
+int32_t s1c_weights_find(const s1c_weights* w, const char* name) {
+  if (!w || !name) return -1;
+  const auto& ts = w->file.tensors();
+  for (size_t i = 0; i < ts.size(); ++i)
+    if (ts[i].name == name) return (int32_t)i;
+  return -1;
+}
+
+s1c_status s1c_weights_tensor(const s1c_weights* w, int32_t i, s1c_tensor* out) {
+  g_create_error.clear();
+  if (!w || !out || i < 0 || (size_t)i >= w->file.tensors().size()) {
+    g_create_error = "tensor index out of range";
+    return S1C_ERR_ARG;
+  }
+  const s1c::st::Tensor& t = w->file.tensors()[(size_t)i];
+  int32_t dt;
+  if (t.dtype == "F32") dt = S1C_DT_F32;
+  else if (t.dtype == "F16") dt = S1C_DT_F16;
+  else if (t.dtype == "BF16") dt = S1C_DT_BF16;
+  else if (t.dtype == "F64") dt = S1C_DT_F64;
+  else {
+    g_create_error = t.name + ": unsupported dtype " + t.dtype;
+    return S1C_ERR_WEIGHTS;
+  }
+  if (t.shape.size() > 4) {
+    g_create_error = t.name + ": more than 4 dimensions";
+    return S1C_ERR_WEIGHTS;
+  }
+  out->name = t.name.c_str();
+  out->dtype = dt;
+  out->ndim = (int32_t)t.shape.size();
+  for (int d = 0; d < 4; ++d) out->shape[d] = d < out->ndim ? t.shape[(size_t)d] : 0;
+  out->data = w->file.data(t);
+  return S1C_OK;
+}
+
+s1c_status s1c_weights_verify(const s1c_weights* w) {
+  g_create_error.clear();
+  if (!w) {
+    g_create_error = "null argument";
+    return S1C_ERR_ARG;
+  }
+  for (const char* prefix : {"encoder.", "type_emb.", "scorer.", "act_head."}) {
+    bool found = false;
+    for (const auto& t : w->file.tensors())
+      if (t.name.compare(0, std::strlen(prefix), prefix) == 0) {
+        found = true;
+        break;
+      }
+    if (!found) {
+      g_create_error = std::string("checkpoint is missing '") + prefix +
+                       "' parameters; expected an RL Agent decision model";
+      return S1C_ERR_WEIGHTS;
+    }
+  }
+  return S1C_OK;
+}
+
+s1c_status s1c_create_from_weights(const s1c_model_desc* desc, const s1c_weights* w, int32_t device,
+                                   s1c_backend** out) {
+  g_create_error.clear();
+  if (!desc || !w || !out) {
+    g_create_error = "null argument";
+    return S1C_ERR_ARG;
+  }
+  std::vector<s1c_tensor> ts;
+  for (int32_t i = 0; i < s1c_weights_count(w); ++i) {
+    s1c_tensor t;
+    if (s1c_weights_tensor(w, i, &t) == S1C_OK) ts.push_back(t);  // integer tensors are not weights
+  }
+  return s1c_create(desc, ts.data(), (int32_t)ts.size(), device, out);
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------------------------
+// Serving
+
+struct s1c_server {
+  s1c::srv::Server srv;
+};
+
+namespace {
+
+s1c_status backend_forward(void* ctx, const s1c_varlen* v, float* logits, float* pooled, const char** err) {
+  s1c_backend* b = static_cast<s1c_backend*>(ctx);
+  const s1c_status st = s1c_forward_varlen(b, v, logits, pooled, nullptr);
+  if (st != S1C_OK && err) *err = s1c_last_error(b);
+  return st;
+}
+
+s1c_status server_start(s1c_server_forward_fn fn, void* const* ctx, int32_t n, int32_t hidden,
+                        const s1c_server_opts* opts, s1c_server** out) {
+  g_create_error.clear();
+  if (!fn || !ctx || n <= 0 || hidden <= 0 || !out) {
+    g_create_error = "bad server arguments";
+    return S1C_ERR_ARG;
+  }
+  *out = nullptr;
+  std::unique_ptr<s1c_server> s(new s1c_server());
+  s1c::srv::Server& v = s->srv;
+  v.fn = fn;
+  v.ctx.assign(ctx, ctx + n);
+  v.hidden = hidden;
+  if (opts) v.opts = *opts;
+  if (v.opts.max_concurrent <= 0) v.opts.max_concurrent = 16;
+  if (v.opts.max_batch_tokens <= 0) v.opts.max_batch_tokens = 16384;
+  if (v.opts.max_batch_rows <= 0) v.opts.max_batch_rows = 1024;
+  if (v.opts.linger_us < 0) v.opts.linger_us = 0;
+  try {
+    for (int32_t w = 0; w < n; ++w) {
+      ++v.alive;
+      try {
+        v.workers.emplace_back([&v, w] { v.run(w); });
+      } catch (...) {
+        --v.alive;
+        throw;
+      }
+    }
+  } catch (const std::exception& e) {
+    {
+      std::lock_guard<std::mutex> lk(v.mu);
+      v.stopping = true;
+    }
+    v.cv_work.notify_all();
+    for (auto& t : v.workers) t.join();
+    g_create_error = std::string("cannot start the workers: ") + e.what();
+    return S1C_ERR_ARG;
+  }
+  *out = s.release();
+  return S1C_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+s1c_status s1c_server_create(s1c_backend* const* backends, int32_t n, const s1c_server_opts* opts, s1c_server** out) {
+  if (!backends || n <= 0) {
+    g_create_error = "no backends";
+    return S1C_ERR_ARG;
+  }
+  int hidden = 0;
+  for (int32_t i = 0; i < n; ++i) {
+    if (!backends[i]) {
+      g_create_error = "null backend";
+      return S1C_ERR_ARG;
+    }
+    if (i > 0 && backends[i]->d != hidden) {
+      g_create_error = "backends of different hidden sizes";
+      return S1C_ERR_ARG;
+    }
+    hidden = backends[i]->d;
+  }
+  return server_start(backend_forward, reinterpret_cast<void* const*>(backends), n, hidden, opts, out);
+}
+
+s1c_status s1c_server_create_with(s1c_server_forward_fn fn, void* const* ctx, int32_t n_workers, int32_t hidden,
+                                  const s1c_server_opts* opts, s1c_server** out) {
+  return server_start(fn, ctx, n_workers, hidden, opts, out);
+}
+
+s1c_status s1c_server_submit(s1c_server* s, const s1c_request* req, uint64_t* ticket) {
+  g_create_error.clear();
+  if (!s || !req || !ticket) {
+    g_create_error = "null argument";
+    return S1C_ERR_ARG;
+  }
+  s1c::srv::Server& v = s->srv;
+  std::unique_lock<std::mutex> lk(v.mu);
+  if ((int32_t)v.jobs.size() >= v.opts.max_concurrent) {
+    ++v.stats.busy_rejections;
+    g_create_error = "server busy, try again later";
+    return S1C_ERR_BUSY;
+  }
+  if (v.stopping || v.alive.load() == 0) {
+    g_create_error = "inference worker is not running";
+    return S1C_ERR_DEAD;
+  }
+  if (req->len <= 0 || !req->ids || (req->n_markers > 0 && !req->marker_pos) || req->n_markers < 0) {
+    g_create_error = "malformed request: empty row or missing marker positions";
+    return S1C_ERR_ARG;
+  }
+  for (int32_t k = 0; k < req->n_markers; ++k)
+    if (req->marker_pos[k] >= (uint32_t)req->len) {
+      g_create_error = "malformed request: marker position " + std::to_string(req->marker_pos[k]) +
+                       " outside a row of " + std::to_string(req->len) + " tokens";
+      return S1C_ERR_ARG;
+    }
+  auto j = std::make_shared<s1c::srv::Job>();
+  j->id = v.next_id++;
+  j->ids.assign(req->ids, req->ids + req->len);
+  if (req->n_markers > 0) j->markers.assign(req->marker_pos, req->marker_pos + req->n_markers);
+  j->qtype = req->qtype;
+  v.jobs[j->id] = j;
+  v.queue.push_back(j);
+  *ticket = j->id;
+  lk.unlock();
+  v.cv_work.notify_one();
+  return S1C_OK;
+}
+
+s1c_status s1c_server_wait(s1c_server* s, uint64_t ticket, int32_t timeout_ms, float* logits, float* pooled,
+                           float* infer_ms) {
+  g_create_error.clear();
+  if (!s) {
+    g_create_error = "null argument";
+    return S1C_ERR_ARG;
+  }
+  s1c::srv::Server& v = s->srv;
+  std::unique_lock<std::mutex> lk(v.mu);
+  auto it = v.jobs.find(ticket);
+  if (it == v.jobs.end()) {
+    g_create_error = "unknown ticket " + std::to_string(ticket);
+    return S1C_ERR_ARG;
+  }
+  std::shared_ptr<s1c::srv::Job> j = it->second;
+  if (timeout_ms < 0) {
+    v.cv_done.wait(lk, [&] { return j->done; });
+  } else if (!v.cv_done.wait_for(lk, std::chrono::milliseconds(timeout_ms), [&] { return j->done; })) {
+    g_create_error = "result not ready";
+    return S1C_ERR_TIMEOUT;
+  }
+  v.jobs.erase(ticket);
+  if (j->status != S1C_OK) {
+    g_create_error = j->error;
+    return j->status;
+  }
+  if (logits && !j->logits.empty()) std::memcpy(logits, j->logits.data(), j->logits.size() * sizeof(float));
+  if (pooled) std::memcpy(pooled, j->pooled.data(), j->pooled.size() * sizeof(float));
+  if (infer_ms) *infer_ms = (float)j->infer_ms;
+  return S1C_OK;
+}
+
+s1c_status s1c_server_cancel(s1c_server* s, uint64_t ticket) {
+  g_create_error.clear();
+  if (!s) {
+    g_create_error = "null argument";
+    return S1C_ERR_ARG;
+  }
+  s1c::srv::Server& v = s->srv;
+  std::lock_guard<std::mutex> lk(v.mu);
+  auto it = v.jobs.find(ticket);
+  if (it == v.jobs.end()) {
+    g_create_error = "unknown ticket " + std::to_string(ticket);
+    return S1C_ERR_ARG;
+  }
+  it->second->cancelled = true;
+  v.jobs.erase(it);
+  return S1C_OK;
+}
+
+s1c_status s1c_server_get_stats(s1c_server* s, s1c_server_stats* out) {
+  if (!s || !out) return S1C_ERR_ARG;
+  s1c::srv::Server& v = s->srv;
+  std::lock_guard<std::mutex> lk(v.mu);
+  *out = v.stats;
+  out->in_flight = (int32_t)v.jobs.size();
+  int32_t q = 0;
+  for (auto& j : v.queue) q += j->cancelled ? 0 : 1;
+  out->queued = q;
+  out->workers_alive = v.alive.load();
+  return S1C_OK;
+}
+
+void s1c_server_stop(s1c_server* s) {
+  if (!s) return;
+  s1c::srv::Server& v = s->srv;
+  {
+    std::lock_guard<std::mutex> lk(v.mu);
+    if (v.stopping && v.workers.empty()) return;
+    v.stopping = true;
+    v.fail_queued_locked("inference worker is not running");
+  }
+  v.cv_work.notify_all();
+  v.cv_done.notify_all();
+  for (auto& t : v.workers)
+    if (t.joinable()) t.join();
+  v.workers.clear();
+  v.cv_done.notify_all();
+}
+
+void s1c_server_destroy(s1c_server* s) {
+  if (!s) return;
+  s1c_server_stop(s);
+  delete s;
 }
 
 }  // extern "C"

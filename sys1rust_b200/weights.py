@@ -105,17 +105,54 @@ class SyntheticWeights:
     def items(self) -> Iterator[Tuple[str, np.ndarray]]:
         return iter(self.tensors.items())
 
-    def save(self, model_dir: str) -> None:
-        """Write ``model.safetensors`` (BF16), ``encoder/config.json`` and
+    def save(self, model_dir: str, dtype: str = "BF16") -> None:
+        """Write ``model.safetensors`` (``BF16``, or ``F16`` as the reference's checkpoints are
+        stored: each bf16 value converted to the nearest half), ``encoder/config.json`` and
         ``rl_agent_config.json`` in the checkpoint layout ``Agent::load`` reads."""
         os.makedirs(os.path.join(model_dir, "encoder"), exist_ok=True)
-        write_safetensors_bf16(os.path.join(model_dir, "model.safetensors"), self.tensors)
+        path = os.path.join(model_dir, "model.safetensors")
+        if dtype == "BF16":
+            write_safetensors_bf16(path, self.tensors)
+        elif dtype == "F16":
+            write_safetensors(path, {k: ("F16", bf16_bits_to_f16_bits(v)) for k, v in self.tensors.items()})
+        else:
+            raise ValueError(f"unsupported checkpoint dtype {dtype}")
         with open(os.path.join(model_dir, "encoder", "config.json"), "w") as f:
             json.dump(self.cfg.encoder.to_value(), f, indent=1)
         with open(os.path.join(model_dir, "rl_agent_config.json"), "w") as f:
             json.dump({"encoder": "encoder", "head_layers": self.cfg.head_layers,
                        "max_len": self.cfg.max_len, "head_max_len": self.cfg.head_max_len,
                        "act_costs": {"ask": 1.0}, "temperature": [1.0, 1.0, 1.0]}, f, indent=1)
+
+
+def bf16_bits_to_f16_bits(bits: np.ndarray) -> np.ndarray:
+    """bf16 bit patterns -> IEEE half bit patterns (round to nearest even)."""
+    f = (bits.astype(np.uint32) << 16).view(np.float32)
+    return f.astype(np.float16).view(np.uint16)
+
+
+_ST_SIZE = {"F64": 8, "F32": 4, "F16": 2, "BF16": 2, "I64": 8, "I32": 4, "U8": 1}
+
+
+def write_safetensors(path: str, tensors: Dict[str, Tuple[str, np.ndarray]]) -> None:
+    """Write ``name -> (dtype, array)`` (arrays holding the raw element bits or values of that
+    dtype) as a safetensors file: 8-byte little-endian header length, JSON header padded with
+    spaces to a multiple of 8 bytes, then the tensors' bytes back to back in header order."""
+    header, off, blobs = {}, 0, []
+    for name, (dt, a) in tensors.items():
+        b = np.ascontiguousarray(a).tobytes()
+        if len(b) != int(np.prod(a.shape)) * _ST_SIZE[dt]:
+            raise ValueError(f"{name}: {len(b)} bytes do not match {dt} x {a.shape}")
+        header[name] = {"dtype": dt, "shape": list(a.shape), "data_offsets": [off, off + len(b)]}
+        off += len(b)
+        blobs.append(b)
+    h = json.dumps(header, separators=(",", ":")).encode()
+    h += b" " * ((8 - len(h) % 8) % 8)
+    with open(path, "wb") as f:
+        f.write(len(h).to_bytes(8, "little"))
+        f.write(h)
+        for b in blobs:
+            f.write(b)
 
 
 def write_safetensors_bf16(path: str, tensors: Dict[str, np.ndarray]) -> None:
