@@ -10,11 +10,11 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 
-def _batch():
+def _batch(vocab):
     from sys1rust_b200.batch import Varlen
     from sys1rust_b200.workloads import _row
     rng = np.random.default_rng(7)
-    return Varlen.from_rows([_row(rng, 1000, L, q) for L, q in [(40, [0, 1]), (97, [2]), (5, [1])]])
+    return Varlen.from_rows([_row(rng, vocab, L, q) for L, q in [(40, [0, 1]), (97, [2]), (5, [1])]])
 
 
 @pytest.mark.parametrize("dtype", ["BF16", "F16"])
@@ -25,7 +25,7 @@ def test_checkpoint_dir_matches_in_memory_tensors(cuda_lib, tmp_path, dtype):
     cfg = small_model()
     w = SyntheticWeights(cfg, seed=11)
     w.save(str(tmp_path), dtype=dtype)
-    v = _batch()
+    v = _batch(cfg.encoder.vocab_size)
     a = CudaBackend.from_dir(str(tmp_path))
     if dtype == "BF16":
         b = CudaBackend.from_synthetic(cfg, w.tensors)

@@ -11,10 +11,10 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 
-def _items(n, seed):
+def _items(n, seed, vocab):
     from sys1rust_b200.workloads import _row
     rng = np.random.default_rng(seed)
-    return [_row(rng, 1000, int(rng.integers(8, 300)), [int(rng.integers(0, 3))]) for _ in range(n)]
+    return [_row(rng, vocab, int(rng.integers(8, 300)), [int(rng.integers(0, 3))]) for _ in range(n)]
 
 
 @pytest.mark.parametrize("workers", [1, 2])
@@ -27,7 +27,7 @@ def test_served_requests_match_single_forwards(cuda_lib, workers):
     cfg = small_model()
     w = SyntheticWeights(cfg, seed=21)
     bes = [CudaBackend.from_synthetic(cfg, w.tensors) for _ in range(workers)]
-    items = _items(40, 5)
+    items = _items(40, 5, cfg.encoder.vocab_size)
     alone = [bes[0].forward_varlen(Varlen.from_rows([it])) for it in items]
     d = cfg.encoder.hidden_size
     with Server(bes, max_concurrent=64, max_batch_tokens=2048) as srv:
