@@ -155,24 +155,6 @@ __global__ void __launch_bounds__(ATT_THREADS, 4) attention_varlen_kernel(const 
       }
     }
 
-    // S = Q K^T for 64 keys: 8 groups of 8 keys.
-    float s[8][4];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
-#pragma unroll
-    for (int ks = 0; ks < 4; ++ks) {
-#pragma unroll
-      for (int jp = 0; jp < 4; ++jp) {
-        // keys 16*jp .. 16*jp+15 (two groups), dims 16*ks .. 16*ks+15
-        const int r = jp * 16 + (lane & 7) + ((lane >> 4) << 3);
-        const int c = ks * 2 + ((lane >> 3) & 1);
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4(k_s0 + buf * TILE_BYTES + swz(r, c), b0, b1, b2, b3);
-        mma_bf16_16816(s[2 * jp], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], b0, b1);
-        mma_bf16_16816(s[2 * jp + 1], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], b2, b3);
-      }
-    }
-
     // Keys this thread's two rows may see, as column offsets [lo, hi) inside the tile: the
     // sequence's [k_lo, k_hi), narrowed to |i - j| <= window on local layers. Masking runs only
     // when some row of the warp does not see the whole tile (edge tiles).
@@ -183,6 +165,37 @@ __global__ void __launch_bounds__(ATT_THREADS, 4) attention_varlen_kernel(const 
       hi0 = min(hi0, s_begin + qpos0 + args.window + 1 - kt0);
       lo1 = max(lo1, s_begin + qpos1 - args.window - kt0);
       hi1 = min(hi1, s_begin + qpos1 + args.window + 1 - kt0);
+    }
+    // 16-key blocks of this tile that some row of the warp sees: [blo, bhi). Blocks outside are
+    // skipped entirely (their scores, exponentials and PV products would all be zero).
+    int blo = min(lo0, lo1), bhi = max(hi0, hi1);
+    blo = __reduce_min_sync(0xffffffffu, blo);
+    bhi = __reduce_max_sync(0xffffffffu, bhi);
+    blo = max(blo, 0) >> 4;
+    bhi = min((max(bhi, 0) + 15) >> 4, ATT_BK / 16);
+
+    // S = Q K^T for 64 keys: 8 groups of 8 keys; per k-step the four K fragments are loaded
+    // before the eight MMAs that use them.
+    float s[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      uint32_t kb[4][4];
+#pragma unroll
+      for (int jp = 0; jp < 4; ++jp) {
+        // keys 16*jp .. 16*jp+15 (two groups), dims 16*ks .. 16*ks+15
+        const int r = jp * 16 + (lane & 7) + ((lane >> 4) << 3);
+        const int c = ks * 2 + ((lane >> 3) & 1);
+        if (jp >= blo && jp < bhi) ldsm_x4(k_s0 + buf * TILE_BYTES + swz(r, c), kb[jp][0], kb[jp][1], kb[jp][2], kb[jp][3]);
+      }
+#pragma unroll
+      for (int jp = 0; jp < 4; ++jp) {
+        if (jp >= blo && jp < bhi) {
+          mma_bf16_16816(s[2 * jp], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], kb[jp][0], kb[jp][1]);
+          mma_bf16_16816(s[2 * jp + 1], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], kb[jp][2], kb[jp][3]);
+        }
+      }
     }
     const bool whole = lo0 <= 0 && hi0 >= ATT_BK && lo1 <= 0 && hi1 >= ATT_BK;
     if (!__all_sync(0xffffffffu, whole)) {
@@ -236,19 +249,24 @@ __global__ void __launch_bounds__(ATT_THREADS, 4) attention_varlen_kernel(const 
       o[j][2] *= corr1; o[j][3] *= corr1;
     }
 
-    // O += P V: 4 k-steps of 16 keys, 8 groups of 8 dims.
+    // O += P V: 4 k-steps of 16 keys (the blocks some row sees), 8 groups of 8 dims; the four
+    // V fragments of a k-step are loaded before its eight MMAs.
 #pragma unroll
     for (int ks = 0; ks < 4; ++ks) {
+      if (ks < blo || ks >= bhi) continue;
       const uint32_t a0 = pa[2 * ks][0], a1 = pa[2 * ks][1], a2 = pa[2 * ks + 1][0], a3 = pa[2 * ks + 1][1];
+      uint32_t vb[4][4];
 #pragma unroll
       for (int jp = 0; jp < 4; ++jp) {
         // keys 16*ks .. +15, dims 16*jp .. +15 (two groups), transposed load
         const int r = ks * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
         const int c = jp * 2 + (lane >> 4);
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4_t(v_s0 + buf * TILE_BYTES + swz(r, c), b0, b1, b2, b3);
-        mma_bf16_16816(o[2 * jp], a0, a1, a2, a3, b0, b1);
-        mma_bf16_16816(o[2 * jp + 1], a0, a1, a2, a3, b2, b3);
+        ldsm_x4_t(v_s0 + buf * TILE_BYTES + swz(r, c), vb[jp][0], vb[jp][1], vb[jp][2], vb[jp][3]);
+      }
+#pragma unroll
+      for (int jp = 0; jp < 4; ++jp) {
+        mma_bf16_16816(o[2 * jp], a0, a1, a2, a3, vb[jp][0], vb[jp][1]);
+        mma_bf16_16816(o[2 * jp + 1], a0, a1, a2, a3, vb[jp][2], vb[jp][3]);
       }
     }
     __syncthreads();

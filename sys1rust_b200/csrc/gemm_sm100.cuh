@@ -54,12 +54,14 @@ struct GemmArgs {
 
 constexpr int GEMM_BM = 128;
 constexpr int GEMM_BK = 64;
-constexpr int GEMM_STAGES = 4;
+constexpr int GEMM_STAGES = 4;  // 128 x 256 tiles: 4 x 48 KB stages
+// 128 x 128 tiles: 6 x 32 KB stages fit beside the staging buffers.
+__host__ __device__ constexpr int gemm_stages(int BN) { return BN >= 256 ? GEMM_STAGES : 6; }
 constexpr int GEMM_THREADS = 192;
 constexpr uint32_t GEMM_STG_BYTES = 4096;  // one staging buffer: 32 rows x 128 bytes
 
 __host__ __device__ constexpr size_t gemm_smem_bytes(int BN) {
-  return (size_t)GEMM_STAGES * (GEMM_BM * GEMM_BK * 2 + BN * GEMM_BK * 2) + 8 * GEMM_STG_BYTES + 1024 /*align*/ +
+  return (size_t)gemm_stages(BN) * (GEMM_BM * GEMM_BK * 2 + BN * GEMM_BK * 2) + 8 * GEMM_STG_BYTES + 1024 /*align*/ +
          256 /*barriers*/;
 }
 
@@ -259,7 +261,7 @@ template <int BN, int EPI>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_bf16_sm100(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmC, const GemmArgs args) {
-  constexpr int BM = GEMM_BM, BK = GEMM_BK, STAGES = GEMM_STAGES;
+  constexpr int BM = GEMM_BM, BK = GEMM_BK, STAGES = gemm_stages(BN);
   constexpr uint32_t A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2, STAGE_BYTES = A_BYTES + B_BYTES;
   constexpr uint32_t TMEM_COLS = 2 * BN;
   static_assert(TMEM_COLS == 32 || TMEM_COLS == 64 || TMEM_COLS == 128 || TMEM_COLS == 256 || TMEM_COLS == 512,

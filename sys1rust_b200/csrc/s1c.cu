@@ -188,6 +188,9 @@ template <int EPI>
 void set_gemm_smem() {
   CK(cudaFuncSetAttribute(gemm_bf16_sm100<GEMM_BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                           (int)gemm_smem_bytes(GEMM_BN)));
+  if constexpr (EPI != EPI_GEGLU)
+    CK(cudaFuncSetAttribute(gemm_bf16_sm100<128, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                            (int)gemm_smem_bytes(128)));
   CK(cudaFuncSetAttribute(gemm2_bf16_sm100<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                           (int)gemm2_smem_bytes()));
 }
@@ -294,8 +297,11 @@ void launch_csk(const CUtensorMap& ta, const WeightMap& tb, const GemmArgs& g, c
 }
 
 // GEMM variant: 0 = by shape (cluster split-K when there are few tiles and an output context is
-// given, else the one-CTA kernel), 1 = one-CTA, 2 = two-CTA, 3 = one-CTA split-K through the fp32
-// workspace and a finalize kernel (at least 2 splits), 4 = cluster split-K.
+// given, else the one-CTA 128 x 256 kernel), 1 = one-CTA 128 x 256, 2 = two-CTA, 3 = one-CTA split-K
+// through the fp32 workspace and a finalize kernel (at least 2 splits), 4 = cluster split-K,
+// 5 = one-CTA 128 x 128 (not for GeGLU). The 128 x 128 tiles would fill the last wave of the SMs
+// better on N = 1024 (6.92 instead of 3.46 waves at 16k tokens) but measured 22 % slower there
+// (half the MMA work per A tile loaded), so the shape rule never picks them.
 template <int EPI>
 void launch_gemm(const CUtensorMap& ta, const WeightMap& tb, const CUtensorMap& tc, const GemmArgs& a0, int num_sms,
                  cudaStream_t st, int variant = 0, const SplitCtx* sk = nullptr, int64_t* extra_launches = nullptr) {
@@ -337,6 +343,12 @@ void launch_gemm(const CUtensorMap& ta, const WeightMap& tb, const CUtensorMap& 
     const int tiles = ((a.M + 255) / 256) * ((a.N + GEMM_BN - 1) / GEMM_BN);
     const int clusters = std::min(tiles, num_sms / 2);
     launch_k(gemm2_bf16_sm100<EPI>, dim3(2 * clusters), dim3(GEMM_THREADS), gemm2_smem_bytes(), st, ta, tb.half, tc, a);
+  } else if (EPI != EPI_GEGLU && variant == 5) {
+    if constexpr (EPI != EPI_GEGLU) {
+      const int tiles = ((a.M + GEMM_BM - 1) / GEMM_BM) * ((a.N + 127) / 128);
+      const int grid = std::min(tiles, num_sms);
+      launch_k(gemm_bf16_sm100<128, EPI>, dim3(grid), dim3(GEMM_THREADS), gemm_smem_bytes(128), st, ta, tb.half, tc, a);
+    }
   } else {
     const int tiles = ((a.M + GEMM_BM - 1) / GEMM_BM) * ((a.N + GEMM_BN - 1) / GEMM_BN);
     const int grid = std::min(tiles, num_sms);
@@ -1575,7 +1587,8 @@ s1c_status s1c_gemm(int32_t epi, const void* d_A, const void* d_B, void* d_out, 
     const bool f32 = epi == EPI_RESID || (epi == EPI_STORE && out_f32);
     const int out_w = (epi == EPI_GEGLU) ? out_cols : N;
     const CUtensorMap ta = make_tmap(d_A, (uint64_t)M, K, K, GEMM_BM);
-    if (variant < 0 || variant > 4) throw S1cError(S1C_ERR_ARG, "variant must be 0, 1, 2, 3 or 4");
+    if (variant < 0 || variant > 5) throw S1cError(S1C_ERR_ARG, "variant must be 0 to 5");
+    if (variant == 5 && epi == EPI_GEGLU) throw S1cError(S1C_ERR_ARG, "GeGLU tiles are 256 wide (variant 5 does not apply)");
     const WeightMap tb = make_wmap(d_B, N, K, K);
     const CUtensorMap tc = make_out_tmap(d_out, f32, (uint64_t)M, out_w, out_w);
     // Split-K workspace of this entry point: one 32 MB buffer per device, kept for the process.

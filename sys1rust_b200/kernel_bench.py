@@ -1,6 +1,8 @@
 """Single-kernel timing through the C ABI, for profiling one kernel on one shape.
 
     python -m sys1rust_b200.kernel_bench gemm --shape wi_geglu --m 16384 [--variant 1] [--reps 20]
+    (variants as s1c_gemm: 0 by shape, 1 one-CTA 128x256, 2 two-CTA, 3 workspace split-K,
+    4 cluster split-K, 5 one-CTA 128x128)
     python -m sys1rust_b200.kernel_bench attention --window 64 --tokens 16384 [--impl 1] [--reps 20]
 
 ``gemm`` runs one encoder GEMM with its fused epilogue (shapes as in ``gemm_sweep``); ``attention``
