@@ -4,18 +4,21 @@
 // Encoder GEMMs of the reference forward (runtime/crates/laya-mlx/src/lib.rs:1363-1390 `mm` and
 // `lin_add`, :1600-1675 the layer loop) and the head's biased linears (:1726-1760) all run here.
 //
-// Structure (one CTA per SM, 192 threads):
+// Structure (one CTA per SM, 64 + 32 x GEMM_EPI_WARPS threads):
 //   warp 0      TMA producer: 128x64 A tile + BNx64 B tile per stage, 128-byte swizzle,
 //               4-stage ring of shared-memory buffers guarded by full/empty mbarriers.
 //   warp 1      allocates 2*BN TMEM columns and issues tcgen05.mma (M=128, N=BN, K=16 per
 //               instruction, fp32 accumulation in TMEM); tcgen05.commit releases a stage when
 //               the MMAs reading it are done and hands a finished accumulator to the epilogue.
-//   warps 2..5  epilogue: tcgen05.ld of the accumulator (one row per thread), the fused math,
-//               then each warp writes its 32-row slice of a 128-byte-wide column block into a
-//               swizzled shared-memory staging buffer and one lane hands it to TMA: a tensor
-//               store for bf16 / fp32 outputs, a tensor reduce-add for the fp32 residual stream.
-//               Global traffic is therefore fully coalesced whatever the row layout. Two
-//               accumulators alternate, so the epilogue of tile i overlaps the MMAs of tile i+1.
+//   warps 2..   epilogue, one (default) or two warps per TMEM lane quadrant (a warp may only read
+//               the 32 TMEM lanes of quadrant warp % 4), each taking its share of the columns:
+//               tcgen05.ld of the accumulator (one row per thread), the fused math, then each
+//               warp writes its 32-row slice of a 128-byte-wide column block into a swizzled
+//               shared-memory staging buffer and one lane hands it to TMA: a tensor store for
+//               bf16 / fp32 outputs, a tensor reduce-add for the fp32 residual stream. Global
+//               traffic is therefore fully coalesced whatever the row layout. Two accumulators
+//               alternate, so the epilogue of tile i overlaps the MMAs of tile i+1 (see
+//               GEMM_EPI_WARPS for what the overlap costs).
 // Tiles are walked n-fastest (tile = m_block * n_blocks + n_block) so CTAs running together
 // share their A rows and stream the whole weight from L2.
 //
@@ -57,7 +60,19 @@ constexpr int GEMM_BK = 64;
 constexpr int GEMM_STAGES = 4;  // 128 x 256 tiles: 4 x 48 KB stages
 // 128 x 128 tiles: 6 x 32 KB stages fit beside the staging buffers.
 __host__ __device__ constexpr int gemm_stages(int BN) { return BN >= 256 ? GEMM_STAGES : 6; }
-constexpr int GEMM_THREADS = 192;
+constexpr int GEMM_THREADS = 192;    // the two-CTA and cluster split-K kernels: 2 + 4 warps
+// Epilogue warps of the persistent one-CTA kernel. The accumulator drains while the next tile's
+// MMAs run, but the epilogue's work still slows the mainloop: without it the mainloop reaches
+// ~1.6 PFLOP/s on the K = 1024 shapes, with it ~1.15-1.23. Measured: the epilogue warps that share
+// an SM sub-partition with the MMA-issuing warp cost the most (a cheap epilogue on that quadrant
+// alone gave +13 %), eight warps were slower than four on GeGLU (1177 vs 1235 TFLOP/s) and equal
+// elsewhere, so four is the default; eight is kept as a build option.
+#ifndef S1C_GEMM_EPI_WARPS
+#define S1C_GEMM_EPI_WARPS 4
+#endif
+constexpr int GEMM_EPI_WARPS = S1C_GEMM_EPI_WARPS;  // the persistent one-CTA kernel: 2 + 4 or 2 + 8 warps
+static_assert(GEMM_EPI_WARPS == 4 || GEMM_EPI_WARPS == 8, "one or two epilogue warps per TMEM lane quadrant");
+constexpr int GEMM1_THREADS = 64 + 32 * GEMM_EPI_WARPS;
 constexpr uint32_t GEMM_STG_BYTES = 4096;  // one staging buffer: 32 rows x 128 bytes
 
 __host__ __device__ constexpr size_t gemm_smem_bytes(int BN) {
@@ -65,7 +80,31 @@ __host__ __device__ constexpr size_t gemm_smem_bytes(int BN) {
          256 /*barriers*/;
 }
 
-S1C_DEV float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
+// GELU(x) = x * Phi(x) = 0.5 x erfc(-x / sqrt(2)) (the reference's erf form, lib.rs:494-510).
+// erfc(z), z >= 0, by the Chebyshev fit of Numerical Recipes (Press, Teukolsky, Vetterling and
+// Flannery, 2nd ed., section 6.2, "erfcc"): erfc(z) = t exp(-z^2 + P(t)), t = 1 / (1 + z / 2), with
+// fractional error below 1.2e-7 for every z; then Phi(x) = 1 - erfc(|x|/sqrt 2) / 2 for x >= 0 and
+// erfc(|x|/sqrt 2) / 2 below. One reciprocal, one exp2 and eleven FMAs, no branch; the GELU's
+// absolute error is below 2e-8 (checked against erf in double precision over [-12, 12]).
+S1C_DEV float gelu_erf(float x) {
+  const float z = fabsf(x) * 0.70710678118654752f;
+  float t;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t) : "f"(fmaf(0.5f, z, 1.0f)));
+  float p = 0.17087277f;
+  p = fmaf(p, t, -0.82215223f);
+  p = fmaf(p, t, 1.48851587f);
+  p = fmaf(p, t, -1.13520398f);
+  p = fmaf(p, t, 0.27886807f);
+  p = fmaf(p, t, -0.18628806f);
+  p = fmaf(p, t, 0.09678418f);
+  p = fmaf(p, t, 0.37409196f);
+  p = fmaf(p, t, 1.00002368f);
+  p = fmaf(p, t, -1.26551223f);
+  float e;  // exp(-z^2 + p) = 2^((p - z^2) log2 e)
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(fmaf(-z, z, p) * 1.4426950408889634f));
+  const float h = 0.5f * t * e;
+  return x * (x >= 0.f ? 1.0f - h : h);
+}
 
 // TMA tensor store / reduce-add of a staged box, and the bulk-group bookkeeping.
 S1C_DEV void tma_store_2d(const void* tmap, const void* src, int x, int y) {
@@ -80,17 +119,26 @@ S1C_DEV void tma_reduce_add_2d(const void* tmap, const void* src, int x, int y) 
 }
 S1C_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 S1C_DEV void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+S1C_DEV void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 S1C_DEV void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // Per-warp staging of 32 rows x 128 bytes with the 128-byte swizzle the output tensor map uses:
 // row r, 16-byte chunk c lives at r*128 + ((c ^ (r & 7)) * 16). Double buffered per warp.
 struct Stager {
-  uint8_t* base;   // this warp's two buffers
+  uint8_t* base;   // this warp's buffers
   uint32_t count;  // units issued so far
   int lane;
+  int nbuf;        // 1 or 2 buffers
 
   // Wait until the buffer about to be written is no longer read by an older store.
   S1C_DEV uint8_t* acquire() {
+    if (nbuf == 1) {
+      if (count >= 1) {
+        if (lane == 0) bulk_wait_read0();
+        __syncwarp();
+      }
+      return base;
+    }
     if (count >= 2) {
       if (lane == 0) bulk_wait_read1();
       __syncwarp();
@@ -109,6 +157,14 @@ struct Stager {
       *reinterpret_cast<uint4*>(buf + lane * 128 + ((c ^ (lane & 7)) << 4)) =
           make_uint4(pack_bf16x2(v[8 * c], v[8 * c + 1]), pack_bf16x2(v[8 * c + 2], v[8 * c + 3]),
                      pack_bf16x2(v[8 * c + 4], v[8 * c + 5]), pack_bf16x2(v[8 * c + 6], v[8 * c + 7]));
+  }
+  // 16 values as bf16 into the 16-byte chunks c and c + 1 of this lane's row.
+  S1C_DEV void put_bf16x16(uint8_t* buf, int c, const float* v) {
+#pragma unroll
+    for (int k = 0; k < 2; ++k)
+      *reinterpret_cast<uint4*>(buf + lane * 128 + (((c + k) ^ (lane & 7)) << 4)) =
+          make_uint4(pack_bf16x2(v[8 * k], v[8 * k + 1]), pack_bf16x2(v[8 * k + 2], v[8 * k + 3]),
+                     pack_bf16x2(v[8 * k + 4], v[8 * k + 5]), pack_bf16x2(v[8 * k + 6], v[8 * k + 7]));
   }
   // Hand the staged box at (x, y) to TMA.
   S1C_DEV void issue(const void* tmap, const uint8_t* buf, int x, int y, bool reduce) {
@@ -134,11 +190,13 @@ S1C_DEV void add_bias32(float* v, const float* bias, int col) {
 
 // Split-K partial sums: the raw fp32 accumulators of one split, stored (32-column units) into that
 // split's slice of the workspace. Each element of a slice is written by exactly one tile.
+// `part` of `parts` (1 or 2) epilogue warps sharing a TMEM lane quadrant takes that share of the
+// tile's column units.
 template <int BN>
 __device__ __forceinline__ void gemm_epilogue_partial(const GemmArgs& args, const CUtensorMap* tmC, Stager& sg,
-                                                      uint32_t t, int y0, int n0) {
+                                                      uint32_t t, int y0, int n0, int part, int parts) {
 #pragma unroll 1
-  for (int c = 0; c < BN / 32; ++c) {
+  for (int c = part * (BN / 32) / parts; c < (part + 1) * (BN / 32) / parts; ++c) {
     float v[32];
     tmem_ld32(t + c * 32, v);
     const int col = n0 + c * 32;
@@ -151,13 +209,14 @@ __device__ __forceinline__ void gemm_epilogue_partial(const GemmArgs& args, cons
 
 template <int BN, int EPI>
 __device__ __forceinline__ void gemm_epilogue_tile(const GemmArgs& args, const CUtensorMap* tmC, Stager& sg,
-                                                   uint32_t t, int row, bool m_ok, int y0, int n0, int n_block) {
+                                                   uint32_t t, int row, bool m_ok, int y0, int n0, int n_block,
+                                                   int part, int parts) {
   if constexpr (EPI == EPI_RESID || EPI == EPI_STORE) {
     const bool f32 = (EPI == EPI_RESID) || args.out_f32;
     if (f32) {
       // fp32 output: 32-column units. Rows past M add (or store) zeros.
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = part * (BN / 32) / parts; c < (part + 1) * (BN / 32) / parts; ++c) {
         float v[32];
         tmem_ld32(t + c * 32, v);
         const int col = n0 + c * 32;
@@ -183,7 +242,7 @@ __device__ __forceinline__ void gemm_epilogue_tile(const GemmArgs& args, const C
     } else {
       // bf16 output: 64-column units.
 #pragma unroll 1
-      for (int c = 0; c < BN / 64; ++c) {
+      for (int c = part * (BN / 64) / parts; c < (part + 1) * (BN / 64) / parts; ++c) {
         float v[64];
         tmem_ld32(t + c * 64, *reinterpret_cast<float(*)[32]>(v));
         tmem_ld32(t + c * 64 + 32, *reinterpret_cast<float(*)[32]>(v + 32));
@@ -217,48 +276,52 @@ __device__ __forceinline__ void gemm_epilogue_tile(const GemmArgs& args, const C
       for (int j = 0; j < 32; ++j) sincosf(p * __ldg(args.inv_freq + j), &sn[j], &cs[j]);
     }
 #pragma unroll 1
-    for (int hh = 0; hh < BN / 64; ++hh) {
-      float x[64];
-      tmem_ld32(t + hh * 64, *reinterpret_cast<float(*)[32]>(x));
-      tmem_ld32(t + hh * 64 + 32, *reinterpret_cast<float(*)[32]>(x + 32));
+    for (int hh = part * (BN / 64) / parts; hh < (part + 1) * (BN / 64) / parts; ++hh) {
       const int col = n0 + hh * 64;
-      if (col >= args.N) continue;
-      if (rope) {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float a = x[j], b = x[j + 32];
-          x[j] = a * cs[j] - b * sn[j];
-          x[j + 32] = a * sn[j] + b * cs[j];
-        }
-      }
+      if (col >= args.N) continue;  // warp-uniform
       uint8_t* buf = sg.acquire();
-      sg.put_bf16x64(buf, x);
+      // the head in two passes of 16 rotate-half pairs (j, j + 32): fewer live registers
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        float lo[16], hi[16];
+        tmem_ld16(t + hh * 64 + q * 16, lo);
+        tmem_ld16(t + hh * 64 + 32 + q * 16, hi);
+        if (rope) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const float a = lo[j], b = hi[j];
+            lo[j] = a * cs[q * 16 + j] - b * sn[q * 16 + j];
+            hi[j] = a * sn[q * 16 + j] + b * cs[q * 16 + j];
+          }
+        }
+        sg.put_bf16x16(buf, 2 * q, lo);
+        sg.put_bf16x16(buf, 4 + 2 * q, hi);
+      }
       sg.issue(tmC, buf, col, y0, false);
     }
   } else {  // EPI_GEGLU, BN == 256: columns [0,128) input, [128,256) gate
     static_assert(EPI != EPI_GEGLU || BN == 256, "GeGLU tiles are 128 input + 128 gate columns");
 #pragma unroll 1
-    for (int u = 0; u < 2; ++u) {
+    for (int u = part * 2 / parts; u < (part + 1) * 2 / parts; ++u) {
       const int ocol = n_block * 128 + u * 64;
-      float a[64];
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        float g[32];
-        tmem_ld32(t + u * 64 + h * 32, *reinterpret_cast<float(*)[32]>(a + h * 32));
-        tmem_ld32(t + 128 + u * 64 + h * 32, g);
-#pragma unroll
-        for (int j = 0; j < 32; ++j) a[h * 32 + j] = gelu_erf(a[h * 32 + j]) * g[j];
-      }
-      if (ocol >= args.out_cols) continue;
+      if (ocol >= args.out_cols) continue;  // warp-uniform
       uint8_t* buf = sg.acquire();
-      sg.put_bf16x64(buf, a);
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {  // 16 input columns and their 16 gate columns at a time
+        float a[16], g[16];
+        tmem_ld16(t + u * 64 + h * 16, a);
+        tmem_ld16(t + 128 + u * 64 + h * 16, g);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) a[j] = gelu_erf(a[j]) * g[j];
+        sg.put_bf16x16(buf, 2 * h, a);
+      }
       sg.issue(tmC, buf, ocol, y0, false);
     }
   }
 }
 
 template <int BN, int EPI>
-__global__ void __launch_bounds__(GEMM_THREADS, 1)
+__global__ void __launch_bounds__(GEMM1_THREADS, 1)
     gemm_bf16_sm100(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmC, const GemmArgs args) {
   constexpr int BM = GEMM_BM, BK = GEMM_BK, STAGES = gemm_stages(BN);
@@ -273,7 +336,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   uint8_t* smem = smem_raw + (((raw_u + 1023u) & ~1023u) - raw_u);
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
-  uint8_t* sStg = sB + STAGES * B_BYTES;  // 4 warps x 2 buffers x 4 KB, 1024-aligned
+  uint8_t* sStg = sB + STAGES * B_BYTES;  // 8 warps x 1 buffer x 4 KB, 1024-aligned
   uint64_t* full = reinterpret_cast<uint64_t*>(sStg + 8 * GEMM_STG_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
@@ -303,7 +366,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 128);
+      mbar_init(&tempty[a], 32 * GEMM_EPI_WARPS);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -362,6 +425,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
+      // The MMA issue loop is kept short: it shares its SM sub-partition with epilogue warps, and
+      // every instruction it waits to issue is a gap in the tensor pipe. Descriptors of stage 0
+      // are built once; a stage's are these plus its byte offset (the start-address field holds
+      // address >> 4, and no stage crosses the field's 256 KB range).
+      const uint64_t adesc0 = sdesc_kmajor_sw128(smem_u32(sA)), bdesc0 = sdesc_kmajor_sw128(smem_u32(sB));
       int s = 0, acc = 0;
       uint32_t ph = 0, aph = 0;
       bool ok = true;
@@ -377,11 +445,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = smem_u32(sA + s * A_BYTES), b0 = smem_u32(sB + s * B_BYTES);
+          // Stepping K by 16 elements adds 32 bytes (2 in the descriptor's >>4 address field).
+          const uint64_t ad = adesc0 + (uint64_t)(s * (A_BYTES >> 4)), bd = bdesc0 + (uint64_t)(s * (B_BYTES >> 4));
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k)
-            umma_bf16(d, sdesc_kmajor_sw128(a0 + k * 32), sdesc_kmajor_sw128(b0 + k * 32), idesc,
-                      (kb != kb0 || k != 0) ? 1u : 0u);
+            umma_bf16(d, ad + 2u * k, bd + 2u * k, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
           umma_commit(&empty[s]);
           if (++s == STAGES) {
             s = 0;
@@ -399,7 +467,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
   } else {
     const int quad = warp & 3;  // TMEM lanes this warp may read: [32*quad, 32*quad + 32)
-    Stager sg{sStg + (warp - 2) * 2 * GEMM_STG_BYTES, 0u, lane};
+    constexpr int PARTS = GEMM_EPI_WARPS / 4, NBUF = 8 / GEMM_EPI_WARPS;
+    const int part = (warp - 2) / 4;  // which share of the tile's columns
+    Stager sg{sStg + (warp - 2) * NBUF * GEMM_STG_BYTES, 0u, lane, NBUF};
     if (lane == 0) prefetch_tmap(&tmC);
     int acc = 0;
     uint32_t aph = 0;
@@ -413,9 +483,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       tc_fence_after();
       const uint32_t t = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
       if (ksp > 1)
-        gemm_epilogue_partial<BN>(args, &tmC, sg, t, (tile % ksp) * args.split_rows + y0, n_block * BN);
+        gemm_epilogue_partial<BN>(args, &tmC, sg, t, (tile % ksp) * args.split_rows + y0, n_block * BN, part, PARTS);
       else
-        gemm_epilogue_tile<BN, EPI>(args, &tmC, sg, t, row, row < args.M, y0, n_block * BN, n_block);
+        gemm_epilogue_tile<BN, EPI>(args, &tmC, sg, t, row, row < args.M, y0, n_block * BN, n_block, part, PARTS);
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
       acc ^= 1;

@@ -205,7 +205,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     }
   } else {
     const int quad = warp & 3;
-    Stager sg{sStg + (warp - 2) * 2 * GEMM_STG_BYTES, 0u, lane};
+    Stager sg{sStg + (warp - 2) * 2 * GEMM_STG_BYTES, 0u, lane, 2};
     if (lane == 0) prefetch_tmap(&tmC);
     int acc = 0;
     uint32_t aph = 0;
@@ -216,7 +216,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
       if (!mbar_wait_warp(&tfull[acc], aph, args.status, DEV_TIMEOUT_EPILOGUE, abort_flag)) break;
       tc_fence_after();
       const uint32_t t = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
-      gemm_epilogue_tile<BN, EPI>(args, &tmC, sg, t, row, row < args.M, y0, n_block * BN, n_block);
+      gemm_epilogue_tile<BN, EPI>(args, &tmC, sg, t, row, row < args.M, y0, n_block * BN, n_block, 0, 1);
       tc_fence_before();
       mbar_arrive_cluster(map_to_rank(smem_u32(&tempty[acc]), 0));
       acc ^= 1;

@@ -327,7 +327,7 @@ void launch_gemm(const CUtensorMap& ta, const WeightMap& tb, const CUtensorMap& 
     const int tiles = (rows / GEMM_BM) * ((a.N + GEMM_BN - 1) / GEMM_BN) * ksp;
     const int grid = std::min(tiles, num_sms);
     const CUtensorMap tw = make_out_tmap(sk->ws, true, (uint64_t)ksp * rows, a.N, a.N);
-    launch_k(gemm_bf16_sm100<GEMM_BN, EPI>, dim3(grid), dim3(GEMM_THREADS), gemm_smem_bytes(GEMM_BN), st, ta, tb.full, tw, a);
+    launch_k(gemm_bf16_sm100<GEMM_BN, EPI>, dim3(grid), dim3(GEMM1_THREADS), gemm_smem_bytes(GEMM_BN), st, ta, tb.full, tw, a);
     CK(cudaGetLastError());
     SplitKFinal f{sk->ws, ksp, rows, a.M, a.N, sk->out, sk->ldo, a.bias, a.act, a.out_f32, a.pos, a.inv_freq,
                   a.rope_cols, a.out_cols};
@@ -347,12 +347,12 @@ void launch_gemm(const CUtensorMap& ta, const WeightMap& tb, const CUtensorMap& 
     if constexpr (EPI != EPI_GEGLU) {
       const int tiles = ((a.M + GEMM_BM - 1) / GEMM_BM) * ((a.N + 127) / 128);
       const int grid = std::min(tiles, num_sms);
-      launch_k(gemm_bf16_sm100<128, EPI>, dim3(grid), dim3(GEMM_THREADS), gemm_smem_bytes(128), st, ta, tb.half, tc, a);
+      launch_k(gemm_bf16_sm100<128, EPI>, dim3(grid), dim3(GEMM1_THREADS), gemm_smem_bytes(128), st, ta, tb.half, tc, a);
     }
   } else {
     const int tiles = ((a.M + GEMM_BM - 1) / GEMM_BM) * ((a.N + GEMM_BN - 1) / GEMM_BN);
     const int grid = std::min(tiles, num_sms);
-    launch_k(gemm_bf16_sm100<GEMM_BN, EPI>, dim3(grid), dim3(GEMM_THREADS), gemm_smem_bytes(GEMM_BN), st, ta, tb.full, tc, a);
+    launch_k(gemm_bf16_sm100<GEMM_BN, EPI>, dim3(grid), dim3(GEMM1_THREADS), gemm_smem_bytes(GEMM_BN), st, ta, tb.full, tc, a);
   }
   CK(cudaGetLastError());
 }
