@@ -125,20 +125,58 @@ __global__ void embed_ln_kernel(const uint32_t* __restrict__ ids, int T, const _
   store_row_bf16<D>(x + (size_t)row * D, r, lane);
 }
 
-template <int D>
-__global__ void layernorm_kernel(const float* __restrict__ in, const int* __restrict__ gather, int rows,
-                                 const float* __restrict__ w, const float* __restrict__ b, float eps,
-                                 __nv_bfloat16* __restrict__ out) {
+// In-place LayerNorm of a register row with the weight (and bias) already in registers.
+template <int D, bool HAS_B>
+S1C_DEV void layernorm_row_w(RowVec<D>& r, const RowVec<D>& w, const RowVec<D>& b, float eps) {
+  constexpr int N = RowVec<D>::CHUNKS * 8;
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < N; ++i) s += r.v[i];
+  const float mean = warp_sum(s) * (1.0f / D);
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    const float d = r.v[i] - mean;
+    q += d * d;
+  }
+  const float rstd = rsqrtf(warp_sum(q) * (1.0f / D) + eps);
+#pragma unroll
+  for (int i = 0; i < N; ++i) r.v[i] = (r.v[i] - mean) * rstd * w.v[i] + (HAS_B ? b.v[i] : 0.f);
+}
+
+// Grid-stride over rows, one warp per row at a time, two rows in flight per warp: the grid is
+// sized to the SMs (every SM gets the same share of rows, no partial last wave), and the
+// LayerNorm weight / bias are read once per warp into registers -- before the dependency wait,
+// since no kernel of the forward writes them.
+template <int D, bool HAS_B>
+__global__ void __launch_bounds__(256) layernorm_kernel(const float* __restrict__ in, const int* __restrict__ gather,
+                                                        int rows, const float* __restrict__ w,
+                                                        const float* __restrict__ b, float eps,
+                                                        __nv_bfloat16* __restrict__ out) {
   pdl_trigger();
-  pdl_wait();
-  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
-  if (row >= rows) return;
-  const int src = gather ? gather[row] : row;
-  RowVec<D> r;
-  load_row_f32<D>(in + (size_t)src * D, r, lane);
-  layernorm_row<D>(r, w, b, eps, lane);
-  store_row_bf16<D>(out + (size_t)row * D, r, lane);
+  RowVec<D> wv, bv;
+  load_row_f32<D>(w, wv, lane);
+  if constexpr (HAS_B) load_row_f32<D>(b, bv, lane);
+  pdl_wait();
+  const int nw = gridDim.x * (blockDim.x >> 5);
+  int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  for (; row + nw < rows; row += 2 * nw) {
+    const int r1 = row + nw;
+    RowVec<D> x0, x1;
+    load_row_f32<D>(in + (size_t)(gather ? gather[row] : row) * D, x0, lane);
+    load_row_f32<D>(in + (size_t)(gather ? gather[r1] : r1) * D, x1, lane);
+    layernorm_row_w<D, HAS_B>(x0, wv, bv, eps);
+    store_row_bf16<D>(out + (size_t)row * D, x0, lane);
+    layernorm_row_w<D, HAS_B>(x1, wv, bv, eps);
+    store_row_bf16<D>(out + (size_t)r1 * D, x1, lane);
+  }
+  if (row < rows) {
+    RowVec<D> x0;
+    load_row_f32<D>(in + (size_t)(gather ? gather[row] : row) * D, x0, lane);
+    layernorm_row_w<D, HAS_B>(x0, wv, bv, eps);
+    store_row_bf16<D>(out + (size_t)row * D, x0, lane);
+  }
 }
 
 template <int D>

@@ -359,9 +359,19 @@ void launch_gemm(const CUtensorMap& ta, const WeightMap& tb, const CUtensorMap& 
 
 template <int D>
 void launch_ln(const float* in, const int* gather, int rows, const float* w, const float* b, float eps, bf16* out,
-               cudaStream_t st) {
+               cudaStream_t st, int num_sms) {
   if (rows <= 0) return;
-  launch_k(layernorm_kernel<D>, dim3((rows + 7) / 8), dim3(256), 0, st, in, gather, rows, w, b, eps, out);
+  // 8 warps per block, one wave of resident blocks at most (register-limited), rows spread evenly
+  // over the grid.
+  auto resident = [](auto kernel) {
+    int n = 0;
+    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, 256, 0));
+    return std::max(n, 1);
+  };
+  static const int per_sm_b = resident(layernorm_kernel<D, true>), per_sm_nb = resident(layernorm_kernel<D, false>);
+  const int blocks = std::max(1, std::min((rows + 7) / 8, (b ? per_sm_b : per_sm_nb) * num_sms));
+  if (b) launch_k(layernorm_kernel<D, true>, dim3(blocks), dim3(256), 0, st, in, gather, rows, w, b, eps, out);
+  else launch_k(layernorm_kernel<D, false>, dim3(blocks), dim3(256), 0, st, in, gather, rows, w, b, eps, out);
   CK(cudaGetLastError());
 }
 
@@ -1004,7 +1014,7 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
   };
   auto ln = [&](const char* name, const float* in, const int* gather, int rows, const float* w, const float* b,
                 float eps, bf16* out) {
-    launch(B, nl, name, 0, (double)rows * d * 6.0, [&] { launch_ln<D>(in, gather, rows, w, b, eps, out, st); });
+    launch(B, nl, name, 0, (double)rows * d * 6.0, [&] { launch_ln<D>(in, gather, rows, w, b, eps, out, st, nsm); });
   };
   const double fl = 2.0 * T;  // GEMM FLOPs per (output column x reduction element)
   // Split-K contexts: the output buffer and pitch the finalize step writes (for residual GEMMs the
