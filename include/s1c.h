@@ -290,6 +290,42 @@ S1C_API void s1c_server_stop(s1c_server* s);
 /* Stop (if needed) and free. No other call on `s` may be running or follow. */
 S1C_API void s1c_server_destroy(s1c_server* s);
 
+/* ---- Decode: answers from the forward's outputs (laya-core/src/decode.rs) -------------------
+ * The arithmetic of `decode_answers` (decode.rs:318-413) on the host: temperature-scaled softmax
+ * over each row's options, entropy confidence, the per-type answer values and the action head's
+ * probability (`ActHead::probs`, decode.rs:232-253, on the features of `act_features`,
+ * decode.rs:257-267). The result object's JSON (labels, legends, 4-decimal rounding) is the
+ * caller's. */
+typedef struct s1c_act_head {
+  int32_t d_in;   /* hidden + 4 */
+  int32_t hidden; /* width of the first layer */
+  int32_t n_act;  /* action classes (len(act_costs) + 1) */
+  const float* w0; /* [hidden, d_in] */
+  const float* b0; /* [hidden] */
+  const float* w2; /* [n_act, hidden] */
+  const float* b2; /* [n_act] */
+} s1c_act_head;
+
+typedef struct s1c_answer {
+  int32_t qtype;            /* 0 choice, 1 score, 2 noul */
+  int32_t k;                /* options of the row (marker_count) */
+  int32_t argmax;           /* most probable option (first maximum) */
+  double score;             /* score: expected level sum_i i p_i */
+  double noul;              /* noul: p of option 1 */
+  double confidence;        /* choice / score: 1 - H(p) / ln k; noul: max(p1, 1 - p1) */
+  double answer_confidence; /* choice: p[argmax]; score: max p; noul: max(p1, 1 - p1) */
+  float act_probability;    /* action head, class 0 */
+} s1c_answer;
+
+/* Decode n rows: logits [n*kmax] (masked slots -1e4) and pooled [n*hidden] as the forward returns
+ * them, marker_count [n], qtype [n], temperature [n] (the row's calibration scale, already
+ * clamped: Temperatures::scale, decode.rs:80-86). probs (nullable) receives [n*kmax] option
+ * probabilities (0 past marker_count). Errors: S1C_ERR_WEIGHTS for an action head whose input is
+ * not hidden + 4 wide (decode.rs:155-207 wording), S1C_ERR_ARG otherwise. */
+S1C_API s1c_status s1c_decode(const float* logits, const float* pooled, int32_t n, int32_t kmax, int32_t hidden,
+                              const int32_t* marker_count, const uint32_t* qtype, const double* temperature,
+                              const s1c_act_head* head, double* probs, s1c_answer* out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -86,6 +86,17 @@ class ServerStats(C.Structure):
                 ("workers_alive", C.c_int32)]
 
 
+class CActHead(C.Structure):
+    _fields_ = [("d_in", C.c_int32), ("hidden", C.c_int32), ("n_act", C.c_int32), ("w0", C.c_void_p),
+                ("b0", C.c_void_p), ("w2", C.c_void_p), ("b2", C.c_void_p)]
+
+
+class CAnswer(C.Structure):
+    _fields_ = [("qtype", C.c_int32), ("k", C.c_int32), ("argmax", C.c_int32), ("score", C.c_double),
+                ("noul", C.c_double), ("confidence", C.c_double), ("answer_confidence", C.c_double),
+                ("act_probability", C.c_float)]
+
+
 # s1c_server_forward_fn
 SERVER_FORWARD_FN = C.CFUNCTYPE(C.c_int32, C.c_void_p, C.POINTER(CVarlen), C.POINTER(C.c_float),
                                 C.POINTER(C.c_float), C.POINTER(C.c_char_p))
@@ -141,6 +152,7 @@ def lib() -> C.CDLL:
         "s1c_server_get_stats": (I32, [P, C.POINTER(ServerStats)]),
         "s1c_server_stop": (None, [P]),
         "s1c_server_destroy": (None, [P]),
+        "s1c_decode": (I32, [P, P, I32, I32, I32, P, P, P, C.POINTER(CActHead), P, C.POINTER(CAnswer)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

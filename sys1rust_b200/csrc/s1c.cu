@@ -33,6 +33,7 @@
 #include "rowwise.cuh"
 #include "safetensors.h"
 #include "server.h"
+#include "decode.h"
 
 using namespace s1c;
 typedef __nv_bfloat16 bf16;
@@ -2098,3 +2099,75 @@ void s1c_server_destroy(s1c_server* s) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------------
+// Decode
+
+extern "C" s1c_status s1c_decode(const float* logits, const float* pooled, int32_t n, int32_t kmax, int32_t hidden,
+                                 const int32_t* marker_count, const uint32_t* qtype, const double* temperature,
+                                 const s1c_act_head* head, double* probs, s1c_answer* out) {
+  g_create_error.clear();
+  if (n < 0 || kmax < 0 || hidden <= 0 || !head || !out || (n > 0 && (!logits || !pooled || !marker_count ||
+                                                                      !qtype || !temperature))) {
+    g_create_error = "bad decode arguments";
+    return S1C_ERR_ARG;
+  }
+  const s1c_act_head& h = *head;
+  if (h.d_in <= 4) {
+    g_create_error = "act_head.0.weight has input width " + std::to_string(h.d_in) +
+                     ", but the action head reads the pooled hidden state plus 4 scalar features, so it needs at least 5";
+    return S1C_ERR_WEIGHTS;
+  }
+  if (h.d_in - 4 != hidden) {
+    g_create_error = "act_head.0.weight has input width " + std::to_string(h.d_in) +
+                     ", which is not the encoder hidden size " + std::to_string(hidden) + " plus 4 scalar features";
+    return S1C_ERR_WEIGHTS;
+  }
+  if (h.hidden <= 0 || h.n_act <= 0 || !h.w0 || !h.b0 || !h.w2 || !h.b2) {
+    g_create_error = "act_head has an empty layer";
+    return S1C_ERR_WEIGHTS;
+  }
+  for (int32_t r = 0; r < n; ++r) {
+    const int k = marker_count[r];
+    if (k < 0 || k > kmax || qtype[r] > 2 || !(temperature[r] > 0.0) || !std::isfinite(temperature[r])) {
+      g_create_error = "row " + std::to_string(r) + ": marker_count, qtype or temperature out of range";
+      return S1C_ERR_ARG;
+    }
+    const float* row = logits + (size_t)r * kmax;
+    std::vector<double> z((size_t)k);
+    for (int i = 0; i < k; ++i) z[(size_t)i] = (double)row[i] / temperature[r];
+    const std::vector<double> p = s1c::dec::softmax_f64(z);
+    s1c_answer a{};
+    a.qtype = (int32_t)qtype[r];
+    a.k = k;
+    int am = 0;
+    for (int i = 1; i < k; ++i)
+      if (p[(size_t)i] > p[(size_t)am]) am = i;
+    a.argmax = am;
+    const double conf = s1c::dec::confidence_from_probs(p, k);
+    if (qtype[r] == 0) {
+      a.confidence = conf;
+      a.answer_confidence = k > 0 ? p[(size_t)am] : 0.0;
+    } else if (qtype[r] == 1) {
+      double es = 0.0, top = 0.0;
+      for (int i = 0; i < k; ++i) {
+        es += (double)i * p[(size_t)i];
+        top = std::max(top, p[(size_t)i]);
+      }
+      a.score = es;
+      a.confidence = conf;
+      a.answer_confidence = top;
+    } else {
+      const double p1 = k > 1 ? p[1] : 0.0;
+      a.noul = p1;
+      a.confidence = a.answer_confidence = std::max(p1, 1.0 - p1);
+    }
+    float feats[4];
+    s1c::dec::act_features(row, kmax, k, feats);
+    a.act_probability = s1c::dec::act_probs(h, pooled + (size_t)r * hidden, feats)[0];
+    out[r] = a;
+    if (probs)
+      for (int i = 0; i < kmax; ++i) probs[(size_t)r * kmax + i] = i < k ? p[(size_t)i] : 0.0;
+  }
+  return S1C_OK;
+}
