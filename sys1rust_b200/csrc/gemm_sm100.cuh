@@ -46,6 +46,9 @@ struct GemmArgs {
   int out_f32;            // EPI_STORE: fp32 output (the output map is fp32, 32-column boxes)
   const int* pos;         // EPI_ROPE: position of each row inside its sequence
   const float* inv_freq;  // EPI_ROPE: [32] inverse frequencies of the layer's theta
+  const float* rope_tab;  // EPI_ROPE, optional: [positions][64] cos | sin of p * inv_freq[j]
+                          // (rope_table_kernel); when set the epilogue reads a row's 32 cos / sin
+                          // pairs instead of evaluating them: 16 loads instead of 32 sincosf
   int rope_cols;          // EPI_ROPE: columns [0, rope_cols) hold q and k heads
   int out_cols;           // EPI_GEGLU: output width I
   int k_splits;           // > 1: split-K; split s stores its fp32 partial sums into rows
@@ -271,9 +274,20 @@ __device__ __forceinline__ void gemm_epilogue_tile(const GemmArgs& args, const C
     const bool rope = n0 < args.rope_cols;  // uniform: q/k tiles never straddle the v columns
     float cs[32], sn[32];
     if (rope) {
-      const float p = m_ok ? (float)__ldg(args.pos + row) : 0.0f;
+      const int pi = m_ok ? __ldg(args.pos + row) : 0;
+      if (args.rope_tab) {
+        const float4* tb = reinterpret_cast<const float4*>(args.rope_tab + (size_t)pi * 64);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) sincosf(p * __ldg(args.inv_freq + j), &sn[j], &cs[j]);
+        for (int i = 0; i < 8; ++i) {
+          const float4 c4 = __ldg(tb + i), s4 = __ldg(tb + 8 + i);
+          cs[4 * i] = c4.x; cs[4 * i + 1] = c4.y; cs[4 * i + 2] = c4.z; cs[4 * i + 3] = c4.w;
+          sn[4 * i] = s4.x; sn[4 * i + 1] = s4.y; sn[4 * i + 2] = s4.z; sn[4 * i + 3] = s4.w;
+        }
+      } else {
+        const float p = (float)pi;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) sincosf(p * __ldg(args.inv_freq + j), &sn[j], &cs[j]);
+      }
     }
 #pragma unroll 1
     for (int hh = part * (BN / 64) / parts; hh < (part + 1) * (BN / 64) / parts; ++hh) {
@@ -500,6 +514,18 @@ __global__ void __launch_bounds__(GEMM1_THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);
   }
+}
+
+// cos | sin of the RoPE angles p * inv_freq[j] for positions [0, P): row p holds cos for
+// j = 0..31 then sin for j = 0..31, each from the fp32 angle exactly as the epilogue forms it.
+__global__ void rope_table_kernel(float* __restrict__ tab, int P, const float* __restrict__ inv_freq) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= P * 32) return;
+  const int p = i >> 5, j = i & 31;
+  float sn, cs;
+  sincosf((float)p * inv_freq[j], &sn, &cs);
+  tab[(size_t)p * 64 + j] = cs;
+  tab[(size_t)p * 64 + 32 + j] = sn;
 }
 
 }  // namespace s1c

@@ -469,6 +469,7 @@ struct s1c_backend {
   bf16* sc_w1 = nullptr;
   WeightMap tm_sc1;
   float* inv_freq[2] = {nullptr, nullptr};  // 0 global theta, 1 local theta
+  float* rope_tab[2] = {nullptr, nullptr};  // [max_pos][64] cos | sin per theta
 
   // activations (capacity in rows, multiples of 128)
   int gemm_variant = 0;   // `gemm=auto|1cta|2cta|splitk|csk`
@@ -614,6 +615,19 @@ float* make_inv_freq_raw(float theta) {
 float* make_inv_freq(s1c_backend& B, float theta) {
   float* d = make_inv_freq_raw(theta);
   B.allocs.push_back(d);
+  return d;
+}
+// The cos | sin table of rope_table_kernel for positions [0, P) (a fresh device allocation).
+float* make_rope_table_raw(const float* d_inv_freq, int P) {
+  float* d = nullptr;
+  CK(cudaMalloc(&d, (size_t)P * 64 * sizeof(float)));
+  rope_table_kernel<<<(P * 32 + 255) / 256, 256>>>(d, P, d_inv_freq);
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    cudaFree(d);
+    throw S1cError(S1C_ERR_CUDA, std::string("RoPE table: ") + cudaGetErrorString(e));
+  }
   return d;
 }
 
@@ -775,6 +789,10 @@ void build(s1c_backend& B, const s1c_model_desc& D, const s1c_tensor* tensors, i
 
   B.inv_freq[0] = make_inv_freq(B, D.global_rope_theta);
   B.inv_freq[1] = make_inv_freq(B, D.local_rope_theta);
+  for (int t = 0; t < 2; ++t) {
+    B.rope_tab[t] = make_rope_table_raw(B.inv_freq[t], std::max(B.max_pos, 1));
+    B.allocs.push_back(B.rope_tab[t]);
+  }
   CK(cudaMalloc(&B.d_status, sizeof(int)));
   CK(cudaMemset(B.d_status, 0, sizeof(int)));
   B.splitk_ws.ensure((size_t)32 << 20);
@@ -1029,6 +1047,7 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
     GemmArgs g = gemm_args(T, 3 * d, d);
     g.pos = pos;
     g.inv_freq = B.inv_freq[l.local ? 1 : 0];
+    g.rope_tab = B.rope_tab[l.local ? 1 : 0];
     g.rope_cols = 2 * d;
     launch(B, nl, "gemm_qkv_rope", fl * 3 * d * d, 0, [&] { launch_gemm<EPI_ROPE>(B.tm_x, l.tm_wqkv, B.to_qkv3, g, nsm, st, B.gemm_variant, &(sk_tmp = sk(qkv, 3 * d)), &nl); });
     attn(l.local ? "attn_local" : "attn_global", B.tm_qkv_att, B.tm_qkv_kv, 0, d, 2 * d, qkv, qkv + d,
@@ -1592,6 +1611,9 @@ s1c_status s1c_gemm(int32_t epi, const void* d_A, const void* d_B, void* d_out, 
         auto key = std::make_pair(dev, rope_theta);
         if (!tables.count(key)) tables[key] = make_inv_freq_raw(rope_theta);
         a.inv_freq = tables[key];
+        static std::map<std::pair<int, float>, float*> rtabs;  // cos | sin tables, positions < 8192
+        if (!rtabs.count(key)) rtabs[key] = make_rope_table_raw(tables[key], 8192);
+        a.rope_tab = rtabs[key];
         if (!d_pos) throw S1cError(S1C_ERR_ARG, "RoPE needs positions");
       }
     }
