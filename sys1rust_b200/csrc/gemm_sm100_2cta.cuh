@@ -167,6 +167,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
   } else if (warp == 1) {
     if (lane == 0 && leader) {
       constexpr uint32_t idesc = idesc_bf16_f32(256, BN);
+      // Stage 0's descriptors built once; a stage's are these plus its byte offset >> 4 (see the
+      // one-CTA kernel); the empty / tfull barriers' cluster addresses are mapped once too.
+      const uint64_t adesc0 = sdesc_kmajor_sw128(smem_u32(sA)), bdesc0 = sdesc_kmajor_sw128(smem_u32(sB));
+      const uint32_t e0r0 = map_to_rank(smem_u32(&empty[0]), 0), e0r1 = map_to_rank(smem_u32(&empty[0]), 1);
       int s = 0, acc = 0;
       uint32_t ph = 0, aph = 0;
       bool ok = true;
@@ -180,14 +184,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = smem_u32(sA + s * A_BYTES), b0 = smem_u32(sB + s * B_BYTES);
+          const uint64_t ad = adesc0 + (uint64_t)(s * (A_BYTES >> 4)), bd = bdesc0 + (uint64_t)(s * (B_BYTES >> 4));
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k)
-            umma2_bf16(d, sdesc_kmajor_sw128(a0 + k * 32), sdesc_kmajor_sw128(b0 + k * 32), idesc,
-                       (kb | k) != 0 ? 1u : 0u);
-          const uint32_t e = smem_u32(&empty[s]);
-          umma2_commit(map_to_rank(e, 0));
-          umma2_commit(map_to_rank(e, 1));
+          for (int k = 0; k < BK / 16; ++k) umma2_bf16(d, ad + 2u * k, bd + 2u * k, idesc, (kb | k) != 0 ? 1u : 0u);
+          umma2_commit(e0r0 + 8u * (uint32_t)s);
+          umma2_commit(e0r1 + 8u * (uint32_t)s);
           if (++s == STAGES) {
             s = 0;
             ph ^= 1u;

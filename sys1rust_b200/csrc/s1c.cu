@@ -338,8 +338,12 @@ void launch_gemm(const CUtensorMap& ta, const WeightMap& tb, const CUtensorMap& 
     if (extra_launches) ++*extra_launches;
     return;
   }
-  // By shape the one-CTA kernel runs: on the encoder shapes the two-CTA kernel measured the same.
-  const bool two = variant == 2;
+  // By shape: the two-CTA kernel for the RoPE, residual and plain stores once its 256 x 256 tiles
+  // fill the SMs (measured at 16k tokens: Wqkv 1253 vs 1212, Wo2 1187 vs 1126, Wo 952 vs 905
+  // TFLOP/s), the one-CTA kernel for GeGLU (1245 vs 1219) and for fewer tiles.
+  const bool two = variant == 2 ||
+                   (variant == 0 && EPI != EPI_GEGLU &&
+                    ((a.M + 255) / 256) * ((a.N + GEMM_BN - 1) / GEMM_BN) * 2 >= num_sms);
   if (two) {
     const int tiles = ((a.M + 255) / 256) * ((a.N + GEMM_BN - 1) / GEMM_BN);
     const int clusters = std::min(tiles, num_sms / 2);

@@ -22,8 +22,11 @@ import json
 import numpy as np
 import torch
 
-from .backend import attention, gemm, interleave_wi
-from .gemm_sweep import SHAPES
+from .backend import EPI_RESID, attention, gemm, interleave_wi
+from .gemm_sweep import SHAPES as SWEEP_SHAPES
+
+# The sweep's three shapes plus the attention output projection Wo (K 1024, N 1024, residual add).
+SHAPES = SWEEP_SHAPES + [("wo_resid", 1024, 1024, EPI_RESID)]
 
 
 def _time(fn, reps: int) -> float:
