@@ -187,12 +187,19 @@ def main():
     cfg = large_model()
     t0 = time.time()
     w = SyntheticWeights(cfg, seed=0)
+    # Two handles of the same model on this GPU, each on its own stream: consecutive batches go to
+    # alternate handles, so one batch's kernels fill the SMs another batch's kernels leave idle
+    # (the partial last wave of a GEMM, latency-bound attention). Measured +3.7 % over one stream;
+    # a third stream added nothing.
     be = CudaBackend.from_synthetic(cfg, w.tensors, device=local, max_tokens=BATCH_TOKENS)
-    log(f"[rank {rank}] model ready in {time.time() - t0:.1f}s: {be.name()}")
-    # A dedicated (non-default) stream: the backend captures per-shape CUDA graphs on it.
+    be2 = CudaBackend.from_synthetic(cfg, w.tensors, device=local, max_tokens=BATCH_TOKENS)
+    log(f"[rank {rank}] model ready in {time.time() - t0:.1f}s: {be.name()} x 2 streams")
+    # Dedicated (non-default) streams: each backend captures per-shape CUDA graphs on its own.
     stream = torch.cuda.Stream()
+    stream2 = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
     be.set_stream(stream.cuda_stream)
+    be2.set_stream(stream2.cuda_stream)
 
     all_reqs, mine = workload(world, rank)
     batches = pack_batches(mine, BATCH_TOKENS)
@@ -201,14 +208,20 @@ def main():
     d_ids = [torch.from_numpy(b.ids.astype(np.int32)).cuda() for b in batches]
     max_n = max(b.n for b in batches)
     max_m = max(b.n * b.kmax for b in batches)
-    d_logits = torch.empty(max(max_m, 1), dtype=torch.float32, device="cuda")
-    d_pooled = torch.empty(max_n * cfg.encoder.hidden_size, dtype=torch.float32, device="cuda")
+    outs = [(torch.empty(max(max_m, 1), dtype=torch.float32, device="cuda"),
+             torch.empty(max_n * cfg.encoder.hidden_size, dtype=torch.float32, device="cuda")) for _ in range(2)]
+    handles = (be, be2)
+    launch_count = [0]
 
-    def step():
-        # every batch of the step enqueued back to back; one wait at the end of the step
-        for b, ids in zip(batches, d_ids):
-            be.forward_device_async(b, ids.data_ptr(), d_logits.data_ptr(), d_pooled.data_ptr())
+    def step(count=False):
+        # every batch of the step enqueued back to back, alternating handles; one wait at the end
+        for i, (b, ids) in enumerate(zip(batches, d_ids)):
+            h = handles[i & 1]
+            h.forward_device_async(b, ids.data_ptr(), outs[i & 1][0].data_ptr(), outs[i & 1][1].data_ptr())
+            if count:
+                launch_count[0] += h.last_launch_count()
         be.synchronize()
+        be2.synchronize()
 
     def barrier():
         torch.cuda.synchronize()
@@ -223,14 +236,14 @@ def main():
     # ---- timed region: device-resident inputs --------------------------------------------
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    launches = 0
     with ClockSampler(local) as clk:
         e0.record(stream)
+        stream2.wait_event(e0)
         for _ in range(args.steps):
-            step()
-            launches += be.last_launch_count() * len(batches)
-        e1.record(stream)
+            step(count=True)
+        e1.record(stream)  # both handles were synchronised at the end of the last step
         barrier()
+    launches = launch_count[0]
     ms = e0.elapsed_time(e1)
     ms_max = max_over_ranks(ms)
     tokens_total = sum(len(r.ids) for r in all_reqs)
@@ -241,50 +254,55 @@ def main():
     barrier()
     p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     p0.record(stream)
-    for _ in range(args.steps):
-        step()
+    for _ in range(args.steps):  # one handle, one stream: per-launch events see each kernel alone
+        for b, ids in zip(batches, d_ids):
+            be.forward_device_async(b, ids.data_ptr(), outs[0][0].data_ptr(), outs[0][1].data_ptr())
+        be.synchronize()
     p1.record(stream)
     barrier()
     prof_ms = p0.elapsed_time(p1)
     prof = be.profile_report()
     be.profile(False)
     kernel_ms = sum(v["ms"] for v in prof.values()) / args.steps
-    # ---- e2e: host buffers through the C ABI, copies inside the timed region --------------
-    be.set_stream(0)  # the backend's own stream
-    for b in batches[:2]:
-        be.forward_varlen(b)
-    barrier()
-    h2d = sum(b.ids.nbytes + b.cu_seqlens.nbytes + b.marker_pos.nbytes + b.marker_count.nbytes + b.qtype.nbytes
-              for b in batches)
-    d2h = sum(4 * (b.n * b.kmax + b.n * cfg.encoder.hidden_size) for b in batches)
-    e2e_steps = max(1, min(args.steps, 3))
-    t_e2e = time.perf_counter()
-    for _ in range(e2e_steps):
-        for b in batches:
-            be.forward_varlen(b)
-    e2e_s = time.perf_counter() - t_e2e
-    e2e_s = max_over_ranks(e2e_s)
-    e2e_value = tokens_total * e2e_steps / e2e_s
-
-    # ---- serving: this rank's requests submitted one by one to the serving queue ------------
-    # (sys1rust_b200.server: cross-request packing into <= BATCH_TOKENS varlen batches on a native
-    # worker thread; host buffers in and out, so copies are inside the timed region)
+    # ---- e2e: the serving API with host buffers, copies inside the timed region -------------
+    # This rank's requests are submitted one by one to the serving queue (sys1rust_b200.server:
+    # one native worker per handle, cross-request packing into <= BATCH_TOKENS varlen batches,
+    # each batch's ids / metadata copied in and its logits / pooled rows copied back) and every
+    # result is collected per request.
     from sys1rust_b200.server import Server
-    with Server([be], max_concurrent=len(mine) + 1, max_batch_tokens=BATCH_TOKENS, linger_us=1000) as srv:
+    be.set_stream(0)  # the backends' own streams
+    be2.set_stream(0)
+    with Server([be, be2], max_concurrent=len(mine) + 1, max_batch_tokens=BATCH_TOKENS, linger_us=1000) as srv:
         def serve_all():
             tk = [srv.submit(it) for it in mine]
             for it, t in zip(mine, tk):
                 srv.wait(t, len(it.markers))
         serve_all()  # warm-up pass
         barrier()
-        t_srv = time.perf_counter()
-        serve_all()
-        srv_s = max_over_ranks(time.perf_counter() - t_srv)
+        e2e_steps = max(1, min(args.steps, 3))
+        t_e2e = time.perf_counter()
+        for _ in range(e2e_steps):
+            serve_all()
+        e2e_s = max_over_ranks(time.perf_counter() - t_e2e)
         srv_stats = srv.stats()
-    server = {"value": tokens_total / srv_s, "unit": "tokens/s", "requests_per_gpu": len(mine),
-              "batches_per_gpu": int(srv_stats["batches"]) // 2,
-              "path": "sys1rust_b200.server.Server over s1c_server_*: requests submitted one by one, packed "
-                      "across requests by the native worker, results collected per request"}
+    e2e_value = tokens_total * e2e_steps / e2e_s
+    # bytes per step: each request's ids, marker positions, qtype, row offset and marker count in,
+    # plus one closing offset per batch; its marker logits and pooled row out (the kmax padding of
+    # a batch's logits rows is not counted)
+    batches_per_step = int(srv_stats["batches"]) // (e2e_steps + 1)
+    h2d = sum(4 * (len(it.ids) + len(it.markers) + 3) for it in mine) + 4 * batches_per_step
+    d2h = sum(4 * (len(it.markers) + cfg.encoder.hidden_size) for it in mine)
+
+    # ---- the same host-buffer path on pre-packed batches, one handle (s1c_forward_varlen) ----
+    for b in batches[:2]:
+        be.forward_varlen(b)
+    barrier()
+    t_b = time.perf_counter()
+    for b in batches:
+        be.forward_varlen(b)
+    batched_s = max_over_ranks(time.perf_counter() - t_b)
+    e2e_batched = {"value": tokens_total / batched_s, "unit": "tokens/s",
+                   "path": "s1c_forward_varlen on the step's pre-packed batches, one handle"}
 
     # ---- latency of one 128-token request (cfg1), host API ---------------------------------
     lat = None
@@ -372,16 +390,19 @@ def main():
                                 "2 decision-head layers + scorer, seeded N(0,0.02) bf16 weights",
                        "tokens_per_step": tokens_total, "batches_per_gpu_step": len(batches),
                        "l2": "inputs larger than L2: 686 MB of encoder weights stream every forward",
-                       "parallelism": f"dp{world} replicas, no data-path collective"},
+                       "parallelism": f"dp{world} replicas, no data-path collective",
+                       "streams_per_gpu": 2},
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h), "steps": e2e_steps,
-                    "path": "s1c_forward_varlen (pageable host arrays -> pinned staging -> device; logits and "
-                            "pooled back to host)"},
+                    "path": "sys1rust_b200.server.Server (s1c_server_*): the step's requests submitted one by one "
+                            "from host arrays, packed across requests by one native worker per handle (2 per "
+                            "GPU), host -> device copies and logits / pooled rows back to host inside the timed "
+                            "region, every result collected per request"},
+            "e2e_batched": e2e_batched,
             "roofline": roof,
             "encoder_gemm_tflops": enc_tflops,
             "cpu_baseline": cpu,
             "latency_cfg1": lat,
-            "server": server,
             "cfg3_tokens_per_s": cfg3_tps,
             "clocks": clk.summary(),
             "gpu_launches": int(launches),
@@ -391,6 +412,7 @@ def main():
         }
         print(json.dumps(line), flush=True)
     be.close()
+    be2.close()
     dist.shutdown(world)
 
 
