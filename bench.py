@@ -56,25 +56,34 @@ def workload(world: int, rank: int):
     return reqs, shard_for_rank(reqs, world, rank)
 
 
-def cpu_oracle_sample(cfg, weights, items, budget_s: float):
-    """tokens/s of the CPU oracle (fp32, all host threads) over requests of the workload, one row per
-    forward, until ``budget_s`` seconds have passed (at least one request)."""
+def cpu_oracle_sample(cfg, weights, items, budget_s: float, kind: str = "torch"):
+    """tokens/s of a CPU restatement (fp32, all host threads) over requests of the workload, one row
+    per forward, until ``budget_s`` seconds have passed (at least one request). ``kind`` "torch" is
+    the PyTorch oracle (oracle/forward_ref.py), "c" the C / OpenMP one (oracle/forward_ref.c)."""
     import torch
-    from oracle.forward_ref import OracleModel
     from sys1rust_b200.batch import collate_to
     torch.set_num_threads(os.cpu_count() or 1)
-    om = OracleModel(cfg, weights.tensors)
-    om.forward(collate_to([items[0]], cfg.encoder.pad_token_id))  # warm
+    if kind == "c":
+        from oracle.forward_c import CForwardModel
+        cm = CForwardModel(cfg, weights.tensors)
+        run = lambda it: cm.forward_row(np.asarray(it.ids), it.markers, it.qtype)
+        cores = int(os.environ.get("OMP_NUM_THREADS", len(os.sched_getaffinity(0))))
+    else:
+        from oracle.forward_ref import OracleModel
+        om = OracleModel(cfg, weights.tensors)
+        run = lambda it: om.forward(collate_to([it], cfg.encoder.pad_token_id))
+        cores = torch.get_num_threads()
+    run(items[0])  # warm
     t0 = time.perf_counter()
     tok = nreq = 0
     for it in items:
-        om.forward(collate_to([it], cfg.encoder.pad_token_id))
+        run(it)
         tok += len(it.ids)
         nreq += 1
         if time.perf_counter() - t0 > budget_s:
             break
     dt = time.perf_counter() - t0
-    return tok / dt, {"cores": torch.get_num_threads(), "tokens": tok, "requests": nreq, "seconds": dt}
+    return tok / dt, {"cores": cores, "tokens": tok, "requests": nreq, "seconds": dt}
 
 
 class ClockSampler:
@@ -372,9 +381,13 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, info = cpu_oracle_sample(cfg, w, mine, 15.0)
+        vc, infoc = cpu_oracle_sample(cfg, w, mine, 10.0, kind="c")
         cpu = {"value": v, "unit": "tokens/s", "cores": info["cores"], "kind": "port",
                "sample": f"{info['requests']} requests / {info['tokens']} tokens of this workload, one row per "
-                         f"forward, {info['seconds']:.1f} s, torch fp32 oracle"}
+                         f"forward, {info['seconds']:.1f} s, torch fp32 oracle",
+               "c_restatement": {"value": vc, "cores": infoc["cores"],
+                                 "sample": f"{infoc['requests']} requests / {infoc['tokens']} tokens, "
+                                           f"{infoc['seconds']:.1f} s, oracle/forward_ref.c (fp32, AVX2, OpenMP)"}}
 
     dist.barrier(world)
     if rank == 0:
