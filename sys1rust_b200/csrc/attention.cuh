@@ -32,6 +32,7 @@ struct AttnArgs {
   const int4* items;                            // work items
   int window;                                   // < 0: global
   float scale_log2;                             // softmax scale * log2(e)
+  int heads;                                    // block b works on item b / heads, head b % heads
 };
 
 constexpr int ATT_BQ = 64, ATT_BK = 64, ATT_D = 64, ATT_THREADS = 128;
@@ -95,8 +96,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 4) attention_varlen_kernel(const 
   __shared__ __align__(128) __nv_bfloat16 sK[2][ATT_BK * ATT_D];
   __shared__ __align__(128) __nv_bfloat16 sV[2][ATT_BK * ATT_D];
 
-  const int4 item = args.items[blockIdx.x];
-  const int head = blockIdx.y;
+  const int4 item = args.items[blockIdx.x / args.heads];
+  const int head = blockIdx.x % args.heads;
   const int seq = item.x, q_first = item.y, q_count = item.z, mode = item.w;
   const int s_begin = args.cu_seqlens[seq], s_end = args.cu_seqlens[seq + 1];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;

@@ -39,7 +39,7 @@ struct AttnTcArgs {
   __nv_bfloat16* o;
   int o_stride;
   int q_col0, k_col0, v_col0;  // column of head 0 of q, k, v in their tensor maps
-  int heads;                   // total heads (CTA y covers heads [y*ATTC_HEADS, ...))
+  int heads;                   // total heads (block b covers heads [(b % groups) * ATTC_HEADS, ...))
   int window;                  // < 0: global
   float scale_log2;
   int* status;
@@ -95,10 +95,11 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int4 item = args.items[blockIdx.x];
+  const int groups = (args.heads + ATTC_HEADS - 1) / ATTC_HEADS;  // block b: item b / groups
+  const int4 item = args.items[blockIdx.x / groups];
   const int seq = item.x, q_first = item.y, q_count = item.z, mode = item.w;
   const int s_begin = args.cu_seqlens[seq], s_end = args.cu_seqlens[seq + 1];
-  const int h0 = blockIdx.y * ATTC_HEADS;
+  const int h0 = (blockIdx.x % groups) * ATTC_HEADS;
   const int nh = min(ATTC_HEADS, args.heads - h0);
   const bool local = args.window >= 0 && mode == 0;
   int k_lo = s_begin, k_hi = s_end;

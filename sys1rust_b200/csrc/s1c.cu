@@ -836,6 +836,15 @@ void validate_varlen(const s1c_backend& B, const s1c_varlen& in) {
   }
 }
 
+// Attention work items with the longest sequences first. The attention grids launch item-major
+// (all heads of one item in consecutive blocks), so the tiles with the most keys start in the
+// first wave and the short ones fill the tail (longest-processing-time order).
+static void longest_first(std::vector<int4>& items, const int* cu) {
+  std::stable_sort(items.begin(), items.end(), [cu](const int4& a, const int4& b) {
+    return cu[a.x + 1] - cu[a.x] > cu[b.x + 1] - cu[b.x];
+  });
+}
+
 HostMeta make_meta(const s1c_varlen& in, int window, int qtile) {
   HostMeta m;
   m.n = in.n;
@@ -866,6 +875,8 @@ HostMeta make_meta(const s1c_varlen& in, int window, int qtile) {
     for (int q = 0; q < rows; q += qtile)
       m.items_rows.push_back(make_int4(r, r * rows + q, std::min(qtile, rows - q), 1));
   }
+  longest_first(m.items_full, m.cu.data());
+  longest_first(m.items_rows, m.cu.data());
   return m;
 }
 
@@ -1020,13 +1031,13 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
     if (B.attn_tc) {
       AttnTcArgs a{dm.cu, items, o, os, q_col0, k_col0, v_col0, d / 64, window, scale_log2, B.d_status};
       launch(B, nl, name, 4.0 * d * pairs, 0, [&] {
-        launch_k(attention_tc_kernel, dim3(dim3(n_items, (d / 64 + ATTC_HEADS - 1) / ATTC_HEADS)), dim3(ATTC_THREADS), ATTC_SMEM, st, 
+        launch_k(attention_tc_kernel, dim3((unsigned)n_items * ((d / 64 + ATTC_HEADS - 1) / ATTC_HEADS)), dim3(ATTC_THREADS), ATTC_SMEM, st,
             tq, tkv, a);
       });
     } else {
-      AttnArgs a{q, k, v, o, qs, ks, vs, os, dm.cu, items, window, scale_log2};
+      AttnArgs a{q, k, v, o, qs, ks, vs, os, dm.cu, items, window, scale_log2, d / 64};
       launch(B, nl, name, 4.0 * d * pairs, 0, [&] {
-        launch_k(attention_varlen_kernel, dim3(dim3(n_items, d / 64)), dim3(ATT_THREADS), 0, st, a);
+        launch_k(attention_varlen_kernel, dim3((unsigned)n_items * (d / 64)), dim3(ATT_THREADS), 0, st, a);
       });
     }
   };
@@ -1681,6 +1692,7 @@ s1c_status s1c_attention(const void* d_q, const void* d_k, const void* d_v, void
       const int base = cu_seqlens[r], len = cu_seqlens[r + 1] - base;
       for (int q = 0; q < len; q += qtile) items.push_back(make_int4(r, base + q, std::min(qtile, len - q), 0));
     }
+    longest_first(items, cu_seqlens);
     const int T = cu_seqlens[n];
     if (sc.cu_cap < (size_t)n + 1) {
       if (sc.d_cu) CK(cudaFree(sc.d_cu));
@@ -1717,7 +1729,8 @@ s1c_status s1c_attention(const void* d_q, const void* d_k, const void* d_v, void
       const CUtensorMap tq = make_tmap(d_q, T, heads * 64, q_stride, ATTC_BQ);
       const CUtensorMap tkv = make_tmap(d_k, T, dv + heads * 64, k_stride, ATTC_BK);
       AttnTcArgs a{d_cu, d_items, static_cast<bf16*>(d_o), o_stride, 0, 0, (int)dv, heads, window, scale_log2, d_status};
-      launch_k(attention_tc_kernel, dim3(dim3((unsigned)items.size(), (heads + ATTC_HEADS - 1) / ATTC_HEADS)), dim3(ATTC_THREADS), ATTC_SMEM, st, tq, tkv, a);
+      launch_k(attention_tc_kernel, dim3((unsigned)items.size() * ((heads + ATTC_HEADS - 1) / ATTC_HEADS)),
+               dim3(ATTC_THREADS), ATTC_SMEM, st, tq, tkv, a);
       cudaError_t e = cudaGetLastError();
       cudaError_t e2 = cudaStreamSynchronize(st);
       int hs = 0;
@@ -1727,8 +1740,9 @@ s1c_status s1c_attention(const void* d_q, const void* d_k, const void* d_v, void
       if (hs) throw S1cError(S1C_ERR_DEVICE_TIMEOUT, "device-side wait ran out (code " + std::to_string(hs) + ")");
     } else {
       AttnArgs a{static_cast<const bf16*>(d_q), static_cast<const bf16*>(d_k), static_cast<const bf16*>(d_v),
-                 static_cast<bf16*>(d_o), q_stride, k_stride, v_stride, o_stride, d_cu, d_items, window, scale_log2};
-      launch_k(attention_varlen_kernel, dim3(dim3((unsigned)items.size(), heads)), dim3(ATT_THREADS), 0, st, a);
+                 static_cast<bf16*>(d_o), q_stride, k_stride, v_stride, o_stride, d_cu, d_items, window, scale_log2,
+                 heads};
+      launch_k(attention_varlen_kernel, dim3((unsigned)items.size() * heads), dim3(ATT_THREADS), 0, st, a);
       cudaError_t e = cudaGetLastError();
       cudaError_t e2 = cudaStreamSynchronize(st);
       if (e != cudaSuccess) throw S1cError(S1C_ERR_CUDA, cudaGetErrorString(e));
