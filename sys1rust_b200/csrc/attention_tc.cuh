@@ -6,20 +6,25 @@
 // with |i - j| <= window (local layers); softmax in fp32, output bf16.
 //
 // One CTA = one tile of up to 128 query rows x ATTC_HEADS heads, processed head after head so
-// the TMA/MMA pipeline never drains between heads; two CTAs share an SM (96 KB of shared memory
-// and 256 TMEM columns each). 192 threads:
-//   warp 0      TMA producer: Q tile [128 x 64] per head (double buffered), K and V tiles
-//               [64 keys x 64] per key step (2-stage ring), 128-byte swizzle.
+// the TMA/MMA pipeline never drains between heads; two or three CTAs share an SM (66 KB of shared
+// memory and 128 TMEM columns each), so their softmax warps hide each other's latency.
+// 192 threads:
+//   warp 0      TMA producer: Q tile [128 x 64] per head, K and V tiles [64 keys x 64] per key
+//               step (2-stage ring), 128-byte swizzle.
 //   warp 1      TMEM owner and MMA issuer:
-//                 S = Q K^T        M=128 N=64 K=64   (K-major A and B)          -> TMEM cols [0,64)
-//                 O_j = P_j V_j    M=128 N=64 K=64   (P K-major from smem, V MN-major) -> TMEM
-//                                  cols [64,128) / [128,192) alternating
+//                 S = Q K^T     M=128 N=64 K=64 (K-major A and B)              -> TMEM cols [0,64)
+//                 O += P V      M=128 N=64 K=64 (P K-major from shared memory, V MN-major)
+//                                                                               -> TMEM cols [64,128)
 //               S of the next key step is issued as soon as the softmax has read the current S.
-//   warps 2..5  softmax, one query row per thread (TMEM lane = row): masks only on tiles that
-//               cross a row's key range, online max / sum in fp32 with p = 2^(s*scale - m) (one
-//               FFMA and one ex2 per score), P rounded to bf16 into one of two shared-memory
-//               buffers in the swizzled K-major layout the MMA reads, O_j folded into a register
-//               accumulator with the running correction, final O / l stored bf16.
+//   warps 2..5  softmax, one query row per thread (TMEM lane = row). Per key step: the row's
+//               maximum m; p = 2^(s * scale - m_ref) with a reference maximum m_ref that is only
+//               raised when m exceeds it by more than 2^8 (p stays <= 256, exact in fp32 and
+//               bf16-representable like any p), in which case the running sum and the O
+//               accumulator in TMEM are rescaled by 2^(m_ref_old - m_ref) once the previous
+//               P V has completed. P is rounded to bf16 into a swizzled K-major shared tile.
+//               32-column halves of S that no row of a warp may see (window edges, a row's
+//               last partial key tile) are neither read nor exponentiated. At the end of a
+//               head O / l is read from TMEM and stored bf16.
 #pragma once
 #include <cuda.h>
 #include "common.cuh"
@@ -27,11 +32,13 @@
 namespace s1c {
 
 constexpr int ATTC_BQ = 128, ATTC_BK = 64, ATTC_THREADS = 192, ATTC_HEADS = 4, ATTC_KV_STAGES = 2;
+constexpr int ATTC_CTAS_PER_SM = 3;
+constexpr uint32_t ATTC_TMEM_COLS = 128;
 constexpr uint32_t ATTC_Q_BYTES = ATTC_BQ * 64 * 2;       // 16 KB
 constexpr uint32_t ATTC_KV_BYTES = ATTC_BK * 64 * 2;      // 8 KB each for K and V
-constexpr uint32_t ATTC_P_BYTES = ATTC_BQ * ATTC_BK * 2;  // 16 KB: one swizzled [128 x 64] block (x2)
-constexpr size_t ATTC_SMEM =
-    2 * ATTC_Q_BYTES + ATTC_KV_STAGES * 2 * ATTC_KV_BYTES + 2 * ATTC_P_BYTES + 1024 + 256;
+constexpr uint32_t ATTC_P_BYTES = ATTC_BQ * ATTC_BK * 2;  // 16 KB: one swizzled [128 x 64] block
+constexpr size_t ATTC_SMEM = ATTC_Q_BYTES + ATTC_KV_STAGES * 2 * ATTC_KV_BYTES + ATTC_P_BYTES + 1024 + 256;
+constexpr float ATTC_RESCALE_LOG2 = 8.0f;  // raise the reference maximum only past 2^8
 
 struct AttnTcArgs {
   const int* cu_seqlens;
@@ -68,29 +75,94 @@ S1C_DEV float ex2f_approx(float x) {
   return y;
 }
 
-__global__ void __launch_bounds__(ATTC_THREADS, 2)
+// Two 32-column TMEM loads with one wait: v[0..31] from taddr, v[32..63] from taddr + 32.
+S1C_DEV void tmem_ld32x2(uint32_t taddr, bool lo, bool hi, float (&v)[64]) {
+  uint32_t r[64];
+  if (lo)
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+  else
+#pragma unroll
+    for (int i = 0; i < 32; ++i) r[i] = 0xff800000u;  // -inf: this half is not read
+  if (hi)
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+          "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
+          "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
+          "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+        : "r"(taddr + 32));
+  else
+#pragma unroll
+    for (int i = 32; i < 64; ++i) r[i] = 0xff800000u;
+  // One hardware wait covers both loads; each asm names its half as read-write so that no use
+  // is scheduled before it.
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                 "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                 "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[32]), "+r"(r[33]), "+r"(r[34]), "+r"(r[35]), "+r"(r[36]), "+r"(r[37]), "+r"(r[38]),
+                 "+r"(r[39]), "+r"(r[40]), "+r"(r[41]), "+r"(r[42]), "+r"(r[43]), "+r"(r[44]), "+r"(r[45]),
+                 "+r"(r[46]), "+r"(r[47]), "+r"(r[48]), "+r"(r[49]), "+r"(r[50]), "+r"(r[51]), "+r"(r[52]),
+                 "+r"(r[53]), "+r"(r[54]), "+r"(r[55]), "+r"(r[56]), "+r"(r[57]), "+r"(r[58]), "+r"(r[59]),
+                 "+r"(r[60]), "+r"(r[61]), "+r"(r[62]), "+r"(r[63])
+               :
+               : "memory");
+#pragma unroll
+  for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// 32 lanes x 32 consecutive fp32 columns to TMEM (completion: tmem_st_wait).
+S1C_DEV void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]), "f"(v[8]),
+      "f"(v[9]), "f"(v[10]), "f"(v[11]), "f"(v[12]), "f"(v[13]), "f"(v[14]), "f"(v[15]), "f"(v[16]), "f"(v[17]),
+      "f"(v[18]), "f"(v[19]), "f"(v[20]), "f"(v[21]), "f"(v[22]), "f"(v[23]), "f"(v[24]), "f"(v[25]), "f"(v[26]),
+      "f"(v[27]), "f"(v[28]), "f"(v[29]), "f"(v[30]), "f"(v[31])
+      : "memory");
+}
+S1C_DEV void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// CTAS = CTAs per SM the registers are budgeted for (2: no spills; 3: twelve softmax warps per SM
+// at 96 registers per thread).
+template <int CTAS>
+__global__ void __launch_bounds__(ATTC_THREADS, CTAS)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
                         const AttnTcArgs args) {
   constexpr int NS = ATTC_KV_STAGES;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_u = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_u + 1023u) & ~1023u) - raw_u);
-  uint8_t* sQ = smem;                              // [2][16 KB]
-  uint8_t* sK = sQ + 2 * ATTC_Q_BYTES;             // [NS][8 KB]
+  uint8_t* sQ = smem;                              // [16 KB]
+  uint8_t* sK = sQ + ATTC_Q_BYTES;                 // [NS][8 KB]
   uint8_t* sV = sK + NS * ATTC_KV_BYTES;           // [NS][8 KB]
-  uint8_t* sP = sV + NS * ATTC_KV_BYTES;           // [2][16 KB]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * ATTC_P_BYTES);
-  uint64_t* q_full = bars + 0;    // [2]
-  uint64_t* q_empty = bars + 2;   // [2]
-  uint64_t* kv_full = bars + 4;   // [NS]
-  uint64_t* kv_empty = bars + 4 + NS;
-  uint64_t* s_full = bars + 4 + 2 * NS;
+  uint8_t* sP = sV + NS * ATTC_KV_BYTES;           // [16 KB]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + ATTC_P_BYTES);
+  uint64_t* q_full = bars + 0;
+  uint64_t* q_empty = bars + 1;
+  uint64_t* kv_full = bars + 2;   // [NS]
+  uint64_t* kv_empty = bars + 2 + NS;
+  uint64_t* s_full = bars + 2 + 2 * NS;
   uint64_t* s_free = s_full + 1;
-  uint64_t* p_full = s_full + 2;  // [2]
-  uint64_t* p_free = s_full + 4;  // [2]
-  uint64_t* o_full = s_full + 6;  // [2]
-  uint64_t* o_free = s_full + 8;  // [2]
-  uint64_t* drain = s_full + 10;
+  uint64_t* p_full = s_full + 2;
+  uint64_t* p_free = s_full + 3;
+  uint64_t* o_full = s_full + 4;
+  uint64_t* o_free = s_full + 5;
+  uint64_t* drain = s_full + 6;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -111,26 +183,24 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
   const int nsteps = nh * nt;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&q_full[i], 1);
-      mbar_init(&q_empty[i], 1);
-      mbar_init(&o_full[i], 1);
-      mbar_init(&o_free[i], 128);
-      mbar_init(&p_full[i], 128);
-      mbar_init(&p_free[i], 1);
-    }
+    mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
     for (int i = 0; i < NS; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
     }
     mbar_init(s_full, 1);
-    mbar_init(s_free, 128);
+    mbar_init(s_free, 4);  // one arrival per softmax warp
+    mbar_init(p_full, 4);
+    mbar_init(p_free, 1);
+    mbar_init(o_full, 1);
+    mbar_init(o_free, 4);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 256);
+    tmem_alloc(tmem_slot, ATTC_TMEM_COLS);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -147,10 +217,11 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
       int issued_q = 0, issued_kv = 0;
       bool ok = true;
       for (int hi = 0; ok && hi < nh; ++hi) {
-        const int h = h0 + hi, qb = hi & 1;
-        if (!mbar_wait(&q_empty[qb], ((hi >> 1) & 1) ^ 1u, args.status, DEV_TIMEOUT_PRODUCER, abort_flag)) break;
-        mbar_arrive_expect_tx(&q_full[qb], ATTC_Q_BYTES);
-        tma_load_2d(sQ + qb * ATTC_Q_BYTES, &tmQ, &q_full[qb], args.q_col0 + h * 64, q_first);
+        const int h = h0 + hi;
+        // the single Q buffer is free once the last S MMA of the previous head has completed
+        if (!mbar_wait(q_empty, (hi & 1) ^ 1u, args.status, DEV_TIMEOUT_PRODUCER, abort_flag)) break;
+        mbar_arrive_expect_tx(q_full, ATTC_Q_BYTES);
+        tma_load_2d(sQ, &tmQ, q_full, args.q_col0 + h * 64, q_first);
         ++issued_q;
         for (int j = 0; j < nt; ++j) {
           const int step = hi * nt + j, s = step % NS;
@@ -165,8 +236,7 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
         }
       }
       // Loads still in flight land before the CTA exits.
-      for (int i = max(0, issued_q - 2); i < issued_q; ++i)
-        mbar_wait(&q_full[i & 1], (i >> 1) & 1, args.status, DEV_TIMEOUT_DRAIN, nullptr);
+      if (issued_q > 0) mbar_wait(q_full, (issued_q - 1) & 1, args.status, DEV_TIMEOUT_DRAIN, nullptr);
       for (int i = max(0, issued_kv - NS); i < issued_kv; ++i)
         mbar_wait(&kv_full[i % NS], (i / NS) & 1, args.status, DEV_TIMEOUT_DRAIN, nullptr);
     }
@@ -175,39 +245,40 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
       constexpr uint32_t idS = idesc_bf16_f32(128, ATTC_BK);
       constexpr uint32_t idO = idesc_bf16_f32_bmn(128, 64);
       const uint32_t tS = tmem, tO = tmem + 64;
+      const uint32_t qa = smem_u32(sQ), pa = smem_u32(sP);
       bool ok = true;
-      // S for step `st`: needs Q of its head and K of its stage.
+      // S for step `st`: needs Q of its head, K of its stage and the softmax done reading S(st - 1).
       auto issue_s = [&](int st) -> bool {
-        const int hi = st / nt, j = st % nt, s = st % NS, qb = hi & 1;
-        if (j == 0 && !mbar_wait(&q_full[qb], (hi >> 1) & 1, args.status, DEV_TIMEOUT_MMA_FULL, abort_flag))
-          return false;
+        const int hi = st / nt, j = st % nt, s = st % NS;
+        if (j == 0 && !mbar_wait(q_full, hi & 1, args.status, DEV_TIMEOUT_MMA_FULL, abort_flag)) return false;
         if (!mbar_wait(&kv_full[s], (st / NS) & 1, args.status, DEV_TIMEOUT_MMA_FULL, abort_flag)) return false;
         if (st > 0 && !mbar_wait(s_free, (st - 1) & 1, args.status, DEV_TIMEOUT_MMA_TEMPTY, abort_flag)) return false;
         tc_fence_after();
-        const uint32_t qa = smem_u32(sQ + qb * ATTC_Q_BYTES), ka = smem_u32(sK + s * ATTC_KV_BYTES);
+        const uint32_t ka = smem_u32(sK + s * ATTC_KV_BYTES);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           umma_bf16(tS, sdesc_kmajor_sw128(qa + k * 32), sdesc_kmajor_sw128(ka + k * 32), idS, k ? 1u : 0u);
         umma_commit(s_full);
-        if (j == nt - 1) umma_commit(&q_empty[qb]);  // Q of this head is no longer read
+        if (j == nt - 1) umma_commit(q_empty);  // Q of this head is no longer read
         return true;
       };
       ok = issue_s(0);
       for (int st = 0; ok && st < nsteps; ++st) {
         if (st + 1 < nsteps && !issue_s(st + 1)) break;
-        const int s = st % NS, ob = st & 1;
-        if (!mbar_wait(&p_full[ob], (st >> 1) & 1, args.status, DEV_TIMEOUT_MMA_FULL, abort_flag)) break;
-        if (st >= 2 && !mbar_wait(&o_free[ob], ((st >> 1) - 1) & 1, args.status, DEV_TIMEOUT_MMA_TEMPTY, abort_flag))
+        const int hi = st / nt, j = st % nt, s = st % NS;
+        if (!mbar_wait(p_full, st & 1, args.status, DEV_TIMEOUT_MMA_FULL, abort_flag)) break;
+        // the first P V of a head overwrites O: the previous head's O must have been read
+        if (j == 0 && hi > 0 && !mbar_wait(o_free, (hi - 1) & 1, args.status, DEV_TIMEOUT_MMA_TEMPTY, abort_flag))
           break;
         tc_fence_after();
-        const uint32_t pa = smem_u32(sP + ob * ATTC_P_BYTES), va = smem_u32(sV + s * ATTC_KV_BYTES);
+        const uint32_t va = smem_u32(sV + s * ATTC_KV_BYTES);
 #pragma unroll
         for (int k = 0; k < ATTC_BK / 16; ++k)
-          umma_bf16(tO + ob * 64, sdesc_kmajor_sw128(pa + k * 32), sdesc_mnmajor_sw128(va + k * 2048), idO,
-                    k ? 1u : 0u);
-        umma_commit(&o_full[ob]);
+          umma_bf16(tO, sdesc_kmajor_sw128(pa + k * 32), sdesc_mnmajor_sw128(va + k * 2048), idO,
+                    (j > 0 || k > 0) ? 1u : 0u);
         umma_commit(&kv_empty[s]);
-        umma_commit(&p_free[ob]);
+        umma_commit(p_free);
+        if (j == nt - 1) umma_commit(o_full);
       }
       umma_commit(drain);
       mbar_wait(drain, 0, args.status, DEV_TIMEOUT_DRAIN, nullptr);
@@ -219,30 +290,31 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
     const uint32_t tS = tmem + lane_off, tO = tmem + lane_off + 64;
     const int qtok = q_first + r;  // query token (mode 0)
     const float sc = args.scale_log2;
-    float o[64];
-    float m = -INFINITY, l = 0.f, corr_prev = 0.f;
+    float m_ref = -INFINITY, l = 0.f;
+    uint8_t* prow = sP + r * 128;
     for (int st = 0; st < nsteps; ++st) {
       const int hi = st / nt, j = st % nt;
       if (j == 0) {
-#pragma unroll
-        for (int i = 0; i < 64; ++i) o[i] = 0.f;
-        m = -INFINITY;
+        m_ref = -INFINITY;
         l = 0.f;
       }
-      if (!mbar_wait_warp(s_full, st & 1, args.status, DEV_TIMEOUT_EPILOGUE, abort_flag)) break;
-      tc_fence_after();
-      float s[64];
-      tmem_ld32(tS, *reinterpret_cast<float(*)[32]>(s));
-      tmem_ld32(tS + 32, *reinterpret_cast<float(*)[32]>(s + 32));
-      tc_fence_before();
-      mbar_arrive(s_free);
-      // Keys this row may see, as column offsets [lo, hi) inside the tile.
+      // Keys this row may see, as column offsets [lo, hi_c) inside the tile; which 32-column
+      // halves any row of this warp may see.
       const int kt0 = k_lo + j * ATTC_BK;
       int lo = 0, hi_c = k_hi - kt0;
       if (local) {
         lo = max(lo, qtok - args.window - kt0);
         hi_c = min(hi_c, qtok + args.window + 1 - kt0);
       }
+      const bool need0 = __any_sync(0xffffffffu, lo < 32 && hi_c > 0);
+      const bool need1 = __any_sync(0xffffffffu, lo < 64 && hi_c > 32);
+      if (!mbar_wait_warp(s_full, st & 1, args.status, DEV_TIMEOUT_EPILOGUE, abort_flag)) break;
+      tc_fence_after();
+      float s[64];
+      tmem_ld32x2(tS, need0, need1, s);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(s_free);
       if (!__all_sync(0xffffffffu, lo <= 0 && hi_c >= ATTC_BK)) {
 #pragma unroll
         for (int c = 0; c < 64; ++c) s[c] = (c >= lo && c < hi_c) ? s[c] : -INFINITY;
@@ -252,66 +324,78 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
       for (int i = 0; i < 8; ++i) pm[i] = s[i];
 #pragma unroll
       for (int c = 8; c < 64; ++c) pm[c & 7] = fmaxf(pm[c & 7], s[c]);
-      float mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])), fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
-      mx = fmaxf(m, mx * sc);
-      const float base = (mx == -INFINITY) ? 0.f : mx;
-      const float corr = ex2f_approx(m - base);
-      m = mx;
-      // P row -> shared memory buffer st & 1 (one swizzled [128 x 64] block), once the PV MMA of
-      // step st - 2 has read that buffer.
-      const int pb = st & 1;
-      if (st >= 2 &&
-          !mbar_wait_warp(&p_free[pb], ((st >> 1) - 1) & 1, args.status, DEV_TIMEOUT_EPILOGUE, abort_flag))
-        break;
-      uint8_t* prow = sP + pb * ATTC_P_BYTES + r * 128;
+      const float mx =
+          fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])), fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7]))) * sc;
+      // Raise the reference maximum only when this tile's maximum passes it by more than 2^8.
+      float factor = 1.f;
+      bool rescale_o = false;
+      if (mx > m_ref + ATTC_RESCALE_LOG2) {
+        factor = ex2f_approx(m_ref - mx);  // 0 while m_ref is -inf
+        rescale_o = l > 0.f;               // O holds earlier P V products of this head
+        l *= factor;
+        m_ref = mx;
+      }
+      const float base = (m_ref == -INFINITY) ? 0.f : m_ref;
       float rsum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        float p[8];
+      for (int half = 0; half < 2; ++half) {
+        if (half ? need1 : need0) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          p[i] = ex2f_approx(fmaf(s[8 * q + i], sc, -base));
-          rsum[i] += p[i];
+          for (int c = half * 32; c < half * 32 + 32; ++c) {
+            s[c] = ex2f_approx(fmaf(s[c], sc, -base));
+            rsum[c & 7] += s[c];
+          }
+        } else {
+#pragma unroll
+          for (int c = half * 32; c < half * 32 + 32; ++c) s[c] = 0.f;
         }
-        *reinterpret_cast<uint4*>(prow + ((q ^ (r & 7)) << 4)) =
-            make_uint4(pack_bf16x2(p[0], p[1]), pack_bf16x2(p[2], p[3]), pack_bf16x2(p[4], p[5]),
-                       pack_bf16x2(p[6], p[7]));
       }
-      const float rs = ((rsum[0] + rsum[1]) + (rsum[2] + rsum[3])) + ((rsum[4] + rsum[5]) + (rsum[6] + rsum[7]));
-      l = l * corr + rs;
-      fence_proxy_async();
-      mbar_arrive(&p_full[pb]);
-      // Fold a finished O_j (same head) into the register accumulator, 32 columns at a time.
-      auto fold = [&](int sj, float cr) -> bool {
-        const int ob = sj & 1;
-        if (!mbar_wait_warp(&o_full[ob], (sj >> 1) & 1, args.status, DEV_TIMEOUT_EPILOGUE, abort_flag)) return false;
+      l += ((rsum[0] + rsum[1]) + (rsum[2] + rsum[3])) + ((rsum[4] + rsum[5]) + (rsum[6] + rsum[7]));
+      // P V of the previous step has completed: the P buffer may be rewritten and O rescaled.
+      if (st > 0 && !mbar_wait_warp(p_free, (st - 1) & 1, args.status, DEV_TIMEOUT_EPILOGUE, abort_flag)) break;
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        *reinterpret_cast<uint4*>(prow + ((q ^ (r & 7)) << 4)) =
+            make_uint4(pack_bf16x2(s[8 * q], s[8 * q + 1]), pack_bf16x2(s[8 * q + 2], s[8 * q + 3]),
+                       pack_bf16x2(s[8 * q + 4], s[8 * q + 5]), pack_bf16x2(s[8 * q + 6], s[8 * q + 7]));
+      if (__any_sync(0xffffffffu, rescale_o)) {
         tc_fence_after();
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
           float t[32];
-          tmem_ld32(tO + ob * 64 + half * 32, t);
+          tmem_ld32(tO + half * 32, t);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[half * 32 + i] = o[half * 32 + i] * cr + t[i];
+          for (int i = 0; i < 32; ++i) t[i] *= factor;
+          tmem_st32(tO + half * 32, t);
+        }
+        tmem_st_wait();
+      }
+      fence_proxy_async();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+      if (j == nt - 1) {
+        // O / l -> bf16, row q_first + r of the output, columns of head h0 + hi
+        if (!mbar_wait_warp(o_full, hi & 1, args.status, DEV_TIMEOUT_EPILOGUE, abort_flag)) break;
+        tc_fence_after();
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        uint4* dst = reinterpret_cast<uint4*>(args.o + (size_t)(q_first + r) * args.o_stride + (h0 + hi) * 64);
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          float t[32];
+          tmem_ld32(tO + half * 32, t);
+          if (r < q_count) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              dst[half * 4 + q] = make_uint4(pack_bf16x2(t[8 * q] * inv, t[8 * q + 1] * inv),
+                                             pack_bf16x2(t[8 * q + 2] * inv, t[8 * q + 3] * inv),
+                                             pack_bf16x2(t[8 * q + 4] * inv, t[8 * q + 5] * inv),
+                                             pack_bf16x2(t[8 * q + 6] * inv, t[8 * q + 7] * inv));
+          }
         }
         tc_fence_before();
-        mbar_arrive(&o_free[ob]);
-        return true;
-      };
-      if (j > 0 && !fold(st - 1, corr_prev)) break;
-      corr_prev = corr;
-      if (j == nt - 1) {
-        if (!fold(st, corr)) break;
-        // O / l -> bf16, row q_first + r of the output, columns of head h0 + hi
-        if (r < q_count) {
-          const float inv = l > 0.f ? 1.f / l : 0.f;
-          uint4* dst = reinterpret_cast<uint4*>(args.o + (size_t)(q_first + r) * args.o_stride + (h0 + hi) * 64);
-#pragma unroll
-          for (int q = 0; q < 8; ++q)
-            dst[q] = make_uint4(pack_bf16x2(o[8 * q] * inv, o[8 * q + 1] * inv),
-                                pack_bf16x2(o[8 * q + 2] * inv, o[8 * q + 3] * inv),
-                                pack_bf16x2(o[8 * q + 4] * inv, o[8 * q + 5] * inv),
-                                pack_bf16x2(o[8 * q + 6] * inv, o[8 * q + 7] * inv));
-        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(o_free);
       }
     }
   }
@@ -319,7 +403,7 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, ATTC_TMEM_COLS);
   }
 }
 

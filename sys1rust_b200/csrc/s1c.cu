@@ -478,7 +478,12 @@ struct s1c_backend {
   // activations (capacity in rows, multiples of 128)
   int gemm_variant = 0;   // `gemm=auto|1cta|2cta|splitk|csk`
   bool pdl = true;        // `pdl=0|1`: programmatic dependent launch between the forward's kernels
-  bool attn_tc = false;  // true: tcgen05 attention (attention_tc.cuh, `attn=tc`); false: mma.sync (attention.cuh)
+  // Attention kernel per call: `attn=auto` (default) runs the tcgen05 kernel (attention_tc.cuh) on
+  // full rows (global encoder layers, head layer 0) and the mma.sync kernel (attention.cuh) on the
+  // sliding window and the pruned head rows, where its 64-row tiles waste less; `attn=tc|tc3|mma`
+  // force one kernel everywhere (tc3: the tcgen05 kernel at 3 CTAs per SM).
+  enum AttnMode { ATTN_AUTO, ATTN_TC, ATTN_MMA } attn_mode = ATTN_AUTO;
+  int attn_tc_ctas = 2;
   int cap_T = 0, cap_R = 0;
   DevBuf h, x, qkv, att, act;          // [cap_T, ...]
   DevBuf h2;                           // head residual stream [cap_T, d] fp32
@@ -812,7 +817,9 @@ struct HostMeta {
   double pairs_global = 0, pairs_local = 0, pairs_rows = 0;  // attended (query, key) pairs per head-set
   std::vector<int> cu, srows, mrows, prows, mcount;
   std::vector<uint32_t> qtype;
-  std::vector<int4> items_full, items_rows;
+  // attention work lists for the two query-tile heights: full rows (encoder, head layer 0) and
+  // the pruned head rows, tiles of 64 (mma.sync kernel) and 128 (tcgen05 kernel)
+  std::vector<int4> items_full, items_rows, items_full_tc, items_rows_tc;
 };
 
 void validate_varlen(const s1c_backend& B, const s1c_varlen& in) {
@@ -845,7 +852,7 @@ static void longest_first(std::vector<int4>& items, const int* cu) {
   });
 }
 
-HostMeta make_meta(const s1c_varlen& in, int window, int qtile) {
+HostMeta make_meta(const s1c_varlen& in, int window) {
   HostMeta m;
   m.n = in.n;
   m.kmax = in.kmax;
@@ -870,13 +877,19 @@ HostMeta make_meta(const s1c_varlen& in, int window, int qtile) {
     m.pairs_global += (double)len * len;
     m.pairs_rows += (double)(1 + in.kmax) * len;
     for (int i = 0; i < len; ++i) m.pairs_local += std::min(i, window) + std::min(len - 1 - i, window) + 1;
-    for (int q = 0; q < len; q += qtile) m.items_full.push_back(make_int4(r, base + q, std::min(qtile, len - q), 0));
     const int rows = 1 + in.kmax;
-    for (int q = 0; q < rows; q += qtile)
-      m.items_rows.push_back(make_int4(r, r * rows + q, std::min(qtile, rows - q), 1));
+    for (int q = 0; q < len; q += ATT_BQ) m.items_full.push_back(make_int4(r, base + q, std::min(ATT_BQ, len - q), 0));
+    for (int q = 0; q < rows; q += ATT_BQ)
+      m.items_rows.push_back(make_int4(r, r * rows + q, std::min(ATT_BQ, rows - q), 1));
+    for (int q = 0; q < len; q += ATTC_BQ)
+      m.items_full_tc.push_back(make_int4(r, base + q, std::min(ATTC_BQ, len - q), 0));
+    for (int q = 0; q < rows; q += ATTC_BQ)
+      m.items_rows_tc.push_back(make_int4(r, r * rows + q, std::min(ATTC_BQ, rows - q), 1));
   }
   longest_first(m.items_full, m.cu.data());
   longest_first(m.items_rows, m.cu.data());
+  longest_first(m.items_full_tc, m.cu.data());
+  longest_first(m.items_rows_tc, m.cu.data());
   return m;
 }
 
@@ -890,6 +903,8 @@ struct DevMeta {
   const uint32_t* qtype;
   const int4* items_full;
   const int4* items_rows;
+  const int4* items_full_tc;
+  const int4* items_rows_tc;
 };
 
 // Stage the metadata (and optionally the ids) in pinned memory and copy it in one transfer.
@@ -909,6 +924,8 @@ DevMeta upload_meta(s1c_backend& B, const HostMeta& m, const uint32_t* host_ids)
       {m.qtype.data(), m.qtype.size() * 4},
       {m.items_full.data(), m.items_full.size() * 16},
       {m.items_rows.data(), m.items_rows.size() * 16},
+      {m.items_full_tc.data(), m.items_full_tc.size() * 16},
+      {m.items_rows_tc.data(), m.items_rows_tc.size() * 16},
   };
   std::vector<size_t> off(parts.size());
   size_t total = 0;
@@ -953,6 +970,8 @@ DevMeta upload_meta(s1c_backend& B, const HostMeta& m, const uint32_t* host_ids)
   dm.qtype = reinterpret_cast<const uint32_t*>(dv + off[6]);
   dm.items_full = reinterpret_cast<const int4*>(dv + off[7]);
   dm.items_rows = reinterpret_cast<const int4*>(dv + off[8]);
+  dm.items_full_tc = reinterpret_cast<const int4*>(dv + off[9]);
+  dm.items_rows_tc = reinterpret_cast<const int4*>(dv + off[10]);
   return dm;
 }
 
@@ -1024,15 +1043,24 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
   // Attention over the items' query tiles: the tcgen05 kernel reads Q/K/V through TMA maps
   // (tq with q at column q_col0, tkv with k at k_col0 and v at v_col0); the mma.sync kernel
   // through the raw pointers and row pitches.
+  // `rows`: the pruned head rows (work lists items_rows*), else full rows (items_full*).
   auto attn = [&](const char* name, const CUtensorMap& tq, const CUtensorMap& tkv, int q_col0, int k_col0,
                   int v_col0, const bf16* q, const bf16* k, const bf16* v, bf16* o, int qs, int ks, int vs, int os,
-                  const int4* items, int n_items, int window, double pairs) {
+                  bool rows, int window, double pairs) {
+    const bool tc = B.attn_mode == s1c_backend::ATTN_TC ||
+                    (B.attn_mode == s1c_backend::ATTN_AUTO && !rows && window < 0);
+    const int4* items = tc ? (rows ? dm.items_rows_tc : dm.items_full_tc) : (rows ? dm.items_rows : dm.items_full);
+    const int n_items = (int)(tc ? (rows ? m.items_rows_tc.size() : m.items_full_tc.size())
+                                 : (rows ? m.items_rows.size() : m.items_full.size()));
     if (n_items == 0) return;
-    if (B.attn_tc) {
+    if (tc) {
       AttnTcArgs a{dm.cu, items, o, os, q_col0, k_col0, v_col0, d / 64, window, scale_log2, B.d_status};
       launch(B, nl, name, 4.0 * d * pairs, 0, [&] {
-        launch_k(attention_tc_kernel, dim3((unsigned)n_items * ((d / 64 + ATTC_HEADS - 1) / ATTC_HEADS)), dim3(ATTC_THREADS), ATTC_SMEM, st,
-            tq, tkv, a);
+        const dim3 grid((unsigned)n_items * ((d / 64 + ATTC_HEADS - 1) / ATTC_HEADS));
+        if (B.attn_tc_ctas == 3)
+          launch_k(attention_tc_kernel<3>, grid, dim3(ATTC_THREADS), ATTC_SMEM, st, tq, tkv, a);
+        else
+          launch_k(attention_tc_kernel<2>, grid, dim3(ATTC_THREADS), ATTC_SMEM, st, tq, tkv, a);
       });
     } else {
       AttnArgs a{q, k, v, o, qs, ks, vs, os, dm.cu, items, window, scale_log2, d / 64};
@@ -1066,7 +1094,7 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
     g.rope_cols = 2 * d;
     launch(B, nl, "gemm_qkv_rope", fl * 3 * d * d, 0, [&] { launch_gemm<EPI_ROPE>(B.tm_x, l.tm_wqkv, B.to_qkv3, g, nsm, st, B.gemm_variant, &(sk_tmp = sk(qkv, 3 * d)), &nl); });
     attn(l.local ? "attn_local" : "attn_global", B.tm_qkv_att, B.tm_qkv_kv, 0, d, 2 * d, qkv, qkv + d,
-         qkv + 2 * d, att, 3 * d, 3 * d, 3 * d, d, dm.items_full, (int)m.items_full.size(), l.local ? B.window : -1,
+         qkv + 2 * d, att, 3 * d, 3 * d, 3 * d, d, false, l.local ? B.window : -1,
          l.local ? m.pairs_local : m.pairs_global);
     GemmArgs go = gemm_args(T, d, d);
     launch(B, nl, "gemm_wo_resid", fl * d * d, 0, [&] { launch_gemm<EPI_RESID>(B.tm_att, l.tm_wo, B.to_h, go, nsm, st, B.gemm_variant, &(sk_tmp = sk(h, d)), &nl); });
@@ -1092,7 +1120,7 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
     g.bias = hl.in_b;
     launch(B, nl, "head_gemm_in", fl * 3 * d * d, 0, [&] { launch_gemm<EPI_STORE>(B.tm_x, hl.tm_in, B.to_qkv3, g, nsm, st, B.gemm_variant, &(sk_tmp = sk(qkv, 3 * d)), &nl); });
     attn("head_attn", B.tm_qkv_att, B.tm_qkv_kv, 0, d, 2 * d, qkv, qkv + d, qkv + 2 * d, att, 3 * d, 3 * d,
-         3 * d, d, dm.items_full, (int)m.items_full.size(), -1, m.pairs_global);
+         3 * d, d, false, -1, m.pairs_global);
     GemmArgs go = gemm_args(T, d, d);
     go.bias = hl.out_b;
     launch(B, nl, "head_gemm_out", fl * d * d, 0, [&] { launch_gemm<EPI_RESID>(B.tm_att, hl.tm_out, B.to_h2, go, nsm, st, B.gemm_variant, &(sk_tmp = sk(h2, d)), &nl); });
@@ -1130,7 +1158,7 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
     gq.bias = hl.in_b;
     launch(B, nl, "head_rows_gemm", flr * d * d, 0, [&] { launch_gemm<EPI_STORE>(B.tm_xs, hl.tm_in_q, B.to_qs, gq, nsm, st, B.gemm_variant, &(sk_tmp = sk(B.qs.p, d)), &nl); });
     attn("head_rows_attn", B.tm_qs_att, B.tm_kv_att, 0, 0, d, B.qs.as<bf16>(), kv, kv + d, B.atts.as<bf16>(), d,
-         2 * d, 2 * d, d, dm.items_rows, (int)m.items_rows.size(), -1, m.pairs_rows);
+         2 * d, 2 * d, d, true, -1, m.pairs_rows);
     GemmArgs go = gemm_args(R, d, d);
     go.bias = hl.out_b;
     launch(B, nl, "head_rows_gemm", flr * d * d, 0,
@@ -1204,7 +1232,7 @@ struct StageOut {
 };
 StageOut enqueue_forward(s1c_backend& B, const s1c_varlen& in, const uint32_t* host_ids, const uint32_t* dev_ids,
                          float* d_hidden) {
-  HostMeta m = make_meta(in, B.window, B.attn_tc ? ATTC_BQ : ATT_BQ);
+  HostMeta m = make_meta(in, B.window);
   ensure_capacity(B, m.T, m.R);
   const size_t nl = (size_t)m.M, np = (size_t)m.n * B.d;
   const size_t need = ((nl + 63) / 64 * 64 + np) * 4;
@@ -1223,7 +1251,8 @@ StageOut enqueue_forward(s1c_backend& B, const s1c_varlen& in, const uint32_t* h
     forward_enqueue(B, m, dm, dm.ids, so.logits, so.pooled, d_hidden);
     return so;
   }
-  const std::vector<int> key = {m.T, m.n, m.kmax, (int)m.items_full.size(), (int)m.items_rows.size()};
+  const std::vector<int> key = {m.T, m.n, m.kmax, (int)m.items_full.size(), (int)m.items_rows.size(),
+                                (int)m.items_full_tc.size(), (int)m.items_rows_tc.size()};
   auto it = B.graphs.find(key);
   if (it == B.graphs.end()) {
     if (B.seen[key]++ < 1) {  // first sighting: launch directly
@@ -1362,8 +1391,16 @@ void apply_settings(s1c_backend& B, const char* spec) {
       else if (v == "csk") B.gemm_variant = 4;
       else throw S1cError(S1C_ERR_CONFIG, "settings: `" + kv + "`: `" + v + "` is not one of auto, 1cta, 2cta, splitk, csk");
     } else if (k == "attn") {
-      if (v == "tc") B.attn_tc = true;
-      else if (v == "mma") B.attn_tc = false;
+      if (v == "auto") {
+        B.attn_mode = s1c_backend::ATTN_AUTO;
+        B.attn_tc_ctas = 2;
+      } else if (v == "tc") {
+        B.attn_mode = s1c_backend::ATTN_TC;
+        B.attn_tc_ctas = 2;
+      } else if (v == "tc3") {
+        B.attn_mode = s1c_backend::ATTN_TC;
+        B.attn_tc_ctas = 3;
+      } else if (v == "mma") B.attn_mode = s1c_backend::ATTN_MMA;
       else throw S1cError(S1C_ERR_CONFIG, "settings: `" + kv + "`: `" + v + "` is not one of tc, mma");
     } else {
       throw S1cError(S1C_ERR_CONFIG, "settings: unknown setting `" + k + "`");
@@ -1465,7 +1502,8 @@ s1c_status s1c_create(const s1c_model_desc* desc, const s1c_tensor* tensors, int
     CK(cudaStreamCreateWithFlags(&b->own_stream, cudaStreamNonBlocking));
     b->stream = b->own_stream;
     set_all_gemm_smem();
-    CK(cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATTC_SMEM));
+    CK(cudaFuncSetAttribute(attention_tc_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATTC_SMEM));
+    CK(cudaFuncSetAttribute(attention_tc_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATTC_SMEM));
     apply_settings(*b, std::getenv("S1C_SETTINGS"));
     build(*b, *desc, tensors, n_tensors);
     CK(cudaDeviceSynchronize());
@@ -1679,14 +1717,14 @@ s1c_status s1c_attention(const void* d_q, const void* d_k, const void* d_v, void
   static AttnScratch scratch[64];
   std::lock_guard<std::mutex> guard(mu);
   try {
-    if (!d_q || !d_k || !d_v || !d_o || !cu_seqlens || n <= 0 || heads <= 0 || (impl != 0 && impl != 1))
+    if (!d_q || !d_k || !d_v || !d_o || !cu_seqlens || n <= 0 || heads <= 0 || impl < 0 || impl > 2)
       throw S1cError(S1C_ERR_ARG, "bad attention arguments");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     int dev = 0;
     CK(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) throw S1cError(S1C_ERR_ARG, "device index out of range");
     AttnScratch& sc = scratch[dev];
-    const int qtile = impl == 0 ? ATTC_BQ : ATT_BQ;
+    const int qtile = impl != 1 ? ATTC_BQ : ATT_BQ;
     std::vector<int4> items;
     for (int r = 0; r < n; ++r) {
       const int base = cu_seqlens[r], len = cu_seqlens[r + 1] - base;
@@ -1714,14 +1752,15 @@ s1c_status s1c_attention(const void* d_q, const void* d_k, const void* d_v, void
     CK(cudaMemcpyAsync(d_cu, cu_seqlens, ((size_t)n + 1) * 4, cudaMemcpyHostToDevice, st));
     CK(cudaMemcpyAsync(d_items, items.data(), items.size() * 16, cudaMemcpyHostToDevice, st));
     const float scale_log2 = scale * 1.4426950408889634f;
-    if (impl == 0) {
+    if (impl != 1) {
       // one map for Q, one for K and V together: V must sit in K's rows at a 64-aligned column
       const ptrdiff_t dv = static_cast<const bf16*>(d_v) - static_cast<const bf16*>(d_k);
       if (v_stride != k_stride || dv < 0 || dv % 64 || dv + heads * 64 > k_stride)
         throw S1cError(S1C_ERR_ARG, "tcgen05 attention needs v in the rows of k (same pitch, 64-aligned column)");
       static bool attr_set[64] = {false};
       if (!attr_set[dev]) {
-        CK(cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATTC_SMEM));
+        CK(cudaFuncSetAttribute(attention_tc_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATTC_SMEM));
+        CK(cudaFuncSetAttribute(attention_tc_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATTC_SMEM));
         attr_set[dev] = true;
       }
       int* d_status = sc.d_status;
@@ -1729,8 +1768,11 @@ s1c_status s1c_attention(const void* d_q, const void* d_k, const void* d_v, void
       const CUtensorMap tq = make_tmap(d_q, T, heads * 64, q_stride, ATTC_BQ);
       const CUtensorMap tkv = make_tmap(d_k, T, dv + heads * 64, k_stride, ATTC_BK);
       AttnTcArgs a{d_cu, d_items, static_cast<bf16*>(d_o), o_stride, 0, 0, (int)dv, heads, window, scale_log2, d_status};
-      launch_k(attention_tc_kernel, dim3((unsigned)items.size() * ((heads + ATTC_HEADS - 1) / ATTC_HEADS)),
-               dim3(ATTC_THREADS), ATTC_SMEM, st, tq, tkv, a);
+      const dim3 grid((unsigned)items.size() * ((heads + ATTC_HEADS - 1) / ATTC_HEADS));
+      if (impl == 2)
+        launch_k(attention_tc_kernel<3>, grid, dim3(ATTC_THREADS), ATTC_SMEM, st, tq, tkv, a);
+      else
+        launch_k(attention_tc_kernel<2>, grid, dim3(ATTC_THREADS), ATTC_SMEM, st, tq, tkv, a);
       cudaError_t e = cudaGetLastError();
       cudaError_t e2 = cudaStreamSynchronize(st);
       int hs = 0;

@@ -106,6 +106,30 @@ def test_large_model_long_rows(cuda_lib):
     check_against_oracle(cfg, w, be, batch)
 
 
+@pytest.mark.parametrize("mode", ["tc", "tc3", "mma"])
+def test_attention_settings_match_oracle(cuda_lib, mode):
+    """The forward with each attention setting forced everywhere (the default `attn=auto` mixes the
+    tcgen05 kernel on full rows with the mma.sync kernel on the window and the pruned head rows)."""
+    import os
+    from sys1rust_b200.backend import CudaBackend
+    from conftest import get_backend
+    cfg, w, _ = get_backend("small:3")
+    old = os.environ.get("S1C_SETTINGS")
+    os.environ["S1C_SETTINGS"] = (old + "," if old else "") + f"attn={mode}"
+    try:
+        be = CudaBackend.from_synthetic(cfg, w.tensors)
+    finally:
+        if old is None:
+            del os.environ["S1C_SETTINGS"]
+        else:
+            os.environ["S1C_SETTINGS"] = old
+    try:
+        items = make_rows(cfg, 24, [1, 2, 9, 17, 40, 64, 65, 130, 300, 700], [0, 1, 2, 3, 4, 2, 5, 3, 6, 9])
+        check_against_oracle(cfg, w, be, collate_to(items, cfg.encoder.pad_token_id))
+    finally:
+        be.close()
+
+
 def test_rows_agree_alone_or_batched(cuda_lib):
     """A row's outputs alone and inside a batch (``laya-core/src/agent.rs:400-442`` checks
     batch-vs-single agreement). Alone, a short row runs its GEMMs split over K, so the fp32 sums

@@ -154,7 +154,7 @@ def _attn_ref(q, k, v, cu, window, scale, heads):
     return out
 
 
-@pytest.mark.parametrize("impl", [1, 0])
+@pytest.mark.parametrize("impl", [1, 0, 2])
 @pytest.mark.parametrize("window", [-1, 64, 3])
 def test_attention_varlen_matches_torch(cuda_lib, window, impl):
     from sys1rust_b200.backend import attention
@@ -167,4 +167,28 @@ def test_attention_varlen_matches_torch(cuda_lib, window, impl):
     attention(qkv.data_ptr(), qkv[:, d:].data_ptr(), qkv[:, 2 * d:].data_ptr(), o.data_ptr(), 3 * d, 3 * d, 3 * d, d,
               heads, cu, window, 0.125, impl=impl)
     ref = _attn_ref(qkv[:, :d], qkv[:, d:2 * d], qkv[:, 2 * d:], cu, window, 0.125, heads)
+    assert _rel_err(o, ref) < 1e-2
+
+
+@pytest.mark.parametrize("impl", [1, 0, 2])
+@pytest.mark.parametrize("window", [-1, 64])
+def test_attention_growing_scores(cuda_lib, window, impl):
+    """Scores with a spread of tens (q, k scaled by 4) whose maximum grows along the row (keys
+    scaled by 1 + 3 j / L): the running maximum rises by more than 2^8 between key tiles, so the
+    tcgen05 kernel's rescale of the TMEM accumulator runs (and the mma.sync kernel's correction)."""
+    from sys1rust_b200.backend import attention
+    heads, d = 16, 1024
+    lens = [70, 200, 513, 1024]
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    T = int(cu[-1])
+    qkv = _rand((T, 3 * d), 29).float()
+    ramp = torch.cat([1 + 3 * torch.arange(L, dtype=torch.float32, device="cuda") / L for L in lens])
+    qkv[:, :d] *= 4
+    qkv[:, d:2 * d] *= 4 * ramp[:, None]
+    qkv = qkv.to(torch.bfloat16)
+    o = torch.empty(T, d, dtype=torch.bfloat16, device="cuda")
+    attention(qkv.data_ptr(), qkv[:, d:].data_ptr(), qkv[:, 2 * d:].data_ptr(), o.data_ptr(), 3 * d, 3 * d, 3 * d, d,
+              heads, cu, window, 0.125, impl=impl)
+    ref = _attn_ref(qkv[:, :d], qkv[:, d:2 * d], qkv[:, 2 * d:], cu, window, 0.125, heads)
+    assert torch.isfinite(o.float()).all()
     assert _rel_err(o, ref) < 1e-2
