@@ -166,9 +166,8 @@ S1C_API s1c_status s1c_gemm(int32_t epi, const void* d_A, const void* d_B, void*
                             int32_t rope_cols, int32_t out_cols, int32_t variant, void* stream);
 
 /* Isolated varlen attention on device pointers (head_dim 64): q/k/v/o with row pitches, host
- * cu_seqlens [n+1]; window < 0 = global. impl 0 = tcgen05 kernel at 2 CTAs per SM, 2 = the same at
- * 3 CTAs per SM (for both, v must lie in k's rows: same pitch, 64-aligned column offset), 1 =
- * mma.sync kernel. Blocks until done. */
+ * cu_seqlens [n+1]; window < 0 = global. impl 0 = tcgen05 kernel (v must lie in k's rows: same
+ * pitch, 64-aligned column offset), 1 = mma.sync kernel. Blocks until done. */
 S1C_API s1c_status s1c_attention(const void* d_q, const void* d_k, const void* d_v, void* d_o, int32_t q_stride,
                                  int32_t k_stride, int32_t v_stride, int32_t o_stride, int32_t heads,
                                  const int32_t* cu_seqlens, int32_t n, int32_t window, float scale, int32_t impl,

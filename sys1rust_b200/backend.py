@@ -471,7 +471,7 @@ def gemm_splitk_noalloc(epi: int, a_ptr: int, b_ptr: int, out_ptr: int, M: int, 
 def attention(q_ptr: int, k_ptr: int, v_ptr: int, o_ptr: int, q_stride: int, k_stride: int, v_stride: int,
               o_stride: int, heads: int, cu_seqlens: np.ndarray, window: int, scale: float, impl: int = 0,
               stream: int = 0) -> None:
-    """impl 0: tcgen05 kernel (2 CTAs per SM); 2: the same at 3 CTAs per SM; 1: mma.sync kernel."""
+    """impl 0: tcgen05 kernel; 1: mma.sync kernel."""
     L = lib()
     cu = np.ascontiguousarray(cu_seqlens, dtype=np.int32)
     rc = L.s1c_attention(q_ptr, k_ptr, v_ptr, o_ptr, q_stride, k_stride, v_stride, o_stride, heads, _ptr(cu),

@@ -6,15 +6,15 @@
 // with |i - j| <= window (local layers); softmax in fp32, output bf16.
 //
 // One CTA = one tile of up to 128 query rows x ATTC_HEADS heads, processed head after head so
-// the TMA/MMA pipeline never drains between heads; two or three CTAs share an SM (66 KB of shared
-// memory and 128 TMEM columns each), so their softmax warps hide each other's latency.
-// 192 threads:
-//   warp 0      TMA producer: Q tile [128 x 64] per head, K and V tiles [64 keys x 64] per key
-//               step (2-stage ring), 128-byte swizzle.
+// the TMA/MMA pipeline never drains between heads; two CTAs share an SM (98 KB of shared memory
+// and 256 TMEM columns each). 192 threads:
+//   warp 0      TMA producer: Q tile [128 x 64] per head (double buffered, so the next head's Q
+//               arrives while this head runs), K and V tiles [64 keys x 64] per key step (3-stage
+//               ring), 128-byte swizzle.
 //   warp 1      TMEM owner and MMA issuer:
 //                 S = Q K^T     M=128 N=64 K=64 (K-major A and B)              -> TMEM cols [0,64)
 //                 O += P V      M=128 N=64 K=64 (P K-major from shared memory, V MN-major)
-//                                                                               -> TMEM cols [64,128)
+//                               -> TMEM cols [64,128) for even heads, [128,192) for odd heads
 //               S of the next key step is issued as soon as the softmax has read the current S.
 //   warps 2..5  softmax, one query row per thread (TMEM lane = row). Per key step: the row's
 //               maximum m; p = 2^(s * scale - m_ref) with a reference maximum m_ref that is only
@@ -23,21 +23,21 @@
 //               accumulator in TMEM are rescaled by 2^(m_ref_old - m_ref) once the previous
 //               P V has completed. P is rounded to bf16 into a swizzled K-major shared tile.
 //               32-column halves of S that no row of a warp may see (window edges, a row's
-//               last partial key tile) are neither read nor exponentiated. At the end of a
-//               head O / l is read from TMEM and stored bf16.
+//               last partial key tile) are neither read nor exponentiated. A finished head's
+//               O / l is read from TMEM and stored bf16 during the next key step, after its
+//               exponentials, by which time the head's last P V has completed.
 #pragma once
 #include <cuda.h>
 #include "common.cuh"
 
 namespace s1c {
 
-constexpr int ATTC_BQ = 128, ATTC_BK = 64, ATTC_THREADS = 192, ATTC_HEADS = 4, ATTC_KV_STAGES = 2;
-constexpr int ATTC_CTAS_PER_SM = 3;
-constexpr uint32_t ATTC_TMEM_COLS = 128;
+constexpr int ATTC_BQ = 128, ATTC_BK = 64, ATTC_THREADS = 192, ATTC_HEADS = 4, ATTC_KV_STAGES = 3;
+constexpr uint32_t ATTC_TMEM_COLS = 256;  // S [0,64), O of even heads [64,128), odd heads [128,192)
 constexpr uint32_t ATTC_Q_BYTES = ATTC_BQ * 64 * 2;       // 16 KB
 constexpr uint32_t ATTC_KV_BYTES = ATTC_BK * 64 * 2;      // 8 KB each for K and V
 constexpr uint32_t ATTC_P_BYTES = ATTC_BQ * ATTC_BK * 2;  // 16 KB: one swizzled [128 x 64] block
-constexpr size_t ATTC_SMEM = ATTC_Q_BYTES + ATTC_KV_STAGES * 2 * ATTC_KV_BYTES + ATTC_P_BYTES + 1024 + 256;
+constexpr size_t ATTC_SMEM = 2 * ATTC_Q_BYTES + ATTC_KV_STAGES * 2 * ATTC_KV_BYTES + ATTC_P_BYTES + 1024 + 256;
 constexpr float ATTC_RESCALE_LOG2 = 8.0f;  // raise the reference maximum only past 2^8
 
 struct AttnTcArgs {
@@ -137,32 +137,29 @@ S1C_DEV void tmem_st32(uint32_t taddr, const float (&v)[32]) {
 }
 S1C_DEV void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// CTAS = CTAs per SM the registers are budgeted for (2: no spills; 3: twelve softmax warps per SM
-// at 96 registers per thread).
-template <int CTAS>
-__global__ void __launch_bounds__(ATTC_THREADS, CTAS)
+__global__ void __launch_bounds__(ATTC_THREADS, 2)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
                         const AttnTcArgs args) {
   constexpr int NS = ATTC_KV_STAGES;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_u = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_u + 1023u) & ~1023u) - raw_u);
-  uint8_t* sQ = smem;                              // [16 KB]
-  uint8_t* sK = sQ + ATTC_Q_BYTES;                 // [NS][8 KB]
+  uint8_t* sQ = smem;                              // [2][16 KB]
+  uint8_t* sK = sQ + 2 * ATTC_Q_BYTES;             // [NS][8 KB]
   uint8_t* sV = sK + NS * ATTC_KV_BYTES;           // [NS][8 KB]
   uint8_t* sP = sV + NS * ATTC_KV_BYTES;           // [16 KB]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sP + ATTC_P_BYTES);
-  uint64_t* q_full = bars + 0;
-  uint64_t* q_empty = bars + 1;
-  uint64_t* kv_full = bars + 2;   // [NS]
-  uint64_t* kv_empty = bars + 2 + NS;
-  uint64_t* s_full = bars + 2 + 2 * NS;
+  uint64_t* q_full = bars + 0;    // [2]
+  uint64_t* q_empty = bars + 2;   // [2]
+  uint64_t* o_full = bars + 4;    // [2]
+  uint64_t* o_free = bars + 6;    // [2]
+  uint64_t* kv_full = bars + 8;   // [NS]
+  uint64_t* kv_empty = bars + 8 + NS;
+  uint64_t* s_full = bars + 8 + 2 * NS;
   uint64_t* s_free = s_full + 1;
   uint64_t* p_full = s_full + 2;
   uint64_t* p_free = s_full + 3;
-  uint64_t* o_full = s_full + 4;
-  uint64_t* o_free = s_full + 5;
-  uint64_t* drain = s_full + 6;
+  uint64_t* drain = s_full + 4;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -183,18 +180,20 @@ __global__ void __launch_bounds__(ATTC_THREADS, CTAS)
   const int nsteps = nh * nt;
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
-    mbar_init(q_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+      mbar_init(&o_full[i], 1);
+      mbar_init(&o_free[i], 4);  // one arrival per softmax warp
+    }
     for (int i = 0; i < NS; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
     }
     mbar_init(s_full, 1);
-    mbar_init(s_free, 4);  // one arrival per softmax warp
+    mbar_init(s_free, 4);
     mbar_init(p_full, 4);
     mbar_init(p_free, 1);
-    mbar_init(o_full, 1);
-    mbar_init(o_free, 4);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -217,11 +216,11 @@ __global__ void __launch_bounds__(ATTC_THREADS, CTAS)
       int issued_q = 0, issued_kv = 0;
       bool ok = true;
       for (int hi = 0; ok && hi < nh; ++hi) {
-        const int h = h0 + hi;
-        // the single Q buffer is free once the last S MMA of the previous head has completed
-        if (!mbar_wait(q_empty, (hi & 1) ^ 1u, args.status, DEV_TIMEOUT_PRODUCER, abort_flag)) break;
-        mbar_arrive_expect_tx(q_full, ATTC_Q_BYTES);
-        tma_load_2d(sQ, &tmQ, q_full, args.q_col0 + h * 64, q_first);
+        const int h = h0 + hi, qb = hi & 1;
+        // Q buffer qb is free once the last S MMA of head hi - 2 has completed
+        if (!mbar_wait(&q_empty[qb], ((hi >> 1) & 1) ^ 1u, args.status, DEV_TIMEOUT_PRODUCER, abort_flag)) break;
+        mbar_arrive_expect_tx(&q_full[qb], ATTC_Q_BYTES);
+        tma_load_2d(sQ + qb * ATTC_Q_BYTES, &tmQ, &q_full[qb], args.q_col0 + h * 64, q_first);
         ++issued_q;
         for (int j = 0; j < nt; ++j) {
           const int step = hi * nt + j, s = step % NS;
@@ -236,7 +235,8 @@ __global__ void __launch_bounds__(ATTC_THREADS, CTAS)
         }
       }
       // Loads still in flight land before the CTA exits.
-      if (issued_q > 0) mbar_wait(q_full, (issued_q - 1) & 1, args.status, DEV_TIMEOUT_DRAIN, nullptr);
+      for (int i = max(0, issued_q - 2); i < issued_q; ++i)
+        mbar_wait(&q_full[i & 1], (i >> 1) & 1, args.status, DEV_TIMEOUT_DRAIN, nullptr);
       for (int i = max(0, issued_kv - NS); i < issued_kv; ++i)
         mbar_wait(&kv_full[i % NS], (i / NS) & 1, args.status, DEV_TIMEOUT_DRAIN, nullptr);
     }
@@ -244,41 +244,42 @@ __global__ void __launch_bounds__(ATTC_THREADS, CTAS)
     if (lane == 0 && nsteps > 0) {
       constexpr uint32_t idS = idesc_bf16_f32(128, ATTC_BK);
       constexpr uint32_t idO = idesc_bf16_f32_bmn(128, 64);
-      const uint32_t tS = tmem, tO = tmem + 64;
-      const uint32_t qa = smem_u32(sQ), pa = smem_u32(sP);
+      const uint32_t tS = tmem, pa = smem_u32(sP);
       bool ok = true;
       // S for step `st`: needs Q of its head, K of its stage and the softmax done reading S(st - 1).
       auto issue_s = [&](int st) -> bool {
-        const int hi = st / nt, j = st % nt, s = st % NS;
-        if (j == 0 && !mbar_wait(q_full, hi & 1, args.status, DEV_TIMEOUT_MMA_FULL, abort_flag)) return false;
+        const int hi = st / nt, j = st % nt, s = st % NS, qb = hi & 1;
+        if (j == 0 && !mbar_wait(&q_full[qb], (hi >> 1) & 1, args.status, DEV_TIMEOUT_MMA_FULL, abort_flag))
+          return false;
         if (!mbar_wait(&kv_full[s], (st / NS) & 1, args.status, DEV_TIMEOUT_MMA_FULL, abort_flag)) return false;
         if (st > 0 && !mbar_wait(s_free, (st - 1) & 1, args.status, DEV_TIMEOUT_MMA_TEMPTY, abort_flag)) return false;
         tc_fence_after();
-        const uint32_t ka = smem_u32(sK + s * ATTC_KV_BYTES);
+        const uint32_t qa = smem_u32(sQ + qb * ATTC_Q_BYTES), ka = smem_u32(sK + s * ATTC_KV_BYTES);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           umma_bf16(tS, sdesc_kmajor_sw128(qa + k * 32), sdesc_kmajor_sw128(ka + k * 32), idS, k ? 1u : 0u);
         umma_commit(s_full);
-        if (j == nt - 1) umma_commit(q_empty);  // Q of this head is no longer read
+        if (j == nt - 1) umma_commit(&q_empty[qb]);  // Q of this head is no longer read
         return true;
       };
       ok = issue_s(0);
       for (int st = 0; ok && st < nsteps; ++st) {
         if (st + 1 < nsteps && !issue_s(st + 1)) break;
-        const int hi = st / nt, j = st % nt, s = st % NS;
+        const int hi = st / nt, j = st % nt, s = st % NS, ob = hi & 1;
         if (!mbar_wait(p_full, st & 1, args.status, DEV_TIMEOUT_MMA_FULL, abort_flag)) break;
-        // the first P V of a head overwrites O: the previous head's O must have been read
-        if (j == 0 && hi > 0 && !mbar_wait(o_free, (hi - 1) & 1, args.status, DEV_TIMEOUT_MMA_TEMPTY, abort_flag))
+        // the first P V of a head overwrites its O buffer: head hi - 2's O must have been read
+        if (j == 0 && hi >= 2 &&
+            !mbar_wait(&o_free[ob], ((hi >> 1) - 1) & 1, args.status, DEV_TIMEOUT_MMA_TEMPTY, abort_flag))
           break;
         tc_fence_after();
-        const uint32_t va = smem_u32(sV + s * ATTC_KV_BYTES);
+        const uint32_t va = smem_u32(sV + s * ATTC_KV_BYTES), tO = tmem + 64 + 64 * ob;
 #pragma unroll
         for (int k = 0; k < ATTC_BK / 16; ++k)
           umma_bf16(tO, sdesc_kmajor_sw128(pa + k * 32), sdesc_mnmajor_sw128(va + k * 2048), idO,
                     (j > 0 || k > 0) ? 1u : 0u);
         umma_commit(&kv_empty[s]);
         umma_commit(p_free);
-        if (j == nt - 1) umma_commit(o_full);
+        if (j == nt - 1) umma_commit(&o_full[ob]);
       }
       umma_commit(drain);
       mbar_wait(drain, 0, args.status, DEV_TIMEOUT_DRAIN, nullptr);
@@ -287,11 +288,41 @@ __global__ void __launch_bounds__(ATTC_THREADS, CTAS)
     const int quad = warp & 3;
     const int r = quad * 32 + lane;  // query row of this thread
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-    const uint32_t tS = tmem + lane_off, tO = tmem + lane_off + 64;
+    const uint32_t tS = tmem + lane_off;
     const int qtok = q_first + r;  // query token (mode 0)
     const float sc = args.scale_log2;
     float m_ref = -INFINITY, l = 0.f;
     uint8_t* prow = sP + r * 128;
+    // O / l of a finished head -> bf16, row q_first + r, columns of head h0 + hd. Deferred to the
+    // next step's exponentials so that the last P V of the head has completed by then.
+    int pend = -1;
+    float l_pend = 0.f;
+    auto epilogue = [&](int hd, float lsum) -> bool {
+      const int ob = hd & 1;
+      if (!mbar_wait_warp(&o_full[ob], (hd >> 1) & 1, args.status, DEV_TIMEOUT_EPILOGUE, abort_flag)) return false;
+      tc_fence_after();
+      const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+      uint4* dst = reinterpret_cast<uint4*>(args.o + (size_t)(q_first + r) * args.o_stride + (h0 + hd) * 64);
+      const uint32_t tO = tmem + lane_off + 64 + 64 * ob;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        float t[32];
+        tmem_ld32(tO + half * 32, t);
+        if (r < q_count) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            dst[half * 4 + q] = make_uint4(pack_bf16x2(t[8 * q] * inv, t[8 * q + 1] * inv),
+                                           pack_bf16x2(t[8 * q + 2] * inv, t[8 * q + 3] * inv),
+                                           pack_bf16x2(t[8 * q + 4] * inv, t[8 * q + 5] * inv),
+                                           pack_bf16x2(t[8 * q + 6] * inv, t[8 * q + 7] * inv));
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&o_free[ob]);
+      return true;
+    };
+    bool ok = true;
     for (int st = 0; st < nsteps; ++st) {
       const int hi = st / nt, j = st % nt;
       if (j == 0) {
@@ -308,7 +339,10 @@ __global__ void __launch_bounds__(ATTC_THREADS, CTAS)
       }
       const bool need0 = __any_sync(0xffffffffu, lo < 32 && hi_c > 0);
       const bool need1 = __any_sync(0xffffffffu, lo < 64 && hi_c > 32);
-      if (!mbar_wait_warp(s_full, st & 1, args.status, DEV_TIMEOUT_EPILOGUE, abort_flag)) break;
+      if (!mbar_wait_warp(s_full, st & 1, args.status, DEV_TIMEOUT_EPILOGUE, abort_flag)) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
       float s[64];
       tmem_ld32x2(tS, need0, need1, s);
@@ -351,8 +385,18 @@ __global__ void __launch_bounds__(ATTC_THREADS, CTAS)
         }
       }
       l += ((rsum[0] + rsum[1]) + (rsum[2] + rsum[3])) + ((rsum[4] + rsum[5]) + (rsum[6] + rsum[7]));
+      if (pend >= 0) {
+        if (!epilogue(pend, l_pend)) {
+          ok = false;
+          break;
+        }
+        pend = -1;
+      }
       // P V of the previous step has completed: the P buffer may be rewritten and O rescaled.
-      if (st > 0 && !mbar_wait_warp(p_free, (st - 1) & 1, args.status, DEV_TIMEOUT_EPILOGUE, abort_flag)) break;
+      if (st > 0 && !mbar_wait_warp(p_free, (st - 1) & 1, args.status, DEV_TIMEOUT_EPILOGUE, abort_flag)) {
+        ok = false;
+        break;
+      }
 #pragma unroll
       for (int q = 0; q < 8; ++q)
         *reinterpret_cast<uint4*>(prow + ((q ^ (r & 7)) << 4)) =
@@ -360,6 +404,7 @@ __global__ void __launch_bounds__(ATTC_THREADS, CTAS)
                        pack_bf16x2(s[8 * q + 4], s[8 * q + 5]), pack_bf16x2(s[8 * q + 6], s[8 * q + 7]));
       if (__any_sync(0xffffffffu, rescale_o)) {
         tc_fence_after();
+        const uint32_t tO = tmem + lane_off + 64 + 64 * (hi & 1);
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
           float t[32];
@@ -375,29 +420,11 @@ __global__ void __launch_bounds__(ATTC_THREADS, CTAS)
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
       if (j == nt - 1) {
-        // O / l -> bf16, row q_first + r of the output, columns of head h0 + hi
-        if (!mbar_wait_warp(o_full, hi & 1, args.status, DEV_TIMEOUT_EPILOGUE, abort_flag)) break;
-        tc_fence_after();
-        const float inv = l > 0.f ? 1.f / l : 0.f;
-        uint4* dst = reinterpret_cast<uint4*>(args.o + (size_t)(q_first + r) * args.o_stride + (h0 + hi) * 64);
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          float t[32];
-          tmem_ld32(tO + half * 32, t);
-          if (r < q_count) {
-#pragma unroll
-            for (int q = 0; q < 4; ++q)
-              dst[half * 4 + q] = make_uint4(pack_bf16x2(t[8 * q] * inv, t[8 * q + 1] * inv),
-                                             pack_bf16x2(t[8 * q + 2] * inv, t[8 * q + 3] * inv),
-                                             pack_bf16x2(t[8 * q + 4] * inv, t[8 * q + 5] * inv),
-                                             pack_bf16x2(t[8 * q + 6] * inv, t[8 * q + 7] * inv));
-          }
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(o_free);
+        pend = hi;
+        l_pend = l;
       }
     }
+    if (ok && pend >= 0) epilogue(pend, l_pend);
   }
   __syncwarp();
   __syncthreads();

@@ -479,11 +479,10 @@ struct s1c_backend {
   int gemm_variant = 0;   // `gemm=auto|1cta|2cta|splitk|csk`
   bool pdl = true;        // `pdl=0|1`: programmatic dependent launch between the forward's kernels
   // Attention kernel per call: `attn=auto` (default) runs the tcgen05 kernel (attention_tc.cuh) on
-  // full rows (global encoder layers, head layer 0) and the mma.sync kernel (attention.cuh) on the
-  // sliding window and the pruned head rows, where its 64-row tiles waste less; `attn=tc|tc3|mma`
-  // force one kernel everywhere (tc3: the tcgen05 kernel at 3 CTAs per SM).
+  // the encoder and head layer 0 (global and sliding window) and the mma.sync kernel
+  // (attention.cuh) on the pruned head rows (1 + kmax queries per row), where its 64-row tiles
+  // waste less; `attn=tc|mma` force one kernel everywhere.
   enum AttnMode { ATTN_AUTO, ATTN_TC, ATTN_MMA } attn_mode = ATTN_AUTO;
-  int attn_tc_ctas = 2;
   int cap_T = 0, cap_R = 0;
   DevBuf h, x, qkv, att, act;          // [cap_T, ...]
   DevBuf h2;                           // head residual stream [cap_T, d] fp32
@@ -1047,8 +1046,7 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
   auto attn = [&](const char* name, const CUtensorMap& tq, const CUtensorMap& tkv, int q_col0, int k_col0,
                   int v_col0, const bf16* q, const bf16* k, const bf16* v, bf16* o, int qs, int ks, int vs, int os,
                   bool rows, int window, double pairs) {
-    const bool tc = B.attn_mode == s1c_backend::ATTN_TC ||
-                    (B.attn_mode == s1c_backend::ATTN_AUTO && !rows && window < 0);
+    const bool tc = B.attn_mode == s1c_backend::ATTN_TC || (B.attn_mode == s1c_backend::ATTN_AUTO && !rows);
     const int4* items = tc ? (rows ? dm.items_rows_tc : dm.items_full_tc) : (rows ? dm.items_rows : dm.items_full);
     const int n_items = (int)(tc ? (rows ? m.items_rows_tc.size() : m.items_full_tc.size())
                                  : (rows ? m.items_rows.size() : m.items_full.size()));
@@ -1057,10 +1055,7 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
       AttnTcArgs a{dm.cu, items, o, os, q_col0, k_col0, v_col0, d / 64, window, scale_log2, B.d_status};
       launch(B, nl, name, 4.0 * d * pairs, 0, [&] {
         const dim3 grid((unsigned)n_items * ((d / 64 + ATTC_HEADS - 1) / ATTC_HEADS));
-        if (B.attn_tc_ctas == 3)
-          launch_k(attention_tc_kernel<3>, grid, dim3(ATTC_THREADS), ATTC_SMEM, st, tq, tkv, a);
-        else
-          launch_k(attention_tc_kernel<2>, grid, dim3(ATTC_THREADS), ATTC_SMEM, st, tq, tkv, a);
+        launch_k(attention_tc_kernel, grid, dim3(ATTC_THREADS), ATTC_SMEM, st, tq, tkv, a);
       });
     } else {
       AttnArgs a{q, k, v, o, qs, ks, vs, os, dm.cu, items, window, scale_log2, d / 64};
@@ -1391,16 +1386,9 @@ void apply_settings(s1c_backend& B, const char* spec) {
       else if (v == "csk") B.gemm_variant = 4;
       else throw S1cError(S1C_ERR_CONFIG, "settings: `" + kv + "`: `" + v + "` is not one of auto, 1cta, 2cta, splitk, csk");
     } else if (k == "attn") {
-      if (v == "auto") {
-        B.attn_mode = s1c_backend::ATTN_AUTO;
-        B.attn_tc_ctas = 2;
-      } else if (v == "tc") {
-        B.attn_mode = s1c_backend::ATTN_TC;
-        B.attn_tc_ctas = 2;
-      } else if (v == "tc3") {
-        B.attn_mode = s1c_backend::ATTN_TC;
-        B.attn_tc_ctas = 3;
-      } else if (v == "mma") B.attn_mode = s1c_backend::ATTN_MMA;
+      if (v == "auto") B.attn_mode = s1c_backend::ATTN_AUTO;
+      else if (v == "tc") B.attn_mode = s1c_backend::ATTN_TC;
+      else if (v == "mma") B.attn_mode = s1c_backend::ATTN_MMA;
       else throw S1cError(S1C_ERR_CONFIG, "settings: `" + kv + "`: `" + v + "` is not one of tc, mma");
     } else {
       throw S1cError(S1C_ERR_CONFIG, "settings: unknown setting `" + k + "`");
@@ -1502,8 +1490,7 @@ s1c_status s1c_create(const s1c_model_desc* desc, const s1c_tensor* tensors, int
     CK(cudaStreamCreateWithFlags(&b->own_stream, cudaStreamNonBlocking));
     b->stream = b->own_stream;
     set_all_gemm_smem();
-    CK(cudaFuncSetAttribute(attention_tc_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATTC_SMEM));
-    CK(cudaFuncSetAttribute(attention_tc_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATTC_SMEM));
+    CK(cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATTC_SMEM));
     apply_settings(*b, std::getenv("S1C_SETTINGS"));
     build(*b, *desc, tensors, n_tensors);
     CK(cudaDeviceSynchronize());
@@ -1717,14 +1704,14 @@ s1c_status s1c_attention(const void* d_q, const void* d_k, const void* d_v, void
   static AttnScratch scratch[64];
   std::lock_guard<std::mutex> guard(mu);
   try {
-    if (!d_q || !d_k || !d_v || !d_o || !cu_seqlens || n <= 0 || heads <= 0 || impl < 0 || impl > 2)
+    if (!d_q || !d_k || !d_v || !d_o || !cu_seqlens || n <= 0 || heads <= 0 || (impl != 0 && impl != 1))
       throw S1cError(S1C_ERR_ARG, "bad attention arguments");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     int dev = 0;
     CK(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) throw S1cError(S1C_ERR_ARG, "device index out of range");
     AttnScratch& sc = scratch[dev];
-    const int qtile = impl != 1 ? ATTC_BQ : ATT_BQ;
+    const int qtile = impl == 0 ? ATTC_BQ : ATT_BQ;
     std::vector<int4> items;
     for (int r = 0; r < n; ++r) {
       const int base = cu_seqlens[r], len = cu_seqlens[r + 1] - base;
@@ -1752,15 +1739,14 @@ s1c_status s1c_attention(const void* d_q, const void* d_k, const void* d_v, void
     CK(cudaMemcpyAsync(d_cu, cu_seqlens, ((size_t)n + 1) * 4, cudaMemcpyHostToDevice, st));
     CK(cudaMemcpyAsync(d_items, items.data(), items.size() * 16, cudaMemcpyHostToDevice, st));
     const float scale_log2 = scale * 1.4426950408889634f;
-    if (impl != 1) {
+    if (impl == 0) {
       // one map for Q, one for K and V together: V must sit in K's rows at a 64-aligned column
       const ptrdiff_t dv = static_cast<const bf16*>(d_v) - static_cast<const bf16*>(d_k);
       if (v_stride != k_stride || dv < 0 || dv % 64 || dv + heads * 64 > k_stride)
         throw S1cError(S1C_ERR_ARG, "tcgen05 attention needs v in the rows of k (same pitch, 64-aligned column)");
       static bool attr_set[64] = {false};
       if (!attr_set[dev]) {
-        CK(cudaFuncSetAttribute(attention_tc_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATTC_SMEM));
-        CK(cudaFuncSetAttribute(attention_tc_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATTC_SMEM));
+        CK(cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATTC_SMEM));
         attr_set[dev] = true;
       }
       int* d_status = sc.d_status;
@@ -1769,10 +1755,7 @@ s1c_status s1c_attention(const void* d_q, const void* d_k, const void* d_v, void
       const CUtensorMap tkv = make_tmap(d_k, T, dv + heads * 64, k_stride, ATTC_BK);
       AttnTcArgs a{d_cu, d_items, static_cast<bf16*>(d_o), o_stride, 0, 0, (int)dv, heads, window, scale_log2, d_status};
       const dim3 grid((unsigned)items.size() * ((heads + ATTC_HEADS - 1) / ATTC_HEADS));
-      if (impl == 2)
-        launch_k(attention_tc_kernel<3>, grid, dim3(ATTC_THREADS), ATTC_SMEM, st, tq, tkv, a);
-      else
-        launch_k(attention_tc_kernel<2>, grid, dim3(ATTC_THREADS), ATTC_SMEM, st, tq, tkv, a);
+      launch_k(attention_tc_kernel, grid, dim3(ATTC_THREADS), ATTC_SMEM, st, tq, tkv, a);
       cudaError_t e = cudaGetLastError();
       cudaError_t e2 = cudaStreamSynchronize(st);
       int hs = 0;

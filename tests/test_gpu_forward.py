@@ -106,7 +106,7 @@ def test_large_model_long_rows(cuda_lib):
     check_against_oracle(cfg, w, be, batch)
 
 
-@pytest.mark.parametrize("mode", ["tc", "tc3", "mma"])
+@pytest.mark.parametrize("mode", ["tc", "mma"])
 def test_attention_settings_match_oracle(cuda_lib, mode):
     """The forward with each attention setting forced everywhere (the default `attn=auto` mixes the
     tcgen05 kernel on full rows with the mma.sync kernel on the window and the pruned head rows)."""

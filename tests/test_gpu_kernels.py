@@ -154,7 +154,7 @@ def _attn_ref(q, k, v, cu, window, scale, heads):
     return out
 
 
-@pytest.mark.parametrize("impl", [1, 0, 2])
+@pytest.mark.parametrize("impl", [1, 0])
 @pytest.mark.parametrize("window", [-1, 64, 3])
 def test_attention_varlen_matches_torch(cuda_lib, window, impl):
     from sys1rust_b200.backend import attention
@@ -170,7 +170,7 @@ def test_attention_varlen_matches_torch(cuda_lib, window, impl):
     assert _rel_err(o, ref) < 1e-2
 
 
-@pytest.mark.parametrize("impl", [1, 0, 2])
+@pytest.mark.parametrize("impl", [1, 0])
 @pytest.mark.parametrize("window", [-1, 64])
 def test_attention_growing_scores(cuda_lib, window, impl):
     """Scores with a spread of tens (q, k scaled by 4) whose maximum grows along the row (keys
