@@ -479,9 +479,9 @@ struct s1c_backend {
   int gemm_variant = 0;   // `gemm=auto|1cta|2cta|splitk|csk`
   bool pdl = true;        // `pdl=0|1`: programmatic dependent launch between the forward's kernels
   // Attention kernel per call: `attn=auto` (default) runs the tcgen05 kernel (attention_tc.cuh) on
-  // the encoder and head layer 0 (global and sliding window) and the mma.sync kernel
-  // (attention.cuh) on the pruned head rows (1 + kmax queries per row), where its 64-row tiles
-  // waste less; `attn=tc|mma` force one kernel everywhere.
+  // the encoder and head layer 0 (global and sliding window) when its grid fills the SMs, and the
+  // mma.sync kernel (attention.cuh) on the pruned head rows (1 + kmax queries per row, where its
+  // 64-row tiles waste less) and on small batches; `attn=tc|mma` force one kernel everywhere.
   enum AttnMode { ATTN_AUTO, ATTN_TC, ATTN_MMA } attn_mode = ATTN_AUTO;
   int cap_T = 0, cap_R = 0;
   DevBuf h, x, qkv, att, act;          // [cap_T, ...]
@@ -1046,7 +1046,12 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
   auto attn = [&](const char* name, const CUtensorMap& tq, const CUtensorMap& tkv, int q_col0, int k_col0,
                   int v_col0, const bf16* q, const bf16* k, const bf16* v, bf16* o, int qs, int ks, int vs, int os,
                   bool rows, int window, double pairs) {
-    const bool tc = B.attn_mode == s1c_backend::ATTN_TC || (B.attn_mode == s1c_backend::ATTN_AUTO && !rows);
+    // auto: the tcgen05 kernel when its grid (query tiles of 128 x groups of ATTC_HEADS heads) fills
+    // the SMs; below that (single short requests) the mma.sync kernel's 64-row, one-head blocks
+    // spread the work wider
+    const size_t tc_blocks = m.items_full_tc.size() * (size_t)((d / 64 + ATTC_HEADS - 1) / ATTC_HEADS);
+    const bool tc = B.attn_mode == s1c_backend::ATTN_TC ||
+                    (B.attn_mode == s1c_backend::ATTN_AUTO && !rows && tc_blocks >= (size_t)nsm);
     const int4* items = tc ? (rows ? dm.items_rows_tc : dm.items_full_tc) : (rows ? dm.items_rows : dm.items_full);
     const int n_items = (int)(tc ? (rows ? m.items_rows_tc.size() : m.items_full_tc.size())
                                  : (rows ? m.items_rows.size() : m.items_full.size()));

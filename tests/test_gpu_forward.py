@@ -106,14 +106,15 @@ def test_large_model_long_rows(cuda_lib):
     check_against_oracle(cfg, w, be, batch)
 
 
-@pytest.mark.parametrize("mode", ["tc", "mma"])
-def test_attention_settings_match_oracle(cuda_lib, mode):
-    """The forward with each attention setting forced everywhere (the default `attn=auto` mixes the
-    tcgen05 kernel on full rows with the mma.sync kernel on the window and the pruned head rows)."""
+@pytest.mark.parametrize("model,mode", [("small:3", "tc"), ("small:3", "mma"), ("large:0", "tc")])
+def test_attention_settings_match_oracle(cuda_lib, model, mode):
+    """The forward with each attention setting forced everywhere (the default `attn=auto` runs the
+    tcgen05 kernel on full rows when its grid fills the SMs, else and on the pruned head rows the
+    mma.sync kernel)."""
     import os
     from sys1rust_b200.backend import CudaBackend
     from conftest import get_backend
-    cfg, w, _ = get_backend("small:3")
+    cfg, w, _ = get_backend(model)
     old = os.environ.get("S1C_SETTINGS")
     os.environ["S1C_SETTINGS"] = (old + "," if old else "") + f"attn={mode}"
     try:
