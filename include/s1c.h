@@ -106,7 +106,11 @@ typedef struct s1c_backend s1c_backend;
 
 /* Build a backend on `device` from named tensors: replaces `MlxBackend::new`
  * (laya-mlx/src/lib.rs:960-1150) / the factory `make_backend` (lib.rs:593-604). Converts every
- * matrix to bf16 and every vector to fp32, interleaves Wi for the GeGLU epilogue, uploads. */
+ * matrix to bf16 and every vector to fp32, interleaves Wi for the GeGLU epilogue, uploads.
+ * The environment variable S1C_SETTINGS, read here, is a comma list of kernel choices (an unknown
+ * key or value fails the call with S1C_ERR_CONFIG): attn=auto|tc|mma (attention kernel; auto:
+ * tcgen05 on full rows when its grid fills the SMs, else mma.sync), gemm=auto|1cta|2cta|splitk|csk,
+ * graphs=0|1 (CUDA graph per batch shape), pdl=0|1 (programmatic dependent launch). */
 S1C_API s1c_status s1c_create(const s1c_model_desc* desc, const s1c_tensor* tensors, int32_t n_tensors, int32_t device,
                       s1c_backend** out);
 S1C_API void s1c_destroy(s1c_backend* b);

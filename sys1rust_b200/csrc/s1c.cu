@@ -1361,8 +1361,8 @@ void pack_batch(const s1c_batch& b, PackedBatch& p) {
 }
 
 // Backend settings, a strict comma list like the reference's `Knobs` (laya-mlx/src/lib.rs:155-259):
-// an unknown key or value is an error naming it. Keys: attn=tc|mma, gemm=auto|1cta|2cta, graphs=0|1,
-// pdl=0|1.
+// an unknown key or value is an error naming it. Keys: attn=auto|tc|mma,
+// gemm=auto|1cta|2cta|splitk|csk, graphs=0|1, pdl=0|1.
 void apply_settings(s1c_backend& B, const char* spec) {
   if (!spec) return;
   std::string s(spec);
