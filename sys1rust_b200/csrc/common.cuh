@@ -226,6 +226,26 @@ S1C_DEV void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Packed pairs of fp32 for Blackwell's f32x2 arithmetic (one FMA / MUL instruction per pair, each
+// lane rounded exactly like the scalar instruction).
+S1C_DEV uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+S1C_DEV uint64_t f2_splat(float v) { return f2_pack(v, v); }
+S1C_DEV void f2_unpack(uint64_t v, float& lo, float& hi) { asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v)); }
+S1C_DEV uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+S1C_DEV uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
 // Shared-memory matrix descriptor for a K-major bf16 tile written by TMA with 128-byte
 // swizzling: rows of 64 elements (128 B), 8-row swizzle atoms of 1024 B stacked along M/N
 // (stride byte offset 1024). The tile base must be 1024-byte aligned; stepping K by 16
