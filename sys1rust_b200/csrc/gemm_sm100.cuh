@@ -334,11 +334,14 @@ __device__ __forceinline__ void gemm_epilogue_tile(const GemmArgs& args, const C
         tmem_ld16(t + hh * 64 + q * 16, lo);
         tmem_ld16(t + hh * 64 + 32 + q * 16, hi);
         if (rope) {
+          // lo' = a cos - b sin, hi' = a sin + b cos on packed pairs of columns (f32x2)
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const float a = lo[j], b = hi[j];
-            lo[j] = a * cs[q * 16 + j] - b * sn[q * 16 + j];
-            hi[j] = a * sn[q * 16 + j] + b * cs[q * 16 + j];
+          for (int j = 0; j < 16; j += 2) {
+            const uint64_t a = f2_pack(lo[j], lo[j + 1]), b = f2_pack(hi[j], hi[j + 1]);
+            const uint64_t c = f2_pack(cs[q * 16 + j], cs[q * 16 + j + 1]);
+            const uint64_t sv = f2_pack(sn[q * 16 + j], sn[q * 16 + j + 1]);
+            f2_unpack(f2_fma(a, c, f2_mul(f2_pack(-hi[j], -hi[j + 1]), sv)), lo[j], lo[j + 1]);
+            f2_unpack(f2_fma(a, sv, f2_mul(b, c)), hi[j], hi[j + 1]);
           }
         }
         sg.put_bf16x16(buf, 2 * q, lo);
