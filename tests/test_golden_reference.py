@@ -76,6 +76,35 @@ def test_window_key_idx_formula():
         assert len(idx) == rows * nc * 3 * s
 
 
+def test_chunked_mask_tables_equal_the_varlen_window_rule():
+    """The reference's chunked local-attention masks on its own padded fixture (``chunked_mask``):
+    key slot j of chunk c is position (c - 1) S + j, valid when inside the row's real tokens; the
+    band allows i + 2S >= j >= i; a padded query row is all true. For every real query the allowed
+    positions are exactly the key range the varlen kernels compute from the row bounds,
+    [max(0, q - w), min(len_b, q + w + 1)) with w = S (attention_tc.cuh / attention.cuh), and no
+    query row is empty."""
+    g = GOLD["chunked_mask"]
+    mask, n, L, S, nc = np.array(g["mask"]), g["n"], g["len"], g["s"], g["nc"]
+    for b in range(n):
+        real = int(mask[b * L:(b + 1) * L].sum())  # right-padded rows: real tokens [0, real)
+        for c in range(nc):
+            slots = [(c - 1) * S + j for j in range(3 * S)]
+            key_ok = [0 <= p < L and mask[b * L + p] == 1 for p in slots]
+            for i in range(S):
+                q = c * S + i
+                padded = q >= L or mask[b * L + q] != 1
+                band = [i + 2 * S >= j >= i for j in range(3 * S)]
+                row = [(k and bd) or padded for k, bd in zip(key_ok, band)]
+                assert any(row), (b, q)
+                if not padded:
+                    got = {p for p, v in zip(slots, row) if v}
+                    k_lo, k_hi = max(0, q - S), min(real, q + S + 1)
+                    assert got == set(range(k_lo, k_hi)), (b, q, got)
+    # row 1's last chunk holds padding only
+    b, c = 1, 3
+    assert not any(0 <= (c - 1) * S + j < L and mask[b * L + (c - 1) * S + j] == 1 for j in range(3 * S))
+
+
 def test_head_scale_matches_reference():
     for hidden, heads, want in GOLD["head_scale"]["cases"]:
         got = float(np.float32(1.0) / np.sqrt(np.float32(hidden // heads)))
