@@ -135,6 +135,19 @@ class ClockSampler:
         return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def arm_config(world: int, tokens_total: int, n_batches: int) -> dict:
+    """The workload both arms report (the reference arm runs a bounded sample of it)."""
+    return {"workload": f"cfg5 shard: {REQ_PER_GPU} lognormal requests per GPU (first "
+                        f"{REQ_PER_GPU * world} of cfg5's stream, LPT by tokens), varlen batches "
+                        f"<= {BATCH_TOKENS} tokens, full forward (encoder + head + scorer)",
+            "model": "ModernBERT-large encoder (28 layers, d 1024, 16x64 heads, GeGLU 2x2624) + "
+                     "2 decision-head layers + scorer, seeded N(0,0.02) bf16 weights",
+            "tokens_per_step": tokens_total, "batches_per_gpu_step": n_batches,
+            "l2": "inputs larger than L2: 686 MB of encoder weights stream every forward",
+            "parallelism": f"dp{world} replicas, no data-path collective",
+            "streams_per_gpu": 2}
+
+
 def run_reference(args):
     """The reference arm: the CPU restatement of the forward (the reference's MLX-CPU path does
     not build here), all host threads, on this arm's workload, each step a bounded sample."""
@@ -145,7 +158,11 @@ def run_reference(args):
     from sys1rust_b200.weights import SyntheticWeights
     cfg = large_model()
     w = SyntheticWeights(cfg, seed=0)
-    _, mine = workload(1, 0)
+    all_reqs, mine = workload(world, 0)
+    from sys1rust_b200.workloads import pack_batches
+    config = arm_config(world, sum(len(r.ids) for r in all_reqs), len(pack_batches(mine, BATCH_TOKENS)))
+    config["reference_arm"] = ("rank 0 times the CPU restatement of the forward on a bounded sample of "
+                               "this shard's requests, one row per forward, all host threads")
     vals = []
     steps = args.steps
     per_step = max(2.0, min(20.0, 90.0 / max(steps + args.warmup, 1)))
@@ -158,8 +175,7 @@ def run_reference(args):
         "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": world,
         "steps": steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"cfg5 shard sample ({REQ_PER_GPU} lognormal requests per GPU), one row per forward",
-                   "model": "ModernBERT-large encoder + decision head + scorer (seeded weights)"},
+        "config": config,
         "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": info["cores"], "kind": "port",
                          "sample": f"~{per_step:.0f} s of requests per step ({info['requests']} requests, "
                                    f"{info['tokens']} tokens in the last step); the reference's MLX-CPU path "
@@ -396,15 +412,7 @@ def main():
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic",
-            "config": {"workload": f"cfg5 shard: {REQ_PER_GPU} lognormal requests per GPU (first "
-                                   f"{REQ_PER_GPU * world} of cfg5's stream, LPT by tokens), varlen batches "
-                                   f"<= {BATCH_TOKENS} tokens, full forward (encoder + head + scorer)",
-                       "model": "ModernBERT-large encoder (28 layers, d 1024, 16x64 heads, GeGLU 2x2624) + "
-                                "2 decision-head layers + scorer, seeded N(0,0.02) bf16 weights",
-                       "tokens_per_step": tokens_total, "batches_per_gpu_step": len(batches),
-                       "l2": "inputs larger than L2: 686 MB of encoder weights stream every forward",
-                       "parallelism": f"dp{world} replicas, no data-path collective",
-                       "streams_per_gpu": 2},
+            "config": arm_config(world, tokens_total, len(batches)),
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h), "steps": e2e_steps,
                     "path": "sys1rust_b200.server.Server (s1c_server_*): the step's requests submitted one by one "
