@@ -204,6 +204,14 @@ S1C_API s1c_status s1c_gemm_splitk_noalloc(int32_t epi, const void* d_A, const v
                                            const int32_t* d_pos, float rope_theta, int32_t rope_cols,
                                            int32_t out_cols, void* stream);
 
+/* Self-test of the device-side failure detection: a kernel waits, with a budget of `budget_ns`
+ * (1e6 .. 2e9), on an mbarrier that nothing completes, once in the single-thread form the TMA and
+ * MMA roles use and once in the warp form the epilogue / softmax roles use. Both waits must give up
+ * and return. codes[0] / codes[1] receive the status codes they recorded (1 and 4, the codes a
+ * forward reports inside S1C_ERR_DEVICE_TIMEOUT), codes[2] / codes[3] whether each wait claimed
+ * success (0). Returns S1C_OK when the kernel ended; the device stays usable. */
+S1C_API s1c_status s1c_selftest_wait_timeout(int32_t device, int64_t budget_ns, int32_t* codes);
+
 /* Number of this library's kernel launches the last forward on this handle enqueued. */
 S1C_API int64_t s1c_last_launch_count(const s1c_backend* b);
 

@@ -153,6 +153,7 @@ def lib() -> C.CDLL:
         "s1c_server_stop": (None, [P]),
         "s1c_server_destroy": (None, [P]),
         "s1c_decode": (I32, [P, P, I32, I32, I32, P, P, P, C.POINTER(CActHead), P, C.POINTER(CAnswer)]),
+        "s1c_selftest_wait_timeout": (I32, [I32, I64, C.POINTER(C.c_int32)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -478,6 +479,17 @@ def attention(q_ptr: int, k_ptr: int, v_ptr: int, o_ptr: int, q_stride: int, k_s
                          len(cu) - 1, window, scale, impl, stream or None)
     if rc != S1C_OK:
         _raise(rc, L.s1c_create_error().decode())
+
+
+def selftest_wait_timeout(device: int = 0, budget_ns: int = 50_000_000) -> list:
+    """Run the bounded-wait self-test kernel (``s1c_selftest_wait_timeout``): returns the four result
+    words [single-thread wait code, warp wait code, single-thread success, warp success]."""
+    L = lib()
+    codes = (C.c_int32 * 4)()
+    rc = L.s1c_selftest_wait_timeout(device, budget_ns, codes)
+    if rc != S1C_OK:
+        _raise(rc, L.s1c_create_error().decode())
+    return list(codes)
 
 
 def interleave_wi(wi: np.ndarray, I: int) -> np.ndarray:

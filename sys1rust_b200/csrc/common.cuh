@@ -95,7 +95,8 @@ S1C_DEV bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 // Wait for the phase with the given parity to complete; false when the wait budget ran out
 // (the status word then holds `code`) or another role already gave up (`abort` set).
-S1C_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code, volatile int* abort) {
+S1C_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code, volatile int* abort,
+                       uint64_t budget_ns = S1C_WAIT_BUDGET_NS) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   const uint64_t t0 = globaltimer();
@@ -103,7 +104,7 @@ S1C_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code, vo
     if (mbar_try_wait(a, parity)) return true;
     if ((it & 63u) == 0) {
       if (abort && *abort) return false;
-      if (globaltimer() - t0 > S1C_WAIT_BUDGET_NS) {
+      if (globaltimer() - t0 > budget_ns) {
         report(status, code);
         if (abort) *abort = 1;
         return false;
@@ -113,7 +114,8 @@ S1C_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code, vo
 }
 
 // Warp-collective bounded wait: every lane polls, the warp leaves together.
-S1C_DEV bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int* status, int code, volatile int* abort) {
+S1C_DEV bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int* status, int code, volatile int* abort,
+                            uint64_t budget_ns = S1C_WAIT_BUDGET_NS) {
   const uint32_t a = smem_u32(bar);
   const int lane = threadIdx.x & 31;
   uint64_t t0 = 0;
@@ -125,7 +127,7 @@ S1C_DEV bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int* status, int cod
       if (lane == 0) {
         const uint64_t now = globaltimer();
         if (t0 == 0) t0 = now;
-        if ((abort && *abort) || now - t0 > S1C_WAIT_BUDGET_NS) give_up = 1;
+        if ((abort && *abort) || now - t0 > budget_ns) give_up = 1;
       }
       give_up = __shfl_sync(0xffffffffu, give_up, 0);
       if (give_up) {

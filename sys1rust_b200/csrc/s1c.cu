@@ -1785,6 +1785,49 @@ s1c_status s1c_attention(const void* d_q, const void* d_k, const void* d_v, void
   }
 }
 
+// Self-test of the bounded device waits: an mbarrier that nothing completes, waited on by one
+// thread (mbar_wait, the producer / MMA form) and by one warp (mbar_wait_warp, the epilogue form)
+// with a short budget. Each wait must give up, record its code in its status word and return, so
+// the kernel ends and the context stays usable. Touches nothing but its four result words.
+__global__ void wait_timeout_selftest_kernel(int* out, uint64_t budget_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const bool done = mbar_wait(&bar, 0, out + 0, DEV_TIMEOUT_PRODUCER, nullptr, budget_ns);
+    out[2] = done ? 1 : 0;
+  } else if (threadIdx.x >= 32) {
+    const bool done = mbar_wait_warp(&bar, 0, out + 1, DEV_TIMEOUT_EPILOGUE, nullptr, budget_ns);
+    if (threadIdx.x == 32) out[3] = done ? 1 : 0;
+  }
+}
+
+s1c_status s1c_selftest_wait_timeout(int32_t device, int64_t budget_ns, int32_t* codes) {
+  try {
+    if (!codes || budget_ns < 1000000 || budget_ns > 2000000000)
+      throw S1cError(S1C_ERR_ARG, "budget_ns must lie in [1e6, 2e9] and codes must not be null");
+    CK(cudaSetDevice(device));
+    int* d_out = nullptr;
+    CK(cudaMalloc(&d_out, 4 * sizeof(int)));
+    cudaError_t e = cudaMemset(d_out, 0, 4 * sizeof(int));
+    if (e == cudaSuccess) {
+      wait_timeout_selftest_kernel<<<1, 64>>>(d_out, (uint64_t)budget_ns);
+      e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpy(codes, d_out, 4 * sizeof(int), cudaMemcpyDeviceToHost);
+    cudaFree(d_out);
+    if (e != cudaSuccess) throw S1cError(S1C_ERR_CUDA, cudaGetErrorString(e));
+    return S1C_OK;
+  } catch (const S1cError& e) {
+    g_create_error = e.what();
+    return e.code;
+  }
+}
+
 s1c_status s1c_gemm_splitk_noalloc(int32_t epi, const void* d_A, const void* d_B, void* d_out, int32_t M, int32_t N,
                                    int32_t K, const float* d_bias, int32_t act, int32_t out_f32, const int32_t* d_pos,
                                    float rope_theta, int32_t rope_cols, int32_t out_cols, void* stream) {
