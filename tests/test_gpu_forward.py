@@ -185,6 +185,13 @@ def test_batch_without_markers(cuda_lib):
     assert out.logits.size == 0 and out.pooled.size == 2 * cfg.encoder.hidden_size
     _, po, _ = oracle(cfg, w, batch)
     assert np.linalg.norm(out.pooled - po) / np.linalg.norm(po) < 5e-2
+    # an empty batch is a no-op on both entry points
+    empty = collate_to([], cfg.encoder.pad_token_id)
+    assert empty.n == 0
+    out = be.forward(empty)
+    assert out.logits.size == 0 and out.pooled.size == 0
+    out = be.forward_varlen(Varlen.from_rows([]))
+    assert out.logits.size == 0 and out.pooled.size == 0
 
 
 def test_malformed_batches_are_errors(cuda_lib):
