@@ -297,8 +297,8 @@ void launch_csk(const CUtensorMap& ta, const WeightMap& tb, const GemmArgs& g, c
   }
 }
 
-// GEMM variant: 0 = by shape (cluster split-K when there are few tiles and an output context is
-// given, else the one-CTA 128 x 256 kernel), 1 = one-CTA 128 x 256, 2 = two-CTA, 3 = one-CTA split-K
+// GEMM variant: 0 = by shape (cluster split-K when there are few tiles, an output context is
+// given and K splits over a cluster, else the one- or two-CTA kernel), 1 = one-CTA 128 x 256, 2 = two-CTA, 3 = one-CTA split-K
 // through the fp32 workspace and a finalize kernel (at least 2 splits), 4 = cluster split-K,
 // 5 = one-CTA 128 x 128 (not for GeGLU). The 128 x 128 tiles would fill the last wave of the SMs
 // better on N = 1024 (6.92 instead of 3.46 waves at 16k tokens) but measured 22 % slower there
@@ -309,8 +309,14 @@ void launch_gemm(const CUtensorMap& ta, const WeightMap& tb, const CUtensorMap& 
   if (a0.M <= 0) return;
   GemmArgs a = a0;
   a.k_splits = 1;
-  // Few output tiles (small token counts): the cluster split-K kernel, one launch per GEMM.
-  if (sk && (variant == 4 || (variant == 0 && ((a.M + GEMM_BM - 1) / GEMM_BM) * ((a.N + GEMM_BN - 1) / GEMM_BN) * 2 <= num_sms))) {
+  // Few output tiles (small token counts): the cluster split-K kernel, one launch per GEMM, when
+  // its plan really splits K over a cluster (C >= 2). With C = 1 every CTA would walk the whole K
+  // range of a 128-wide tile: the plain kernels are faster there (measured at 16k-SM scale: Wqkv
+  // M = 512 9.8 vs 20.6 us, Wo2 M = 2048 18.6 vs 39.0 us).
+  bool csk = sk && variant == 4;
+  if (sk && variant == 0 && ((a.M + GEMM_BM - 1) / GEMM_BM) * ((a.N + GEMM_BN - 1) / GEMM_BN) * 2 <= num_sms)
+    csk = plan_csk(a.M, a.N, a.K, num_sms, EPI == EPI_GEGLU).C >= 2;
+  if (csk) {
     launch_csk<EPI>(ta, tb, a, *sk, num_sms, st);
     CK(cudaGetLastError());
     return;
