@@ -11,10 +11,15 @@ tokens (LPT): weak scaling, and at N = 8 exactly cfg5's 8192 requests. Ranks sha
 data path (replicas, no collective); the barrier and the max-over-ranks reduction are the only
 collectives. ``value`` is the whole job's tokens / max-over-ranks device time.
 
-Rank 0 prints one JSON line. Extra keys: ``e2e`` (the same metric through the host-buffer C ABI,
-copies included), ``roofline`` (dominant kernel, from per-launch CUDA events over the timed
-region), ``cpu_baseline`` (the CPU oracle on a bounded sample, N = 1 only), ``latency_cfg1`` (p50 ms
-of one 128-token request through the host API), ``clocks`` (nvidia-smi during the timed region).
+Each GPU runs two handles of the model on two streams and alternates its batches between them.
+Rank 0 prints one JSON line. Extra keys: ``e2e`` (the same requests submitted one by one from host
+arrays to the serving queue, one native worker per handle, copies and result collection included;
+``e2e_batched``: the pre-packed batches through ``s1c_forward_varlen``), ``roofline`` (dominant
+kernel, from per-launch CUDA events over a second, single-stream pass of the timed steps),
+``cpu_baseline`` (the PyTorch oracle on a bounded sample, with the C restatement beside it; N = 1
+only), ``latency_cfg1`` (p50 ms of one 128-token request through the host API), ``cfg3_tokens_per_s``,
+``clocks`` (nvidia-smi during the timed region), ``gpu_launches`` (this library's launches in the
+timed region).
 """
 from __future__ import annotations
 
@@ -32,7 +37,7 @@ sys.path.insert(0, ROOT)
 
 METRIC = "encoder tokens/sec/GPU (packed varlen) at 1/2/4/8 B200; p50 ms per 128-tok request"
 # DRAM bytes (read + write) per algorithmic FLOP of a kernel, from one ncu capture
-# (profiles/gemm_wi_geglu_M16384.md: 84.49 MB for 176.09 GFLOP at M = 16384); a launch's traffic is
+# (profiles/gemm_wi_geglu_M16384.md: 84.8 MB for 176.09 GFLOP at M = 16384); a launch's traffic is
 # this times its FLOPs.
 DRAM_BYTES_PER_FLOP = {"gemm_wi_geglu": 84.80e6 / 176.09e9}
 REQ_PER_GPU = 1024
