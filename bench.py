@@ -36,9 +36,8 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "encoder tokens/sec/GPU (packed varlen) at 1/2/4/8 B200; p50 ms per 128-tok request"
-# DRAM bytes (read + write) per algorithmic FLOP of a kernel, from one ncu capture
-# (profiles/gemm_wi_geglu_M16384.md: 84.8 MB for 176.09 GFLOP at M = 16384); a launch's traffic is
-# this times its FLOPs.
+# DRAM bytes (read + write) per algorithmic FLOP of a kernel, from one ncu capture of the Wi + GeGLU
+# GEMM at M = 16384 (84.8 MB for 176.09 GFLOP); a launch's traffic is this times its FLOPs.
 DRAM_BYTES_PER_FLOP = {"gemm_wi_geglu": 84.80e6 / 176.09e9}
 REQ_PER_GPU = 1024
 BATCH_TOKENS = 16384

@@ -1,7 +1,7 @@
 """The C structs of ``include/s1c.h`` and their ctypes mirrors in ``sys1rust_b200.backend`` have the
 same size and field offsets: a probe compiled with the system C compiler against the header prints
-``sizeof`` / ``offsetof`` for every field, and the test compares them with ctypes. This is the
-layout the reference-side FFI binding (``INTEGRATION.md``) relies on as well."""
+``sizeof`` / ``offsetof`` for every field, and the test compares them with ctypes. A Rust FFI
+binding of the header relies on the same layout."""
 import os
 import shutil
 import subprocess
