@@ -1,5 +1,5 @@
 // The serving front of the library: a request queue in front of one worker thread per GPU that
-// packs queued requests from many clients into varlen batches (SURVEY "next" row 1).
+// packs queued requests from many clients into varlen batches.
 //
 // It keeps the reference server's contract (runtime/crates/sys1rust/src/worker.rs,
 // runtime/crates/sys1rust/src/http.rs:168-230) and replaces its one-request-at-a-time inference
