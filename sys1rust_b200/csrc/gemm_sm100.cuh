@@ -243,10 +243,35 @@ __device__ __forceinline__ void gemm_epilogue_partial(const GemmArgs& args, cons
   }
 }
 
+// cos / sin of one row's RoPE angles (32 pairs, the angle p * inv_freq[j] formed in fp32,
+// split_rope.metal:46-76), fetched for a tile before its accumulator is ready so that the table's
+// latency overlaps the tile's MMAs: from the per-position table, else by sincosf. Tiles of the v
+// columns (n0 >= rope_cols) fetch nothing.
+struct RopeRow {
+  float cs[32], sn[32];
+};
+S1C_DEV void rope_prefetch(const GemmArgs& args, int row, bool m_ok, int n0, RopeRow& rr) {
+  if (n0 >= args.rope_cols) return;
+  const int pi = m_ok ? __ldg(args.pos + row) : 0;
+  if (args.rope_tab) {
+    const float4* tb = reinterpret_cast<const float4*>(args.rope_tab + (size_t)pi * 64);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 c4 = __ldg(tb + i), s4 = __ldg(tb + 8 + i);
+      rr.cs[4 * i] = c4.x; rr.cs[4 * i + 1] = c4.y; rr.cs[4 * i + 2] = c4.z; rr.cs[4 * i + 3] = c4.w;
+      rr.sn[4 * i] = s4.x; rr.sn[4 * i + 1] = s4.y; rr.sn[4 * i + 2] = s4.z; rr.sn[4 * i + 3] = s4.w;
+    }
+  } else {
+    const float p = (float)pi;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) sincosf(p * __ldg(args.inv_freq + j), &rr.sn[j], &rr.cs[j]);
+  }
+}
+
 template <int BN, int EPI>
 __device__ __forceinline__ void gemm_epilogue_tile(const GemmArgs& args, const CUtensorMap* tmC, Stager& sg,
                                                    uint32_t t, int row, bool m_ok, int y0, int n0, int n_block,
-                                                   int part, int parts) {
+                                                   int part, int parts, const RopeRow& rr) {
   if constexpr (EPI == EPI_RESID || EPI == EPI_STORE) {
     const bool f32 = (EPI == EPI_RESID) || args.out_f32;
     if (f32) {
@@ -301,27 +326,12 @@ __device__ __forceinline__ void gemm_epilogue_tile(const GemmArgs& args, const C
       }
     }
   } else if constexpr (EPI == EPI_ROPE) {
-    // Rotate-half RoPE of every 64-wide q/k head in the tile at this row's position: the angle is
-    // p * inv_freq[j] in fp32 (split_rope.metal:46-76); its cos/sin are computed once per row and
-    // shared by the tile's heads.
+    // Rotate-half RoPE of every 64-wide q/k head in the tile at this row's position, with the
+    // row's cos / sin (`rr`, fetched by rope_prefetch before the accumulator wait) shared by the
+    // tile's heads.
     const bool rope = n0 < args.rope_cols;  // uniform: q/k tiles never straddle the v columns
-    float cs[32], sn[32];
-    if (rope) {
-      const int pi = m_ok ? __ldg(args.pos + row) : 0;
-      if (args.rope_tab) {
-        const float4* tb = reinterpret_cast<const float4*>(args.rope_tab + (size_t)pi * 64);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float4 c4 = __ldg(tb + i), s4 = __ldg(tb + 8 + i);
-          cs[4 * i] = c4.x; cs[4 * i + 1] = c4.y; cs[4 * i + 2] = c4.z; cs[4 * i + 3] = c4.w;
-          sn[4 * i] = s4.x; sn[4 * i + 1] = s4.y; sn[4 * i + 2] = s4.z; sn[4 * i + 3] = s4.w;
-        }
-      } else {
-        const float p = (float)pi;
-#pragma unroll
-        for (int j = 0; j < 32; ++j) sincosf(p * __ldg(args.inv_freq + j), &sn[j], &cs[j]);
-      }
-    }
+    const float(&cs)[32] = rr.cs;
+    const float(&sn)[32] = rr.sn;
 #pragma unroll 1
     for (int hh = part * (BN / 64) / parts; hh < (part + 1) * (BN / 64) / parts; ++hh) {
       const int col = n0 + hh * 64;
@@ -535,13 +545,18 @@ __global__ void __launch_bounds__(GEMM1_THREADS, 1)
       const int m0 = mb * BM;
       const int y0 = m0 + quad * 32;
       const int row = y0 + lane;
+      RopeRow rr;
+      if constexpr (EPI == EPI_ROPE) {
+        if (ksp == 1) rope_prefetch(args, row, row < args.M, n_block * BN, rr);
+      }
       if (!mbar_wait_warp(&tfull[acc], aph, args.status, DEV_TIMEOUT_EPILOGUE, abort_flag)) break;
       tc_fence_after();
       const uint32_t t = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
       if (ksp > 1)
         gemm_epilogue_partial<BN>(args, &tmC, sg, t, (tile % ksp) * args.split_rows + y0, n_block * BN, part, PARTS);
       else
-        gemm_epilogue_tile<BN, EPI>(args, &tmC, sg, t, row, row < args.M, y0, n_block * BN, n_block, part, PARTS);
+        gemm_epilogue_tile<BN, EPI>(args, &tmC, sg, t, row, row < args.M, y0, n_block * BN, n_block, part, PARTS,
+                                    rr);
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
       acc ^= 1;

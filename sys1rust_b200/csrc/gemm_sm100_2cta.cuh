@@ -214,10 +214,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
       const int m0 = (tile / num_n) * 256 + (int)rank * 128, n_block = tile % num_n;
       const int y0 = m0 + quad * 32;
       const int row = y0 + lane;
+      RopeRow rr;
+      if constexpr (EPI == EPI_ROPE) rope_prefetch(args, row, row < args.M, n_block * BN, rr);
       if (!mbar_wait_warp(&tfull[acc], aph, args.status, DEV_TIMEOUT_EPILOGUE, abort_flag)) break;
       tc_fence_after();
       const uint32_t t = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
-      gemm_epilogue_tile<BN, EPI>(args, &tmC, sg, t, row, row < args.M, y0, n_block * BN, n_block, 0, 1);
+      gemm_epilogue_tile<BN, EPI>(args, &tmC, sg, t, row, row < args.M, y0, n_block * BN, n_block, 0, 1, rr);
       tc_fence_before();
       mbar_arrive_cluster(map_to_rank(smem_u32(&tempty[acc]), 0));
       acc ^= 1;
