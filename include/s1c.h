@@ -42,6 +42,7 @@ typedef int32_t s1c_status;
 #define S1C_ERR_BUSY (-7)           /* serving: admission cap reached, "server busy, try again later" (503, Retry-After: 1) */
 #define S1C_ERR_DEAD (-8)           /* serving: no inference worker, "inference worker is not running" (503) */
 #define S1C_ERR_TIMEOUT (-9)        /* serving: result not ready within the wait's timeout; the ticket stays valid */
+#define S1C_ERR_SELFCHECK (-10)     /* load check: a kernel differs from the plain computation and no checked kernel can take its place */
 
 /* Tensor element types accepted at load (the conversions of laya-core/src/weights.rs:82-115). */
 #define S1C_DT_F32 0
@@ -110,7 +111,17 @@ typedef struct s1c_backend s1c_backend;
  * The environment variable S1C_SETTINGS, read here, is a comma list of kernel choices (an unknown
  * key or value fails the call with S1C_ERR_CONFIG): attn=auto|tc|mma (attention kernel; auto:
  * tcgen05 on full rows when its grid fills the SMs, else mma.sync), gemm=auto|1cta|2cta|splitk|csk,
- * graphs=0|1 (CUDA graph per batch shape), pdl=0|1 (programmatic dependent launch). */
+ * graphs=0|1 (CUDA graph per batch shape), pdl=0|1 (programmatic dependent launch),
+ * check=0|1 (default 1) and check_fail=<kernel>[+<kernel>...].
+ * Load check (the reference's load-time kernel checks and fallback rule, lib.rs:319-362): every
+ * kernel the forward can pick runs once on small seeded problems (GEMMs with each epilogue,
+ * attention global and sliding window over ragged rows) and is compared with a double-precision
+ * host computation, each output element within 1e-2 * (1 + |expected|). A failing two-CTA or
+ * cluster split-K GEMM or tcgen05 attention is turned off for this handle (one stderr line; the
+ * one-CTA GEMM / mma.sync attention take its work; s1c_active_kernels names it); a failing
+ * one-CTA GEMM or mma.sync attention, or a failing kernel forced by the settings, fails the call
+ * with S1C_ERR_SELFCHECK. check_fail (1cta, 2cta, csk, splitk, tc, mma) plants a wrong expected
+ * value in those kernels' checks, for tests of the fallback rule. */
 S1C_API s1c_status s1c_create(const s1c_model_desc* desc, const s1c_tensor* tensors, int32_t n_tensors, int32_t device,
                       s1c_backend** out);
 S1C_API void s1c_destroy(s1c_backend* b);

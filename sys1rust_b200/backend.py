@@ -28,6 +28,7 @@ HEADER = os.path.join(os.path.dirname(HERE), "include", "s1c.h")
 S1C_OK, S1C_ERR_ARG, S1C_ERR_CUDA, S1C_ERR_WEIGHTS, S1C_ERR_CONFIG, S1C_ERR_DEVICE_TIMEOUT, S1C_ERR_UNSUPPORTED = \
     0, -1, -2, -3, -4, -5, -6
 S1C_ERR_BUSY, S1C_ERR_DEAD, S1C_ERR_TIMEOUT = -7, -8, -9
+S1C_ERR_SELFCHECK = -10
 DT_F32, DT_F16, DT_BF16 = 0, 1, 2
 
 

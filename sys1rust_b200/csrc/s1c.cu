@@ -168,6 +168,10 @@ CUtensorMap make_out_tmap(const void* ptr, bool f32, uint64_t rows, uint64_t col
 // common.cuh): the kernel may start while its predecessor drains, and waits on the device before
 // touching the predecessor's data.
 thread_local bool t_pdl = true;
+// GEMM kernels the load check turned off for the handle whose forward is being enqueued on this
+// thread (launch_gemm's shape rule then never picks them).
+constexpr int GEMM_OFF_2CTA = 1, GEMM_OFF_CSK = 2;
+thread_local int t_gemm_off = 0;
 template <typename... P, typename... A>
 void launch_k(void (*kernel)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, A&&... args) {
   cudaLaunchConfig_t cfg = {};
@@ -314,7 +318,8 @@ void launch_gemm(const CUtensorMap& ta, const WeightMap& tb, const CUtensorMap& 
   // range of a 128-wide tile: the plain kernels are faster there (measured at 16k-SM scale: Wqkv
   // M = 512 9.8 vs 20.6 us, Wo2 M = 2048 18.6 vs 39.0 us).
   bool csk = sk && variant == 4;
-  if (sk && variant == 0 && ((a.M + GEMM_BM - 1) / GEMM_BM) * ((a.N + GEMM_BN - 1) / GEMM_BN) * 2 <= num_sms)
+  if (sk && variant == 0 && !(t_gemm_off & GEMM_OFF_CSK) &&
+      ((a.M + GEMM_BM - 1) / GEMM_BM) * ((a.N + GEMM_BN - 1) / GEMM_BN) * 2 <= num_sms)
     csk = plan_csk(a.M, a.N, a.K, num_sms, EPI == EPI_GEGLU).C >= 2;
   if (csk) {
     launch_csk<EPI>(ta, tb, a, *sk, num_sms, st);
@@ -348,7 +353,7 @@ void launch_gemm(const CUtensorMap& ta, const WeightMap& tb, const CUtensorMap& 
   // fill the SMs (measured at 16k tokens: Wqkv 1253 vs 1212, Wo2 1187 vs 1126, Wo 952 vs 905
   // TFLOP/s), the one-CTA kernel for GeGLU (1245 vs 1219) and for fewer tiles.
   const bool two = variant == 2 ||
-                   (variant == 0 && EPI != EPI_GEGLU &&
+                   (variant == 0 && EPI != EPI_GEGLU && !(t_gemm_off & GEMM_OFF_2CTA) &&
                     ((a.M + 255) / 256) * ((a.N + GEMM_BN - 1) / GEMM_BN) * 2 >= num_sms);
   if (two) {
     const int tiles = ((a.M + 255) / 256) * ((a.N + GEMM_BN - 1) / GEMM_BN);
@@ -489,6 +494,12 @@ struct s1c_backend {
   // mma.sync kernel (attention.cuh) on the pruned head rows (1 + kmax queries per row, where its
   // 64-row tiles waste less) and on small batches; `attn=tc|mma` force one kernel everywhere.
   enum AttnMode { ATTN_AUTO, ATTN_TC, ATTN_MMA } attn_mode = ATTN_AUTO;
+  // Load-time kernel self-check (`check=0|1`, `check_fail=`; selfcheck()).
+  bool check = true;
+  bool checked = false;
+  int gemm_off = 0;          // GEMM_OFF_* bits set by the check
+  std::string check_fail;    // kernels whose check gets a planted wrong expected value ('+'-separated)
+  std::string check_report;  // kernels the check turned off ('+'-separated)
   int cap_T = 0, cap_R = 0;
   DevBuf h, x, qkv, att, act;          // [cap_T, ...]
   DevBuf h2;                           // head residual stream [cap_T, d] fp32
@@ -1206,6 +1217,10 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
 void forward_enqueue(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uint32_t* d_ids, float* d_logits,
                      float* d_pooled, float* d_hidden) {
   t_pdl = B.pdl;
+  t_gemm_off = B.gemm_off;
+  struct Reset {
+    ~Reset() { t_gemm_off = 0; }
+  } reset;
   switch (B.d) {
     case 256: run_forward<256>(B, m, dm, d_ids, d_logits, d_pooled, d_hidden); break;
     case 768: run_forward<768>(B, m, dm, d_ids, d_logits, d_pooled, d_hidden); break;
@@ -1401,6 +1416,21 @@ void apply_settings(s1c_backend& B, const char* spec) {
       else if (v == "tc") B.attn_mode = s1c_backend::ATTN_TC;
       else if (v == "mma") B.attn_mode = s1c_backend::ATTN_MMA;
       else throw S1cError(S1C_ERR_CONFIG, "settings: `" + kv + "`: `" + v + "` is not one of tc, mma");
+    } else if (k == "check") {
+      if (v == "1") B.check = true;
+      else if (v == "0") B.check = false;
+      else throw S1cError(S1C_ERR_CONFIG, "settings: `" + kv + "`: `" + v + "` is not 0 or 1");
+    } else if (k == "check_fail") {
+      size_t a = 0;
+      while (a <= v.size()) {
+        size_t e = v.find('+', a);
+        if (e == std::string::npos) e = v.size();
+        const std::string kern = v.substr(a, e - a);
+        if (kern != "1cta" && kern != "2cta" && kern != "csk" && kern != "splitk" && kern != "tc" && kern != "mma")
+          throw S1cError(S1C_ERR_CONFIG, "settings: `" + kv + "`: `" + kern + "` is not one of 1cta, 2cta, csk, splitk, tc, mma");
+        a = e + 1;
+      }
+      B.check_fail = v;
     } else {
       throw S1cError(S1C_ERR_CONFIG, "settings: unknown setting `" + k + "`");
     }
@@ -1424,6 +1454,352 @@ s1c_status guarded(s1c_backend* b, F&& f) {
     b->last_error = "unknown error";
     return S1C_ERR_ARG;
   }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Load-time kernel self-check (setting `check=1`)
+//
+// The reference checks its fused kernels once at load against the op chains they replace and turns
+// a kernel that does not reproduce them off for that load, with one line on stderr
+// (laya-mlx/src/lib.rs:319-362, split_rope.rs:258-266). Here each kernel the forward can pick runs
+// once on small seeded problems through the same launch code as the forward, and its output is
+// compared with a plain computation on the host in double precision over the same bf16 inputs:
+//   * GEMMs: the one-CTA, two-CTA and cluster split-K kernels (and the workspace split-K path when
+//     `gemm=splitk` forces it), each with the bias + ReLU store, the bias + GELU fp32 store, the
+//     residual add, the RoPE and the GeGLU epilogues, at M = 300 (a partial last tile);
+//   * attention: the tcgen05 and mma.sync kernels, global and sliding window, over four ragged
+//     sequences (200, 63, 129 and 1 tokens).
+// An output passes when every element is within 1e-2 * (1 + |expected|) (bf16 output rounding is
+// 2^-9 relative; a wrong tile, a missed mask or a lost accumulator is off by O(1)). A faster kernel
+// that fails is turned off for this handle when a checked kernel can take its place (two-CTA or
+// cluster split-K -> one-CTA GEMM; tcgen05 -> mma.sync attention), with one line on stderr and the
+// change named in s1c_active_kernels. A failing one-CTA GEMM or mma.sync attention, or a failing
+// kernel that the settings force, fails s1c_create with S1C_ERR_SELFCHECK.
+//
+// `check_fail=<kernel>[+<kernel>...]` (1cta, 2cta, csk, splitk, tc, mma) plants a wrong value in the
+// host-side expected result of those kernels' checks: it lets tests drive the fallback rule (the
+// reference's tests do the same by handing `rope_kernels` a failing build) without a faulty kernel.
+
+constexpr double CHECK_TOL = 1e-2;
+
+struct CheckRng {
+  uint64_t s;
+  float uniform() {  // [-1, 1), splitmix64
+    s += 0x9E3779B97F4A7C15ull;
+    uint64_t z = s;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    z ^= z >> 31;
+    return (float)((double)(z >> 40) * (1.0 / 8388608.0)) - 1.0f;
+  }
+};
+
+// max over elements of |got - want| / (1 + |want|); NaN when any output is not finite
+double scaled_err(const std::vector<float>& got, const std::vector<double>& want) {
+  double e = 0;
+  for (size_t i = 0; i < want.size(); ++i) {
+    if (!std::isfinite(got[i])) return std::nan("");
+    e = std::max(e, std::fabs((double)got[i] - want[i]) / (1.0 + std::fabs(want[i])));
+  }
+  return e;
+}
+
+std::vector<float> download(const void* d, size_t n, bool f32) {
+  std::vector<float> out(n);
+  if (f32) {
+    CK(cudaMemcpy(out.data(), d, n * 4, cudaMemcpyDeviceToHost));
+  } else {
+    std::vector<uint16_t> raw(n);
+    CK(cudaMemcpy(raw.data(), d, n * 2, cudaMemcpyDeviceToHost));
+    for (size_t i = 0; i < n; ++i) out[i] = bf16_bits_to_f32(raw[i]);
+  }
+  return out;
+}
+
+struct CheckBufs {
+  std::vector<void*> p;
+  ~CheckBufs() {
+    for (void* q : p) cudaFree(q);
+  }
+  template <class T>
+  T* upload(const std::vector<T>& v) {
+    void* q = nullptr;
+    CK(cudaMalloc(&q, std::max<size_t>(v.size(), 1) * sizeof(T)));
+    p.push_back(q);
+    CK(cudaMemcpy(q, v.data(), v.size() * sizeof(T), cudaMemcpyHostToDevice));
+    return static_cast<T*>(q);
+  }
+  void* alloc(size_t bytes) {
+    void* q = nullptr;
+    CK(cudaMalloc(&q, bytes));
+    p.push_back(q);
+    return q;
+  }
+};
+
+double gelu_exact(double x) { return 0.5 * x * (1.0 + std::erf(x / std::sqrt(2.0))); }
+
+// The GEMM problem of the check: A [300, 320] and B [768, 320] bf16 (unit-variance products), a
+// bias, a residual, row positions, and A B^T over the bf16 inputs in double.
+struct GemmCheck {
+  static constexpr int M = 300, N = 768, K = 320, I = 384, ROPE_COLS = 512;
+  static constexpr float THETA = 10000.0f;
+  std::vector<uint16_t> a, b;
+  std::vector<float> bias, resid;
+  std::vector<int32_t> pos;
+  std::vector<double> c;
+  GemmCheck() : a((size_t)M * K), b((size_t)N * K), bias(N), resid((size_t)M * N), pos(M), c((size_t)M * N) {
+    CheckRng rng{0x5e1fc4ec0001ull};
+    const float sb = 3.0f / std::sqrt((float)K);
+    for (auto& x : a) x = f32_to_bf16_bits(rng.uniform());
+    for (auto& x : b) x = f32_to_bf16_bits(rng.uniform() * sb);
+    for (auto& x : bias) x = 0.5f * rng.uniform();
+    for (auto& x : resid) x = rng.uniform();
+    for (int m = 0; m < M; ++m) pos[m] = (m * 37) % 1000;
+    std::vector<double> af(a.size()), bfv(b.size());
+    for (size_t i = 0; i < a.size(); ++i) af[i] = bf16_bits_to_f32(a[i]);
+    for (size_t i = 0; i < b.size(); ++i) bfv[i] = bf16_bits_to_f32(b[i]);
+    for (int m = 0; m < M; ++m)
+      for (int n = 0; n < N; ++n) {
+        const double* ar = &af[(size_t)m * K];
+        const double* br = &bfv[(size_t)n * K];
+        double s = 0;
+        for (int k = 0; k < K; ++k) s += ar[k] * br[k];
+        c[(size_t)m * N + n] = s;
+      }
+  }
+  // Expected output of epilogue case `cs`: 0 bias + ReLU (bf16), 1 bias + GELU (fp32), 2 residual
+  // + bias (fp32), 3 RoPE on the first ROPE_COLS columns (bf16), 4 GeGLU of the interleaved tiles
+  // (bf16, I columns).
+  std::vector<double> want(int cs) const {
+    std::vector<double> w(cs == 4 ? (size_t)M * I : (size_t)M * N);
+    float inv_freq[32];
+    const float lbase = std::log2(THETA);
+    for (int i = 0; i < 32; ++i) inv_freq[i] = std::exp2(-((float)i / 32.0f) * lbase);
+    for (int m = 0; m < M; ++m) {
+      const double* row = &c[(size_t)m * N];
+      if (cs == 4) {
+        for (int j = 0; j < I; ++j) {
+          const int t = j / 128, cc = j % 128;
+          w[(size_t)m * I + j] = gelu_exact(row[256 * t + cc]) * row[256 * t + 128 + cc];
+        }
+        continue;
+      }
+      for (int n = 0; n < N; ++n) {
+        double v = row[n];
+        if (cs == 0) v = std::max(v + bias[n], 0.0);
+        else if (cs == 1) v = gelu_exact(v + bias[n]);
+        else if (cs == 2) v = (double)resid[(size_t)m * N + n] + v + bias[n];
+        else if (n < ROPE_COLS) {
+          const int h0 = n / 64 * 64, i = n % 64, j = i % 32;
+          const float ang = (float)pos[m] * inv_freq[j];  // the kernel's fp32 angle
+          const double cs_ = std::cos((double)ang), sn = std::sin((double)ang);
+          const double lo = row[h0 + j], hi = row[h0 + 32 + j];
+          v = i < 32 ? lo * cs_ - hi * sn : lo * sn + hi * cs_;
+        }
+        w[(size_t)m * N + n] = v;
+      }
+    }
+    return w;
+  }
+};
+
+// One GEMM kernel (s1c_gemm variant: 1 one-CTA, 2 two-CTA, 3 workspace split-K, 4 cluster split-K)
+// through the five epilogue cases; returns the largest scaled error (NaN for a non-finite output).
+double check_gemm_kernel(const GemmCheck& g, const std::vector<std::vector<double>>& want, cudaStream_t st,
+                         int variant, bool plant) {
+  using G = GemmCheck;
+  CheckBufs bufs;
+  const uint16_t* dA = bufs.upload(g.a);
+  const uint16_t* dB = bufs.upload(g.b);
+  const float* dBias = bufs.upload(g.bias);
+  const int32_t* dPos = bufs.upload(g.pos);
+  void* dOut = bufs.alloc((size_t)G::M * G::N * 4);
+  double worst = 0;
+  for (int cs = 0; cs < 5; ++cs) {
+    static const int epi_of[5] = {EPI_STORE, EPI_STORE, EPI_RESID, EPI_ROPE, EPI_GEGLU};
+    const int epi = epi_of[cs], f32 = (cs == 1 || cs == 2) ? 1 : 0;
+    const int act = cs == 0 ? ACT_RELU : cs == 1 ? ACT_GELU : ACT_NONE;
+    const float* bp = cs <= 2 ? dBias : nullptr;
+    if (cs == 2) CK(cudaMemcpy(dOut, g.resid.data(), g.resid.size() * 4, cudaMemcpyHostToDevice));
+    const s1c_status rc = s1c_gemm(epi, dA, dB, dOut, G::M, G::N, G::K, bp, act, f32, dPos, G::THETA, G::ROPE_COLS,
+                                   G::I, variant, st);
+    if (rc != S1C_OK) throw S1cError(rc, "load check: GEMM launch: " + g_create_error);
+    CK(cudaStreamSynchronize(st));
+    std::vector<double> w = want[cs];
+    if (plant) w[w.size() / 2] += 1.0;
+    const double e = scaled_err(download(dOut, w.size(), f32 != 0), w);
+    if (std::isnan(e)) return e;
+    worst = std::max(worst, e);
+  }
+  return worst;
+}
+
+// The attention problem of the check: four ragged sequences (200, 63, 129, 1 tokens) of 4 heads in
+// the forward's qkv layout [T, 3 x 256] (q scaled by 2 for sharper rows), and softmax(q k^T / 8) v
+// in double over each query's key set: the whole sequence (window < 0) or |i - j| <= window.
+struct AttnCheck {
+  static constexpr int H = 4, D = H * 64, W = 3 * D;
+  std::vector<int32_t> cu = {0, 200, 263, 392, 393};
+  std::vector<uint16_t> qkv;
+  AttnCheck() {
+    const int T = cu.back();
+    qkv.resize((size_t)T * W);
+    CheckRng rng{0xa77e0001ull};
+    for (int t = 0; t < T; ++t)
+      for (int c = 0; c < W; ++c) qkv[(size_t)t * W + c] = f32_to_bf16_bits((c < D ? 2.0f : 1.0f) * rng.uniform());
+  }
+  std::vector<double> want(int window) const {
+    const int n = (int)cu.size() - 1, T = cu[n];
+    std::vector<double> f(qkv.size()), w((size_t)T * D), p;
+    for (size_t i = 0; i < qkv.size(); ++i) f[i] = bf16_bits_to_f32(qkv[i]);
+    for (int r = 0; r < n; ++r)
+      for (int i = cu[r]; i < cu[r + 1]; ++i)
+        for (int h = 0; h < H; ++h) {
+          const int j0 = window < 0 ? cu[r] : std::max(cu[r], i - window);
+          const int j1 = window < 0 ? cu[r + 1] : std::min(cu[r + 1], i + window + 1);
+          p.assign((size_t)(j1 - j0), 0.0);
+          double mx = -1e300;
+          for (int j = j0; j < j1; ++j) {
+            double s = 0;
+            for (int e = 0; e < 64; ++e) s += f[(size_t)i * W + h * 64 + e] * f[(size_t)j * W + D + h * 64 + e];
+            p[j - j0] = s * 0.125;
+            mx = std::max(mx, p[j - j0]);
+          }
+          double sum = 0;
+          for (double& x : p) sum += (x = std::exp(x - mx));
+          for (int e = 0; e < 64; ++e) {
+            double o = 0;
+            for (int j = j0; j < j1; ++j) o += p[j - j0] * f[(size_t)j * W + 2 * D + h * 64 + e];
+            w[(size_t)i * D + h * 64 + e] = o / sum;
+          }
+        }
+    return w;
+  }
+};
+
+// One attention kernel (impl 0 tcgen05, 1 mma.sync), global (want[0]) then sliding window with
+// the model's half-width (want[1]); the largest scaled error.
+double check_attention_kernel(const AttnCheck& a, const std::vector<double> (&want)[2], int window,
+                              cudaStream_t st, int impl, bool plant) {
+  using A = AttnCheck;
+  const int n = (int)a.cu.size() - 1, T = a.cu[n];
+  CheckBufs bufs;
+  const uint16_t* q = bufs.upload(a.qkv);
+  void* d_o = bufs.alloc((size_t)T * A::D * 2);
+  double worst = 0;
+  for (int pass = 0; pass < 2; ++pass) {
+    const s1c_status rc = s1c_attention(q, q + A::D, q + 2 * A::D, d_o, A::W, A::W, A::W, A::D, A::H, a.cu.data(), n,
+                                        pass == 0 ? -1 : window, 0.125f, impl, st);
+    if (rc != S1C_OK) throw S1cError(rc, "load check: attention launch: " + g_create_error);
+    std::vector<double> w = want[pass];
+    if (plant) w[w.size() / 3] += 1.0;
+    const double e = scaled_err(download(d_o, w.size(), false), w);
+    if (std::isnan(e)) return e;
+    worst = std::max(worst, e);
+  }
+  return worst;
+}
+
+std::string fmt_err(double e) {
+  char buf[64];
+  std::snprintf(buf, sizeof buf, "%.3g", e);
+  return buf;
+}
+
+void selfcheck(s1c_backend& B) {
+  auto planted = [&](const char* k) {
+    const std::string& s = B.check_fail;
+    size_t i = 0;
+    while (i <= s.size()) {
+      size_t j = s.find('+', i);
+      if (j == std::string::npos) j = s.size();
+      if (s.compare(i, j - i, k) == 0) return true;
+      i = j + 1;
+    }
+    return false;
+  };
+  const bool pdl = t_pdl;
+  t_pdl = false;  // plain stream order between the check's launches and its copies
+  struct Restore {
+    bool v;
+    ~Restore() { t_pdl = v; }
+  } restore{pdl};
+  cudaStream_t st = B.stream;
+  B.check_report.clear();
+  auto refuse = [&](const std::string& what, double e) {
+    throw S1cError(S1C_ERR_SELFCHECK, "load check: " + what + " differs from the plain computation (max scaled error " +
+                                          fmt_err(e) + ", limit " + fmt_err(CHECK_TOL) + ")");
+  };
+  auto note = [&](const std::string& what, const char* key, const std::string& instead, double e) {
+    std::fprintf(stderr, "s1c: %s is off for this load, %s runs instead: max scaled error %s (limit %s)\n",
+                 what.c_str(), instead.c_str(), fmt_err(e).c_str(), fmt_err(CHECK_TOL).c_str());
+    if (!B.check_report.empty()) B.check_report += "+";
+    B.check_report += key;
+  };
+  const GemmCheck g;
+  std::vector<std::vector<double>> gw;
+  for (int cs = 0; cs < 5; ++cs) gw.push_back(g.want(cs));
+  const AttnCheck ac;
+  const std::vector<double> aw[2] = {ac.want(-1), ac.want(B.window)};
+  auto gemm = [&](int variant, const char* k) { return check_gemm_kernel(g, gw, st, variant, planted(k)); };
+  auto attn = [&](int impl, const char* k) { return check_attention_kernel(ac, aw, B.window, st, impl, planted(k)); };
+
+  const double e1 = gemm(1, "1cta");
+  if (!(e1 <= CHECK_TOL)) refuse("the one-CTA GEMM", e1);
+  const double am = attn(1, "mma");
+  if (!(am <= CHECK_TOL)) refuse("the mma.sync attention", am);
+  if (B.gemm_variant == 3) {
+    const double es = gemm(3, "splitk");
+    if (!(es <= CHECK_TOL)) refuse("the workspace split-K GEMM (forced by gemm=splitk)", es);
+  }
+  if (B.gemm_variant == 0 || B.gemm_variant == 2) {
+    const double e2 = gemm(2, "2cta");
+    if (!(e2 <= CHECK_TOL)) {
+      if (B.gemm_variant == 2) refuse("the two-CTA GEMM (forced by gemm=2cta)", e2);
+      B.gemm_off |= GEMM_OFF_2CTA;
+      note("the two-CTA GEMM", "2cta", "the one-CTA GEMM", e2);
+    }
+  }
+  if (B.gemm_variant == 0 || B.gemm_variant == 4) {
+    const double ek = gemm(4, "csk");
+    if (!(ek <= CHECK_TOL)) {
+      if (B.gemm_variant == 4) refuse("the cluster split-K GEMM (forced by gemm=csk)", ek);
+      B.gemm_off |= GEMM_OFF_CSK;
+      note("the cluster split-K GEMM", "csk", "the one-CTA GEMM", ek);
+    }
+  }
+  if (B.attn_mode != s1c_backend::ATTN_MMA) {
+    const double at = attn(0, "tc");
+    if (!(at <= CHECK_TOL)) {
+      if (B.attn_mode == s1c_backend::ATTN_TC) refuse("the tcgen05 attention (forced by attn=tc)", at);
+      B.attn_mode = s1c_backend::ATTN_MMA;
+      note("the tcgen05 attention", "tc", "the mma.sync attention", at);
+    }
+  }
+  B.checked = true;
+}
+
+// `Backend::active_kernels`: the kernels this handle's forward can launch under its settings and
+// load check, and the check's outcome.
+void describe_kernels(s1c_backend& B) {
+  std::string g;
+  switch (B.gemm_variant) {
+    case 1: g = "gemm_tcgen05_1cta"; break;
+    case 2: g = "gemm_tcgen05_2cta"; break;
+    case 3: g = "gemm_tcgen05_1cta_splitk,splitk_finalize"; break;
+    case 4: g = "gemm_tcgen05_cluster_splitk"; break;
+    default:
+      g = "gemm_tcgen05_1cta";
+      if (!(B.gemm_off & GEMM_OFF_2CTA)) g += ",gemm_tcgen05_2cta";
+      if (!(B.gemm_off & GEMM_OFF_CSK)) g += ",gemm_tcgen05_cluster_splitk";
+  }
+  std::string s = "epilogues(rope,geglu,residual,bias_act)," + g;
+  if (B.attn_mode != s1c_backend::ATTN_MMA) s += ",attention_varlen_tcgen05";
+  if (B.attn_mode != s1c_backend::ATTN_TC) s += ",attention_varlen_mma";
+  s += ",embed_ln,layernorm,final_to_head,scorer_logits";
+  if (B.checked) s += B.check_report.empty() ? ",load_check(passed)" : ",load_check(off:" + B.check_report + ")";
+  B.kernels = s;
 }
 
 }  // namespace
@@ -1505,6 +1881,8 @@ s1c_status s1c_create(const s1c_model_desc* desc, const s1c_tensor* tensors, int
     apply_settings(*b, std::getenv("S1C_SETTINGS"));
     build(*b, *desc, tensors, n_tensors);
     CK(cudaDeviceSynchronize());
+    if (b->check) selfcheck(*b);
+    describe_kernels(*b);
   } catch (const S1cError& e) {
     g_create_error = e.what();
     return e.code;
