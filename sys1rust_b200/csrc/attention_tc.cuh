@@ -9,11 +9,12 @@
 // the TMA/MMA pipeline never drains between heads; two CTAs share an SM (98 KB of shared memory
 // and 256 TMEM columns each). 192 threads:
 //   warp 0      TMA producer: Q tile [128 x 64] per head (double buffered, so the next head's Q
-//               arrives while this head runs), K and V tiles [64 keys x 64] per key step (3-stage
+//               arrives while this head runs), K and V tiles [64 keys x 64] per key step (4-stage
 //               ring), 128-byte swizzle.
 //   warp 1      TMEM owner and MMA issuer:
-//                 S = Q K^T     M=128 N=64 K=64 (K-major A and B)              -> TMEM cols [0,64)
-//                 O += P V      M=128 N=64 K=64 (P K-major from shared memory, V MN-major)
+//                 S = Q K^T     M=128 N=64 K=64 (K-major A and B from shared memory)
+//                               -> TMEM cols [0,64)
+//                 O += P V      M=128 N=64 K=64 (P from TMEM, V MN-major from shared memory)
 //                               -> TMEM cols [64,128) for even heads, [128,192) for odd heads
 //               S of the next key step is issued as soon as the softmax has read the current S.
 //   warps 2..5  softmax, one query row per thread (TMEM lane = row). Per key step: the row's
@@ -21,7 +22,10 @@
 //               raised when m exceeds it by more than 2^8 (p stays <= 256, exact in fp32 and
 //               bf16-representable like any p), in which case the running sum and the O
 //               accumulator in TMEM are rescaled by 2^(m_ref_old - m_ref) once the previous
-//               P V has completed. P is rounded to bf16 into a swizzled K-major shared tile.
+//               P V has completed. P is rounded to bf16 pairs and written to TMEM (cols
+//               [192,224) for even key steps, [224,256) for odd ones), where the P V MMA reads
+//               it as its A operand: no shared-memory round trip and no proxy fence, and a row
+//               may run one key step ahead of the P V that reads its previous P.
 //               32-column halves of S that no row of a warp may see (window edges, a row's
 //               last partial key tile) are neither read nor exponentiated. A finished head's
 //               O / l is read from TMEM and stored bf16 during the next key step, after its
@@ -32,12 +36,14 @@
 
 namespace s1c {
 
-constexpr int ATTC_BQ = 128, ATTC_BK = 64, ATTC_THREADS = 192, ATTC_HEADS = 4, ATTC_KV_STAGES = 3;
-constexpr uint32_t ATTC_TMEM_COLS = 256;  // S [0,64), O of even heads [64,128), odd heads [128,192)
+constexpr int ATTC_BQ = 128, ATTC_BK = 64, ATTC_THREADS = 192, ATTC_HEADS = 4, ATTC_KV_STAGES = 4;
+// TMEM columns: S [0,64), O of even heads [64,128), odd heads [128,192), P (bf16 pairs) of even
+// key steps [192,224), odd key steps [224,256)
+constexpr uint32_t ATTC_TMEM_COLS = 256;
+constexpr uint32_t ATTC_TMEM_P = 192;
 constexpr uint32_t ATTC_Q_BYTES = ATTC_BQ * 64 * 2;       // 16 KB
 constexpr uint32_t ATTC_KV_BYTES = ATTC_BK * 64 * 2;      // 8 KB each for K and V
-constexpr uint32_t ATTC_P_BYTES = ATTC_BQ * ATTC_BK * 2;  // 16 KB: one swizzled [128 x 64] block
-constexpr size_t ATTC_SMEM = 2 * ATTC_Q_BYTES + ATTC_KV_STAGES * 2 * ATTC_KV_BYTES + ATTC_P_BYTES + 1024 + 256;
+constexpr size_t ATTC_SMEM = 2 * ATTC_Q_BYTES + ATTC_KV_STAGES * 2 * ATTC_KV_BYTES + 1024 + 256;
 constexpr float ATTC_RESCALE_LOG2 = 8.0f;  // raise the reference maximum only past 2^8
 
 struct AttnTcArgs {
@@ -137,6 +143,16 @@ S1C_DEV void tmem_st32(uint32_t taddr, const float (&v)[32]) {
 }
 S1C_DEV void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// D (TMEM) (+)= A (TMEM: row i in lane i, two bf16 of consecutive k per 32-bit column) * B (shared
+// memory descriptor).
+S1C_DEV void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 __global__ void __launch_bounds__(ATTC_THREADS, 2)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
                         const AttnTcArgs args) {
@@ -147,8 +163,7 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
   uint8_t* sQ = smem;                              // [2][16 KB]
   uint8_t* sK = sQ + 2 * ATTC_Q_BYTES;             // [NS][8 KB]
   uint8_t* sV = sK + NS * ATTC_KV_BYTES;           // [NS][8 KB]
-  uint8_t* sP = sV + NS * ATTC_KV_BYTES;           // [16 KB]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + ATTC_P_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + NS * ATTC_KV_BYTES);
   uint64_t* q_full = bars + 0;    // [2]
   uint64_t* q_empty = bars + 2;   // [2]
   uint64_t* o_full = bars + 4;    // [2]
@@ -157,9 +172,9 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
   uint64_t* kv_empty = bars + 8 + NS;
   uint64_t* s_full = bars + 8 + 2 * NS;
   uint64_t* s_free = s_full + 1;
-  uint64_t* p_full = s_full + 2;
-  uint64_t* p_free = s_full + 3;
-  uint64_t* drain = s_full + 4;
+  uint64_t* p_full = s_full + 2;  // [2]: P of even / odd key steps written
+  uint64_t* p_free = s_full + 4;  // [2]: P V of even / odd key steps completed
+  uint64_t* drain = s_full + 6;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -192,8 +207,10 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
     }
     mbar_init(s_full, 1);
     mbar_init(s_free, 4);
-    mbar_init(p_full, 4);
-    mbar_init(p_free, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&p_full[i], 4);
+      mbar_init(&p_free[i], 1);
+    }
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -244,7 +261,7 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
     if (lane == 0 && nsteps > 0) {
       constexpr uint32_t idS = idesc_bf16_f32(128, ATTC_BK);
       constexpr uint32_t idO = idesc_bf16_f32_bmn(128, 64);
-      const uint32_t tS = tmem, pa = smem_u32(sP);
+      const uint32_t tS = tmem;
       bool ok = true;
       // S for step `st`: needs Q of its head, K of its stage and the softmax done reading S(st - 1).
       auto issue_s = [&](int st) -> bool {
@@ -265,20 +282,20 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
       ok = issue_s(0);
       for (int st = 0; ok && st < nsteps; ++st) {
         if (st + 1 < nsteps && !issue_s(st + 1)) break;
-        const int hi = st / nt, j = st % nt, s = st % NS, ob = hi & 1;
-        if (!mbar_wait(p_full, st & 1, args.status, DEV_TIMEOUT_MMA_FULL, abort_flag)) break;
+        const int hi = st / nt, j = st % nt, s = st % NS, ob = hi & 1, pb = st & 1;
+        if (!mbar_wait(&p_full[pb], (st >> 1) & 1, args.status, DEV_TIMEOUT_MMA_FULL, abort_flag)) break;
         // the first P V of a head overwrites its O buffer: head hi - 2's O must have been read
         if (j == 0 && hi >= 2 &&
             !mbar_wait(&o_free[ob], ((hi >> 1) - 1) & 1, args.status, DEV_TIMEOUT_MMA_TEMPTY, abort_flag))
           break;
         tc_fence_after();
         const uint32_t va = smem_u32(sV + s * ATTC_KV_BYTES), tO = tmem + 64 + 64 * ob;
+        const uint32_t tP = tmem + ATTC_TMEM_P + 32 * pb;
 #pragma unroll
         for (int k = 0; k < ATTC_BK / 16; ++k)
-          umma_bf16(tO, sdesc_kmajor_sw128(pa + k * 32), sdesc_mnmajor_sw128(va + k * 2048), idO,
-                    (j > 0 || k > 0) ? 1u : 0u);
+          umma_bf16_ts(tO, tP + 8 * k, sdesc_mnmajor_sw128(va + k * 2048), idO, (j > 0 || k > 0) ? 1u : 0u);
         umma_commit(&kv_empty[s]);
-        umma_commit(p_free);
+        umma_commit(&p_free[pb]);
         if (j == nt - 1) umma_commit(&o_full[ob]);
       }
       umma_commit(drain);
@@ -292,7 +309,6 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
     const int qtok = q_first + r;  // query token (mode 0)
     const float sc = args.scale_log2;
     float m_ref = -INFINITY, l = 0.f;
-    uint8_t* prow = sP + r * 128;
     // O / l of a finished head -> bf16, row q_first + r, columns of head h0 + hd. Deferred to the
     // next step's exponentials so that the last P V of the head has completed by then.
     int pend = -1;
@@ -392,17 +408,25 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
         }
         pend = -1;
       }
-      // P V of the previous step has completed: the P buffer may be rewritten and O rescaled.
-      if (st > 0 && !mbar_wait_warp(p_free, (st - 1) & 1, args.status, DEV_TIMEOUT_EPILOGUE, abort_flag)) {
+      // P buffer st & 1 is free once the P V of step st - 2 has completed.
+      const int pb = st & 1;
+      if (st > 1 && !mbar_wait_warp(&p_free[pb], ((st >> 1) - 1) & 1, args.status, DEV_TIMEOUT_EPILOGUE, abort_flag)) {
         ok = false;
         break;
       }
+      {
+        float pk[32];
 #pragma unroll
-      for (int q = 0; q < 8; ++q)
-        *reinterpret_cast<uint4*>(prow + ((q ^ (r & 7)) << 4)) =
-            make_uint4(pack_bf16x2(s[8 * q], s[8 * q + 1]), pack_bf16x2(s[8 * q + 2], s[8 * q + 3]),
-                       pack_bf16x2(s[8 * q + 4], s[8 * q + 5]), pack_bf16x2(s[8 * q + 6], s[8 * q + 7]));
+        for (int i = 0; i < 32; ++i) pk[i] = __uint_as_float(pack_bf16x2(s[2 * i], s[2 * i + 1]));
+        tmem_st32(tmem + lane_off + ATTC_TMEM_P + 32 * pb, pk);
+      }
       if (__any_sync(0xffffffffu, rescale_o)) {
+        // O is rescaled after the previous step's P V has completed
+        if (st > 0 &&
+            !mbar_wait_warp(&p_free[pb ^ 1], ((st - 1) >> 1) & 1, args.status, DEV_TIMEOUT_EPILOGUE, abort_flag)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
         const uint32_t tO = tmem + lane_off + 64 + 64 * (hi & 1);
 #pragma unroll
@@ -413,12 +437,11 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
           for (int i = 0; i < 32; ++i) t[i] *= factor;
           tmem_st32(tO + half * 32, t);
         }
-        tmem_st_wait();
       }
-      fence_proxy_async();
+      tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
+      if (lane == 0) mbar_arrive(&p_full[pb]);
       if (j == nt - 1) {
         pend = hi;
         l_pend = l;
