@@ -1307,6 +1307,7 @@ StageOut enqueue_forward(s1c_backend& B, const s1c_varlen& in, const uint32_t* h
 void forward_host(s1c_backend& B, const s1c_varlen& in, float* logits, float* pooled, float* hidden) {
   validate_varlen(B, in);
   if (in.n == 0) return;
+  if (!in.ids) throw S1cError(S1C_ERR_ARG, "null batch array");
   const int T = in.cu_seqlens[in.n];
   for (int t = 0; t < T; ++t)
     if (in.ids[t] >= (uint32_t)B.V) throw S1cError(S1C_ERR_ARG, "token " + std::to_string(t) + ": id outside the vocabulary");
@@ -1338,6 +1339,7 @@ void forward_device(s1c_backend& B, const s1c_varlen& in, const uint32_t* d_ids,
                     float* d_hidden) {
   validate_varlen(B, in);
   if (in.n == 0) return;
+  if (!d_ids || !d_pooled || (in.kmax > 0 && !d_logits)) throw S1cError(S1C_ERR_ARG, "null device pointer");
   const StageOut so = enqueue_forward(B, in, nullptr, d_ids, d_hidden);
   if (so.n_logits)
     CK(cudaMemcpyAsync(d_logits, so.logits, so.n_logits * 4, cudaMemcpyDeviceToDevice, B.stream));
@@ -2022,6 +2024,7 @@ s1c_status s1c_gemm(int32_t epi, const void* d_A, const void* d_B, void* d_out, 
       throw S1cError(S1C_ERR_ARG, "bad GEMM arguments (K must be a multiple of 8, N of 32)");
     int dev = 0, n_sms = 0;
     CK(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) throw S1cError(S1C_ERR_ARG, "device index out of range");
     CK(cudaDeviceGetAttribute(&n_sms, cudaDevAttrMultiProcessorCount, dev));
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     GemmArgs a{};

@@ -211,6 +211,16 @@ def test_malformed_batches_are_errors(cuda_lib):
     bad_marker.marker_pos[good.kmax] = 10  # row 1 has 4 tokens
     with pytest.raises(BackendError, match="marker"):
         be.forward(bad_marker)
+    # a null token array on the host-buffer entry point is an argument error, not a crash
+    import ctypes as C
+    from sys1rust_b200.backend import S1C_ERR_ARG, lib
+    v = Varlen.from_rows(make_rows(cfg, 28, [5], [1]))
+    cv, keep = be._cvarlen(v)
+    cv.ids = None
+    lg = np.zeros(max(v.n * v.kmax, 1), np.float32)
+    pl = np.zeros(v.n * cfg.encoder.hidden_size, np.float32)
+    rc = lib().s1c_forward_varlen(be._h, C.byref(cv), lg.ctypes.data, pl.ctypes.data, None)
+    assert rc == S1C_ERR_ARG and "null" in be._err()
     # the handle stays usable after an error
     out = be.forward(good)
     assert np.all(np.isfinite(out.pooled))
