@@ -14,6 +14,7 @@ collectives. ``value`` is the whole job's tokens / max-over-ranks device time.
 Each GPU runs two handles of the model on two streams and alternates its batches between them.
 Rank 0 prints one JSON line. Extra keys: ``e2e`` (the same requests submitted one by one from host
 arrays to the serving queue, one native worker per handle, copies and result collection included;
+the timed steps' requests form one stream, so the queue does not drain between steps;
 ``e2e_batched``: the pre-packed batches through ``s1c_forward_varlen``), ``roofline`` (dominant
 kernel, from per-launch CUDA events over a second, single-stream pass of the timed steps),
 ``cpu_baseline`` (the PyTorch oracle on a bounded sample, with the C restatement beside it; N = 1
@@ -301,17 +302,20 @@ def main():
     from sys1rust_b200.server import Server
     be.set_stream(0)  # the backends' own streams
     be2.set_stream(0)
-    with Server([be, be2], max_concurrent=len(mine) + 1, max_batch_tokens=BATCH_TOKENS, linger_us=1000) as srv:
-        def serve_all():
-            tk = [srv.submit(it) for it in mine]
-            for it, t in zip(mine, tk):
-                srv.wait(t, len(it.markers))
-        serve_all()  # warm-up pass
+    # The timed steps' requests arrive as one stream, as under continuous load: step k + 1's
+    # requests are queued while step k's are still being served, so the queue does not drain
+    # between steps; every request's result is still collected.
+    e2e_steps = max(1, min(args.steps, 3))
+    with Server([be, be2], max_concurrent=e2e_steps * len(mine) + 1, max_batch_tokens=BATCH_TOKENS,
+                linger_us=1000) as srv:
+        def serve_all(steps):
+            tk = [srv.submit(it) for _ in range(steps) for it in mine]
+            for i, t in enumerate(tk):
+                srv.wait(t, len(mine[i % len(mine)].markers))
+        serve_all(1)  # warm-up pass
         barrier()
-        e2e_steps = max(1, min(args.steps, 3))
         t_e2e = time.perf_counter()
-        for _ in range(e2e_steps):
-            serve_all()
+        serve_all(e2e_steps)
         e2e_s = max_over_ranks(time.perf_counter() - t_e2e)
         srv_stats = srv.stats()
     e2e_value = tokens_total * e2e_steps / e2e_s
@@ -422,7 +426,8 @@ def main():
                     "path": "sys1rust_b200.server.Server (s1c_server_*): the step's requests submitted one by one "
                             "from host arrays, packed across requests by one native worker per handle (2 per "
                             "GPU), host -> device copies and logits / pooled rows back to host inside the timed "
-                            "region, every result collected per request"},
+                            "region, every result collected per request; the timed steps' requests form one "
+                            "stream (no queue drain between steps)"},
             "e2e_batched": e2e_batched,
             "roofline": roof,
             "encoder_gemm_tflops": enc_tflops,
