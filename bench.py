@@ -201,6 +201,10 @@ def main():
     if args.impl == "reference":
         return run_reference(args)
     args.warmup = max(args.warmup, 3)
+    # the in-tree library, compiled here if it is missing or older than its sources (nvcc ships
+    # with the image; concurrent ranks serialise on a file lock)
+    from sys1rust_b200 import build as lib_build
+    lib_build.build()
 
     import torch
     from sys1rust_b200 import dist

@@ -6,6 +6,7 @@ runtime; the driver's tensor-map encoder is looked up at run time.
 """
 from __future__ import annotations
 
+import fcntl
 import os
 import shutil
 import subprocess
@@ -44,9 +45,20 @@ def up_to_date() -> bool:
 
 
 def build(force: bool = False, verbose: bool = False) -> str:
+    """Compile the library unless it is newer than every source. Safe to call from several
+    processes at once (e.g. every rank of a torchrun job): one compiles under a file lock while the
+    others wait and then find the library up to date."""
     if not force and up_to_date():
         return LIB
-    tmp = LIB + ".tmp"
+    with open(LIB + ".lock", "w") as lock:
+        fcntl.flock(lock, fcntl.LOCK_EX)
+        if not force and up_to_date():
+            return LIB
+        return _compile(verbose)
+
+
+def _compile(verbose: bool) -> str:
+    tmp = f"{LIB}.{os.getpid()}.tmp"
     cmd = [nvcc(), *NVCC_FLAGS, "-shared", "-o", tmp, os.path.join(CSRC, "s1c.cu"), "-lcudart"]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
