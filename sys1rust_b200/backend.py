@@ -29,7 +29,7 @@ S1C_OK, S1C_ERR_ARG, S1C_ERR_CUDA, S1C_ERR_WEIGHTS, S1C_ERR_CONFIG, S1C_ERR_DEVI
     0, -1, -2, -3, -4, -5, -6
 S1C_ERR_BUSY, S1C_ERR_DEAD, S1C_ERR_TIMEOUT = -7, -8, -9
 S1C_ERR_SELFCHECK = -10
-DT_F32, DT_F16, DT_BF16 = 0, 1, 2
+DT_F32, DT_F16, DT_BF16, DT_F64 = 0, 1, 2, 3
 
 
 class BackendError(RuntimeError):
@@ -196,7 +196,7 @@ class BackendOutput:
     hidden: Optional[np.ndarray] = None
 
 
-_DT_NAME = {DT_F32: "F32", DT_F16: "F16", DT_BF16: "BF16", 3: "F64"}
+_DT_NAME = {DT_F32: "F32", DT_F16: "F16", DT_BF16: "BF16", DT_F64: "F64"}
 _DT_NP = {"F32": np.float32, "F16": np.uint16, "BF16": np.uint16, "F64": np.float64}
 
 
@@ -305,7 +305,7 @@ class CudaBackend:
             keep.append(data)
             nb = name.encode()
             keep.append(nb)
-            code = {"F32": DT_F32, "F16": DT_F16, "BF16": DT_BF16, "F64": 3}[dt]
+            code = {"F32": DT_F32, "F16": DT_F16, "BF16": DT_BF16, "F64": DT_F64}[dt]
             sh = (C.c_int64 * 4)(*(list(shape) + [0] * (4 - len(shape))))
             arr[i] = Tensor(nb, code, len(shape), sh, data.ctypes.data)
         h = C.c_void_p()

@@ -56,3 +56,17 @@ def test_create_without_gpu_fails_cleanly(built):
     rc = L.s1c_create(ctypes.byref(desc), (Tensor * 1)(), 0, 0, ctypes.byref(h))
     assert rc < 0
     assert L.s1c_create_error()
+
+
+def test_python_constants_match_the_header():
+    """Every status code and tensor type of ``include/s1c.h`` has the same value in the Python
+    mirror, so errors map to the same exception classes on both sides of the ABI."""
+    import re
+    from sys1rust_b200 import backend
+    with open(os.path.join(ROOT, "include", "s1c.h")) as f:
+        text = f.read()
+    defs = {m.group(1): int(m.group(2)) for m in re.finditer(r"#define (S1C_(?:OK|ERR_\w+|DT_\w+))\s+\(?(-?\d+)\)?", text)}
+    assert {"S1C_OK", "S1C_ERR_ARG", "S1C_ERR_SELFCHECK", "S1C_DT_BF16"} <= set(defs)
+    for name, value in defs.items():
+        py = name if hasattr(backend, name) else name.replace("S1C_", "", 1)
+        assert getattr(backend, py, None) == value, (name, value, getattr(backend, py, None))
