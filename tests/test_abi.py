@@ -70,3 +70,22 @@ def test_python_constants_match_the_header():
     for name, value in defs.items():
         py = name if hasattr(backend, name) else name.replace("S1C_", "", 1)
         assert getattr(backend, py, None) == value, (name, value, getattr(backend, py, None))
+
+
+def test_ctypes_signatures_match_the_header():
+    """The Python binding declares each function with as many arguments as ``include/s1c.h``
+    gives it (a mismatch would pass garbage through the ABI without an error)."""
+    import re
+    with open(os.path.join(ROOT, "include", "s1c.h")) as f:
+        text = re.sub(r"/\*.*?\*/", "", f.read(), flags=re.S)
+    text = re.sub(r"typedef\s+\w+\s*\(\s*\*\s*\w+\s*\)\s*\([^;]*\);", "", text)
+    decl = {}
+    for m in re.finditer(r"\b(s1c_[a-z_]+)\s*\(([^;]*?)\)\s*;", text):
+        params = m.group(2).strip()
+        decl[m.group(1)] = 0 if params in ("", "void") else params.count(",") + 1
+    assert set(decl) == set(header_functions())
+    L = lib()
+    for name, n in decl.items():
+        fn = getattr(L, name)
+        assert fn.argtypes is not None, name
+        assert len(fn.argtypes) == n, (name, len(fn.argtypes), n)
