@@ -200,3 +200,26 @@ def test_malformed_rows_are_refused_at_submit():
         with pytest.raises(BackendError, match="marker position 9 outside a row of 5 tokens"):
             srv.submit(EncodedItem([5, 6, 7, 8, 9], [9], 2))
         assert srv.stats()["in_flight"] == 0
+
+
+def test_repeated_waves_stream_through_without_draining():
+    """Three waves of the same requests queued back to back (the serving benchmark's stream): two
+    workers pack across wave boundaries, and every ticket gets its own request's result even though
+    the waves repeat the same contents."""
+    fake = Fake()
+    items = [_item(i, 5 + (7 * i) % 40, n_markers=1 + i % 3) for i in range(40)]
+    waves = 3
+    with Server(forward=fake, n_workers=2, hidden=HIDDEN, max_concurrent=waves * len(items) + 1,
+                max_batch_tokens=200) as srv:
+        tickets = [srv.submit(it) for _ in range(waves) for it in items]
+        assert len(set(tickets)) == len(tickets)
+        for i, tk in enumerate(tickets):
+            it = items[i % len(items)]
+            logits, pooled, _ = srv.wait(tk, len(it.markers))
+            want_l, want_p = _expect(it)
+            assert np.array_equal(logits, want_l) and np.array_equal(pooled, want_p)
+        st = srv.stats()
+        assert st["rows"] == waves * len(items) and st["failed_batches"] == 0
+    # batches stayed within the token limit and every queued request ran exactly once
+    assert all(b["tokens"] <= 200 or len(b["rows"]) == 1 for b in fake.batches)
+    assert sum(len(b["rows"]) for b in fake.batches) == waves * len(items)
