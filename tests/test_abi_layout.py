@@ -1,8 +1,8 @@
 """The C structs of ``include/s1c.h`` and their ctypes mirrors in ``sys1rust_b200.backend`` have the
 same size, field offsets and field sizes: a probe compiled with the system C compiler against the
 header prints ``sizeof`` / ``offsetof`` for every field, and the test compares them with ctypes. The
-Rust binding given in INTEGRATION.md is checked the same way, and its functions' arity and status
-constants against the header."""
+Rust cuda-ffi binding written out in the repository's integration guide is checked the same way,
+and its functions' arity and status constants against the header."""
 import os
 import shutil
 import subprocess
@@ -50,7 +50,7 @@ def test_struct_layouts_match_the_header(tmp_path):
             assert got[(cname, fname + ".size")] == getattr(py, fname).size, (cname, fname)
 
 
-# The Rust cuda-ffi crate given as source in INTEGRATION.md cannot be compiled here (no cargo): its
+# The Rust cuda-ffi crate, written out in the integration guide's rust blocks, has no cargo here: its
 # #[repr(C)] structs are checked field by field against the header through ctypes structures built
 # from the Rust field types (repr(C) lays them out as C does), and its extern functions' arity
 # against the header's declarations.
