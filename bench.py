@@ -61,10 +61,25 @@ def workload(world: int, rank: int):
     return reqs, shard_for_rank(reqs, world, rank)
 
 
+CPU_SAMPLE_REQUESTS = 32
+
+
+def cpu_sample_requests():
+    """The fixed request sample both CPU legs time: the first 1024 requests of the cfg5 stream
+    sorted by length, every 32nd one (32 requests stratified by length, ~7 k tokens). The same
+    requests at every N and in every step, so the reference rate does not depend on which requests
+    a step happened to draw."""
+    from sys1rust_b200.workloads import cfg5_requests
+    reqs = sorted(cfg5_requests(n=REQ_PER_GPU, seed=1), key=lambda r: len(r.ids))
+    step = len(reqs) // CPU_SAMPLE_REQUESTS
+    return [reqs[i * step + step // 2] for i in range(CPU_SAMPLE_REQUESTS)]
+
+
 def cpu_oracle_sample(cfg, weights, items, budget_s: float, kind: str = "torch"):
-    """tokens/s of a CPU restatement (fp32, all host threads) over requests of the workload, one row
-    per forward, until ``budget_s`` seconds have passed (at least one request). ``kind`` "torch" is
-    the PyTorch oracle (oracle/forward_ref.py), "c" the C / OpenMP one (oracle/forward_ref.c)."""
+    """tokens/s (total tokens / total seconds) of a CPU restatement (fp32, all host threads) over
+    requests of the workload, one row per forward, until every request has run or ``budget_s``
+    seconds have passed (at least one request). ``kind`` "torch" is the PyTorch oracle
+    (oracle/forward_ref.py), "c" the C / OpenMP one (oracle/forward_ref.c)."""
     import torch
     from sys1rust_b200.batch import collate_to
     torch.set_num_threads(os.cpu_count() or 1)
@@ -168,23 +183,32 @@ def run_reference(args):
     config = arm_config(world, sum(len(r.ids) for r in all_reqs), len(pack_batches(mine, BATCH_TOKENS)))
     config["reference_arm"] = ("rank 0 times the CPU restatement of the forward on a bounded sample of "
                                "this shard's requests, one row per forward, all host threads")
+    config["reference_arm"] += (f"; at N > 1 only rank 0 runs it, so the value is one host's rate, not "
+                                f"N hosts'")
+    sample = cpu_sample_requests()
+    sample_tokens = sum(len(r.ids) for r in sample)
     vals = []
     steps = args.steps
-    per_step = max(2.0, min(20.0, 90.0 / max(steps + args.warmup, 1)))
     for s in range(args.warmup + steps):
-        v, info = cpu_oracle_sample(cfg, w, mine[s * 3:] + mine[:s * 3], per_step)
+        v, info = cpu_oracle_sample(cfg, w, sample, 60.0)
         if s >= args.warmup:
             vals.append(v)
     v = float(np.median(vals))
+    vc, infoc = cpu_oracle_sample(cfg, w, sample, 60.0, kind="c")
     line = {
         "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": world,
         "steps": steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": config,
         "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": info["cores"], "kind": "port",
-                         "sample": f"~{per_step:.0f} s of requests per step ({info['requests']} requests, "
-                                   f"{info['tokens']} tokens in the last step); the reference's MLX-CPU path "
-                                   "needs cargo + MLX, absent here"},
+                         "sample": f"each step the same {len(sample)} requests ({sample_tokens} tokens, cfg5 "
+                                   f"stratified by length), one row per forward, torch fp32 oracle; median "
+                                   f"of the timed steps; the reference's MLX-CPU path needs cargo + MLX, "
+                                   f"absent here",
+                         "steps_tokens_per_s": vals,
+                         "c_restatement": {"value": vc, "cores": infoc["cores"],
+                                           "sample": "the same requests once, oracle/forward_ref.c (fp32, "
+                                                     "AVX2, OpenMP)"}},
         "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -227,6 +251,10 @@ def main():
     # a third stream added nothing.
     be = CudaBackend.from_synthetic(cfg, w.tensors, device=local, max_tokens=BATCH_TOKENS)
     be2 = CudaBackend.from_synthetic(cfg, w.tensors, device=local, max_tokens=BATCH_TOKENS)
+    # load-time warm-up (the reference warms its length buckets at load): one captured graph per
+    # packed-token bucket on each handle
+    be.warmup()
+    be2.warmup()
     log(f"[rank {rank}] model ready in {time.time() - t0:.1f}s: {be.name()} x 2 streams")
     # Dedicated (non-default) streams: each backend captures per-shape CUDA graphs on its own.
     stream = torch.cuda.Stream()
@@ -280,6 +308,7 @@ def main():
     launches = launch_count[0]
     ms = e0.elapsed_time(e1)
     ms_max = max_over_ranks(ms)
+    per_rank = dist.gather_over_ranks([ms / args.steps, len(batches), tokens_mine], world, rank, device="cuda")
     tokens_total = sum(len(r.ids) for r in all_reqs)
     value = tokens_total * args.steps / (ms_max / 1e3)
 
@@ -352,7 +381,15 @@ def main():
         be.forward_varlen(one)
         ts.append((time.perf_counter() - t) * 1e3)
     lat = {"p50_ms": float(np.median(ts)), "p90_ms": float(np.percentile(ts, 90)), "n": len(ts),
-           "path": "s1c_forward_varlen, host buffers, copies included"}
+           "path": "s1c_forward_varlen, host buffers, copies included; the same request 50 times"}
+    # ---- latency over single requests whose shapes never repeat --------------------------
+    from sys1rust_b200.latency import stream_latency
+    from sys1rust_b200.workloads import latency_stream
+    lat_stream = stream_latency(be, latency_stream(200))
+    lat_stream.update({"workload": "200 single requests, lengths U[64, 200], 1-3 questions, no (length, "
+                                   "marker count) repeated, each run once",
+                       "path": "s1c_forward_varlen, host buffers, copies included; packed-token buckets "
+                               "with graphs captured by warmup() at load"})
 
     # ---- cfg3: 64 requests U[64,512] in one varlen batch, device-resident -----------------
     c3 = Varlen.from_rows(cfg3())
@@ -408,11 +445,13 @@ def main():
     # ---- CPU baseline (rank 0, N = 1) -----------------------------------------------------
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v, info = cpu_oracle_sample(cfg, w, mine, 15.0)
-        vc, infoc = cpu_oracle_sample(cfg, w, mine, 10.0, kind="c")
+        sample = cpu_sample_requests()
+        v, info = cpu_oracle_sample(cfg, w, sample, 30.0)
+        vc, infoc = cpu_oracle_sample(cfg, w, sample, 30.0, kind="c")
         cpu = {"value": v, "unit": "tokens/s", "cores": info["cores"], "kind": "port",
-               "sample": f"{info['requests']} requests / {info['tokens']} tokens of this workload, one row per "
-                         f"forward, {info['seconds']:.1f} s, torch fp32 oracle",
+               "sample": f"{info['requests']} requests / {info['tokens']} tokens of this workload (cfg5 "
+                         f"stratified by length, the reference arm's sample), one row per forward, "
+                         f"{info['seconds']:.1f} s, torch fp32 oracle",
                "c_restatement": {"value": vc, "cores": infoc["cores"],
                                  "sample": f"{infoc['requests']} requests / {infoc['tokens']} tokens, "
                                            f"{infoc['seconds']:.1f} s, oracle/forward_ref.c (fp32, AVX2, OpenMP)"}}
@@ -424,7 +463,11 @@ def main():
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic",
-            "config": arm_config(world, tokens_total, len(batches)),
+            "config": {**arm_config(world, tokens_total, len(batches)),
+                       "value_reading": f"value is the whole job's tokens/s over all {world} GPU(s); per GPU "
+                                        f"that is {value / world:.0f} tokens/s (value_per_gpu)"},
+            "per_rank": [{"rank": r, "ms_per_step": p[0], "batches": int(p[1]), "tokens": int(p[2])}
+                         for r, p in enumerate(per_rank)],
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h), "steps": e2e_steps,
                     "path": "sys1rust_b200.server.Server (s1c_server_*): the step's requests submitted one by one "
@@ -437,6 +480,7 @@ def main():
             "encoder_gemm_tflops": enc_tflops,
             "cpu_baseline": cpu,
             "latency_cfg1": lat,
+            "latency_stream": lat_stream,
             "cfg3_tokens_per_s": cfg3_tps,
             "clocks": clk.summary(),
             "gpu_launches": int(launches),

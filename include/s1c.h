@@ -112,7 +112,15 @@ typedef struct s1c_backend s1c_backend;
  * key or value fails the call with S1C_ERR_CONFIG): attn=auto|tc|mma (attention kernel; auto:
  * tcgen05 on full rows when its grid fills the SMs, else mma.sync), gemm=auto|1cta|2cta|splitk|csk,
  * graphs=0|1 (CUDA graph per batch shape), pdl=0|1 (programmatic dependent launch),
+ * buckets=<tokens>:<tokens>:... (packed-token buckets, default 128:256:...:1024:1280:...:2048;
+ * buckets=0 turns them off), warm=<rows>:... (row counts s1c_warmup runs at every bucket, default 1),
  * check=0|1 (default 1) and check_fail=<kernel>[+<kernel>...].
+ * Buckets (the reference's `buckets` / `warm` settings, laya-mlx/src/lib.rs:89-94): a batch of n
+ * rows whose packed tokens fit a bucket runs as the bucket's shape, with dummy rows (at least one,
+ * row count a power of two up to 64) holding the remaining tokens and marker slots padded to a
+ * multiple of 4. The dummy rows are computed apart from the batch's rows and dropped, so a bucket's
+ * CUDA graph (captured at the shape's first forward or by s1c_warmup) replays every batch of that
+ * shape; larger batches run their exact shape (graph captured at its second forward).
  * Load check (the reference's load-time kernel checks and fallback rule, lib.rs:319-362): every
  * kernel the forward can pick runs once on small seeded problems (GEMMs with each epilogue,
  * attention global and sliding window over ragged rows) and is compared with a double-precision
@@ -124,6 +132,11 @@ typedef struct s1c_backend s1c_backend;
  * value in those kernels' checks, for tests of the fallback rule. */
 S1C_API s1c_status s1c_create(const s1c_model_desc* desc, const s1c_tensor* tensors, int32_t n_tensors, int32_t device,
                       s1c_backend** out);
+/* s1c_create with the settings given as a string (the comma list above; NULL reads S1C_SETTINGS),
+ * for hosts that pass `BackendOptions::tuning` (laya-core/src/backend.rs:22-42) instead of setting
+ * the environment. The key `parallel_load` (the runtime's own setting) is accepted and ignored. */
+S1C_API s1c_status s1c_create_with_settings(const s1c_model_desc* desc, const s1c_tensor* tensors, int32_t n_tensors,
+                                            int32_t device, const char* settings, s1c_backend** out);
 S1C_API void s1c_destroy(s1c_backend* b);
 S1C_API const char* s1c_last_error(const s1c_backend* b);
 /* Error text of the last call without a backend handle that failed on the calling thread
@@ -136,7 +149,8 @@ S1C_API const char* s1c_name(const s1c_backend* b);
 S1C_API const char* s1c_active_kernels(const s1c_backend* b);
 /* `Backend::padded_len` (backend.rs:121-123): the varlen path needs no padding. */
 S1C_API size_t s1c_padded_len(const s1c_backend* b, size_t len, size_t rows);
-/* `Backend::warmup` (backend.rs:125-127). */
+/* `Backend::warmup` (backend.rs:125-127): one forward per (bucket, `warm=` row count) as the
+ * reference's warm_buckets (lib.rs:1152-1173), which captures each such bucket shape's CUDA graph. */
 S1C_API s1c_status s1c_warmup(s1c_backend* b);
 
 /* `Backend::forward` (backend.rs:112; MlxBackend::forward lib.rs:1833-1863): logits [n*kmax]
@@ -164,7 +178,9 @@ S1C_API s1c_status s1c_synchronize(s1c_backend* b);
 
 /* `Backend::encoder_hidden` (backend.rs:128-132; lib.rs:1869-1878): [n*len*hidden] f32 in the
  * padded layout. Real positions hold the encoder's final hidden state; padding positions are
- * never computed by the varlen path and are written as 0. */
+ * never computed by the varlen path and are written as 0. This differs from the reference, whose
+ * hook runs the encoder in the padded layout and so returns computed states at padding positions
+ * too; the logits and pooled rows of `forward` do not depend on them. */
 S1C_API s1c_status s1c_encoder_hidden(s1c_backend* b, const s1c_batch* batch, float* out);
 
 /* Isolated GEMM on device pointers (the encoder GEMM sweep and kernel tests): out = epi(A B^T)
@@ -209,7 +225,9 @@ S1C_API size_t s1c_profile_report(const s1c_backend* b, char* buf, size_t cap);
  * else the call returns S1C_ERR_ARG with the limit in s1c_create_error(). The first call on a
  * device looks up that device's array addresses (make it before any stream capture). All calls
  * share the array and the last call's partial sums stay in it; calls whose work overlaps on the
- * GPU race on it. The call does not synchronise. */
+ * GPU race on it. The call does not synchronise. A bounded device-side wait that runs out inside
+ * these kernels is not reported by this entry point (its status word is never read back): the
+ * call returns S1C_OK and the output is incomplete. */
 S1C_API s1c_status s1c_gemm_splitk_noalloc(int32_t epi, const void* d_A, const void* d_B, void* d_out, int32_t M,
                                            int32_t N, int32_t K, const float* d_bias, int32_t act, int32_t out_f32,
                                            const int32_t* d_pos, float rope_theta, int32_t rope_cols,

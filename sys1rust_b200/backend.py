@@ -117,6 +117,8 @@ def lib() -> C.CDLL:
     P, I32, I64, F32, SZ = C.c_void_p, C.c_int32, C.c_int64, C.c_float, C.c_size_t
     sig = {
         "s1c_create": (I32, [C.POINTER(ModelDesc), C.POINTER(Tensor), I32, I32, C.POINTER(P)]),
+        "s1c_create_with_settings": (I32, [C.POINTER(ModelDesc), C.POINTER(Tensor), I32, I32, C.c_char_p,
+                                           C.POINTER(P)]),
         "s1c_destroy": (None, [P]),
         "s1c_last_error": (C.c_char_p, [P]),
         "s1c_create_error": (C.c_char_p, []),
@@ -287,7 +289,10 @@ class CudaBackend:
                          cfg.head_layers, e.max_position_embeddings, max_tokens)
 
     def __init__(self, cfg: ModelConfig, tensors: Optional[Dict[str, Tuple[str, Tuple[int, ...], np.ndarray]]],
-                 device: int = 0, max_tokens: int = 16384, weights_file: Optional[WeightsFile] = None):
+                 device: int = 0, max_tokens: int = 16384, weights_file: Optional[WeightsFile] = None,
+                 settings: Optional[str] = None):
+        """``settings``: the library's comma list of kernel / bucket settings (``s1c_create_with_settings``);
+        None reads the ``S1C_SETTINGS`` environment variable."""
         L = lib()
         desc = self._desc(cfg, max_tokens)
         if weights_file is not None:
@@ -309,16 +314,18 @@ class CudaBackend:
             sh = (C.c_int64 * 4)(*(list(shape) + [0] * (4 - len(shape))))
             arr[i] = Tensor(nb, code, len(shape), sh, data.ctypes.data)
         h = C.c_void_p()
-        rc = L.s1c_create(C.byref(desc), arr, len(tensors), device, C.byref(h))
+        rc = L.s1c_create_with_settings(C.byref(desc), arr, len(tensors), device,
+                                        settings.encode() if settings is not None else None, C.byref(h))
         if rc != S1C_OK:
             _raise(rc, L.s1c_create_error().decode())
         self._h = h
         self.device = device
 
     @staticmethod
-    def from_synthetic(cfg: ModelConfig, weights, device: int = 0, max_tokens: int = 16384) -> "CudaBackend":
+    def from_synthetic(cfg: ModelConfig, weights, device: int = 0, max_tokens: int = 16384,
+                       settings: Optional[str] = None) -> "CudaBackend":
         t = {name: ("BF16", bits.shape, bits) for name, bits in weights.items()}
-        return CudaBackend(cfg, t, device=device, max_tokens=max_tokens)
+        return CudaBackend(cfg, t, device=device, max_tokens=max_tokens, settings=settings)
 
     @staticmethod
     def from_dir(model_dir: str, device: int = 0, max_tokens: int = 16384) -> "CudaBackend":

@@ -99,6 +99,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 4) attention_varlen_kernel(const 
   const int4 item = args.items[blockIdx.x / args.heads];
   const int head = blockIdx.x % args.heads;
   const int seq = item.x, q_first = item.y, q_count = item.z, mode = item.w;
+  if (q_count <= 0) return;  // an empty item (work lists filled up to a bucket's fixed length)
   const int s_begin = args.cu_seqlens[seq], s_end = args.cu_seqlens[seq + 1];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int hcol = head * ATT_D;

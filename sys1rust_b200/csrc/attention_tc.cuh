@@ -182,6 +182,7 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
   const int groups = (args.heads + ATTC_HEADS - 1) / ATTC_HEADS;  // block b: item b / groups
   const int4 item = args.items[blockIdx.x / groups];
   const int seq = item.x, q_first = item.y, q_count = item.z, mode = item.w;
+  if (q_count <= 0) return;  // an empty item (work lists filled up to a bucket's fixed length)
   const int s_begin = args.cu_seqlens[seq], s_end = args.cu_seqlens[seq + 1];
   const int h0 = (blockIdx.x % groups) * ATTC_HEADS;
   const int nh = min(ATTC_HEADS, args.heads - h0);

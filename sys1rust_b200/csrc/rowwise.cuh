@@ -181,7 +181,7 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const float* __restrict_
 
 template <int D>
 __global__ void final_to_head_kernel(const float* __restrict__ h, int T, const float* __restrict__ final_w, float eps,
-                                     float* __restrict__ hidden_out, const int* __restrict__ token_row,
+                                     float* __restrict__ hidden_out, int hidden_rows, const int* __restrict__ token_row,
                                      const uint32_t* __restrict__ qtype, const float* __restrict__ type_emb,
                                      const float* __restrict__ n1w, const float* __restrict__ n1b,
                                      float* __restrict__ h2, __nv_bfloat16* __restrict__ x) {
@@ -193,7 +193,7 @@ __global__ void final_to_head_kernel(const float* __restrict__ h, int T, const f
   RowVec<D> r;
   load_row_f32<D>(h + (size_t)row * D, r, lane);
   layernorm_row<D>(r, final_w, nullptr, eps, lane);
-  if (hidden_out) store_row_f32<D>(hidden_out + (size_t)row * D, r, lane);
+  if (hidden_out && row < hidden_rows) store_row_f32<D>(hidden_out + (size_t)row * D, r, lane);
   const uint32_t qt = qtype[token_row[row]];
   RowVec<D> te;
   load_row_f32<D>(type_emb + (size_t)qt * D, te, lane);

@@ -535,20 +535,39 @@ struct s1c_backend {
 
   // CUDA graphs of whole forwards, keyed by the shape that fixes every launch configuration and
   // every buffer offset: (tokens, rows, kmax, attention items, pruned-row items). Kernel arguments
-  // point only at the backend's own buffers, so a graph replays any batch of that shape. A shape
-  // is captured the second time it is seen; all graphs are dropped when a buffer moves.
+  // point only at the backend's own buffers, so a graph replays any batch of that shape. A bucket
+  // shape is captured the first time it is seen, any other shape the second time; at most
+  // MAX_GRAPHS graphs are kept (the least recently replayed one goes first) and at most MAX_SEEN
+  // shapes are remembered; all graphs are dropped when a buffer moves.
   bool use_graphs = true;
   struct Graph {
     cudaGraphExec_t exec = nullptr;
     int64_t launches = 0;
+    uint64_t last_used = 0;
   };
+  static constexpr size_t MAX_GRAPHS = 128, MAX_SEEN = 4096;
   std::map<std::vector<int>, Graph> graphs;
   std::map<std::vector<int>, int> seen;
+  uint64_t graph_clock = 0;
   void drop_graphs() {
     for (auto& kv : graphs) cudaGraphExecDestroy(kv.second.exec);
     graphs.clear();
     seen.clear();
   }
+  void evict_graphs(size_t keep) {
+    if (graphs.size() > keep && stream) cudaStreamSynchronize(stream);  // no evicted graph still runs
+    while (graphs.size() > keep) {
+      auto lru = graphs.begin();
+      for (auto i = graphs.begin(); i != graphs.end(); ++i)
+        if (i->second.last_used < lru->second.last_used) lru = i;
+      cudaGraphExecDestroy(lru->second.exec);
+      graphs.erase(lru);
+    }
+  }
+  // Packed-token buckets (`buckets=`, ascending; empty: exact shapes) and the row counts that
+  // s1c_warmup runs at every bucket (`warm=`).
+  std::vector<int> buckets = {128, 256, 384, 512, 640, 768, 896, 1024, 1280, 1536, 1792, 2048};
+  std::vector<int> warm_rows = {1};
 
   ~s1c_backend() {
     if (stream) cudaStreamSynchronize(stream);
@@ -830,6 +849,7 @@ void build(s1c_backend& B, const s1c_model_desc& D, const s1c_tensor* tensors, i
 
 struct HostMeta {
   int n = 0, kmax = 0, T = 0, R = 0, M = 0;  // rows, kmax, tokens, scorer rows n(1+kmax), markers n*kmax
+  int hidden_rows = 0;                        // tokens whose final hidden state is written out
   double pairs_global = 0, pairs_local = 0, pairs_rows = 0;  // attended (query, key) pairs per head-set
   std::vector<int> cu, srows, mrows, prows, mcount;
   std::vector<uint32_t> qtype;
@@ -868,7 +888,14 @@ static void longest_first(std::vector<int4>& items, const int* cu) {
   });
 }
 
-HostMeta make_meta(const s1c_varlen& in, int window) {
+// Work items (query tiles) of the first `n_items` rows only; with `pad` set, every list is then
+// filled with empty items (q_count 0, which the attention kernels skip) up to the fixed lengths of
+// a bucket shape, so that the grids of a bucket's captured graph fit any batch of the bucket.
+struct ItemPad {
+  bool on = false;
+  int full = 0, rows = 0, full_tc = 0, rows_tc = 0;
+};
+HostMeta make_meta(const s1c_varlen& in, int window, int n_items, const ItemPad& pad) {
   HostMeta m;
   m.n = in.n;
   m.kmax = in.kmax;
@@ -889,6 +916,7 @@ HostMeta make_meta(const s1c_varlen& in, int window) {
       m.srows[r * (1 + in.kmax) + 1 + k] = base + (int)in.marker_pos[(size_t)r * in.kmax + k];
       m.mrows[r * in.kmax + k] = r * (1 + in.kmax) + 1 + k;
     }
+    if (r >= n_items) continue;
     const int len = m.cu[r + 1] - base;
     m.pairs_global += (double)len * len;
     m.pairs_rows += (double)(1 + in.kmax) * len;
@@ -906,6 +934,16 @@ HostMeta make_meta(const s1c_varlen& in, int window) {
   longest_first(m.items_rows, m.cu.data());
   longest_first(m.items_full_tc, m.cu.data());
   longest_first(m.items_rows_tc, m.cu.data());
+  if (pad.on) {
+    auto fill = [](std::vector<int4>& v, int count, int mode) {
+      if ((int)v.size() > count) throw S1cError(S1C_ERR_ARG, "internal: bucket work list overflow");
+      v.resize(count, make_int4(0, 0, 0, mode));
+    };
+    fill(m.items_full, pad.full, 0);
+    fill(m.items_rows, pad.rows, 1);
+    fill(m.items_full_tc, pad.full_tc, 0);
+    fill(m.items_rows_tc, pad.rows_tc, 1);
+  }
   return m;
 }
 
@@ -1126,7 +1164,7 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
 
   // final_norm, + type embedding, head layer 0's norm1
   launch(B, nl, "final_to_head", 0, Td * (4 + 4 + 2 + (d_hidden ? 4 : 0)), [&] {
-    launch_k(final_to_head_kernel<D>, dim3((T + 7) / 8), dim3(256), 0, st, h, T, B.final_norm, B.eps, d_hidden, trow, dm.qtype,
+    launch_k(final_to_head_kernel<D>, dim3((T + 7) / 8), dim3(256), 0, st, h, T, B.final_norm, B.eps, d_hidden, m.hidden_rows, trow, dm.qtype,
                                                          B.type_emb, B.head[0].n1w, B.head[0].n1b, h2, x);
   });
 
@@ -1242,18 +1280,94 @@ void check_status(s1c_backend& B) {
   }
 }
 
+// Shape buckets (settings `buckets=`, `warm=`; the reference's length buckets and load-time
+// warm-up, laya-mlx/src/lib.rs:89-94, :1152-1173, :1826-1831). A batch whose packed tokens fit a
+// bucket runs as the bucket's shape: its rows first, then `nb - n` dummy rows (token id 0, no
+// markers) that hold the bucket's remaining tokens, markers padded to `kb` slots per row. Dummy
+// rows get no attention work items: their tokens' attention outputs are never written, so
+// whatever those rows compute stays in their own rows (every kernel but attention is row-local,
+// and attention only reads keys of a query's own row) and is dropped with them. The work lists
+// are filled with empty items to lengths fixed by (T, nb, kb), so one captured graph per bucket
+// shape replays every batch of that shape. Row counts are bucketed to powers of two (2 .. 64, at
+// least one dummy row), marker slots to multiples of 4.
+constexpr int BUCKET_MAX_ROWS = 64;
+struct BucketShape {
+  int T = 0, n = 0, kmax = 0;
+};
+bool pick_bucket(const s1c_backend& B, const s1c_varlen& in, BucketShape& out) {
+  if (B.buckets.empty() || in.n == 0) return false;
+  const int T = in.cu_seqlens[in.n];
+  int nb = 2;
+  while (nb < in.n + 1) nb *= 2;
+  if (nb > BUCKET_MAX_ROWS) return false;
+  for (int t : B.buckets) {
+    const int pad = t - T;
+    if (pad < nb - in.n) continue;  // every dummy row holds at least one token
+    if ((int64_t)pad > (int64_t)(nb - in.n) * B.max_pos) return false;  // dummy rows stay within max_position
+    out.T = t;
+    out.n = nb;
+    out.kmax = std::max(4, (in.kmax + 3) / 4 * 4);
+    return true;
+  }
+  return false;
+}
+ItemPad bucket_item_pad(const BucketShape& bs) {
+  // sum over rows of ceil(len / tile) <= ceil(T / tile) + rows
+  ItemPad p;
+  p.on = true;
+  p.full = (bs.T + ATT_BQ - 1) / ATT_BQ + bs.n;
+  p.full_tc = (bs.T + ATTC_BQ - 1) / ATTC_BQ + bs.n;
+  p.rows = bs.n * ((1 + bs.kmax + ATT_BQ - 1) / ATT_BQ);
+  p.rows_tc = bs.n * ((1 + bs.kmax + ATTC_BQ - 1) / ATTC_BQ);
+  return p;
+}
+// The batch `in` laid out as bucket shape `bs` (ids only when they come from the host).
+struct BucketBatch {
+  std::vector<uint32_t> ids, mpos, qtype;
+  std::vector<int32_t> cu, mcount;
+  s1c_varlen v{};
+};
+void make_bucket_batch(const s1c_varlen& in, const uint32_t* host_ids, const BucketShape& bs, BucketBatch& o) {
+  const int T = in.cu_seqlens[in.n], nd = bs.n - in.n, pad = bs.T - T;
+  o.cu.assign(in.cu_seqlens, in.cu_seqlens + in.n + 1);
+  for (int r = 0; r < nd; ++r) o.cu.push_back(T + (int)((int64_t)pad * (r + 1) / nd));  // pad tokens spread evenly
+  o.mcount.assign(bs.n, 0);
+  o.qtype.assign(bs.n, 0);
+  o.mpos.assign((size_t)bs.n * bs.kmax, 0);
+  for (int r = 0; r < in.n; ++r) {
+    o.mcount[r] = in.marker_count[r];
+    o.qtype[r] = in.qtype[r];
+    for (int k = 0; k < in.kmax; ++k) o.mpos[(size_t)r * bs.kmax + k] = in.marker_pos[(size_t)r * in.kmax + k];
+  }
+  if (host_ids) {
+    o.ids.assign(bs.T, 0u);
+    std::memcpy(o.ids.data(), host_ids, (size_t)T * 4);
+  }
+  o.v = s1c_varlen{bs.n, bs.kmax, host_ids ? o.ids.data() : nullptr, o.cu.data(), o.mpos.data(), o.mcount.data(),
+                   o.qtype.data()};
+}
+
 // Enqueue one forward. Token ids come from the host (`host_ids`, staged with the metadata) or
 // from device memory (`dev_ids`, copied into the arena); logits and pooled land in `out_stage`;
-// `d_hidden` (nullable) receives the encoder's final hidden state directly. With graphs on, a
-// shape seen before replays its captured graph instead of launching kernel by kernel.
+// `d_hidden` (nullable) receives the encoder's final hidden state of the batch's own tokens.
+// With graphs on, a bucket shape replays its graph from its first sighting on (captured then),
+// any other shape from its third (captured at the second).
 struct StageOut {
-  float* logits;
-  float* pooled;
-  size_t n_logits, n_pooled;
+  float* logits;   // [n, kstride] (the batch's rows; slots past kmax belong to the bucket)
+  float* pooled;   // [n, d]
+  size_t n_logits, n_pooled;  // n * kstride, n * d
+  int n = 0, kmax = 0, kstride = 0;
 };
 StageOut enqueue_forward(s1c_backend& B, const s1c_varlen& in, const uint32_t* host_ids, const uint32_t* dev_ids,
                          float* d_hidden) {
-  HostMeta m = make_meta(in, B.window);
+  BucketShape bs;
+  BucketBatch bb;
+  const bool bucketed = pick_bucket(B, in, bs);
+  if (bucketed) make_bucket_batch(in, host_ids, bs, bb);
+  const s1c_varlen& run = bucketed ? bb.v : in;
+  const int T_in = in.cu_seqlens[in.n];
+  HostMeta m = make_meta(run, B.window, in.n, bucketed ? bucket_item_pad(bs) : ItemPad{});
+  m.hidden_rows = T_in;
   ensure_capacity(B, m.T, m.R);
   const size_t nl = (size_t)m.M, np = (size_t)m.n * B.d;
   const size_t need = ((nl + 63) / 64 * 64 + np) * 4;
@@ -1262,10 +1376,14 @@ StageOut enqueue_forward(s1c_backend& B, const s1c_varlen& in, const uint32_t* h
     B.drop_graphs();
     B.out_stage.ensure(need * 2);
   }
-  StageOut so{B.out_stage.as<float>(), B.out_stage.as<float>() + (nl + 63) / 64 * 64, nl, np};
-  DevMeta dm = upload_meta(B, m, host_ids);
-  if (dev_ids)
-    CK(cudaMemcpyAsync(const_cast<uint32_t*>(dm.ids), dev_ids, (size_t)m.T * 4, cudaMemcpyDeviceToDevice, B.stream));
+  StageOut so{B.out_stage.as<float>(), B.out_stage.as<float>() + (nl + 63) / 64 * 64,
+              in.kmax ? (size_t)in.n * run.kmax : 0, (size_t)in.n * B.d, in.n, in.kmax, run.kmax};
+  DevMeta dm = upload_meta(B, m, host_ids ? run.ids : nullptr);
+  if (dev_ids) {
+    CK(cudaMemcpyAsync(const_cast<uint32_t*>(dm.ids), dev_ids, (size_t)T_in * 4, cudaMemcpyDeviceToDevice, B.stream));
+    if (m.T > T_in)
+      CK(cudaMemsetAsync(const_cast<uint32_t*>(dm.ids) + T_in, 0, (size_t)(m.T - T_in) * 4, B.stream));
+  }
   const bool graphable = B.use_graphs && !d_hidden && !B.prof_on && B.stream != nullptr &&
                          B.stream != cudaStreamLegacy && B.stream != cudaStreamPerThread;
   if (!graphable) {
@@ -1276,11 +1394,14 @@ StageOut enqueue_forward(s1c_backend& B, const s1c_varlen& in, const uint32_t* h
                                 (int)m.items_full_tc.size(), (int)m.items_rows_tc.size()};
   auto it = B.graphs.find(key);
   if (it == B.graphs.end()) {
-    if (B.seen[key]++ < 1) {  // first sighting: launch directly
-      forward_enqueue(B, m, dm, dm.ids, so.logits, so.pooled, nullptr);
-      return so;
+    if (!bucketed) {
+      if (B.seen.size() >= s1c_backend::MAX_SEEN) B.seen.clear();  // forget one-off shapes
+      if (B.seen[key]++ < 1) {  // first sighting of an unbucketed shape: launch directly
+        forward_enqueue(B, m, dm, dm.ids, so.logits, so.pooled, nullptr);
+        return so;
+      }
     }
-    if (B.graphs.size() >= 64) B.drop_graphs();
+    B.evict_graphs(s1c_backend::MAX_GRAPHS - 1);
     cudaGraph_t g = nullptr;
     CK(cudaStreamBeginCapture(B.stream, cudaStreamCaptureModeThreadLocal));
     try {
@@ -1296,8 +1417,10 @@ StageOut enqueue_forward(s1c_backend& B, const s1c_varlen& in, const uint32_t* h
     cudaGraphDestroy(g);
     if (e != cudaSuccess) throw S1cError(S1C_ERR_CUDA, std::string("cudaGraphInstantiate: ") + cudaGetErrorString(e));
     gr.launches = B.launches;
+    B.seen.erase(key);
     it = B.graphs.emplace(key, gr).first;
   }
+  it->second.last_used = ++B.graph_clock;
   CK(cudaGraphLaunch(it->second.exec, B.stream));
   B.launches = it->second.launches;
   return so;
@@ -1329,7 +1452,11 @@ void forward_host(s1c_backend& B, const s1c_varlen& in, float* logits, float* po
   CK(cudaMemcpyAsync(ho + so.n_logits, so.pooled, so.n_pooled * 4, cudaMemcpyDeviceToHost, B.stream));
   if (nh) CK(cudaMemcpyAsync(ho + so.n_logits + so.n_pooled, hid_dev.p, nh * 4, cudaMemcpyDeviceToHost, B.stream));
   check_status(B);
-  if (so.n_logits) std::memcpy(logits, ho, so.n_logits * 4);
+  if (so.n_logits) {
+    if (so.kstride == so.kmax) std::memcpy(logits, ho, so.n_logits * 4);
+    else
+      for (int r = 0; r < so.n; ++r) std::memcpy(logits + (size_t)r * so.kmax, ho + (size_t)r * so.kstride, (size_t)so.kmax * 4);
+  }
   std::memcpy(pooled, ho + so.n_logits, so.n_pooled * 4);
   if (nh) std::memcpy(hidden, ho + so.n_logits + so.n_pooled, nh * 4);
 }
@@ -1341,8 +1468,13 @@ void forward_device(s1c_backend& B, const s1c_varlen& in, const uint32_t* d_ids,
   if (in.n == 0) return;
   if (!d_ids || !d_pooled || (in.kmax > 0 && !d_logits)) throw S1cError(S1C_ERR_ARG, "null device pointer");
   const StageOut so = enqueue_forward(B, in, nullptr, d_ids, d_hidden);
-  if (so.n_logits)
-    CK(cudaMemcpyAsync(d_logits, so.logits, so.n_logits * 4, cudaMemcpyDeviceToDevice, B.stream));
+  if (so.n_logits && so.kmax) {
+    if (so.kstride == so.kmax)
+      CK(cudaMemcpyAsync(d_logits, so.logits, so.n_logits * 4, cudaMemcpyDeviceToDevice, B.stream));
+    else
+      CK(cudaMemcpy2DAsync(d_logits, (size_t)so.kmax * 4, so.logits, (size_t)so.kstride * 4, (size_t)so.kmax * 4,
+                           (size_t)so.n, cudaMemcpyDeviceToDevice, B.stream));
+  }
   CK(cudaMemcpyAsync(d_pooled, so.pooled, so.n_pooled * 4, cudaMemcpyDeviceToDevice, B.stream));
 }
 
@@ -1385,7 +1517,8 @@ void pack_batch(const s1c_batch& b, PackedBatch& p) {
 
 // Backend settings, a strict comma list like the reference's `Knobs` (laya-mlx/src/lib.rs:155-259):
 // an unknown key or value is an error naming it. Keys: attn=auto|tc|mma,
-// gemm=auto|1cta|2cta|splitk|csk, graphs=0|1, pdl=0|1.
+// gemm=auto|1cta|2cta|splitk|csk, graphs=0|1, pdl=0|1, buckets=<t>:<t>... (packed-token buckets,
+// 0 = none), warm=<rows>:... (row counts s1c_warmup runs at every bucket), check=0|1, check_fail=.
 void apply_settings(s1c_backend& B, const char* spec) {
   if (!spec) return;
   std::string s(spec);
@@ -1418,6 +1551,30 @@ void apply_settings(s1c_backend& B, const char* spec) {
       else if (v == "tc") B.attn_mode = s1c_backend::ATTN_TC;
       else if (v == "mma") B.attn_mode = s1c_backend::ATTN_MMA;
       else throw S1cError(S1C_ERR_CONFIG, "settings: `" + kv + "`: `" + v + "` is not one of tc, mma");
+    } else if (k == "buckets" || k == "warm") {
+      // colon list of positive whole numbers; `buckets=0` turns the buckets off
+      std::vector<int> vals;
+      size_t a = 0;
+      while (a <= v.size()) {
+        size_t e = v.find(':', a);
+        if (e == std::string::npos) e = v.size();
+        const std::string t = v.substr(a, e - a);
+        a = e + 1;
+        char* end = nullptr;
+        const long x = t.empty() ? -1 : std::strtol(t.c_str(), &end, 10);
+        if (t.empty() || *end || x < 0 || x > (1 << 24))
+          throw S1cError(S1C_ERR_CONFIG, "settings: `" + kv + "`: `" + t + "` is not a whole number");
+        if (x > 0) vals.push_back((int)x);
+      }
+      std::sort(vals.begin(), vals.end());
+      vals.erase(std::unique(vals.begin(), vals.end()), vals.end());
+      if (k == "buckets") B.buckets = vals;
+      else B.warm_rows = vals;
+    } else if (k == "parallel_load") {
+      // the runtime's own setting (BackendOptions::parallel_load, laya-core/src/backend.rs:44-66),
+      // accepted here as the reference's backends accept it
+      if (!v.empty() && v != "0" && v != "1")
+        throw S1cError(S1C_ERR_CONFIG, "settings: `" + kv + "`: `" + v + "` is not 0 or 1");
     } else if (k == "check") {
       if (v == "1") B.check = true;
       else if (v == "0") B.check = false;
@@ -1822,6 +1979,13 @@ static __device__ __align__(256) float s1c_noalloc_scratch[NOALLOC_SCRATCH_FLOAT
 static __device__ __align__(256) float s1c_noalloc_inv_freq[32];
 static __device__ __align__(256) int s1c_noalloc_status;
 
+// RoPE frequencies of the allocation-free GEMM: the 32 values travel as a kernel argument (copied
+// at launch), so no host buffer has to outlive the call.
+struct InvFreq32 {
+  float v[32];
+};
+__global__ void noalloc_set_inv_freq_kernel(float* dst, const InvFreq32 f) { dst[threadIdx.x] = f.v[threadIdx.x]; }
+
 namespace {
 
 struct NoAllocDevice {
@@ -1858,6 +2022,11 @@ extern "C" {
 
 s1c_status s1c_create(const s1c_model_desc* desc, const s1c_tensor* tensors, int32_t n_tensors, int32_t device,
                       s1c_backend** out) {
+  return s1c_create_with_settings(desc, tensors, n_tensors, device, nullptr, out);
+}
+
+s1c_status s1c_create_with_settings(const s1c_model_desc* desc, const s1c_tensor* tensors, int32_t n_tensors,
+                                    int32_t device, const char* settings, s1c_backend** out) {
   g_create_error.clear();
   if (!desc || !out || (n_tensors > 0 && !tensors)) {
     g_create_error = "null argument";
@@ -1880,7 +2049,7 @@ s1c_status s1c_create(const s1c_model_desc* desc, const s1c_tensor* tensors, int
     b->stream = b->own_stream;
     set_all_gemm_smem();
     CK(cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATTC_SMEM));
-    apply_settings(*b, std::getenv("S1C_SETTINGS"));
+    apply_settings(*b, settings ? settings : std::getenv("S1C_SETTINGS"));
     build(*b, *desc, tensors, n_tensors);
     CK(cudaDeviceSynchronize());
     if (b->check) selfcheck(*b);
@@ -1944,11 +2113,26 @@ size_t s1c_profile_report(const s1c_backend* b, char* buf, size_t cap) {
 
 s1c_status s1c_warmup(s1c_backend* b) {
   return guarded(b, [&] {
-    // One forward per shape class: a single short row and a multi-row batch.
-    for (int n : {1, 4}) {
+    // One forward per (bucket, warm row count) as the reference's warm_buckets (lib.rs:1152-1173):
+    // rows of equal length filling the bucket's tokens less one per dummy row, two markers each,
+    // so every bucket shape a single request (or `warm=` rows) lands in has its graph captured.
+    // Without buckets: one short row and one 4-row batch.
+    std::vector<std::pair<int, int>> shapes;  // (rows, tokens per row)
+    if (b->buckets.empty()) {
+      shapes = {{1, 64}, {4, 64}};
+    } else {
+      for (int t : b->buckets)
+        for (int n : b->warm_rows) {
+          int nb = 2;
+          while (nb < n + 1) nb *= 2;
+          const int per = (t - (nb - n)) / n;
+          if (nb <= BUCKET_MAX_ROWS && per >= 3 && per <= b->max_pos) shapes.push_back({n, per});
+        }
+    }
+    for (auto [n, len] : shapes) {
       std::vector<int32_t> cu(n + 1);
-      for (int r = 0; r <= n; ++r) cu[r] = r * 64;
-      std::vector<uint32_t> ids((size_t)n * 64, 0), mpos((size_t)n * 2), qt(n, 0);
+      for (int r = 0; r <= n; ++r) cu[r] = r * len;
+      std::vector<uint32_t> ids((size_t)n * len, 0), mpos((size_t)n * 2), qt(n, 0);
       std::vector<int32_t> mc(n, 2);
       for (int r = 0; r < n; ++r) { mpos[2 * r] = 1; mpos[2 * r + 1] = 2; }
       s1c_varlen v{n, 2, ids.data(), cu.data(), mpos.data(), mc.data(), qt.data()};
@@ -2238,10 +2422,11 @@ s1c_status s1c_gemm_splitk_noalloc(int32_t epi, const void* d_A, const void* d_B
     a.M = M; a.N = N; a.K = K; a.bias = d_bias; a.act = act; a.out_f32 = out_f32;
     a.pos = d_pos; a.rope_cols = rope_cols; a.out_cols = out_cols; a.status = nd.status;
     if (epi == EPI_ROPE) {
-      float inv[32];
+      InvFreq32 inv;
       const float lbase = std::log2(rope_theta);
-      for (int i = 0; i < 32; ++i) inv[i] = std::exp2(-((float)i / 32.0f) * lbase);
-      CK(cudaMemcpyAsync(nd.inv_freq, inv, sizeof inv, cudaMemcpyHostToDevice, st));
+      for (int i = 0; i < 32; ++i) inv.v[i] = std::exp2(-((float)i / 32.0f) * lbase);
+      noalloc_set_inv_freq_kernel<<<1, 32, 0, st>>>(nd.inv_freq, inv);
+      CK(cudaGetLastError());
       a.inv_freq = nd.inv_freq;
     }
     const bool f32 = epi == EPI_RESID || (epi == EPI_STORE && out_f32);

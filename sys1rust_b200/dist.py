@@ -77,6 +77,19 @@ def sum_over_ranks(x: float, world: int, device=None) -> float:
     return float(t.item())
 
 
+def gather_over_ranks(values, world: int, rank: int, device=None) -> list:
+    """Every rank's ``values`` (a list of floats of the same length on every rank), as a list
+    indexed by rank: one summing all-reduce of a [world, len] table each rank fills one row of."""
+    if world <= 1:
+        return [list(map(float, values))]
+    import torch
+    import torch.distributed as dist
+    t = torch.zeros(world, len(values), dtype=torch.float64, device=device)
+    t[rank] = torch.tensor([float(v) for v in values], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return t.cpu().tolist()
+
+
 def shutdown(world: int) -> None:
     if world > 1:
         import torch.distributed as dist

@@ -1,12 +1,17 @@
-"""Single-request latency (benchmark config 1): one row of 128 tokens with one noul question through
-the host API (``s1c_forward_varlen``: host buffers in, logits and pooled rows back on the host).
+"""Single-request latency through the host API (``s1c_forward_varlen``: host buffers in, logits and
+pooled rows back on the host).
 
-    python -m sys1rust_b200.latency [--reps 50] [--warm 5]
+    python -m sys1rust_b200.latency [--reps 50] [--warm 5] [--stream 200]
 
-Builds the ModernBERT-large model from seeded weights, runs ``--warm`` forwards (the second one
-records the shape's CUDA graph), then prints one JSON line: p50 / p90 wall milliseconds per call
-over ``--reps`` calls and the device milliseconds of a forward run back to back from device-
-resident inputs (CUDA events).
+Builds the ModernBERT-large model from seeded weights and runs ``warmup()`` (the reference warms
+its length buckets at load, ``laya-mlx/src/lib.rs:1152-1173``; here that captures one CUDA graph
+per packed-token bucket). Then prints one JSON line with:
+
+* ``cfg1``: p50 / p90 wall milliseconds over ``--reps`` calls of benchmark config 1 (one row of
+  128 tokens, one noul question), and the device milliseconds of that forward run back to back
+  from device-resident inputs (CUDA events);
+* ``stream``: p50 / p90 over ``--stream`` single requests whose shapes never repeat (lengths
+  U[64, 200], 1-3 questions; ``workloads.latency_stream``), each run once.
 """
 from __future__ import annotations
 
@@ -17,10 +22,25 @@ import time
 import numpy as np
 
 
+def stream_latency(be, reqs) -> dict:
+    """Wall milliseconds of each request of ``reqs`` run once through ``forward_varlen``."""
+    from .batch import Varlen
+    ts = []
+    for it in reqs:
+        v = Varlen.from_rows([it])
+        t = time.perf_counter()
+        be.forward_varlen(v)
+        ts.append((time.perf_counter() - t) * 1e3)
+    return {"p50_ms": float(np.median(ts)), "p90_ms": float(np.percentile(ts, 90)),
+            "max_ms": float(np.max(ts)), "n": len(ts),
+            "distinct_shapes": len({(len(r.ids), len(r.markers)) for r in reqs})}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reps", type=int, default=50)
     ap.add_argument("--warm", type=int, default=5)
+    ap.add_argument("--stream", type=int, default=200)
     ap.add_argument("--device", type=int, default=0)
     args = ap.parse_args()
 
@@ -29,11 +49,16 @@ def main():
     from .batch import Varlen
     from .config import large_model
     from .weights import SyntheticWeights
-    from .workloads import cfg1
+    from .workloads import cfg1, latency_stream
 
     cfg = large_model()
     w = SyntheticWeights(cfg, seed=0)
     be = CudaBackend.from_synthetic(cfg, w.tensors, device=args.device, max_tokens=4096)
+    t0 = time.perf_counter()
+    be.warmup()
+    warm_s = time.perf_counter() - t0
+    stream = stream_latency(be, latency_stream(args.stream)) if args.stream else None
+
     one = Varlen.from_rows(cfg1())
     for _ in range(args.warm):
         be.forward_varlen(one)
@@ -57,10 +82,11 @@ def main():
     e1.record(st)
     be.synchronize()
     torch.cuda.synchronize()
-    print(json.dumps({"workload": "cfg1: 1 row x 128 tokens, 1 noul question", "p50_ms": float(np.median(ts)),
-                      "p90_ms": float(np.percentile(ts, 90)), "reps": args.reps,
-                      "device_ms_per_forward": e0.elapsed_time(e1) / args.reps,
-                      "launches_per_forward": be.last_launch_count()}))
+    print(json.dumps({"cfg1": {"workload": "1 row x 128 tokens, 1 noul question", "p50_ms": float(np.median(ts)),
+                               "p90_ms": float(np.percentile(ts, 90)), "reps": args.reps,
+                               "device_ms_per_forward": e0.elapsed_time(e1) / args.reps,
+                               "launches_per_forward": be.last_launch_count()},
+                      "stream": stream, "warmup_s": warm_s}))
     be.close()
 
 

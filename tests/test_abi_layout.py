@@ -1,8 +1,9 @@
 """The C structs of ``include/s1c.h`` and their ctypes mirrors in ``sys1rust_b200.backend`` have the
 same size, field offsets and field sizes: a probe compiled with the system C compiler against the
 header prints ``sizeof`` / ``offsetof`` for every field, and the test compares them with ctypes. The
-Rust cuda-ffi binding written out in the repository's integration guide is checked the same way,
-and its functions' arity and status constants against the header."""
+Rust cuda-ffi crate (``rust/cuda-ffi/src/lib.rs``) is checked the same way, and its functions'
+arity and status constants against the header; the laya-cuda crate calls only functions it
+declares."""
 import os
 import shutil
 import subprocess
@@ -50,18 +51,19 @@ def test_struct_layouts_match_the_header(tmp_path):
             assert got[(cname, fname + ".size")] == getattr(py, fname).size, (cname, fname)
 
 
-# The Rust cuda-ffi crate, written out in the integration guide's rust blocks, has no cargo here: its
-# #[repr(C)] structs are checked field by field against the header through ctypes structures built
-# from the Rust field types (repr(C) lays them out as C does), and its extern functions' arity
-# against the header's declarations.
+# The Rust cuda-ffi crate is not compiled here (no cargo in this image): its #[repr(C)] structs are
+# checked field by field against the header through ctypes structures built from the Rust field
+# types (repr(C) lays them out as C does), and its extern functions' arity against the header's
+# declarations.
+RUST_FFI = os.path.join(ROOT, "rust", "cuda-ffi", "src", "lib.rs")
+RUST_BACKEND = os.path.join(ROOT, "rust", "laya-cuda", "src", "lib.rs")
 _RUST_CTYPES = {"i32": bk.C.c_int32, "u32": bk.C.c_uint32, "i64": bk.C.c_int64, "u64": bk.C.c_uint64,
                 "f32": bk.C.c_float, "f64": bk.C.c_double, "usize": bk.C.c_size_t, "u8": bk.C.c_uint8}
 
 
 def _rust_source():
-    import re
-    with open(os.path.join(ROOT, "INTEGRATION.md")) as f:
-        return "\n".join(re.findall(r"```rust\n(.*?)```", f.read(), re.S))
+    with open(RUST_FFI) as f:
+        return f.read()
 
 
 def _rust_type(t):
@@ -109,13 +111,28 @@ def test_rust_binding_functions_match_the_header():
         p = m.group(2).strip()
         decl[m.group(1)] = 0 if p in ("", "void") else p.count(",") + 1
     fns = re.findall(r"pub fn (s1c_\w+)\s*\(([^)]*)\)", src)
-    assert len(fns) >= 20
+    assert {name for name, _ in fns} == set(decl)  # every header function, nothing else
     for name, params in fns:
         assert name in decl, name
         n = 0 if not params.strip() else params.count(",") + 1 - (1 if params.strip().endswith(",") else 0)
         assert n == decl[name], (name, n, decl[name])
     consts = dict(re.findall(r"pub const (S1C_\w+): i32 = (-?\d+);", src))
     with open(os.path.join(ROOT, "include", "s1c.h")) as f:
-        hdr_consts = dict(re.findall(r"#define (S1C_ERR_\w+) \((-?\d+)\)", f.read()))
+        hdr_consts = dict(re.findall(r"#define (S1C_(?:OK|ERR_\w+|DT_\w+))\s+\(?(-?\d+)\)?", f.read()))
+    assert set(consts) == set(hdr_consts)  # every status code and dtype
     for name, v in consts.items():
         assert hdr_consts[name] == v, name
+
+
+def test_rust_backend_calls_only_declared_functions():
+    """laya-cuda (the Backend implementation) calls libs1c only through functions cuda-ffi declares,
+    and implements the trait methods the reference's backends implement."""
+    import re
+    decl = set(re.findall(r"pub fn (s1c_\w+)", _rust_source()))
+    with open(RUST_BACKEND) as f:
+        src = f.read()
+    used = set(re.findall(r"ffi::(s1c_[a-z_]+)\s*\(", src))
+    assert used and used <= decl, used - decl
+    for m in ("fn name", "fn forward", "fn active_kernels", "fn padded_len", "fn warmup", "fn encoder_hidden",
+              "pub fn make_backend", "pub fn factory"):
+        assert m in src, m
