@@ -117,8 +117,8 @@ typedef struct s1c_backend s1c_backend;
  * check=0|1 (default 1) and check_fail=<kernel>[+<kernel>...].
  * Buckets (the reference's `buckets` / `warm` settings, laya-mlx/src/lib.rs:89-94): a batch of n
  * rows whose packed tokens fit a bucket runs as the bucket's shape, with dummy rows (at least one,
- * row count a power of two up to 64) holding the remaining tokens and marker slots padded to a
- * multiple of 4. The dummy rows are computed apart from the batch's rows and dropped, so a bucket's
+ * row count a power of two up to 64; none when the tokens fill the bucket) holding the remaining
+ * tokens and marker slots padded to a multiple of 4. The dummy rows are computed apart from the batch's rows and dropped, so a bucket's
  * CUDA graph (captured at the shape's first forward or by s1c_warmup) replays every batch of that
  * shape; larger batches run their exact shape (graph captured at its second forward).
  * Load check (the reference's load-time kernel checks and fallback rule, lib.rs:319-362): every

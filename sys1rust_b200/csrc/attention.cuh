@@ -111,7 +111,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 4) attention_varlen_kernel(const 
     k_lo = max(s_begin, s_begin + p0 - args.window);
     k_hi = min(s_end, s_begin + p1 + args.window + 1);
   }
-  const int n_tiles = (k_hi - k_lo + ATT_BK - 1) / ATT_BK;
+  const int n_tiles = max(0, k_hi - k_lo + ATT_BK - 1) / ATT_BK;
 
   const uint32_t q_s = smem_u32(sQ);
   const uint32_t k_s0 = smem_u32(sK[0]), v_s0 = smem_u32(sV[0]);

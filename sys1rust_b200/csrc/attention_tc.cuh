@@ -192,7 +192,7 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
     k_lo = max(s_begin, q_first - args.window);
     k_hi = min(s_end, q_first + q_count + args.window);
   }
-  const int nt = (k_hi - k_lo + ATTC_BK - 1) / ATTC_BK;
+  const int nt = max(0, k_hi - k_lo + ATTC_BK - 1) / ATTC_BK;
   const int nsteps = nh * nt;
 
   if (threadIdx.x == 0) {
@@ -366,15 +366,31 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(s_free);
+      // Keys outside [lo, hi_c) are masked only in the halves where some row of the warp has a
+      // boundary (halves no row sees were not read and hold -inf): one bit test per column. Tiles
+      // every row of the warp sees whole (most key steps of global layers) skip all of it.
       if (!__all_sync(0xffffffffu, lo <= 0 && hi_c >= ATTC_BK)) {
 #pragma unroll
-        for (int c = 0; c < 64; ++c) s[c] = (c >= lo && c < hi_c) ? s[c] : -INFINITY;
+        for (int half = 0; half < 2; ++half) {
+          const int c0 = half * 32;
+          if ((half ? need1 : need0) && !__all_sync(0xffffffffu, lo <= c0 && hi_c >= c0 + 32)) {
+            const int a = min(max(lo - c0, 0), 32), b = min(max(hi_c - c0, 0), 32);
+            const uint32_t vis = (b >= 32 ? 0xffffffffu : (1u << b) - 1u) & ~(a >= 32 ? 0xffffffffu : (1u << a) - 1u);
+#pragma unroll
+            for (int c = 0; c < 32; ++c) s[c0 + c] = (vis & (1u << c)) ? s[c0 + c] : -INFINITY;
+          }
+        }
       }
-      float pm[8];  // 8 independent partial maxima, then a tree
+      float pm[8];  // 8 independent partial maxima over the halves read, then a tree
 #pragma unroll
-      for (int i = 0; i < 8; ++i) pm[i] = s[i];
+      for (int i = 0; i < 8; ++i) pm[i] = -INFINITY;
 #pragma unroll
-      for (int c = 8; c < 64; ++c) pm[c & 7] = fmaxf(pm[c & 7], s[c]);
+      for (int half = 0; half < 2; ++half) {
+        if (half ? need1 : need0) {
+#pragma unroll
+          for (int c = half * 32; c < half * 32 + 32; ++c) pm[c & 7] = fmaxf(pm[c & 7], s[c]);
+        }
+      }
       const float mx =
           fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])), fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7]))) * sc;
       // Raise the reference maximum only when this tile's maximum passes it by more than 2^8.

@@ -852,6 +852,10 @@ struct HostMeta {
   int hidden_rows = 0;                        // tokens whose final hidden state is written out
   double pairs_global = 0, pairs_local = 0, pairs_rows = 0;  // attended (query, key) pairs per head-set
   std::vector<int> cu, srows, mrows, prows, mcount;
+  // attention key range of every row, (begin, end) token pairs: the row's own tokens, or with
+  // `real_len` its real tokens only (padding tokens attend them but are never keys); a work
+  // item's x field is 2 * row, so the kernels read its range at acu[x], acu[x + 1]
+  std::vector<int> acu;
   std::vector<uint32_t> qtype;
   // attention work lists for the two query-tile heights: full rows (encoder, head layer 0) and
   // the pruned head rows, tiles of 64 (mma.sync kernel) and 128 (tcgen05 kernel)
@@ -882,9 +886,9 @@ void validate_varlen(const s1c_backend& B, const s1c_varlen& in) {
 // Attention work items with the longest sequences first. The attention grids launch item-major
 // (all heads of one item in consecutive blocks), so the tiles with the most keys start in the
 // first wave and the short ones fill the tail (longest-processing-time order).
-static void longest_first(std::vector<int4>& items, const int* cu) {
-  std::stable_sort(items.begin(), items.end(), [cu](const int4& a, const int4& b) {
-    return cu[a.x + 1] - cu[a.x] > cu[b.x + 1] - cu[b.x];
+static void longest_first(std::vector<int4>& items, const int* acu) {
+  std::stable_sort(items.begin(), items.end(), [acu](const int4& a, const int4& b) {
+    return acu[a.x + 1] - acu[a.x] > acu[b.x + 1] - acu[b.x];
   });
 }
 
@@ -895,7 +899,7 @@ struct ItemPad {
   bool on = false;
   int full = 0, rows = 0, full_tc = 0, rows_tc = 0;
 };
-HostMeta make_meta(const s1c_varlen& in, int window, int n_items, const ItemPad& pad) {
+HostMeta make_meta(const s1c_varlen& in, int window, int n_items, const ItemPad& pad, const int* real_len = nullptr) {
   HostMeta m;
   m.n = in.n;
   m.kmax = in.kmax;
@@ -908,8 +912,11 @@ HostMeta make_meta(const s1c_varlen& in, int window, int n_items, const ItemPad&
   m.srows.resize(m.R);
   m.prows.resize(in.n);
   m.mrows.resize(m.M);
+  m.acu.resize(2 * (size_t)in.n);
   for (int r = 0; r < in.n; ++r) {
     const int base = m.cu[r];
+    m.acu[2 * r] = base;
+    m.acu[2 * r + 1] = real_len ? base + real_len[r] : m.cu[r + 1];
     m.srows[r * (1 + in.kmax)] = base;
     m.prows[r] = r * (1 + in.kmax);
     for (int k = 0; k < in.kmax; ++k) {
@@ -922,18 +929,19 @@ HostMeta make_meta(const s1c_varlen& in, int window, int n_items, const ItemPad&
     m.pairs_rows += (double)(1 + in.kmax) * len;
     for (int i = 0; i < len; ++i) m.pairs_local += std::min(i, window) + std::min(len - 1 - i, window) + 1;
     const int rows = 1 + in.kmax;
-    for (int q = 0; q < len; q += ATT_BQ) m.items_full.push_back(make_int4(r, base + q, std::min(ATT_BQ, len - q), 0));
+    for (int q = 0; q < len; q += ATT_BQ)
+      m.items_full.push_back(make_int4(2 * r, base + q, std::min(ATT_BQ, len - q), 0));
     for (int q = 0; q < rows; q += ATT_BQ)
-      m.items_rows.push_back(make_int4(r, r * rows + q, std::min(ATT_BQ, rows - q), 1));
+      m.items_rows.push_back(make_int4(2 * r, r * rows + q, std::min(ATT_BQ, rows - q), 1));
     for (int q = 0; q < len; q += ATTC_BQ)
-      m.items_full_tc.push_back(make_int4(r, base + q, std::min(ATTC_BQ, len - q), 0));
+      m.items_full_tc.push_back(make_int4(2 * r, base + q, std::min(ATTC_BQ, len - q), 0));
     for (int q = 0; q < rows; q += ATTC_BQ)
-      m.items_rows_tc.push_back(make_int4(r, r * rows + q, std::min(ATTC_BQ, rows - q), 1));
+      m.items_rows_tc.push_back(make_int4(2 * r, r * rows + q, std::min(ATTC_BQ, rows - q), 1));
   }
-  longest_first(m.items_full, m.cu.data());
-  longest_first(m.items_rows, m.cu.data());
-  longest_first(m.items_full_tc, m.cu.data());
-  longest_first(m.items_rows_tc, m.cu.data());
+  longest_first(m.items_full, m.acu.data());
+  longest_first(m.items_rows, m.acu.data());
+  longest_first(m.items_full_tc, m.acu.data());
+  longest_first(m.items_rows_tc, m.acu.data());
   if (pad.on) {
     auto fill = [](std::vector<int4>& v, int count, int mode) {
       if ((int)v.size() > count) throw S1cError(S1C_ERR_ARG, "internal: bucket work list overflow");
@@ -950,6 +958,7 @@ HostMeta make_meta(const s1c_varlen& in, int window, int n_items, const ItemPad&
 struct DevMeta {
   const uint32_t* ids;
   const int* cu;
+  const int* acu;
   const int* srows;
   const int* mrows;
   const int* prows;
@@ -980,6 +989,7 @@ DevMeta upload_meta(s1c_backend& B, const HostMeta& m, const uint32_t* host_ids)
       {m.items_rows.data(), m.items_rows.size() * 16},
       {m.items_full_tc.data(), m.items_full_tc.size() * 16},
       {m.items_rows_tc.data(), m.items_rows_tc.size() * 16},
+      {m.acu.data(), m.acu.size() * 4},
   };
   std::vector<size_t> off(parts.size());
   size_t total = 0;
@@ -1026,6 +1036,7 @@ DevMeta upload_meta(s1c_backend& B, const HostMeta& m, const uint32_t* host_ids)
   dm.items_rows = reinterpret_cast<const int4*>(dv + off[8]);
   dm.items_full_tc = reinterpret_cast<const int4*>(dv + off[9]);
   dm.items_rows_tc = reinterpret_cast<const int4*>(dv + off[10]);
+  dm.acu = reinterpret_cast<const int*>(dv + off[11]);
   return dm;
 }
 
@@ -1112,13 +1123,13 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
                                  : (rows ? m.items_rows.size() : m.items_full.size()));
     if (n_items == 0) return;
     if (tc) {
-      AttnTcArgs a{dm.cu, items, o, os, q_col0, k_col0, v_col0, d / 64, window, scale_log2, B.d_status};
+      AttnTcArgs a{dm.acu, items, o, os, q_col0, k_col0, v_col0, d / 64, window, scale_log2, B.d_status};
       launch(B, nl, name, 4.0 * d * pairs, 0, [&] {
         const dim3 grid((unsigned)n_items * ((d / 64 + ATTC_HEADS - 1) / ATTC_HEADS));
         launch_k(attention_tc_kernel, grid, dim3(ATTC_THREADS), ATTC_SMEM, st, tq, tkv, a);
       });
     } else {
-      AttnArgs a{q, k, v, o, qs, ks, vs, os, dm.cu, items, window, scale_log2, d / 64};
+      AttnArgs a{q, k, v, o, qs, ks, vs, os, dm.acu, items, window, scale_log2, d / 64};
       launch(B, nl, name, 4.0 * d * pairs, 0, [&] {
         launch_k(attention_varlen_kernel, dim3((unsigned)n_items * (d / 64)), dim3(ATT_THREADS), 0, st, a);
       });
@@ -1283,13 +1294,15 @@ void check_status(s1c_backend& B) {
 // Shape buckets (settings `buckets=`, `warm=`; the reference's length buckets and load-time
 // warm-up, laya-mlx/src/lib.rs:89-94, :1152-1173, :1826-1831). A batch whose packed tokens fit a
 // bucket runs as the bucket's shape: its rows first, then `nb - n` dummy rows (token id 0, no
-// markers) that hold the bucket's remaining tokens, markers padded to `kb` slots per row. Dummy
+// markers) that hold the bucket's remaining tokens (none when the tokens fill the bucket exactly),
+// markers padded to `kb` slots per row. Dummy
 // rows get no attention work items: their tokens' attention outputs are never written, so
 // whatever those rows compute stays in their own rows (every kernel but attention is row-local,
 // and attention only reads keys of a query's own row) and is dropped with them. The work lists
 // are filled with empty items to lengths fixed by (T, nb, kb), so one captured graph per bucket
-// shape replays every batch of that shape. Row counts are bucketed to powers of two (2 .. 64, at
-// least one dummy row), marker slots to multiples of 4.
+// shape replays every batch of that shape. Row counts are bucketed to powers of two up to 64 (at
+// least one dummy row whenever there are tokens to hold), marker slots to 4, or to a multiple of
+// 16 past 4 (the pruned head rows are one 128-row tile either way for a few rows).
 constexpr int BUCKET_MAX_ROWS = 64;
 struct BucketShape {
   int T = 0, n = 0, kmax = 0;
@@ -1297,16 +1310,21 @@ struct BucketShape {
 bool pick_bucket(const s1c_backend& B, const s1c_varlen& in, BucketShape& out) {
   if (B.buckets.empty() || in.n == 0) return false;
   const int T = in.cu_seqlens[in.n];
-  int nb = 2;
+  if (in.n > BUCKET_MAX_ROWS) return false;
+  int nb = 2;  // with padding tokens: room for at least one dummy row
   while (nb < in.n + 1) nb *= 2;
-  if (nb > BUCKET_MAX_ROWS) return false;
   for (int t : B.buckets) {
     const int pad = t - T;
-    if (pad < nb - in.n) continue;  // every dummy row holds at least one token
-    if ((int64_t)pad > (int64_t)(nb - in.n) * B.max_pos) return false;  // dummy rows stay within max_position
+    if (pad < 0) continue;
+    int rows = in.n;  // the tokens fill the bucket: no dummy rows
+    if (pad > 0) {
+      if (nb > BUCKET_MAX_ROWS || pad < nb - in.n) continue;  // every dummy row holds at least one token
+      if ((int64_t)pad > (int64_t)(nb - in.n) * B.max_pos) return false;  // dummy rows within max_position
+      rows = nb;
+    }
     out.T = t;
-    out.n = nb;
-    out.kmax = std::max(4, (in.kmax + 3) / 4 * 4);
+    out.n = rows;
+    out.kmax = in.kmax <= 4 ? 4 : (in.kmax + 15) / 16 * 16;
     return true;
   }
   return false;
@@ -1359,14 +1377,14 @@ struct StageOut {
   int n = 0, kmax = 0, kstride = 0;
 };
 StageOut enqueue_forward(s1c_backend& B, const s1c_varlen& in, const uint32_t* host_ids, const uint32_t* dev_ids,
-                         float* d_hidden) {
+                         float* d_hidden, const int* real_len = nullptr) {
   BucketShape bs;
   BucketBatch bb;
-  const bool bucketed = pick_bucket(B, in, bs);
+  const bool bucketed = !real_len && pick_bucket(B, in, bs);
   if (bucketed) make_bucket_batch(in, host_ids, bs, bb);
   const s1c_varlen& run = bucketed ? bb.v : in;
   const int T_in = in.cu_seqlens[in.n];
-  HostMeta m = make_meta(run, B.window, in.n, bucketed ? bucket_item_pad(bs) : ItemPad{});
+  HostMeta m = make_meta(run, B.window, in.n, bucketed ? bucket_item_pad(bs) : ItemPad{}, real_len);
   m.hidden_rows = T_in;
   ensure_capacity(B, m.T, m.R);
   const size_t nl = (size_t)m.M, np = (size_t)m.n * B.d;
@@ -1426,8 +1444,11 @@ StageOut enqueue_forward(s1c_backend& B, const s1c_varlen& in, const uint32_t* h
   return so;
 }
 
-// Host-buffer forward: ids and metadata copied in, logits / pooled / hidden copied out.
-void forward_host(s1c_backend& B, const s1c_varlen& in, float* logits, float* pooled, float* hidden) {
+// Host-buffer forward: ids and metadata copied in, logits / pooled / hidden copied out. With
+// `real_len`, row r's first real_len[r] tokens are its real tokens and the rest padding tokens that
+// attend them (never attended themselves).
+void forward_host(s1c_backend& B, const s1c_varlen& in, float* logits, float* pooled, float* hidden,
+                  const int* real_len = nullptr) {
   validate_varlen(B, in);
   if (in.n == 0) return;
   if (!in.ids) throw S1cError(S1C_ERR_ARG, "null batch array");
@@ -1437,7 +1458,7 @@ void forward_host(s1c_backend& B, const s1c_varlen& in, float* logits, float* po
   const size_t nh = hidden ? (size_t)T * B.d : 0;
   DevBuf hid_dev;
   if (nh) hid_dev.ensure(nh * 4);
-  const StageOut so = enqueue_forward(B, in, in.ids, nullptr, nh ? hid_dev.as<float>() : nullptr);
+  const StageOut so = enqueue_forward(B, in, in.ids, nullptr, nh ? hid_dev.as<float>() : nullptr, real_len);
   const size_t out_bytes = (so.n_logits + so.n_pooled + nh) * 4;
   if (out_bytes > B.h_out_bytes) {
     CK(cudaStreamSynchronize(B.stream));
@@ -2113,32 +2134,39 @@ size_t s1c_profile_report(const s1c_backend* b, char* buf, size_t cap) {
 
 s1c_status s1c_warmup(s1c_backend* b) {
   return guarded(b, [&] {
-    // One forward per (bucket, warm row count) as the reference's warm_buckets (lib.rs:1152-1173):
-    // rows of equal length filling the bucket's tokens less one per dummy row, two markers each,
-    // so every bucket shape a single request (or `warm=` rows) lands in has its graph captured.
-    // Without buckets: one short row and one 4-row batch.
+    // Forwards per (bucket, warm row count) as the reference's warm_buckets (lib.rs:1152-1173):
+    // rows of equal length, once filling the bucket exactly and once leaving room for the dummy
+    // rows, each with 2 and with 16 markers (the two marker-slot buckets of up to 16 markers), so
+    // the bucket shapes a batch of that many rows can land in have their graphs captured. Without
+    // buckets: one short row and one 4-row batch.
     std::vector<std::pair<int, int>> shapes;  // (rows, tokens per row)
     if (b->buckets.empty()) {
       shapes = {{1, 64}, {4, 64}};
     } else {
       for (int t : b->buckets)
         for (int n : b->warm_rows) {
+          if (n > BUCKET_MAX_ROWS) continue;
+          if (t % n == 0 && t / n >= 3 && t / n <= b->max_pos) shapes.push_back({n, t / n});
           int nb = 2;
           while (nb < n + 1) nb *= 2;
           const int per = (t - (nb - n)) / n;
           if (nb <= BUCKET_MAX_ROWS && per >= 3 && per <= b->max_pos) shapes.push_back({n, per});
         }
     }
-    for (auto [n, len] : shapes) {
-      std::vector<int32_t> cu(n + 1);
-      for (int r = 0; r <= n; ++r) cu[r] = r * len;
-      std::vector<uint32_t> ids((size_t)n * len, 0), mpos((size_t)n * 2), qt(n, 0);
-      std::vector<int32_t> mc(n, 2);
-      for (int r = 0; r < n; ++r) { mpos[2 * r] = 1; mpos[2 * r + 1] = 2; }
-      s1c_varlen v{n, 2, ids.data(), cu.data(), mpos.data(), mc.data(), qt.data()};
-      std::vector<float> lg((size_t)n * 2), pl((size_t)n * b->d);
-      forward_host(*b, v, lg.data(), pl.data(), nullptr);
-    }
+    for (auto [n, len] : shapes)
+      for (int k : {2, 16}) {
+        if (k > len) continue;
+        std::vector<int32_t> cu(n + 1);
+        for (int r = 0; r <= n; ++r) cu[r] = r * len;
+        std::vector<uint32_t> ids((size_t)n * len, 0), mpos((size_t)n * k), qt(n, 0);
+        std::vector<int32_t> mc(n, k);
+        for (int r = 0; r < n; ++r)
+          for (int i = 0; i < k; ++i) mpos[(size_t)r * k + i] = (uint32_t)i;
+        s1c_varlen v{n, k, ids.data(), cu.data(), mpos.data(), mc.data(), qt.data()};
+        std::vector<float> lg((size_t)n * k), pl((size_t)n * b->d);
+        forward_host(*b, v, lg.data(), pl.data(), nullptr);
+        if (b->buckets.empty()) break;
+      }
   });
 }
 
@@ -2162,15 +2190,36 @@ s1c_status s1c_encoder_hidden(s1c_backend* b, const s1c_batch* batch, float* out
   return guarded(b, [&] {
     if (!batch || !out) throw S1cError(S1C_ERR_ARG, "null argument");
     PackedBatch p;
-    pack_batch(*batch, p);
-    const size_t d = b->d;
-    std::vector<float> lg(batch->n * batch->kmax), pl(batch->n * d), hid((size_t)p.ids.size() * d);
-    forward_host(*b, p.v, lg.data(), pl.data(), hid.data());
-    std::memset(out, 0, batch->n * batch->len * d * sizeof(float));
-    for (size_t r = 0; r < batch->n; ++r) {
-      const size_t s = batch->seq_lens[r];
-      std::memcpy(out + r * batch->len * d, hid.data() + (size_t)p.cu[r] * d, s * d * sizeof(float));
+    pack_batch(*batch, p);  // checks the mask against seq_lens
+    validate_varlen(*b, p.v);
+    // The reference's hook runs the padded layout (lib.rs:1865-1878): a padding position is the
+    // batch's padding id at its padded index, attending its row's real keys through the -1e4 key
+    // mask; real positions never attend it. Here each row runs its real tokens and then padding
+    // tokens as queries whose key range is the row's real tokens. A padding position farther than
+    // the window from every real token sees only masked keys in the reference's sliding-window
+    // layers (a softmax over -1e4 entries); those positions are not computed and stay 0.
+    const bool any_local = std::find(b->local.begin(), b->local.end(), 1) != b->local.end();
+    const size_t n = batch->n, len = batch->len, d = b->d;
+    PackedBatch q;
+    std::vector<int> real(n), keep(n);
+    q.cu.assign(1, 0);
+    for (size_t r = 0; r < n; ++r) {
+      const size_t sl = batch->seq_lens[r];
+      real[r] = (int)sl;
+      keep[r] = (int)(any_local ? std::min(len, sl + (size_t)b->window) : len);
+      q.ids.insert(q.ids.end(), batch->input_ids + r * len, batch->input_ids + r * len + keep[r]);
+      q.cu.push_back((int32_t)q.ids.size());
     }
+    q.mcount = p.mcount;
+    q.qtype = p.qtype;
+    q.mpos = p.mpos;
+    q.v = s1c_varlen{(int32_t)n, (int32_t)batch->kmax, q.ids.data(), q.cu.data(), q.mpos.data(), q.mcount.data(),
+                     q.qtype.data()};
+    std::vector<float> lg(n * batch->kmax), pl(n * d), hid(q.ids.size() * d);
+    if (n) forward_host(*b, q.v, lg.data(), pl.data(), hid.data(), real.data());
+    std::memset(out, 0, n * len * d * sizeof(float));
+    for (size_t r = 0; r < n; ++r)
+      std::memcpy(out + r * len * d, hid.data() + (size_t)q.cu[r] * d, (size_t)keep[r] * d * sizeof(float));
   });
 }
 

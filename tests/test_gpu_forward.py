@@ -65,15 +65,18 @@ def check_against_oracle(cfg, w, be, batch):
     # probabilities per question
     for pg, pw in zip(question_probs(got.logits, batch), question_probs(lo, batch)):
         assert np.abs(pg - pw).max() < PROB_ABS
-    # argmax where the margin is clear
-    err = np.abs(got.logits - lo).max()
+    # argmax: equal to the oracle's wherever its top-two margin exceeds twice the measured logit
+    # error; in every row the option picked has an oracle logit within that error of the best
+    err = float(np.abs(got.logits - lo).max()) if got.logits.size else 0.0
     for r in range(batch.n):
         c = int(batch.marker_count[r])
         if c >= 2:
             z = lo[r * batch.kmax: r * batch.kmax + c]
+            gi = int(np.argmax(got.logits[r * batch.kmax: r * batch.kmax + c]))
+            assert z[gi] >= z.max() - 2 * err
             srt = np.sort(z)
             if srt[-1] - srt[-2] > 2 * err:
-                assert np.argmax(got.logits[r * batch.kmax: r * batch.kmax + c]) == np.argmax(z)
+                assert gi == np.argmax(z)
     assert np.all(np.isfinite(got.pooled))
     prel = np.linalg.norm(got.pooled - po) / np.linalg.norm(po)
     assert prel < 5e-2, f"pooled rel err {prel}"
@@ -172,8 +175,35 @@ def test_padded_and_varlen_entry_points_agree(cuda_lib):
     assert np.array_equal(a.logits, b.logits) and np.array_equal(a.pooled, b.pooled)
     hid = be.encoder_hidden(batch).reshape(batch.n, batch.len, -1)
     am = batch.attention_mask.reshape(batch.n, batch.len).astype(bool)
-    assert np.array_equal(hid[am], b.hidden.reshape(-1, cfg.encoder.hidden_size))
-    assert np.all(hid[~am] == 0)
+    # the hook also runs the padding positions near the real tokens, so its GEMMs see more rows:
+    # equal to rounding, not bit for bit
+    ref = b.hidden.reshape(-1, cfg.encoder.hidden_size)
+    assert np.linalg.norm(hid[am] - ref) / np.linalg.norm(ref) < 1e-2
+
+
+@pytest.mark.parametrize("name", ["small:3", "large:0"])
+def test_encoder_hidden_at_padding_positions(cuda_lib, name):
+    """``encoder_hidden`` in the padded layout (``lib.rs:1865-1878``): padding positions within the
+    sliding window of a real token hold the reference's computed state (the oracle runs the padded
+    layout with the -1e4 key mask); positions farther away see only masked keys in the reference's
+    window layers and are 0 here."""
+    from conftest import get_backend
+    cfg, w, be = get_backend(name)
+    batch = collate_to(make_rows(cfg, 70, [1, 63, 300], [0, 3, 5]), cfg.encoder.pad_token_id)
+    hid = be.encoder_hidden(batch).reshape(batch.n, batch.len, -1)
+    _, _, ho = oracle(cfg, w, batch)
+    ho = np.asarray(ho).reshape(batch.n, batch.len, -1)
+    win = cfg.encoder.window()
+    for r, sl in enumerate(batch.seq_lens):
+        keep = min(batch.len, int(sl) + win)
+        got, want = hid[r, :keep], ho[r, :keep]
+        rel = np.linalg.norm(got - want) / np.linalg.norm(want)
+        assert rel < HIDDEN_REL, (r, rel)
+        pad = slice(int(sl), keep)
+        if keep > sl:  # the padding positions alone
+            rel_p = np.linalg.norm(hid[r, pad] - ho[r, pad]) / np.linalg.norm(ho[r, pad])
+            assert rel_p < HIDDEN_REL, (r, rel_p)
+        assert np.all(hid[r, keep:] == 0)
 
 
 def test_batch_without_markers(cuda_lib):
@@ -252,3 +282,34 @@ def test_graph_replay_matches_direct_launches(cuda_lib):
     assert np.array_equal(ob.logits, rb.logits) and np.array_equal(ob.pooled, rb.pooled)
     assert not np.array_equal(ob.pooled, outs[0].pooled)
     direct.close()
+
+
+def test_tied_options_pick_the_first(cuda_lib):
+    """Two marker slots on the same token get bit-identical logits (the same hidden row through the
+    same scorer), so their tie is exact on both sides; the answer's argmax is then the first of the
+    tied options, as the reference's decode takes the first maximum."""
+    from conftest import get_backend
+    from sys1rust_b200.batch import EncodedItem
+    from sys1rust_b200.decode import ActHead, Temperatures, decode
+    cfg, w, be = get_backend("small:3")
+    rows = make_rows(cfg, 71, [40, 90], [0, 0])
+    best = []
+    for it in rows:
+        # find the row's best marker position, then offer it twice after a worse option
+        probe = EncodedItem(it.ids, list(range(1, len(it.ids) - 1)), 0)
+        lg = be.forward(collate_to([probe], cfg.encoder.pad_token_id)).logits
+        p_best, p_worse = 1 + int(np.argmax(lg)), 1 + int(np.argmin(lg))
+        best.append(EncodedItem(it.ids, [p_worse, p_best, p_best], 0))
+    batch = collate_to(best, cfg.encoder.pad_token_id)
+    out = be.forward(batch)
+    lo, _, _ = oracle(cfg, w, batch)
+    for r in range(batch.n):
+        z = out.logits[r * batch.kmax: r * batch.kmax + 3]
+        assert z[1] == z[2] and z[1] > z[0]
+        assert lo[r * batch.kmax + 1] == lo[r * batch.kmax + 2]
+        assert int(np.argmax(z)) == 1 == int(np.argmax(lo[r * batch.kmax: r * batch.kmax + 3]))
+    d = cfg.encoder.hidden_size
+    head = ActHead(np.zeros((4, d + 4), np.float32), np.zeros(4, np.float32), np.zeros((2, 4), np.float32),
+                   np.zeros(2, np.float32))
+    answers, _ = decode(out.logits, out.pooled, batch.marker_count, batch.qtype, batch.kmax, d, Temperatures(), head)
+    assert [a["argmax"] for a in answers] == [1, 1]
