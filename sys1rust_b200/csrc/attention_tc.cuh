@@ -13,23 +13,27 @@
 //               ring), 128-byte swizzle.
 //   warp 1      TMEM owner and MMA issuer:
 //                 S = Q K^T     M=128 N=64 K=64 (K-major A and B from shared memory)
-//                               -> TMEM cols [0,64)
+//                               -> TMEM cols [0,64) for even key steps, [64,128) for odd ones
 //                 O += P V      M=128 N=64 K=64 (P from TMEM, V MN-major from shared memory)
-//                               -> TMEM cols [64,128) for even heads, [128,192) for odd heads
-//               S of the next key step is issued as soon as the softmax has read the current S.
+//                               -> TMEM cols [128,192) for even heads, [192,256) for odd heads
+//               The softmax writes P over the first 32 columns of its step's S buffer (bf16
+//               pairs), and S of step st + 2 is issued into the same buffer right after P V of
+//               step st: this thread's tcgen05 operations run in issue order, so P V has read P
+//               before S overwrites it. S of a step is thus issued a whole key step ahead,
+//               without waiting for the softmax to read the previous S.
 //   warps 2..5  softmax, one query row per thread (TMEM lane = row). Per key step: the row's
 //               maximum m; p = 2^(s * scale - m_ref) with a reference maximum m_ref that is only
 //               raised when m exceeds it by more than 2^8 (p stays <= 256, exact in fp32 and
 //               bf16-representable like any p), in which case the running sum and the O
 //               accumulator in TMEM are rescaled by 2^(m_ref_old - m_ref) once the previous
-//               P V has completed. P is rounded to bf16 pairs and written to TMEM (cols
-//               [192,224) for even key steps, [224,256) for odd ones), where the P V MMA reads
-//               it as its A operand: no shared-memory round trip and no proxy fence, and a row
-//               may run one key step ahead of the P V that reads its previous P.
+//               P V has completed. P is rounded to bf16 pairs and written to TMEM over the S it
+//               came from, where the P V MMA reads it as its A operand: no shared-memory round
+//               trip and no proxy fence.
 //               32-column halves of S that no row of a warp may see (window edges, a row's
-//               last partial key tile) are neither read nor exponentiated. A finished head's
-//               O / l is read from TMEM and stored bf16 during the next key step, after its
-//               exponentials, by which time the head's last P V has completed.
+//               last partial key tile) are neither read nor exponentiated; keys past a row's
+//               bounds are masked only in halves where some row of the warp has a boundary.
+//               A finished head's O / l is read from TMEM and stored bf16 during the next key
+//               step, after its exponentials, by which time the head's last P V has completed.
 #pragma once
 #include <cuda.h>
 #include "common.cuh"
@@ -37,10 +41,10 @@
 namespace s1c {
 
 constexpr int ATTC_BQ = 128, ATTC_BK = 64, ATTC_THREADS = 192, ATTC_HEADS = 4, ATTC_KV_STAGES = 4;
-// TMEM columns: S [0,64), O of even heads [64,128), odd heads [128,192), P (bf16 pairs) of even
-// key steps [192,224), odd key steps [224,256)
+// TMEM columns: S (then P, bf16 pairs, over its first 32 columns) of even key steps [0,64), of odd
+// key steps [64,128); O of even heads [128,192), of odd heads [192,256)
 constexpr uint32_t ATTC_TMEM_COLS = 256;
-constexpr uint32_t ATTC_TMEM_P = 192;
+constexpr uint32_t ATTC_TMEM_O = 128;
 constexpr uint32_t ATTC_Q_BYTES = ATTC_BQ * 64 * 2;       // 16 KB
 constexpr uint32_t ATTC_KV_BYTES = ATTC_BK * 64 * 2;      // 8 KB each for K and V
 constexpr size_t ATTC_SMEM = 2 * ATTC_Q_BYTES + ATTC_KV_STAGES * 2 * ATTC_KV_BYTES + 1024 + 256;
@@ -170,10 +174,9 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
   uint64_t* o_free = bars + 6;    // [2]
   uint64_t* kv_full = bars + 8;   // [NS]
   uint64_t* kv_empty = bars + 8 + NS;
-  uint64_t* s_full = bars + 8 + 2 * NS;
-  uint64_t* s_free = s_full + 1;
-  uint64_t* p_full = s_full + 2;  // [2]: P of even / odd key steps written
-  uint64_t* p_free = s_full + 4;  // [2]: P V of even / odd key steps completed
+  uint64_t* s_full = bars + 8 + 2 * NS;  // [2]: S of even / odd key steps computed
+  uint64_t* p_full = s_full + 2;          // [2]: P of even / odd key steps written
+  uint64_t* p_free = s_full + 4;          // [2]: P V of even / odd key steps completed
   uint64_t* drain = s_full + 6;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -206,9 +209,8 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
     }
-    mbar_init(s_full, 1);
-    mbar_init(s_free, 4);
     for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 4);
       mbar_init(&p_free[i], 1);
     }
@@ -262,42 +264,42 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
     if (lane == 0 && nsteps > 0) {
       constexpr uint32_t idS = idesc_bf16_f32(128, ATTC_BK);
       constexpr uint32_t idO = idesc_bf16_f32_bmn(128, 64);
-      const uint32_t tS = tmem;
       bool ok = true;
-      // S for step `st`: needs Q of its head, K of its stage and the softmax done reading S(st - 1).
+      // S for step `st` into TMEM buffer st & 1: needs Q of its head and K of its stage; issued
+      // after P V of step st - 2, which read the P held in that buffer.
       auto issue_s = [&](int st) -> bool {
-        const int hi = st / nt, j = st % nt, s = st % NS, qb = hi & 1;
+        const int hi = st / nt, j = st % nt, s = st % NS, qb = hi & 1, sb = st & 1;
         if (j == 0 && !mbar_wait(&q_full[qb], (hi >> 1) & 1, args.status, DEV_TIMEOUT_MMA_FULL, abort_flag))
           return false;
         if (!mbar_wait(&kv_full[s], (st / NS) & 1, args.status, DEV_TIMEOUT_MMA_FULL, abort_flag)) return false;
-        if (st > 0 && !mbar_wait(s_free, (st - 1) & 1, args.status, DEV_TIMEOUT_MMA_TEMPTY, abort_flag)) return false;
         tc_fence_after();
         const uint32_t qa = smem_u32(sQ + qb * ATTC_Q_BYTES), ka = smem_u32(sK + s * ATTC_KV_BYTES);
+        const uint32_t tS = tmem + 64 * sb;
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           umma_bf16(tS, sdesc_kmajor_sw128(qa + k * 32), sdesc_kmajor_sw128(ka + k * 32), idS, k ? 1u : 0u);
-        umma_commit(s_full);
+        umma_commit(&s_full[sb]);
         if (j == nt - 1) umma_commit(&q_empty[qb]);  // Q of this head is no longer read
         return true;
       };
-      ok = issue_s(0);
+      ok = issue_s(0) && (nsteps < 2 || issue_s(1));
       for (int st = 0; ok && st < nsteps; ++st) {
-        if (st + 1 < nsteps && !issue_s(st + 1)) break;
-        const int hi = st / nt, j = st % nt, s = st % NS, ob = hi & 1, pb = st & 1;
-        if (!mbar_wait(&p_full[pb], (st >> 1) & 1, args.status, DEV_TIMEOUT_MMA_FULL, abort_flag)) break;
+        const int hi = st / nt, j = st % nt, s = st % NS, ob = hi & 1, sb = st & 1;
+        if (!mbar_wait(&p_full[sb], (st >> 1) & 1, args.status, DEV_TIMEOUT_MMA_FULL, abort_flag)) break;
         // the first P V of a head overwrites its O buffer: head hi - 2's O must have been read
         if (j == 0 && hi >= 2 &&
             !mbar_wait(&o_free[ob], ((hi >> 1) - 1) & 1, args.status, DEV_TIMEOUT_MMA_TEMPTY, abort_flag))
           break;
         tc_fence_after();
-        const uint32_t va = smem_u32(sV + s * ATTC_KV_BYTES), tO = tmem + 64 + 64 * ob;
-        const uint32_t tP = tmem + ATTC_TMEM_P + 32 * pb;
+        const uint32_t va = smem_u32(sV + s * ATTC_KV_BYTES), tO = tmem + ATTC_TMEM_O + 64 * ob;
+        const uint32_t tP = tmem + 64 * sb;
 #pragma unroll
         for (int k = 0; k < ATTC_BK / 16; ++k)
           umma_bf16_ts(tO, tP + 8 * k, sdesc_mnmajor_sw128(va + k * 2048), idO, (j > 0 || k > 0) ? 1u : 0u);
         umma_commit(&kv_empty[s]);
-        umma_commit(&p_free[pb]);
+        umma_commit(&p_free[sb]);
         if (j == nt - 1) umma_commit(&o_full[ob]);
+        if (st + 2 < nsteps && !issue_s(st + 2)) break;
       }
       umma_commit(drain);
       mbar_wait(drain, 0, args.status, DEV_TIMEOUT_DRAIN, nullptr);
@@ -306,7 +308,6 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
     const int quad = warp & 3;
     const int r = quad * 32 + lane;  // query row of this thread
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-    const uint32_t tS = tmem + lane_off;
     const int qtok = q_first + r;  // query token (mode 0)
     const float sc = args.scale_log2;
     float m_ref = -INFINITY, l = 0.f;
@@ -320,7 +321,7 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
       tc_fence_after();
       const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
       uint4* dst = reinterpret_cast<uint4*>(args.o + (size_t)(q_first + r) * args.o_stride + (h0 + hd) * 64);
-      const uint32_t tO = tmem + lane_off + 64 + 64 * ob;
+      const uint32_t tO = tmem + lane_off + ATTC_TMEM_O + 64 * ob;
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         float t[32];
@@ -356,16 +357,15 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
       }
       const bool need0 = __any_sync(0xffffffffu, lo < 32 && hi_c > 0);
       const bool need1 = __any_sync(0xffffffffu, lo < 64 && hi_c > 32);
-      if (!mbar_wait_warp(s_full, st & 1, args.status, DEV_TIMEOUT_EPILOGUE, abort_flag)) {
+      const int sb = st & 1;
+      const uint32_t tS = tmem + lane_off + 64 * sb;
+      if (!mbar_wait_warp(&s_full[sb], (st >> 1) & 1, args.status, DEV_TIMEOUT_EPILOGUE, abort_flag)) {
         ok = false;
         break;
       }
       tc_fence_after();
       float s[64];
       tmem_ld32x2(tS, need0, need1, s);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(s_free);
       // Keys outside [lo, hi_c) are masked only in the halves where some row of the warp has a
       // boundary (halves no row sees were not read and hold -inf): one bit test per column. Tiles
       // every row of the warp sees whole (most key steps of global layers) skip all of it.
@@ -425,27 +425,23 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
         }
         pend = -1;
       }
-      // P buffer st & 1 is free once the P V of step st - 2 has completed.
-      const int pb = st & 1;
-      if (st > 1 && !mbar_wait_warp(&p_free[pb], ((st >> 1) - 1) & 1, args.status, DEV_TIMEOUT_EPILOGUE, abort_flag)) {
-        ok = false;
-        break;
-      }
       {
+        // P over the S it came from (S of this step is in registers; P V of step st - 2, which
+        // read the P held here before, ran ahead of the S MMA that wrote this step's S)
         float pk[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) pk[i] = __uint_as_float(pack_bf16x2(s[2 * i], s[2 * i + 1]));
-        tmem_st32(tmem + lane_off + ATTC_TMEM_P + 32 * pb, pk);
+        tmem_st32(tS, pk);
       }
       if (__any_sync(0xffffffffu, rescale_o)) {
         // O is rescaled after the previous step's P V has completed
         if (st > 0 &&
-            !mbar_wait_warp(&p_free[pb ^ 1], ((st - 1) >> 1) & 1, args.status, DEV_TIMEOUT_EPILOGUE, abort_flag)) {
+            !mbar_wait_warp(&p_free[sb ^ 1], ((st - 1) >> 1) & 1, args.status, DEV_TIMEOUT_EPILOGUE, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t tO = tmem + lane_off + 64 + 64 * (hi & 1);
+        const uint32_t tO = tmem + lane_off + ATTC_TMEM_O + 64 * (hi & 1);
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
           float t[32];
@@ -458,7 +454,7 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[pb]);
+      if (lane == 0) mbar_arrive(&p_full[sb]);
       if (j == nt - 1) {
         pend = hi;
         l_pend = l;

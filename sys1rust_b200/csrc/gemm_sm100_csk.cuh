@@ -1,7 +1,7 @@
 // Cluster split-K bf16 GEMM for few output tiles (small token counts: the single-request path).
 //
 // A GEMM with M of one or two 128-row blocks has too few output tiles to put every SM on the
-// weights. Here a thread-block cluster of C CTAs (C = 1, 2, 4 or 8) computes one 128 x BN output
+// weights. Here a thread-block cluster of C CTAs (C = 1, 2 or 4, CSK_MAX_C) computes one 128 x BN output
 // tile (BN = 64 or 128): CTA r of the cluster accumulates the tile over K blocks
 // [r * nk / C, (r + 1) * nk / C) in its own TMEM. Rows [s * 128 / C, (s + 1) * 128 / C) of the
 // result belong to CTA s: as soon as its accumulator is ready, every CTA stages its partial tile
@@ -39,7 +39,7 @@ namespace s1c {
 
 struct CskArgs {
   int M, N, K;
-  int C;              // CTAs per cluster = K splits (1, 2, 4 or 8); the grid is tiles * C CTAs
+  int C;              // CTAs per cluster = K splits (1, 2 or 4); the grid is tiles * C CTAs
   void* out;          // bf16 output, or fp32 (EPI_RESID, or EPI_STORE with out_f32)
   int ldo;            // output row pitch in elements
   const float* bias;  // EPI_STORE / EPI_RESID, optional
@@ -52,7 +52,10 @@ struct CskArgs {
   int* status;
 };
 
-constexpr int CSK_MAX_C = 8;
+// Largest cluster the launch plan uses. In the single-request forward (CUDA graph, weights streaming from HBM) clusters of 8 measured slower than
+// clusters of at most 4 (128 tokens: 1.53 vs 1.26 ms per forward; 200 tokens: 2.03 vs 1.51 ms): the
+// partial-tile exchange grows with C while the weight stream is already spread over the SMs.
+constexpr int CSK_MAX_C = 4;
 
 template <int BN>
 __host__ __device__ constexpr size_t csk_smem_bytes() {
