@@ -114,7 +114,11 @@ typedef struct s1c_backend s1c_backend;
  * graphs=0|1 (CUDA graph per batch shape), pdl=0|1 (programmatic dependent launch),
  * buckets=<tokens>:<tokens>:... (packed-token buckets, default 128:256:...:1024:1280:...:2048;
  * buckets=0 turns them off), warm=<rows>:... (row counts s1c_warmup runs at every bucket, default 1),
- * check=0|1 (default 1) and check_fail=<kernel>[+<kernel>...].
+ * trace=0|1, layers=0|1, ops=0|1 (the reference's tracing knobs: per forward a stderr line with the
+ * shape, the graph use, the host enqueue and the device time; per encoder layer device times; per
+ * kernel summed device times; layers and ops launch kernel by kernel; with the asynchronous entry
+ * point the lines describe the last forward before s1c_synchronize), check=0|1 (default 1) and
+ * check_fail=<kernel>[+<kernel>...].
  * Buckets (the reference's `buckets` / `warm` settings, laya-mlx/src/lib.rs:89-94): a batch of n
  * rows whose packed tokens fit a bucket runs as the bucket's shape, with dummy rows (at least one,
  * row count a power of two up to 64; none when the tokens fill the bucket) holding the remaining

@@ -11,7 +11,10 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -462,8 +465,20 @@ struct s1c_backend {
   int64_t launches = 0;
   cudaStream_t own_stream = nullptr;
 
-  // per-launch profiling (s1c_profile)
+  // per-launch profiling (s1c_profile; the `ops` trace turns it on for its forwards)
   bool prof_on = false;
+  bool prof_user = false;  // s1c_profile(on)
+  // Tracing (`trace=1`, `layers=1`, `ops=1`, the reference's knobs of those names,
+  // laya-mlx/src/lib.rs:75-80, :1555-1579, :1842-1850): per forward one stderr line with the
+  // shape, the graph use, the host enqueue time and the device time (`trace`); the device time of
+  // every encoder layer (`layers`); the summed device time of every kernel (`ops`). `layers` and
+  // `ops` launch kernel by kernel (no graphs), like the reference's per-layer evaluation.
+  bool trace = false, trace_layers = false, trace_ops = false;
+  cudaEvent_t tr_ev[2] = {nullptr, nullptr};
+  std::vector<cudaEvent_t> layer_ev;
+  double tr_enqueue_us = 0;
+  bool tr_pending = false;
+  std::string tr_desc;
   std::vector<cudaEvent_t> ev_pool;
   size_t ev_used = 0;
   std::vector<ProfRec> prof_pending;
@@ -573,6 +588,9 @@ struct s1c_backend {
     if (stream) cudaStreamSynchronize(stream);
     if (own_stream) cudaStreamSynchronize(own_stream);
     for (cudaEvent_t e : ev_pool) cudaEventDestroy(e);
+    for (cudaEvent_t e : layer_ev) cudaEventDestroy(e);
+    for (cudaEvent_t e : tr_ev)
+      if (e) cudaEventDestroy(e);
     for (void* p : allocs) cudaFree(p);
     if (d_status) cudaFree(d_status);
     if (h_status) cudaFreeHost(h_status);
@@ -1152,6 +1170,11 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
 
   for (int i = 0; i < B.L; ++i) {
     const EncLayer& l = B.layers[i];
+    if (B.trace_layers) CK(cudaEventRecord(B.layer_ev[i], st));
+    nvtxRangePushA(l.local ? "s1c encoder layer (window)" : "s1c encoder layer (global)");
+    struct Pop {
+      ~Pop() { nvtxRangePop(); }
+    } pop;
     if (i > 0) ln("ln_attn", h, nullptr, T, l.attn_norm, nullptr, B.eps, x);
     GemmArgs g = gemm_args(T, 3 * d, d);
     g.pos = pos;
@@ -1173,6 +1196,7 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
            [&] { launch_gemm<EPI_RESID>(B.tm_act_i, l.tm_wo2, B.to_h, g2, nsm, st, B.gemm_variant, &(sk_tmp = sk(h, d)), &nl); });
   }
 
+  if (B.trace_layers) CK(cudaEventRecord(B.layer_ev[B.L], st));
   // final_norm, + type embedding, head layer 0's norm1
   launch(B, nl, "final_to_head", 0, Td * (4 + 4 + 2 + (d_hidden ? 4 : 0)), [&] {
     launch_k(final_to_head_kernel<D>, dim3((T + 7) / 8), dim3(256), 0, st, h, T, B.final_norm, B.eps, d_hidden, m.hidden_rows, trow, dm.qtype,
@@ -1278,10 +1302,43 @@ void forward_enqueue(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const
   }
 }
 
+// The trace lines of the last traced forward (after its stream has drained).
+void trace_report(s1c_backend& B, const std::map<std::string, ProfStat>& ops_before) {
+  if (!B.tr_pending) return;
+  B.tr_pending = false;
+  float dev_ms = 0.f;
+  CK(cudaEventElapsedTime(&dev_ms, B.tr_ev[0], B.tr_ev[1]));
+  if (B.trace)
+    std::fprintf(stderr, "s1c trace: %s enqueue %.1f us device %.3f ms\n", B.tr_desc.c_str(), B.tr_enqueue_us, dev_ms);
+  if (B.trace_layers && (int)B.layer_ev.size() == B.L + 1) {
+    std::string line = "s1c layers (ms):";
+    char buf[32];
+    for (int i = 0; i < B.L; ++i) {
+      float ms = 0.f;
+      CK(cudaEventElapsedTime(&ms, B.layer_ev[i], B.layer_ev[i + 1]));
+      std::snprintf(buf, sizeof buf, " %d:%.3f", i, ms);
+      line += buf;
+    }
+    std::fprintf(stderr, "%s\n", line.c_str());
+  }
+  if (B.trace_ops) {
+    for (const auto& kv : B.prof_stats) {
+      auto it = ops_before.find(kv.first);
+      const double ms = kv.second.ms - (it == ops_before.end() ? 0.0 : it->second.ms);
+      const int64_t n = kv.second.launches - (it == ops_before.end() ? 0 : it->second.launches);
+      if (n > 0) std::fprintf(stderr, "s1c ops: %-16s %4lld launches %8.3f ms\n", kv.first.c_str(), (long long)n, ms);
+    }
+    if (!B.prof_user) B.prof_stats.clear();
+  }
+}
+
 void check_status(s1c_backend& B) {
   CK(cudaMemcpyAsync(B.h_status, B.d_status, sizeof(int), cudaMemcpyDeviceToHost, B.stream));
   CK(cudaStreamSynchronize(B.stream));
+  const std::map<std::string, ProfStat> ops_before = B.trace_ops && B.prof_user ? B.prof_stats
+                                                                                 : std::map<std::string, ProfStat>{};
   if (!B.prof_pending.empty()) prof_collect(B);
+  trace_report(B, ops_before);
   if (*B.h_status != 0) {
     const int code = *B.h_status;
     CK(cudaMemsetAsync(B.d_status, 0, sizeof(int), B.stream));
@@ -1376,8 +1433,39 @@ struct StageOut {
   size_t n_logits, n_pooled;  // n * kstride, n * d
   int n = 0, kmax = 0, kstride = 0;
 };
+StageOut enqueue_forward_impl(s1c_backend& B, const s1c_varlen& in, const uint32_t* host_ids, const uint32_t* dev_ids,
+                              float* d_hidden, const int* real_len, std::string& how);
 StageOut enqueue_forward(s1c_backend& B, const s1c_varlen& in, const uint32_t* host_ids, const uint32_t* dev_ids,
                          float* d_hidden, const int* real_len = nullptr) {
+  nvtxRangePushA("s1c forward");
+  struct Pop {
+    ~Pop() { nvtxRangePop(); }
+  } pop;
+  const bool tracing = B.trace || B.trace_layers || B.trace_ops;
+  B.prof_on = B.prof_user || B.trace_ops;
+  if (!tracing) {
+    std::string how;
+    return enqueue_forward_impl(B, in, host_ids, dev_ids, d_hidden, real_len, how);
+  }
+  for (cudaEvent_t& e : B.tr_ev)
+    if (!e) CK(cudaEventCreate(&e));
+  if (B.trace_layers && B.layer_ev.empty()) {
+    B.layer_ev.resize(B.L + 1);
+    for (cudaEvent_t& e : B.layer_ev) CK(cudaEventCreate(&e));
+  }
+  const auto t0 = std::chrono::steady_clock::now();
+  CK(cudaEventRecord(B.tr_ev[0], B.stream));
+  std::string how;
+  const StageOut so = enqueue_forward_impl(B, in, host_ids, dev_ids, d_hidden, real_len, how);
+  CK(cudaEventRecord(B.tr_ev[1], B.stream));
+  B.tr_enqueue_us = std::chrono::duration<double, std::micro>(std::chrono::steady_clock::now() - t0).count();
+  B.tr_pending = true;
+  B.tr_desc = "rows " + std::to_string(in.n) + " tokens " + std::to_string(in.cu_seqlens[in.n]) + " kmax " +
+              std::to_string(in.kmax) + " " + how + " launches " + std::to_string(B.launches);
+  return so;
+}
+StageOut enqueue_forward_impl(s1c_backend& B, const s1c_varlen& in, const uint32_t* host_ids, const uint32_t* dev_ids,
+                              float* d_hidden, const int* real_len, std::string& how) {
   BucketShape bs;
   BucketBatch bb;
   const bool bucketed = !real_len && pick_bucket(B, in, bs);
@@ -1402,9 +1490,12 @@ StageOut enqueue_forward(s1c_backend& B, const s1c_varlen& in, const uint32_t* h
     if (m.T > T_in)
       CK(cudaMemsetAsync(const_cast<uint32_t*>(dm.ids) + T_in, 0, (size_t)(m.T - T_in) * 4, B.stream));
   }
-  const bool graphable = B.use_graphs && !d_hidden && !B.prof_on && B.stream != nullptr &&
+  how = bucketed ? "bucket " + std::to_string(m.T) + "x" + std::to_string(m.n) + "x" + std::to_string(m.kmax)
+                 : std::string("exact shape");
+  const bool graphable = B.use_graphs && !d_hidden && !B.prof_on && !B.trace_layers && B.stream != nullptr &&
                          B.stream != cudaStreamLegacy && B.stream != cudaStreamPerThread;
   if (!graphable) {
+    how += ", direct";
     forward_enqueue(B, m, dm, dm.ids, so.logits, so.pooled, d_hidden);
     return so;
   }
@@ -1415,6 +1506,7 @@ StageOut enqueue_forward(s1c_backend& B, const s1c_varlen& in, const uint32_t* h
     if (!bucketed) {
       if (B.seen.size() >= s1c_backend::MAX_SEEN) B.seen.clear();  // forget one-off shapes
       if (B.seen[key]++ < 1) {  // first sighting of an unbucketed shape: launch directly
+        how += ", direct (first sighting)";
         forward_enqueue(B, m, dm, dm.ids, so.logits, so.pooled, nullptr);
         return so;
       }
@@ -1437,6 +1529,9 @@ StageOut enqueue_forward(s1c_backend& B, const s1c_varlen& in, const uint32_t* h
     gr.launches = B.launches;
     B.seen.erase(key);
     it = B.graphs.emplace(key, gr).first;
+    how += ", graph captured";
+  } else {
+    how += ", graph replayed";
   }
   it->second.last_used = ++B.graph_clock;
   CK(cudaGraphLaunch(it->second.exec, B.stream));
@@ -1591,6 +1686,12 @@ void apply_settings(s1c_backend& B, const char* spec) {
       vals.erase(std::unique(vals.begin(), vals.end()), vals.end());
       if (k == "buckets") B.buckets = vals;
       else B.warm_rows = vals;
+    } else if (k == "trace" || k == "layers" || k == "ops") {
+      bool on;
+      if (v.empty() || v == "1") on = true;
+      else if (v == "0") on = false;
+      else throw S1cError(S1C_ERR_CONFIG, "settings: `" + kv + "`: `" + v + "` is not 0 or 1");
+      (k == "trace" ? B.trace : k == "layers" ? B.trace_layers : B.trace_ops) = on;
     } else if (k == "parallel_load") {
       // the runtime's own setting (BackendOptions::parallel_load, laya-core/src/backend.rs:44-66),
       // accepted here as the reference's backends accept it
@@ -2108,7 +2209,8 @@ s1c_status s1c_set_stream(s1c_backend* b, void* stream) {
 
 s1c_status s1c_profile(s1c_backend* b, int32_t on) {
   return guarded(b, [&] {
-    b->prof_on = on != 0;
+    b->prof_user = on != 0;
+    b->prof_on = b->prof_user || b->trace_ops;
     b->prof_stats.clear();
     b->prof_pending.clear();
     b->ev_used = 0;

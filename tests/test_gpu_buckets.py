@@ -123,3 +123,24 @@ def test_bucket_settings_are_checked(cuda_lib):
         assert np.all(np.isfinite(out.pooled))
     finally:
         be.close()
+
+
+def test_trace_layers_and_ops_lines(cuda_lib, capfd):
+    """`trace`, `layers` and `ops` (the reference's tracing knobs) print one line per forward, the
+    device time of every encoder layer and the per-kernel sums to stderr; outputs are unchanged."""
+    from conftest import get_backend
+    cfg, w, be = get_backend("small:3")
+    v = Varlen.from_rows(make_rows(cfg, 80, [50, 70], [2, 3]))
+    ref = be.forward_varlen(v)
+    capfd.readouterr()
+    tr = backend_with(cfg, w, "trace=1,layers=1,ops")
+    try:
+        out = tr.forward_varlen(v)
+        err = capfd.readouterr().err
+        assert "s1c trace: rows 2 tokens 120 kmax 3 bucket 128x4x4, direct" in err, err
+        layer_line = [l for l in err.splitlines() if l.startswith("s1c layers (ms):")]
+        assert len(layer_line) == 1 and len(layer_line[0].split()) == 3 + cfg.encoder.num_hidden_layers
+        assert "s1c ops: gemm_qkv_rope" in err and "attn_global" in err
+        assert np.array_equal(out.logits, ref.logits) and np.array_equal(out.pooled, ref.pooled)
+    finally:
+        tr.close()
