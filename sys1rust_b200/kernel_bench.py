@@ -4,6 +4,7 @@
     (variants as s1c_gemm: 0 by shape, 1 one-CTA 128x256, 2 two-CTA, 3 workspace split-K,
     4 cluster split-K, 5 one-CTA 128x128)
     python -m sys1rust_b200.kernel_bench attention --window 64 --tokens 16384 [--impl 1] [--reps 20]
+    python -m sys1rust_b200.kernel_bench forward --workload cfg5 [--warm 3]
 
 ``gemm`` runs one encoder GEMM with its fused epilogue (shapes as in ``gemm_sweep``); ``attention``
 runs the varlen attention over a packed batch of cfg5-distributed sequence lengths (lognormal,
@@ -108,6 +109,49 @@ def bench_attention(tokens: int, window: int, impl: int, reps: int, heads: int =
             "ms_per_call": ms, "tflops_per_call": flops / (ms / 1e3) / 1e12, "flops": flops}
 
 
+def bench_forward(workload: str, warm: int) -> dict:
+    """``warm`` untimed passes, then one pass, of a whole workload through the forward on one
+    handle and stream (load check off, no warm-up captures): ``cfg5`` the bench's 15 varlen batches of
+    one GPU's cfg5 share, ``cfg1`` one 128-token request. Every pass launches the same kernels, so
+    an ncu launch list can skip ``warm`` passes (``launches_per_pass`` each) and capture the last."""
+    from .backend import CudaBackend
+    from .batch import Varlen
+    from .config import large_model
+    from .dist import shard_for_rank
+    from .weights import SyntheticWeights
+    from .workloads import cfg1, cfg5_requests, pack_batches
+    cfg = large_model()
+    w = SyntheticWeights(cfg, seed=0)
+    be = CudaBackend.from_synthetic(cfg, w.tensors, max_tokens=16384, settings="check=0")
+    st = torch.cuda.Stream()
+    be.set_stream(st.cuda_stream)
+    if workload == "cfg1":
+        batches = [Varlen.from_rows(cfg1())]
+    else:
+        batches = pack_batches(shard_for_rank(cfg5_requests(n=1024, seed=1), 1, 0), 16384)
+    ids = [torch.from_numpy(b.ids.astype(np.int32)).cuda() for b in batches]
+    lg = torch.empty(max(max(b.n * b.kmax for b in batches), 1), device="cuda")
+    pl = torch.empty(max(b.n for b in batches) * cfg.encoder.hidden_size, device="cuda")
+    per_pass = 0
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for p in range(warm + 1):
+        if p == warm:
+            torch.cuda.synchronize()
+            e0.record(st)
+        n = 0
+        for b, i in zip(batches, ids):
+            be.forward_device_async(b, i.data_ptr(), lg.data_ptr(), pl.data_ptr())
+            n += be.last_launch_count()
+        be.synchronize()
+        per_pass = n
+    e1.record(st)
+    torch.cuda.synchronize()
+    be.close()
+    return {"kernel": "forward", "workload": workload, "batches": len(batches),
+            "tokens": int(sum(b.total for b in batches)), "launches_per_pass": per_pass, "warm": warm,
+            "ms_last_pass": e0.elapsed_time(e1)}
+
+
 def main():
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="kernel", required=True)
@@ -121,9 +165,14 @@ def main():
     a.add_argument("--window", type=int, default=64)
     a.add_argument("--impl", type=int, default=1)
     a.add_argument("--reps", type=int, default=20)
+    f = sub.add_parser("forward")
+    f.add_argument("--workload", default="cfg5", choices=["cfg5", "cfg1"])
+    f.add_argument("--warm", type=int, default=3)
     args = ap.parse_args()
     if args.kernel == "gemm":
         r = bench_gemm(args.shape, args.m, args.variant, args.reps)
+    elif args.kernel == "forward":
+        r = bench_forward(args.workload, args.warm)
     else:
         r = bench_attention(args.tokens, args.window, args.impl, args.reps)
     print(json.dumps(r))
