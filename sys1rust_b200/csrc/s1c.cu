@@ -1797,9 +1797,16 @@ std::vector<float> download(const void* d, size_t n, bool f32) {
   return out;
 }
 
+// Device buffers of one check. Uploads go through the check's stream and are waited for: the
+// handle's stream does not synchronise with the legacy default stream, and a plain cudaMemcpy from
+// pageable memory may return before its DMA has landed, so a kernel on the handle's stream could
+// otherwise read an upload that is still in flight.
 struct CheckBufs {
+  cudaStream_t st;
   std::vector<void*> p;
+  explicit CheckBufs(cudaStream_t s) : st(s) {}
   ~CheckBufs() {
+    if (st) cudaStreamSynchronize(st);
     for (void* q : p) cudaFree(q);
   }
   template <class T>
@@ -1807,8 +1814,13 @@ struct CheckBufs {
     void* q = nullptr;
     CK(cudaMalloc(&q, std::max<size_t>(v.size(), 1) * sizeof(T)));
     p.push_back(q);
-    CK(cudaMemcpy(q, v.data(), v.size() * sizeof(T), cudaMemcpyHostToDevice));
+    copy_in(q, v);
     return static_cast<T*>(q);
+  }
+  template <class T>
+  void copy_in(void* q, const std::vector<T>& v) {
+    CK(cudaMemcpyAsync(q, v.data(), v.size() * sizeof(T), cudaMemcpyHostToDevice, st));
+    CK(cudaStreamSynchronize(st));
   }
   void* alloc(size_t bytes) {
     void* q = nullptr;
@@ -1890,7 +1902,7 @@ struct GemmCheck {
 double check_gemm_kernel(const GemmCheck& g, const std::vector<std::vector<double>>& want, cudaStream_t st,
                          int variant, bool plant) {
   using G = GemmCheck;
-  CheckBufs bufs;
+  CheckBufs bufs(st);
   const uint16_t* dA = bufs.upload(g.a);
   const uint16_t* dB = bufs.upload(g.b);
   const float* dBias = bufs.upload(g.bias);
@@ -1902,7 +1914,7 @@ double check_gemm_kernel(const GemmCheck& g, const std::vector<std::vector<doubl
     const int epi = epi_of[cs], f32 = (cs == 1 || cs == 2) ? 1 : 0;
     const int act = cs == 0 ? ACT_RELU : cs == 1 ? ACT_GELU : ACT_NONE;
     const float* bp = cs <= 2 ? dBias : nullptr;
-    if (cs == 2) CK(cudaMemcpy(dOut, g.resid.data(), g.resid.size() * 4, cudaMemcpyHostToDevice));
+    if (cs == 2) bufs.copy_in(dOut, g.resid);
     const s1c_status rc = s1c_gemm(epi, dA, dB, dOut, G::M, G::N, G::K, bp, act, f32, dPos, G::THETA, G::ROPE_COLS,
                                    G::I, variant, st);
     if (rc != S1C_OK) throw S1cError(rc, "load check: GEMM launch: " + g_create_error);
@@ -1965,7 +1977,7 @@ double check_attention_kernel(const AttnCheck& a, const std::vector<double> (&wa
                               cudaStream_t st, int impl, bool plant) {
   using A = AttnCheck;
   const int n = (int)a.cu.size() - 1, T = a.cu[n];
-  CheckBufs bufs;
+  CheckBufs bufs(st);
   const uint16_t* q = bufs.upload(a.qkv);
   void* d_o = bufs.alloc((size_t)T * A::D * 2);
   double worst = 0;
@@ -2372,6 +2384,7 @@ s1c_status s1c_gemm(int32_t epi, const void* d_A, const void* d_B, void* d_out, 
       if (!d_status_dummy[dev]) {
         CK(cudaMalloc(&d_status_dummy[dev], sizeof(int)));
         CK(cudaMemset(d_status_dummy[dev], 0, sizeof(int)));
+        CK(cudaDeviceSynchronize());  // zeroed before any kernel on the caller's stream writes it
       }
       a.status = d_status_dummy[dev];
       if (epi == EPI_ROPE) {
