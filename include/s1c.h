@@ -122,9 +122,10 @@ typedef struct s1c_backend s1c_backend;
  * Buckets (the reference's `buckets` / `warm` settings, laya-mlx/src/lib.rs:89-94): a batch of n
  * rows whose packed tokens fit a bucket runs as the bucket's shape, with dummy rows (at least one,
  * row count a power of two up to 64; none when the tokens fill the bucket) holding the remaining
- * tokens and marker slots padded to a multiple of 4. The dummy rows are computed apart from the batch's rows and dropped, so a bucket's
- * CUDA graph (captured at the shape's first forward or by s1c_warmup) replays every batch of that
- * shape; larger batches run their exact shape (graph captured at its second forward).
+ * tokens, and marker slots padded to 4 (past 4 markers, to a multiple of 16). The dummy rows are
+ * computed apart from the batch's rows and dropped, so a bucket's CUDA graph (captured at the
+ * shape's first forward or by s1c_warmup) replays every batch of that shape; larger batches run
+ * their exact shape (graph captured at its second forward).
  * Load check (the reference's load-time kernel checks and fallback rule, lib.rs:319-362): every
  * kernel the forward can pick runs once on small seeded problems (GEMMs with each epilogue,
  * attention global and sliding window over ragged rows) and is compared with a double-precision
@@ -181,10 +182,13 @@ S1C_API s1c_status s1c_forward_device_async(s1c_backend* b, const s1c_varlen* in
 S1C_API s1c_status s1c_synchronize(s1c_backend* b);
 
 /* `Backend::encoder_hidden` (backend.rs:128-132; lib.rs:1869-1878): [n*len*hidden] f32 in the
- * padded layout. Real positions hold the encoder's final hidden state; padding positions are
- * never computed by the varlen path and are written as 0. This differs from the reference, whose
- * hook runs the encoder in the padded layout and so returns computed states at padding positions
- * too; the logits and pooled rows of `forward` do not depend on them. */
+ * padded layout, as the reference's hook computes it: real positions hold the encoder's final
+ * hidden state, and so do padding positions within local_attention / 2 of the row's last real
+ * token (the batch's padding id at its padded index, attending the row's real tokens; no real
+ * position attends it). Padding positions farther away are written as 0: in the reference's
+ * sliding-window layers every key they may see is masked (a softmax over -1e4 entries only), which
+ * this path does not reproduce. The logits and pooled rows of `forward` do not depend on padding
+ * positions. */
 S1C_API s1c_status s1c_encoder_hidden(s1c_backend* b, const s1c_batch* batch, float* out);
 
 /* Isolated GEMM on device pointers (the encoder GEMM sweep and kernel tests): out = epi(A B^T)
