@@ -184,8 +184,9 @@ impl Backend for CudaBackend {
         Self::check(*h, rc)
     }
 
-    /// Real positions hold the encoder's final hidden state; padding positions are 0 (the
-    /// reference computes them; `forward` does not depend on them).
+    /// Real positions hold the encoder's final hidden state, and so do padding positions within
+    /// `local_attention / 2` of the row's last real token, as the reference computes them;
+    /// padding positions farther away are 0 (`forward` does not depend on any of them).
     fn encoder_hidden(&self, b: &Batch) -> Result<Option<Vec<f32>>> {
         let h = self.h.lock().unwrap();
         let cb = Self::cbatch(b);
