@@ -194,7 +194,8 @@ S1C_API s1c_status s1c_encoder_hidden(s1c_backend* b, const s1c_batch* batch, fl
 /* Isolated GEMM on device pointers (the encoder GEMM sweep and kernel tests): out = epi(A B^T)
  * with A [M,K] and B [N,K] bf16 row-major. epi: 0 store (act 0 none / 1 ReLU / 2 GELU, bias
  * nullable, out_f32), 1 RoPE (q,k heads in columns [0, rope_cols), positions d_pos below 8192, theta),
- * 2 GeGLU (B interleaved per 128 rows, out [M, out_cols] bf16), 3 fp32 residual add in place.
+ * 2 GeGLU (B interleaved per 128 rows, out [M, out_cols] bf16), 3 fp32 residual add in place,
+ * 4 f16 residual add in place (the encoder's residual stream; bias nullable).
  * variant: 0 by shape, 1 one-CTA 128x256 tiles, 2 two-CTA 256x256 tiles (cta_group::2), 3 one-CTA with
  * the K dimension split across CTAs (fp32 partial sums reduced in a workspace, then the epilogue),
  * 4 cluster split-K (the CTAs of a thread-block cluster split K and reduce their partial tiles

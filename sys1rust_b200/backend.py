@@ -450,7 +450,7 @@ class CudaBackend:
 
 
 # -- isolated kernels (tests, GEMM sweep) ---------------------------------------------------
-EPI_STORE, EPI_ROPE, EPI_GEGLU, EPI_RESID = 0, 1, 2, 3
+EPI_STORE, EPI_ROPE, EPI_GEGLU, EPI_RESID, EPI_RESID16 = 0, 1, 2, 3, 4
 
 
 def gemm(epi: int, a_ptr: int, b_ptr: int, out_ptr: int, M: int, N: int, K: int, bias_ptr: int = 0, act: int = 0,

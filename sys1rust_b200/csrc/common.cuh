@@ -8,6 +8,7 @@
 // surfaces as S1C_ERR_DEVICE_TIMEOUT instead of a hung GPU.
 #pragma once
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -62,6 +63,13 @@ S1C_DEV uint32_t pack_bf16x2(float lo, float hi) {
 }
 S1C_DEV float bf16_lo(uint32_t v) { return __uint_as_float(v << 16); }
 S1C_DEV float bf16_hi(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
+
+// f16 helpers (the encoder's residual stream)
+S1C_DEV uint32_t pack_f16x2(float lo, float hi) {
+  __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+S1C_DEV float2 unpack_f16x2(uint32_t v) { return __half22float2(*reinterpret_cast<__half2*>(&v)); }
 
 // ---------------------------------------------------------------------------------------
 // mbarrier

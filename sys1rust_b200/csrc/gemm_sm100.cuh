@@ -29,19 +29,23 @@
 //   EPI_GEGLU  the encoder's Wi with its rows interleaved per 128 (input 128 | gate 128 per
 //              256-wide tile): out = gelu_erf(input) * gate (lib.rs:367-368, :494-510), bf16 [M, I].
 //   EPI_RESID  fp32 residual stream update: out += acc (+ bias) (lib.rs:1375-1390), one fp32 add per
-//              element performed by the TMA reduction.
+//              element performed by the TMA reduction (the head's residual streams).
+//   EPI_RESID16 the encoder's residual stream, stored f16 as the reference stores it (its f16
+//              model's `lin_add`, lib.rs:1373-1390): out += f16(acc (+ bias)), the f16 add performed
+//              by the TMA reduction; half the bytes of the fp32 stream in the Wo / Wo2 epilogues and
+//              the LayerNorms that read it.
 #pragma once
 #include <cuda.h>
 #include "common.cuh"
 
 namespace s1c {
 
-enum Epi : int { EPI_STORE = 0, EPI_ROPE = 1, EPI_GEGLU = 2, EPI_RESID = 3 };
+enum Epi : int { EPI_STORE = 0, EPI_ROPE = 1, EPI_GEGLU = 2, EPI_RESID = 3, EPI_RESID16 = 4 };
 enum Act : int { ACT_NONE = 0, ACT_RELU = 1, ACT_GELU = 2 };
 
 struct GemmArgs {
   int M, N, K;
-  const float* bias;      // [N] or null (EPI_STORE, EPI_RESID)
+  const float* bias;      // [N] or null (EPI_STORE, EPI_RESID, EPI_RESID16)
   int act;                // EPI_STORE activation
   int out_f32;            // EPI_STORE: fp32 output (the output map is fp32, 32-column boxes)
   const int* pos;         // EPI_ROPE: position of each row inside its sequence
@@ -194,6 +198,13 @@ struct Stager {
           make_uint4(pack_bf16x2(v[8 * c], v[8 * c + 1]), pack_bf16x2(v[8 * c + 2], v[8 * c + 3]),
                      pack_bf16x2(v[8 * c + 4], v[8 * c + 5]), pack_bf16x2(v[8 * c + 6], v[8 * c + 7]));
   }
+  S1C_DEV void put_f16x64(uint8_t* buf, const float* v) {
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+      *reinterpret_cast<uint4*>(buf + lane * 128 + ((c ^ (lane & 7)) << 4)) =
+          make_uint4(pack_f16x2(v[8 * c], v[8 * c + 1]), pack_f16x2(v[8 * c + 2], v[8 * c + 3]),
+                     pack_f16x2(v[8 * c + 4], v[8 * c + 5]), pack_f16x2(v[8 * c + 6], v[8 * c + 7]));
+  }
   // 16 values as bf16 into the 16-byte chunks c and c + 1 of this lane's row.
   S1C_DEV void put_bf16x16(uint8_t* buf, int c, const float* v) {
 #pragma unroll
@@ -272,8 +283,8 @@ template <int BN, int EPI>
 __device__ __forceinline__ void gemm_epilogue_tile(const GemmArgs& args, const CUtensorMap* tmC, Stager& sg,
                                                    uint32_t t, int row, bool m_ok, int y0, int n0, int n_block,
                                                    int part, int parts, const RopeRow& rr) {
-  if constexpr (EPI == EPI_RESID || EPI == EPI_STORE) {
-    const bool f32 = (EPI == EPI_RESID) || args.out_f32;
+  if constexpr (EPI == EPI_RESID || EPI == EPI_STORE || EPI == EPI_RESID16) {
+    const bool f32 = (EPI == EPI_RESID) || (EPI == EPI_STORE && args.out_f32);
     if (f32) {
       // fp32 output: 32-column units. Rows past M add (or store) zeros.
 #pragma unroll 1
@@ -301,7 +312,8 @@ __device__ __forceinline__ void gemm_epilogue_tile(const GemmArgs& args, const C
         sg.issue(tmC, buf, col, y0, EPI == EPI_RESID);
       }
     } else {
-      // bf16 output: 64-column units.
+      // 16-bit output, 64-column units: bf16 stores, or the f16 residual stream's reduce-add
+      // (rows past M add zeros).
 #pragma unroll 1
       for (int c = part * (BN / 64) / parts; c < (part + 1) * (BN / 64) / parts; ++c) {
         float v[64];
@@ -313,16 +325,24 @@ __device__ __forceinline__ void gemm_epilogue_tile(const GemmArgs& args, const C
           add_bias32(v, args.bias, col);
           if (col + 32 < args.N) add_bias32(v + 32, args.bias, col + 32);
         }
-        if (args.act == ACT_RELU) {
+        if constexpr (EPI == EPI_RESID16) {
+          if (!m_ok) {
 #pragma unroll
-          for (int j = 0; j < 64; ++j) v[j] = fmaxf(v[j], 0.0f);
-        } else if (args.act == ACT_GELU) {
+            for (int j = 0; j < 64; ++j) v[j] = 0.f;
+          }
+        } else {
+          if (args.act == ACT_RELU) {
 #pragma unroll
-          for (int j = 0; j < 64; ++j) v[j] = gelu_erf(v[j]);
+            for (int j = 0; j < 64; ++j) v[j] = fmaxf(v[j], 0.0f);
+          } else if (args.act == ACT_GELU) {
+#pragma unroll
+            for (int j = 0; j < 64; ++j) v[j] = gelu_erf(v[j]);
+          }
         }
         uint8_t* buf = sg.acquire();
-        sg.put_bf16x64(buf, v);
-        sg.issue(tmC, buf, col, y0, false);
+        if constexpr (EPI == EPI_RESID16) sg.put_f16x64(buf, v);
+        else sg.put_bf16x64(buf, v);
+        sg.issue(tmC, buf, col, y0, EPI == EPI_RESID16);
       }
     }
   } else if constexpr (EPI == EPI_ROPE) {

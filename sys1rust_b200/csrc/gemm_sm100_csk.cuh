@@ -26,8 +26,9 @@
 // Epilogues are those of the persistent kernel (gemm_sm100.cuh): EPI_STORE (bias, ReLU / GELU,
 // bf16 or fp32 out), EPI_ROPE (rotate-half RoPE of q/k heads, split_rope.metal:46-76), EPI_GEGLU
 // (gelu_erf(input) * gate, lib.rs:494-510; a 128-wide tile is 64 input rows of Wi loaded next to
-// the 64 matching gate rows, two TMA boxes of the 128 | 128 interleaved weight) and EPI_RESID
-// (fp32 residual += result, lib.rs:1375-1390; one owner per element, so one deterministic add).
+// the 64 matching gate rows, two TMA boxes of the 128 | 128 interleaved weight), EPI_RESID
+// (fp32 residual += result, lib.rs:1375-1390; one owner per element, so one deterministic add) and
+// EPI_RESID16 (the f16 residual stream: f16(residual + result), one rounding).
 //
 // Every wait is bounded (common.cuh); on a timeout a role stops issuing work, but every thread still
 // passes both cluster barrier phases, so no CTA of the cluster is left waiting.
@@ -40,9 +41,9 @@ namespace s1c {
 struct CskArgs {
   int M, N, K;
   int C;              // CTAs per cluster = K splits (1, 2 or 4); the grid is tiles * C CTAs
-  void* out;          // bf16 output, or fp32 (EPI_RESID, or EPI_STORE with out_f32)
+  void* out;          // bf16 output, fp32 (EPI_RESID, or EPI_STORE with out_f32), f16 (EPI_RESID16)
   int ldo;            // output row pitch in elements
-  const float* bias;  // EPI_STORE / EPI_RESID, optional
+  const float* bias;  // EPI_STORE / EPI_RESID / EPI_RESID16, optional
   int act;            // EPI_STORE
   int out_f32;        // EPI_STORE
   const int* pos;     // EPI_ROPE
@@ -193,6 +194,15 @@ S1C_DEV void csk_prepare(const CskArgs& args, int it, int R, int row0, int n0, i
       const float4 h0 = o[0], h1 = o[1];
       x.side[8] = h0.x; x.side[9] = h0.y; x.side[10] = h0.z; x.side[11] = h0.w;
       x.side[12] = h1.x; x.side[13] = h1.y; x.side[14] = h1.z; x.side[15] = h1.w;
+    } else if constexpr (EPI == EPI_RESID16) {
+      const uint4 u = *reinterpret_cast<const uint4*>(static_cast<const __half*>(args.out) + (size_t)x.grow * args.ldo + gcol);
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = unpack_f16x2(w[i]);
+        x.side[8 + 2 * i] = f.x;
+        x.side[9 + 2 * i] = f.y;
+      }
     }
   }
 }
@@ -230,6 +240,11 @@ S1C_DEV void csk_finish(const CskArgs& args, const float* recv, int C, uint32_t 
       float4* o = reinterpret_cast<float4*>(static_cast<float*>(args.out) + (size_t)x.grow * args.ldo + x.col);
       o[0] = make_float4(x.side[8] + v[0], x.side[9] + v[1], x.side[10] + v[2], x.side[11] + v[3]);
       o[1] = make_float4(x.side[12] + v[4], x.side[13] + v[5], x.side[14] + v[6], x.side[15] + v[7]);
+    } else if constexpr (EPI == EPI_RESID16) {
+      // f16(residual + (acc + bias)): the sum rounded once
+      *reinterpret_cast<uint4*>(static_cast<__half*>(args.out) + (size_t)x.grow * args.ldo + x.col) =
+          make_uint4(pack_f16x2(x.side[8] + v[0], x.side[9] + v[1]), pack_f16x2(x.side[10] + v[2], x.side[11] + v[3]),
+                     pack_f16x2(x.side[12] + v[4], x.side[13] + v[5]), pack_f16x2(x.side[14] + v[6], x.side[15] + v[7]));
     } else {
       if (args.act == ACT_RELU) {
 #pragma unroll

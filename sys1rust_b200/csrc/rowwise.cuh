@@ -1,11 +1,13 @@
 // Row-wise memory-bound kernels: one warp per row of d values, 16-byte vector accesses,
 // warp-shuffle reductions, two-pass (mean, then centred variance) LayerNorm statistics in fp32.
 //
-//   embed_ln      tok_emb gather + bias-free emb_norm (lib.rs:1534-1551); writes the fp32
-//                 residual stream and its bf16 copy (layer 0's attn_norm is the identity,
-//                 lib.rs:993-997, so that copy is the first Wqkv input).
-//   layernorm     fp32 rows -> LayerNorm (weight, optional bias) -> bf16 (lib.rs:630-641),
-//                 optionally through a row gather (the scorer's marker rows, lib.rs:1787-1795).
+//   embed_ln      tok_emb gather + bias-free emb_norm (lib.rs:1534-1551); writes the encoder's
+//                 residual stream (f16, the reference's storage type) and its bf16 copy (layer
+//                 0's attn_norm is the identity, lib.rs:993-997, so that copy is the first Wqkv
+//                 input).
+//   layernorm     f16 (encoder) or fp32 (head) rows -> LayerNorm (weight, optional bias) -> bf16
+//                 (lib.rs:630-641), optionally through a row gather (the scorer's marker rows,
+//                 lib.rs:1787-1795).
 //   final_to_head final_norm (lib.rs:1689), + type_emb of the row's qtype (lib.rs:1702-1708),
 //                 then the first head layer's norm1 (lib.rs:1735): one pass over the row.
 //   gather_rows   fp32 row gather (pooled rows, the pruned head layer's residual rows).
@@ -41,6 +43,34 @@ S1C_DEV void load_row_bf16(const __nv_bfloat16* src, RowVec<D>& r, int lane) {
     float* o = r.v + c * 8;
     o[0] = bf16_lo(u.x); o[1] = bf16_hi(u.x); o[2] = bf16_lo(u.y); o[3] = bf16_hi(u.y);
     o[4] = bf16_lo(u.z); o[5] = bf16_hi(u.z); o[6] = bf16_lo(u.w); o[7] = bf16_hi(u.w);
+  }
+}
+template <int D>
+S1C_DEV void load_row_f16(const __half* src, RowVec<D>& r, int lane) {
+#pragma unroll
+  for (int c = 0; c < RowVec<D>::CHUNKS; ++c) {
+    const uint4 u = *reinterpret_cast<const uint4*>(src + c * 256 + lane * 8);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+    float* o = r.v + c * 8;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = unpack_f16x2(w[i]);
+      o[2 * i] = f.x;
+      o[2 * i + 1] = f.y;
+    }
+  }
+}
+template <int D>
+S1C_DEV void load_row(const float* src, RowVec<D>& r, int lane) { load_row_f32<D>(src, r, lane); }
+template <int D>
+S1C_DEV void load_row(const __half* src, RowVec<D>& r, int lane) { load_row_f16<D>(src, r, lane); }
+template <int D>
+S1C_DEV void store_row_f16(__half* dst, const RowVec<D>& r, int lane) {
+#pragma unroll
+  for (int c = 0; c < RowVec<D>::CHUNKS; ++c) {
+    const float* o = r.v + c * 8;
+    *reinterpret_cast<uint4*>(dst + c * 256 + lane * 8) =
+        make_uint4(pack_f16x2(o[0], o[1]), pack_f16x2(o[2], o[3]), pack_f16x2(o[4], o[5]), pack_f16x2(o[6], o[7]));
   }
 }
 template <int D>
@@ -106,7 +136,7 @@ S1C_DEV void layernorm_row(RowVec<D>& r, const float* w, const float* b, float e
 
 template <int D>
 __global__ void embed_ln_kernel(const uint32_t* __restrict__ ids, int T, const __nv_bfloat16* __restrict__ tok_emb,
-                                int vocab, const float* __restrict__ w, float eps, float* __restrict__ h,
+                                int vocab, const float* __restrict__ w, float eps, __half* __restrict__ h,
                                 __nv_bfloat16* __restrict__ x, int* status) {
   pdl_trigger();
   pdl_wait();
@@ -121,7 +151,7 @@ __global__ void embed_ln_kernel(const uint32_t* __restrict__ ids, int T, const _
   RowVec<D> r;
   load_row_bf16<D>(tok_emb + (size_t)id * D, r, lane);
   layernorm_row<D>(r, w, nullptr, eps, lane);
-  store_row_f32<D>(h + (size_t)row * D, r, lane);
+  store_row_f16<D>(h + (size_t)row * D, r, lane);
   store_row_bf16<D>(x + (size_t)row * D, r, lane);
 }
 
@@ -149,8 +179,8 @@ S1C_DEV void layernorm_row_w(RowVec<D>& r, const RowVec<D>& w, const RowVec<D>& 
 // LayerNorm weight / bias are read once per warp into registers -- before the dependency wait,
 // since no kernel of the forward writes them. (Prefetching each warp's next two rows into L2 with
 // a bulk prefetch measured 4-5 % slower in the forward.)
-template <int D, bool HAS_B>
-__global__ void __launch_bounds__(256) layernorm_kernel(const float* __restrict__ in, const int* __restrict__ gather,
+template <int D, bool HAS_B, typename TIn>
+__global__ void __launch_bounds__(256) layernorm_kernel(const TIn* __restrict__ in, const int* __restrict__ gather,
                                                         int rows, const float* __restrict__ w,
                                                         const float* __restrict__ b, float eps,
                                                         __nv_bfloat16* __restrict__ out) {
@@ -165,8 +195,8 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const float* __restrict_
   for (; row + nw < rows; row += 2 * nw) {
     const int r1 = row + nw;
     RowVec<D> x0, x1;
-    load_row_f32<D>(in + (size_t)(gather ? gather[row] : row) * D, x0, lane);
-    load_row_f32<D>(in + (size_t)(gather ? gather[r1] : r1) * D, x1, lane);
+    load_row<D>(in + (size_t)(gather ? gather[row] : row) * D, x0, lane);
+    load_row<D>(in + (size_t)(gather ? gather[r1] : r1) * D, x1, lane);
     layernorm_row_w<D, HAS_B>(x0, wv, bv, eps);
     store_row_bf16<D>(out + (size_t)row * D, x0, lane);
     layernorm_row_w<D, HAS_B>(x1, wv, bv, eps);
@@ -174,14 +204,14 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const float* __restrict_
   }
   if (row < rows) {
     RowVec<D> x0;
-    load_row_f32<D>(in + (size_t)(gather ? gather[row] : row) * D, x0, lane);
+    load_row<D>(in + (size_t)(gather ? gather[row] : row) * D, x0, lane);
     layernorm_row_w<D, HAS_B>(x0, wv, bv, eps);
     store_row_bf16<D>(out + (size_t)row * D, x0, lane);
   }
 }
 
 template <int D>
-__global__ void final_to_head_kernel(const float* __restrict__ h, int T, const float* __restrict__ final_w, float eps,
+__global__ void final_to_head_kernel(const __half* __restrict__ h, int T, const float* __restrict__ final_w, float eps,
                                      float* __restrict__ hidden_out, int hidden_rows, const int* __restrict__ token_row,
                                      const uint32_t* __restrict__ qtype, const float* __restrict__ type_emb,
                                      const float* __restrict__ n1w, const float* __restrict__ n1b,
@@ -192,7 +222,7 @@ __global__ void final_to_head_kernel(const float* __restrict__ h, int T, const f
   const int lane = threadIdx.x & 31;
   if (row >= T) return;
   RowVec<D> r;
-  load_row_f32<D>(h + (size_t)row * D, r, lane);
+  load_row_f16<D>(h + (size_t)row * D, r, lane);
   layernorm_row<D>(r, final_w, nullptr, eps, lane);
   if (hidden_out && row < hidden_rows) store_row_f32<D>(hidden_out + (size_t)row * D, r, lane);
   const uint32_t qt = qtype[token_row[row]];

@@ -7,6 +7,8 @@
 //   embed_ln -> 28 x [LN, GEMM+RoPE, attention, GEMM+residual, LN, GEMM+GeGLU, GEMM+residual]
 //   -> final LN + type embedding + head norm1 -> head layers (last one pruned to the scorer's
 //   rows, lib.rs:1728-1748) -> scorer -> logits / pooled.
+// The encoder's residual stream is stored f16, as the reference's f16 model stores it (the
+// residual GEMMs add into it in place); the head's residual streams are fp32.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
@@ -95,6 +97,10 @@ float f16_bits_to_f32(uint16_t h) {
   std::memcpy(&f, &u, 4);
   return f;
 }
+uint16_t f32_to_f16_bits(float f) {
+  const __half_raw r = __float2half_rn(f);  // round to nearest even (cuda_fp16, host side)
+  return r.x;
+}
 float bf16_bits_to_f32(uint16_t b) {
   uint32_t u = (uint32_t)b << 16;
   float f;
@@ -129,9 +135,10 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
 }
 
 // 2D row-major matrix [rows, cols] (row pitch `ld` elements) tiled in boxes of box_rows x 128 bytes
-// with the 128-byte swizzle: bf16 boxes are 64 elements wide, fp32 boxes 32.
-CUtensorMap make_tmap_t(const void* ptr, bool f32, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows) {
-  const uint64_t es = f32 ? 4 : 2;
+// with the 128-byte swizzle: bf16 / f16 boxes are 64 elements wide, fp32 boxes 32.
+CUtensorMap make_tmap_dt(const void* ptr, CUtensorMapDataType dt, uint64_t rows, uint64_t cols, uint64_t ld,
+                         uint32_t box_rows) {
+  const uint64_t es = dt == CU_TENSOR_MAP_DATA_TYPE_FLOAT32 ? 4 : 2;
   if ((reinterpret_cast<uintptr_t>(ptr) & 15) || (ld * es) % 16)
     throw S1cError(S1C_ERR_ARG, "TMA operand must be 16-byte aligned with a 16-byte multiple row pitch");
   CUtensorMap m;
@@ -139,12 +146,15 @@ CUtensorMap make_tmap_t(const void* ptr, bool f32, uint64_t rows, uint64_t cols,
   cuuint64_t strides[1] = {ld * es};
   cuuint32_t box[2] = {(cuuint32_t)(128 / es), box_rows};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = get_encode_fn()(&m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
-                               const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+  CUresult r = get_encode_fn()(&m, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) throw S1cError(S1C_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
   return m;
+}
+CUtensorMap make_tmap_t(const void* ptr, bool f32, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows) {
+  return make_tmap_dt(ptr, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rows, cols, ld,
+                      box_rows);
 }
 // K-major bf16 GEMM / attention operand [rows, k], boxes of box_rows x 64 elements.
 CUtensorMap make_tmap(const void* ptr, uint64_t rows, uint64_t k, uint64_t ld, uint32_t box_rows) {
@@ -162,6 +172,10 @@ WeightMap make_wmap(const void* ptr, uint64_t rows, uint64_t k, uint64_t ld) {
 // GEMM output map: boxes of 32 rows x 128 bytes (one epilogue warp's slice).
 CUtensorMap make_out_tmap(const void* ptr, bool f32, uint64_t rows, uint64_t cols, uint64_t ld) {
   return make_tmap_t(ptr, f32, rows, cols, ld, 32);
+}
+// The same for an f16 output (the encoder's residual stream, EPI_RESID16).
+CUtensorMap make_out_tmap_f16(const void* ptr, uint64_t rows, uint64_t cols, uint64_t ld) {
+  return make_tmap_dt(ptr, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, rows, cols, ld, 32);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -212,16 +226,19 @@ void set_all_gemm_smem() {
   set_csk_smem<128, EPI_ROPE>();
   set_csk_smem<128, EPI_GEGLU>();
   set_csk_smem<128, EPI_RESID>();
+  set_csk_smem<128, EPI_RESID16>();
   set_csk_smem<64, EPI_STORE>();
   set_csk_smem<64, EPI_ROPE>();
   set_csk_smem<64, EPI_RESID>();
+  set_csk_smem<64, EPI_RESID16>();
   set_gemm_smem<EPI_STORE>();
   set_gemm_smem<EPI_ROPE>();
   set_gemm_smem<EPI_GEGLU>();
   set_gemm_smem<EPI_RESID>();
+  set_gemm_smem<EPI_RESID16>();
 }
 
-// Where a GEMM's output goes, for the split-K path: the output buffer and its row pitch (the fp32
+// Where a GEMM's output goes, for the split-K path: the output buffer and its row pitch (the
 // residual stream for residual GEMMs), and the fp32 workspace that holds one slice of partial sums
 // per split.
 struct SplitCtx {
@@ -376,8 +393,8 @@ void launch_gemm(const CUtensorMap& ta, const WeightMap& tb, const CUtensorMap& 
   CK(cudaGetLastError());
 }
 
-template <int D>
-void launch_ln(const float* in, const int* gather, int rows, const float* w, const float* b, float eps, bf16* out,
+template <int D, typename TIn>
+void launch_ln(const TIn* in, const int* gather, int rows, const float* w, const float* b, float eps, bf16* out,
                cudaStream_t st, int num_sms) {
   if (rows <= 0) return;
   // 8 warps per block, one wave of resident blocks at most (register-limited), rows spread evenly
@@ -387,10 +404,11 @@ void launch_ln(const float* in, const int* gather, int rows, const float* w, con
     CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, 256, 0));
     return std::max(n, 1);
   };
-  static const int per_sm_b = resident(layernorm_kernel<D, true>), per_sm_nb = resident(layernorm_kernel<D, false>);
+  static const int per_sm_b = resident(layernorm_kernel<D, true, TIn>),
+                   per_sm_nb = resident(layernorm_kernel<D, false, TIn>);
   const int blocks = std::max(1, std::min((rows + 7) / 8, (b ? per_sm_b : per_sm_nb) * num_sms));
-  if (b) launch_k(layernorm_kernel<D, true>, dim3(blocks), dim3(256), 0, st, in, gather, rows, w, b, eps, out);
-  else launch_k(layernorm_kernel<D, false>, dim3(blocks), dim3(256), 0, st, in, gather, rows, w, b, eps, out);
+  if (b) launch_k(layernorm_kernel<D, true, TIn>, dim3(blocks), dim3(256), 0, st, in, gather, rows, w, b, eps, out);
+  else launch_k(layernorm_kernel<D, false, TIn>, dim3(blocks), dim3(256), 0, st, in, gather, rows, w, b, eps, out);
   CK(cudaGetLastError());
 }
 
@@ -516,14 +534,14 @@ struct s1c_backend {
   std::string check_fail;    // kernels whose check gets a planted wrong expected value ('+'-separated)
   std::string check_report;  // kernels the check turned off ('+'-separated)
   int cap_T = 0, cap_R = 0;
-  DevBuf h, x, qkv, att, act;          // [cap_T, ...]
+  DevBuf h, x, qkv, att, act;          // [cap_T, ...]; h: the encoder's residual stream, f16
   DevBuf h2;                           // head residual stream [cap_T, d] fp32
   DevBuf xs, qs, atts, hs, fs, xm, sh; // scorer rows [cap_R, ...]
   CUtensorMap tm_x, tm_att, tm_act_i, tm_act_f, tm_xs, tm_atts, tm_fs, tm_xm;
   // tcgen05 attention maps: Q boxes of ATTC_BQ rows, K/V boxes of ATTC_BK rows
   CUtensorMap tm_qkv_att, tm_qkv_kv, tm_kv_att, tm_qs_att;
   // GEMM output maps (32-row boxes): bf16 qkv as [T,3d] and [T,2d], act as [T,I] and [T,F];
-  // fp32 residual streams h, h2; scorer-row buffers.
+  // residual streams h (f16) and h2 (fp32); scorer-row buffers.
   CUtensorMap to_qkv3, to_kv2, to_act_i, to_act_f, to_h, to_h2, to_qs, to_hs, to_fs, to_sh;
 
   // Metadata: a forward's small host arrays (and the token ids when they come from the host) are
@@ -701,7 +719,7 @@ void ensure_capacity(s1c_backend& B, int T, int R) {
     CK(cudaStreamSynchronize(B.stream));
     B.drop_graphs();
     const size_t wide = (size_t)std::max(B.Ipad / 2, B.F);
-    B.h.ensure((size_t)cap * B.d * 4);
+    B.h.ensure((size_t)cap * B.d * 2);
     B.h2.ensure((size_t)cap * B.d * 4);
     B.x.ensure((size_t)cap * B.d * 2);
     B.qkv.ensure((size_t)cap * 3 * B.d * 2);
@@ -722,7 +740,7 @@ void ensure_capacity(s1c_backend& B, int T, int R) {
     B.to_kv2 = make_out_tmap(B.qkv.p, false, cap, 2 * B.d, 2 * B.d);
     B.to_act_i = make_out_tmap(B.act.p, false, cap, B.I, B.I);
     B.to_act_f = make_out_tmap(B.act.p, false, cap, B.F, B.F);
-    B.to_h = make_out_tmap(B.h.p, true, cap, B.d, B.d);
+    B.to_h = make_out_tmap_f16(B.h.p, cap, B.d, B.d);
     B.to_h2 = make_out_tmap(B.h2.p, true, cap, B.d, B.d);
     B.tm_att = make_tmap(B.att.p, cap, B.d, B.d, GEMM_BM);
     B.tm_act_i = make_tmap(B.act.p, cap, B.I, B.I, GEMM_BM);
@@ -1108,7 +1126,7 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
   int64_t nl = 0;
   int* pos = B.tok.as<int>();
   int* trow = pos + B.cap_T;
-  float* h = B.h.as<float>();
+  __half* h = B.h.as<__half>();
   float* h2 = B.h2.as<float>();
   bf16* x = B.x.as<bf16>();
   bf16* qkv = B.qkv.as<bf16>();
@@ -1119,7 +1137,7 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
   launch(B, nl, "prep_tokens", 0, 8.0 * T, [&] {
     launch_k(prep_tokens_kernel, dim3((T + 255) / 256), dim3(256), 0, st, dm.cu, m.n, T, pos, trow);
   });
-  launch(B, nl, "embed_ln", 0, 8.0 * Td, [&] {
+  launch(B, nl, "embed_ln", 0, 6.0 * Td, [&] {
     launch_k(embed_ln_kernel<D>, dim3((T + 7) / 8), dim3(256), 0, st, d_ids, T, B.tok_emb, B.V, B.emb_norm, B.eps, h, x, B.d_status);
   });
 
@@ -1158,13 +1176,14 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
     a.M = M; a.N = N; a.K = K; a.status = B.d_status;
     return a;
   };
-  auto ln = [&](const char* name, const float* in, const int* gather, int rows, const float* w, const float* b,
+  auto ln = [&](const char* name, const auto* in, const int* gather, int rows, const float* w, const float* b,
                 float eps, bf16* out) {
-    launch(B, nl, name, 0, (double)rows * d * 6.0, [&] { launch_ln<D>(in, gather, rows, w, b, eps, out, st, nsm); });
+    launch(B, nl, name, 0, (double)rows * d * (sizeof(*in) + 2.0),
+           [&] { launch_ln<D>(in, gather, rows, w, b, eps, out, st, nsm); });
   };
   const double fl = 2.0 * T;  // GEMM FLOPs per (output column x reduction element)
   // Split-K contexts: the output buffer and pitch the finalize step writes (for residual GEMMs the
-  // fp32 stream it adds to).
+  // stream it adds to).
   auto sk = [&](void* out, int ldo) { return SplitCtx{B.splitk_ws.as<float>(), B.splitk_ws.bytes, out, ldo}; };
   SplitCtx sk_tmp{};
 
@@ -1186,19 +1205,19 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
          qkv + 2 * d, att, 3 * d, 3 * d, 3 * d, d, false, l.local ? B.window : -1,
          l.local ? m.pairs_local : m.pairs_global);
     GemmArgs go = gemm_args(T, d, d);
-    launch(B, nl, "gemm_wo_resid", fl * d * d, 0, [&] { launch_gemm<EPI_RESID>(B.tm_att, l.tm_wo, B.to_h, go, nsm, st, B.gemm_variant, &(sk_tmp = sk(h, d)), &nl); });
+    launch(B, nl, "gemm_wo_resid", fl * d * d, 0, [&] { launch_gemm<EPI_RESID16>(B.tm_att, l.tm_wo, B.to_h, go, nsm, st, B.gemm_variant, &(sk_tmp = sk(h, d)), &nl); });
     ln("ln_mlp", h, nullptr, T, l.mlp_norm, nullptr, B.eps, x);
     GemmArgs gi = gemm_args(T, B.Ipad, d);
     gi.out_cols = B.I;
     launch(B, nl, "gemm_wi_geglu", fl * 2 * B.I * d, 0, [&] { launch_gemm<EPI_GEGLU>(B.tm_x, l.tm_wi, B.to_act_i, gi, nsm, st, B.gemm_variant, &(sk_tmp = sk(act, B.I)), &nl); });
     GemmArgs g2 = gemm_args(T, d, B.I);
     launch(B, nl, "gemm_wo2_resid", fl * B.I * d, 0,
-           [&] { launch_gemm<EPI_RESID>(B.tm_act_i, l.tm_wo2, B.to_h, g2, nsm, st, B.gemm_variant, &(sk_tmp = sk(h, d)), &nl); });
+           [&] { launch_gemm<EPI_RESID16>(B.tm_act_i, l.tm_wo2, B.to_h, g2, nsm, st, B.gemm_variant, &(sk_tmp = sk(h, d)), &nl); });
   }
 
   if (B.trace_layers) CK(cudaEventRecord(B.layer_ev[B.L], st));
   // final_norm, + type embedding, head layer 0's norm1
-  launch(B, nl, "final_to_head", 0, Td * (4 + 4 + 2 + (d_hidden ? 4 : 0)), [&] {
+  launch(B, nl, "final_to_head", 0, Td * (2 + 4 + 2 + (d_hidden ? 4 : 0)), [&] {
     launch_k(final_to_head_kernel<D>, dim3((T + 7) / 8), dim3(256), 0, st, h, T, B.final_norm, B.eps, d_hidden, m.hidden_rows, trow, dm.qtype,
                                                          B.type_emb, B.head[0].n1w, B.head[0].n1b, h2, x);
   });
@@ -1747,7 +1766,8 @@ s1c_status guarded(s1c_backend* b, F&& f) {
 // compared with a plain computation on the host in double precision over the same bf16 inputs:
 //   * GEMMs: the one-CTA, two-CTA and cluster split-K kernels (and the workspace split-K path when
 //     `gemm=splitk` forces it), each with the bias + ReLU store, the bias + GELU fp32 store, the
-//     residual add, the RoPE and the GeGLU epilogues, at M = 300 (a partial last tile);
+//     fp32 and f16 residual adds, the RoPE and the GeGLU epilogues, at M = 300 (a partial last
+//     tile);
 //   * attention: the tcgen05 and mma.sync kernels, global and sliding window, over four ragged
 //     sequences (200, 63, 129 and 1 tokens).
 // An output passes when every element is within 1e-2 * (1 + |expected|) (bf16 output rounding is
@@ -1785,14 +1805,15 @@ double scaled_err(const std::vector<float>& got, const std::vector<double>& want
   return e;
 }
 
-std::vector<float> download(const void* d, size_t n, bool f32) {
+// Output of a check as floats: fp32, bf16 or (f16) f16 elements.
+std::vector<float> download(const void* d, size_t n, bool f32, bool f16 = false) {
   std::vector<float> out(n);
   if (f32) {
     CK(cudaMemcpy(out.data(), d, n * 4, cudaMemcpyDeviceToHost));
   } else {
     std::vector<uint16_t> raw(n);
     CK(cudaMemcpy(raw.data(), d, n * 2, cudaMemcpyDeviceToHost));
-    for (size_t i = 0; i < n; ++i) out[i] = bf16_bits_to_f32(raw[i]);
+    for (size_t i = 0; i < n; ++i) out[i] = f16 ? f16_bits_to_f32(raw[i]) : bf16_bits_to_f32(raw[i]);
   }
   return out;
 }
@@ -1837,17 +1858,20 @@ double gelu_exact(double x) { return 0.5 * x * (1.0 + std::erf(x / std::sqrt(2.0
 struct GemmCheck {
   static constexpr int M = 300, N = 768, K = 320, I = 384, ROPE_COLS = 512;
   static constexpr float THETA = 10000.0f;
-  std::vector<uint16_t> a, b;
+  std::vector<uint16_t> a, b, resid16;
   std::vector<float> bias, resid;
   std::vector<int32_t> pos;
   std::vector<double> c;
-  GemmCheck() : a((size_t)M * K), b((size_t)N * K), bias(N), resid((size_t)M * N), pos(M), c((size_t)M * N) {
+  GemmCheck()
+      : a((size_t)M * K), b((size_t)N * K), resid16((size_t)M * N), bias(N), resid((size_t)M * N), pos(M),
+        c((size_t)M * N) {
     CheckRng rng{0x5e1fc4ec0001ull};
     const float sb = 3.0f / std::sqrt((float)K);
     for (auto& x : a) x = f32_to_bf16_bits(rng.uniform());
     for (auto& x : b) x = f32_to_bf16_bits(rng.uniform() * sb);
     for (auto& x : bias) x = 0.5f * rng.uniform();
     for (auto& x : resid) x = rng.uniform();
+    for (size_t i = 0; i < resid.size(); ++i) resid16[i] = f32_to_f16_bits(resid[i]);
     for (int m = 0; m < M; ++m) pos[m] = (m * 37) % 1000;
     std::vector<double> af(a.size()), bfv(b.size());
     for (size_t i = 0; i < a.size(); ++i) af[i] = bf16_bits_to_f32(a[i]);
@@ -1863,7 +1887,7 @@ struct GemmCheck {
   }
   // Expected output of epilogue case `cs`: 0 bias + ReLU (bf16), 1 bias + GELU (fp32), 2 residual
   // + bias (fp32), 3 RoPE on the first ROPE_COLS columns (bf16), 4 GeGLU of the interleaved tiles
-  // (bf16, I columns).
+  // (bf16, I columns), 5 residual + bias on the f16 residual (f16).
   std::vector<double> want(int cs) const {
     std::vector<double> w(cs == 4 ? (size_t)M * I : (size_t)M * N);
     float inv_freq[32];
@@ -1883,6 +1907,7 @@ struct GemmCheck {
         if (cs == 0) v = std::max(v + bias[n], 0.0);
         else if (cs == 1) v = gelu_exact(v + bias[n]);
         else if (cs == 2) v = (double)resid[(size_t)m * N + n] + v + bias[n];
+        else if (cs == 5) v = (double)f16_bits_to_f32(resid16[(size_t)m * N + n]) + v + bias[n];
         else if (n < ROPE_COLS) {
           const int h0 = n / 64 * 64, i = n % 64, j = i % 32;
           const float ang = (float)pos[m] * inv_freq[j];  // the kernel's fp32 angle
@@ -1898,7 +1923,7 @@ struct GemmCheck {
 };
 
 // One GEMM kernel (s1c_gemm variant: 1 one-CTA, 2 two-CTA, 3 workspace split-K, 4 cluster split-K)
-// through the five epilogue cases; returns the largest scaled error (NaN for a non-finite output).
+// through the six epilogue cases; returns the largest scaled error (NaN for a non-finite output).
 double check_gemm_kernel(const GemmCheck& g, const std::vector<std::vector<double>>& want, cudaStream_t st,
                          int variant, bool plant) {
   using G = GemmCheck;
@@ -1909,19 +1934,20 @@ double check_gemm_kernel(const GemmCheck& g, const std::vector<std::vector<doubl
   const int32_t* dPos = bufs.upload(g.pos);
   void* dOut = bufs.alloc((size_t)G::M * G::N * 4);
   double worst = 0;
-  for (int cs = 0; cs < 5; ++cs) {
-    static const int epi_of[5] = {EPI_STORE, EPI_STORE, EPI_RESID, EPI_ROPE, EPI_GEGLU};
+  for (int cs = 0; cs < 6; ++cs) {
+    static const int epi_of[6] = {EPI_STORE, EPI_STORE, EPI_RESID, EPI_ROPE, EPI_GEGLU, EPI_RESID16};
     const int epi = epi_of[cs], f32 = (cs == 1 || cs == 2) ? 1 : 0;
     const int act = cs == 0 ? ACT_RELU : cs == 1 ? ACT_GELU : ACT_NONE;
-    const float* bp = cs <= 2 ? dBias : nullptr;
+    const float* bp = (cs <= 2 || cs == 5) ? dBias : nullptr;
     if (cs == 2) bufs.copy_in(dOut, g.resid);
+    if (cs == 5) bufs.copy_in(dOut, g.resid16);
     const s1c_status rc = s1c_gemm(epi, dA, dB, dOut, G::M, G::N, G::K, bp, act, f32, dPos, G::THETA, G::ROPE_COLS,
                                    G::I, variant, st);
     if (rc != S1C_OK) throw S1cError(rc, "load check: GEMM launch: " + g_create_error);
     CK(cudaStreamSynchronize(st));
     std::vector<double> w = want[cs];
     if (plant) w[w.size() / 2] += 1.0;
-    const double e = scaled_err(download(dOut, w.size(), f32 != 0), w);
+    const double e = scaled_err(download(dOut, w.size(), f32 != 0, cs == 5), w);
     if (std::isnan(e)) return e;
     worst = std::max(worst, e);
   }
@@ -2032,7 +2058,7 @@ void selfcheck(s1c_backend& B) {
   };
   const GemmCheck g;
   std::vector<std::vector<double>> gw;
-  for (int cs = 0; cs < 5; ++cs) gw.push_back(g.want(cs));
+  for (int cs = 0; cs < 6; ++cs) gw.push_back(g.want(cs));
   const AttnCheck ac;
   const std::vector<double> aw[2] = {ac.want(-1), ac.want(B.window)};
   auto gemm = [&](int variant, const char* k) { return check_gemm_kernel(g, gw, st, variant, planted(k)); };
@@ -2403,7 +2429,8 @@ s1c_status s1c_gemm(int32_t epi, const void* d_A, const void* d_B, void* d_out, 
     if (variant < 0 || variant > 5) throw S1cError(S1C_ERR_ARG, "variant must be 0 to 5");
     if (variant == 5 && epi == EPI_GEGLU) throw S1cError(S1C_ERR_ARG, "GeGLU tiles are 256 wide (variant 5 does not apply)");
     const WeightMap tb = make_wmap(d_B, N, K, K);
-    const CUtensorMap tc = make_out_tmap(d_out, f32, (uint64_t)M, out_w, out_w);
+    const CUtensorMap tc = epi == EPI_RESID16 ? make_out_tmap_f16(d_out, (uint64_t)M, out_w, out_w)
+                                              : make_out_tmap(d_out, f32, (uint64_t)M, out_w, out_w);
     // Split-K workspace of this entry point: one 32 MB buffer per device, kept for the process.
     static float* ws_dev[64] = {nullptr};
     {
@@ -2416,6 +2443,7 @@ s1c_status s1c_gemm(int32_t epi, const void* d_A, const void* d_B, void* d_out, 
       case EPI_ROPE: launch_gemm<EPI_ROPE>(ta, tb, tc, a, n_sms, st, variant, &sk); break;
       case EPI_GEGLU: launch_gemm<EPI_GEGLU>(ta, tb, tc, a, n_sms, st, variant, &sk); break;
       case EPI_RESID: launch_gemm<EPI_RESID>(ta, tb, tc, a, n_sms, st, variant, &sk); break;
+      case EPI_RESID16: launch_gemm<EPI_RESID16>(ta, tb, tc, a, n_sms, st, variant, &sk); break;
       default: throw S1cError(S1C_ERR_ARG, "unknown epilogue");
     }
     return S1C_OK;

@@ -12,9 +12,9 @@ struct SplitKFinal {
   const float* ws;    // [splits][rows][N] fp32 partial sums
   int splits, rows;   // slices and rows per slice
   int M, N;
-  void* out;          // output (bf16, or fp32 when out_f32)
+  void* out;          // output (bf16, or fp32 when out_f32 / EPI_RESID, f16 for EPI_RESID16)
   int ldo;            // output row pitch, elements
-  const float* bias;  // EPI_STORE
+  const float* bias;  // EPI_STORE / EPI_RESID / EPI_RESID16
   int act, out_f32;   // EPI_STORE
   const int* pos;     // EPI_ROPE
   const float* inv_freq;
@@ -89,6 +89,21 @@ __global__ void splitk_finalize_kernel(const SplitKFinal f) {
     b.z += v[6] + (bias ? bias[c + 6] : 0.f); b.w += v[7] + (bias ? bias[c + 7] : 0.f);
     dst[0] = a;
     dst[1] = b;
+  } else if constexpr (EPI == EPI_RESID16) {
+    // f16(residual + (sum + bias)): the sum rounded once
+    const int c = g * 8;
+    slice_sum8(f, r, c, v);
+    uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(f.out) + (size_t)r * f.ldo + c);
+    const uint4 u = *dst;
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 h = unpack_f16x2(w[i]);
+      o[i] = pack_f16x2(h.x + (v[2 * i] + (f.bias ? f.bias[c + 2 * i] : 0.f)),
+                        h.y + (v[2 * i + 1] + (f.bias ? f.bias[c + 2 * i + 1] : 0.f)));
+    }
+    *dst = make_uint4(o[0], o[1], o[2], o[3]);
   } else {  // EPI_STORE
     const int c = g * 8;
     slice_sum8(f, r, c, v);

@@ -1,6 +1,6 @@
 """Encoder GEMM sweep (benchmark config 4): M in {128, 512, 2048, 8192, 32768} against the three
 encoder shapes with their fused epilogues -- Wqkv (K 1024, N 3072, RoPE), Wi (K 1024, N 5248,
-GeGLU) and Wo2 (K 2624, N 1024, fp32 residual add) -- with A and B drawn N(0, 1) from a seed.
+GeGLU) and Wo2 (K 2624, N 1024, the f16 residual add of the forward) -- with A and B drawn N(0, 1) from a seed.
 
 ``python -m sys1rust_b200.gemm_sweep [--variants 1,2] [--cublas]`` prints one JSON line per
 (shape, M, variant): achieved TFLOP/s from CUDA events over repeated launches (inputs larger than
@@ -15,9 +15,9 @@ import json
 import numpy as np
 import torch
 
-from .backend import EPI_GEGLU, EPI_RESID, EPI_ROPE, gemm, interleave_wi
+from .backend import EPI_GEGLU, EPI_RESID16, EPI_ROPE, gemm, interleave_wi
 
-SHAPES = [("wqkv_rope", 1024, 3072, EPI_ROPE), ("wi_geglu", 1024, 5248, EPI_GEGLU), ("wo2_resid", 2624, 1024, EPI_RESID)]
+SHAPES = [("wqkv_rope", 1024, 3072, EPI_ROPE), ("wi_geglu", 1024, 5248, EPI_GEGLU), ("wo2_resid", 2624, 1024, EPI_RESID16)]
 MS = [128, 512, 2048, 8192, 32768]
 
 
@@ -35,7 +35,7 @@ def run(variants=(1, 2), cublas=False, reps=20, seed=0):
         else:
             b = torch.randn(N, K, generator=g).to(torch.bfloat16).cuda()
             Nk = N
-            o = torch.empty(Mmax, N, dtype=torch.float32 if epi == EPI_RESID else torch.bfloat16, device="cuda")
+            o = torch.zeros(Mmax, N, dtype=torch.float16 if epi == EPI_RESID16 else torch.bfloat16, device="cuda")
         pos = torch.from_numpy((np.arange(Mmax) % 512).astype(np.int32)).cuda()
         flops_per_row = 2.0 * K * N
         for M in MS:

@@ -23,11 +23,12 @@ import json
 import numpy as np
 import torch
 
-from .backend import EPI_RESID, attention, gemm, interleave_wi
+from .backend import EPI_RESID16, attention, gemm, interleave_wi
 from .gemm_sweep import SHAPES as SWEEP_SHAPES
 
-# The sweep's three shapes plus the attention output projection Wo (K 1024, N 1024, residual add).
-SHAPES = SWEEP_SHAPES + [("wo_resid", 1024, 1024, EPI_RESID)]
+# The sweep's three shapes plus the attention output projection Wo (K 1024, N 1024, the f16
+# residual add).
+SHAPES = SWEEP_SHAPES + [("wo_resid", 1024, 1024, EPI_RESID16)]
 
 
 def _time(fn, reps: int) -> float:
@@ -44,7 +45,7 @@ def _time(fn, reps: int) -> float:
 
 
 def bench_gemm(shape: str, M: int, variant: int, reps: int, seed: int = 0) -> dict:
-    from .backend import EPI_GEGLU, EPI_RESID
+    from .backend import EPI_GEGLU
     name, K, N, epi = next(s for s in SHAPES if s[0] == shape)
     g = torch.Generator().manual_seed(seed)
     a = torch.randn(M, K, generator=g).to(torch.bfloat16).cuda()
@@ -54,7 +55,7 @@ def bench_gemm(shape: str, M: int, variant: int, reps: int, seed: int = 0) -> di
         o = torch.empty(M, N // 2, dtype=torch.bfloat16, device="cuda")
     else:
         b = torch.randn(N, K, generator=g).to(torch.bfloat16).cuda()
-        o = torch.zeros(M, N, dtype=torch.float32 if epi == EPI_RESID else torch.bfloat16, device="cuda")
+        o = torch.zeros(M, N, dtype=torch.float16 if epi == EPI_RESID16 else torch.bfloat16, device="cuda")
     pos = torch.from_numpy((np.arange(M) % 512).astype(np.int32)).cuda()
 
     def launch():

@@ -68,6 +68,22 @@ def test_gemm_residual_in_place(cuda_lib, variant):
     assert _rel_err(h, ref) < 1e-4
 
 
+@pytest.mark.parametrize("variant", VARIANTS)
+def test_gemm_residual_f16_in_place(cuda_lib, variant):
+    """The encoder's residual stream is f16: out = f16(h + A B^T + bias), the add done by the TMA
+    reduction (one-CTA / two-CTA tiles: f16(h + f16(acc))) or once in fp32 (split-K paths). Bound:
+    two f16 roundings, 2^-10 relative to the largest output."""
+    from sys1rust_b200.backend import EPI_RESID16, gemm
+    M, N, K = 333, 1024, 2624
+    a, b = _rand((M, K), 6), _rand((N, K), 7)
+    bias = torch.randn(N, generator=torch.Generator().manual_seed(9)).float().cuda()
+    h = torch.randn(M, N, generator=torch.Generator().manual_seed(8)).half().cuda()
+    ref = h.float() + a.float() @ b.float().t() + bias
+    gemm(EPI_RESID16, a.data_ptr(), b.data_ptr(), h.data_ptr(), M, N, K, bias_ptr=bias.data_ptr(), variant=variant)
+    torch.cuda.synchronize()
+    assert _rel_err(h, ref) < 2e-3
+
+
 @pytest.mark.parametrize("M", [1, 17, 128, 200, 256])
 @pytest.mark.parametrize("N,K", [(1024, 64), (1024, 128), (1024, 1024), (3072, 1024), (1024, 2624), (256, 4096)])
 def test_cluster_split_k_shapes(cuda_lib, M, N, K):
@@ -87,6 +103,16 @@ def test_cluster_split_k_shapes(cuda_lib, M, N, K):
         torch.cuda.synchronize()
         outs.append(h)
     assert _rel_err(outs[0], h0 + a.float() @ b.float().t()) < 1e-4
+    assert torch.equal(outs[0], outs[1])
+    from sys1rust_b200.backend import EPI_RESID16
+    h16 = h0.half()
+    outs = []
+    for _ in range(2):
+        h = h16.clone()
+        gemm(EPI_RESID16, a.data_ptr(), b.data_ptr(), h.data_ptr(), M, N, K, variant=4)
+        torch.cuda.synchronize()
+        outs.append(h)
+    assert _rel_err(outs[0], h16.float() + a.float() @ b.float().t()) < 2e-3
     assert torch.equal(outs[0], outs[1])
 
 
