@@ -7,7 +7,7 @@ A step is one pass over this GPU's share of the cfg5 serving workload: 1024 requ
 (lognormal lengths, median 200, sigma 0.6, clipped to [32, 1024]; 1-10 questions each), packed
 into varlen batches of at most 16384 tokens, each batch one full forward (encoder + decision head +
 scorer). At N GPUs the job is the first N x 1024 requests of the cfg5 stream, shard-balanced by
-tokens (LPT): weak scaling, and at N = 8 exactly cfg5's 8192 requests. Ranks share nothing on the
+estimated cost (LPT over GEMM work plus the quadratic global attention): weak scaling, and at N = 8 exactly cfg5's 8192 requests. Ranks share nothing on the
 data path (replicas, no collective); the barrier and the max-over-ranks reduction are the only
 collectives. ``value`` is the whole job's tokens / max-over-ranks device time.
 
@@ -158,7 +158,7 @@ class ClockSampler:
 def arm_config(world: int, tokens_total: int, n_batches: int) -> dict:
     """The workload both arms report (the reference arm runs a bounded sample of it)."""
     return {"workload": f"cfg5 shard: {REQ_PER_GPU} lognormal requests per GPU (first "
-                        f"{REQ_PER_GPU * world} of cfg5's stream, LPT by tokens), varlen batches "
+                        f"{REQ_PER_GPU * world} of cfg5's stream, LPT by estimated cost), varlen batches "
                         f"<= {BATCH_TOKENS} tokens, full forward (encoder + head + scorer)",
             "model": "ModernBERT-large encoder (28 layers, d 1024, 16x64 heads, GeGLU 2x2624) + "
                      "2 decision-head layers + scorer, seeded N(0,0.02) bf16 weights",
