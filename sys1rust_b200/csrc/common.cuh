@@ -162,6 +162,19 @@ S1C_DEV void tma_load_2d(void* dst, const void* tmap, uint64_t* bar, int x, int 
 S1C_DEV void prefetch_tmap(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }
+// Bring [p, p + bytes) of global memory into L2 (bulk prefetch; nothing to wait for). p and bytes
+// are multiples of 16.
+S1C_DEV void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+// This CTA's share of an L2 prefetch of `bytes` at `p` spread over the grid: a 16-byte-aligned
+// slice per CTA, issued in pieces of at most 32 KB.
+S1C_DEV void prefetch_l2_share(const void* p, size_t bytes) {
+  const size_t chunk = ((bytes + gridDim.x - 1) / gridDim.x + 15) & ~(size_t)15;
+  const size_t b0 = (size_t)blockIdx.x * chunk, b1 = b0 + chunk < bytes ? b0 + chunk : bytes;
+  for (size_t o = b0; o < b1; o += 32768)
+    prefetch_l2_bulk(static_cast<const uint8_t*>(p) + o, (uint32_t)(b1 - o < 32768 ? b1 - o : 32768));
+}
 
 // ---------------------------------------------------------------------------------------
 // tcgen05: tensor memory allocation, MMA, commit, loads.

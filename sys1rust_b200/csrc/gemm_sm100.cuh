@@ -60,6 +60,8 @@ struct GemmArgs {
                           // splitk_finalize sums the slices in order and applies the epilogue
   int split_rows;         // rows of one workspace slice (M rounded up to the tile height)
   int* status;
+  const void* pf;         // cluster split-K only: the next GEMM's weights, prefetched into L2
+  size_t pf_bytes;
 };
 
 constexpr int GEMM_BM = 128;

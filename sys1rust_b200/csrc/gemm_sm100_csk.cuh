@@ -51,6 +51,10 @@ struct CskArgs {
   int rope_cols;
   int out_cols;       // EPI_GEGLU: I
   int* status;
+  // The next GEMM's weights, prefetched into L2 while this one runs (null = none); a multiple of
+  // 16 bytes at a 16-byte-aligned address.
+  const void* pf;
+  size_t pf_bytes;
 };
 
 // Largest cluster the launch plan uses. In the single-request forward (CUDA graph, weights streaming from HBM) clusters of 8 measured slower than
@@ -299,6 +303,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const int R = BM / C;  // rows owned by each CTA
   const uint32_t slot_floats = (uint32_t)(R * BN);
 
+  // The next GEMM's weights into L2 (independent of every earlier kernel, so before the dependency
+  // wait), issued by an epilogue thread that is idle until the mainloop ends.
+  if (threadIdx.x == 64 && args.pf) prefetch_l2_share(args.pf, args.pf_bytes);
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);

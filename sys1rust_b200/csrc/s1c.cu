@@ -313,6 +313,7 @@ void launch_csk(const CUtensorMap& ta, const WeightMap& tb, const GemmArgs& g, c
   a.bias = g.bias; a.act = g.act; a.out_f32 = g.out_f32;
   a.pos = g.pos; a.inv_freq = g.inv_freq; a.rope_cols = g.rope_cols; a.out_cols = g.out_cols;
   a.status = g.status;
+  a.pf = g.pf; a.pf_bytes = g.pf_bytes;
   if constexpr (EPI == EPI_GEGLU) {
     launch_csk_bn<128, EPI>(ta, tb.quarter, a, p.tiles, st);
   } else {
@@ -1200,17 +1201,27 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
     g.inv_freq = B.inv_freq[l.local ? 1 : 0];
     g.rope_tab = B.rope_tab[l.local ? 1 : 0];
     g.rope_cols = 2 * d;
+    // Each encoder GEMM names the next one's weights: the cluster split-K kernel (small batches,
+    // where every GEMM streams its weights from HBM) prefetches them into L2 while it runs.
+    g.pf = l.wo;
+    g.pf_bytes = (size_t)d * d * 2;
     launch(B, nl, "gemm_qkv_rope", fl * 3 * d * d, 0, [&] { launch_gemm<EPI_ROPE>(B.tm_x, l.tm_wqkv, B.to_qkv3, g, nsm, st, B.gemm_variant, &(sk_tmp = sk(qkv, 3 * d)), &nl); });
     attn(l.local ? "attn_local" : "attn_global", B.tm_qkv_att, B.tm_qkv_kv, 0, d, 2 * d, qkv, qkv + d,
          qkv + 2 * d, att, 3 * d, 3 * d, 3 * d, d, false, l.local ? B.window : -1,
          l.local ? m.pairs_local : m.pairs_global);
     GemmArgs go = gemm_args(T, d, d);
+    go.pf = l.wi;
+    go.pf_bytes = (size_t)B.Ipad * d * 2;
     launch(B, nl, "gemm_wo_resid", fl * d * d, 0, [&] { launch_gemm<EPI_RESID16>(B.tm_att, l.tm_wo, B.to_h, go, nsm, st, B.gemm_variant, &(sk_tmp = sk(h, d)), &nl); });
     ln("ln_mlp", h, nullptr, T, l.mlp_norm, nullptr, B.eps, x);
     GemmArgs gi = gemm_args(T, B.Ipad, d);
     gi.out_cols = B.I;
+    gi.pf = l.wo2;
+    gi.pf_bytes = (size_t)d * B.I * 2;
     launch(B, nl, "gemm_wi_geglu", fl * 2 * B.I * d, 0, [&] { launch_gemm<EPI_GEGLU>(B.tm_x, l.tm_wi, B.to_act_i, gi, nsm, st, B.gemm_variant, &(sk_tmp = sk(act, B.I)), &nl); });
     GemmArgs g2 = gemm_args(T, d, B.I);
+    g2.pf = i + 1 < B.L ? static_cast<const void*>(B.layers[i + 1].wqkv) : static_cast<const void*>(B.head[0].in_w);
+    g2.pf_bytes = (size_t)3 * d * d * 2;
     launch(B, nl, "gemm_wo2_resid", fl * B.I * d, 0,
            [&] { launch_gemm<EPI_RESID16>(B.tm_act_i, l.tm_wo2, B.to_h, g2, nsm, st, B.gemm_variant, &(sk_tmp = sk(h, d)), &nl); });
   }
