@@ -15,7 +15,7 @@
 //               tcgen05.ld of the accumulator (one row per thread), the fused math, then each
 //               warp writes its 32-row slice of a 128-byte-wide column block into a swizzled
 //               shared-memory staging buffer and one lane hands it to TMA: a tensor store for
-//               bf16 / fp32 outputs, a tensor reduce-add for the fp32 residual stream. Global
+//               bf16 / fp32 outputs, a tensor reduce-add for the residual streams. Global
 //               traffic is therefore fully coalesced whatever the row layout. Two accumulators
 //               alternate, so the epilogue of tile i overlaps the MMAs of tile i+1 (see
 //               GEMM_EPI_WARPS for what the overlap costs).
