@@ -5,17 +5,19 @@
 // a row attends the keys j of the same row, all of them (global layers, head layers) or those
 // with |i - j| <= window (local layers); softmax in fp32, output bf16.
 //
-// One CTA = one tile of up to 128 query rows x ATTC_HEADS heads, processed head after head so
-// the TMA/MMA pipeline never drains between heads; two CTAs share an SM (98 KB of shared memory
-// and 256 TMEM columns each). 192 threads:
-//   warp 0      TMA producer: Q tile [128 x 64] per head (double buffered, so the next head's Q
-//               arrives while this head runs), K and V tiles [64 keys x 64] per key step (4-stage
+// Persistent: a unit of work is one head of one tile of up to 128 query rows (unit u = item
+// u / heads, head u % heads; items sorted longest first); the grid is two CTAs per SM (98 KB of
+// shared memory and 256 TMEM columns each) and CTA b takes units b, b + grid, b + 2 grid, ...
+// back to back, so the TMA/MMA pipeline never drains between units and the last wave is one unit
+// deep, not four heads. 192 threads:
+//   warp 0      TMA producer: Q tile [128 x 64] per unit (double buffered, so the next unit's Q
+//               arrives while this one runs), K and V tiles [64 keys x 64] per key step (4-stage
 //               ring), 128-byte swizzle.
 //   warp 1      TMEM owner and MMA issuer:
 //                 S = Q K^T     M=128 N=64 K=64 (K-major A and B from shared memory)
 //                               -> TMEM cols [0,64) for even key steps, [64,128) for odd ones
 //                 O += P V      M=128 N=64 K=64 (P from TMEM, V MN-major from shared memory)
-//                               -> TMEM cols [128,192) for even heads, [192,256) for odd heads
+//                               -> TMEM cols [128,192) for even units, [192,256) for odd units
 //               The softmax writes P over the first 32 columns of its step's S buffer (bf16
 //               pairs), and S of step st + 2 is issued into the same buffer right after P V of
 //               step st: this thread's tcgen05 operations run in issue order, so P V has read P
@@ -32,15 +34,17 @@
 //               32-column halves of S that no row of a warp may see (window edges, a row's
 //               last partial key tile) are neither read nor exponentiated; keys past a row's
 //               bounds are masked only in halves where some row of the warp has a boundary.
-//               A finished head's O / l is read from TMEM and stored bf16 during the next key
-//               step, after its exponentials, by which time the head's last P V has completed.
+//               A finished unit's O / l is read from TMEM and stored bf16 during the next key
+//               step, after its exponentials, by which time the unit's last P V has completed.
 #pragma once
 #include <cuda.h>
 #include "common.cuh"
 
 namespace s1c {
 
-constexpr int ATTC_BQ = 128, ATTC_BK = 64, ATTC_THREADS = 192, ATTC_HEADS = 4, ATTC_KV_STAGES = 4;
+constexpr int ATTC_BQ = 128, ATTC_BK = 64, ATTC_THREADS = 192, ATTC_KV_STAGES = 4;
+// `attn=auto` picks this kernel when a launch has at least ATTC_HEADS units per SM.
+constexpr int ATTC_HEADS = 4;
 // TMEM columns: S (then P, bf16 pairs, over its first 32 columns) of even key steps [0,64), of odd
 // key steps [64,128); O of even heads [128,192), of odd heads [192,256)
 constexpr uint32_t ATTC_TMEM_COLS = 256;
@@ -56,11 +60,52 @@ struct AttnTcArgs {
   __nv_bfloat16* o;
   int o_stride;
   int q_col0, k_col0, v_col0;  // column of head 0 of q, k, v in their tensor maps
-  int heads;                   // total heads (block b covers heads [(b % groups) * ATTC_HEADS, ...))
+  int heads;                   // heads per item: unit u of the launch is (item u / heads, head u % heads)
   int window;                  // < 0: global
   float scale_log2;
   int* status;
+  int n_items;                 // items in the work list (the grid strides over n_items * heads units)
 };
+
+// One unit of work: one head of one item (a tile of up to 128 query rows), with its key range
+// [k_lo, k_hi) and its number of 64-key steps nt (0: an empty item, filled in to a bucket's fixed
+// work-list length, or no keys; such units are skipped by every role alike).
+struct AttcUnit {
+  int q_first, q_count, mode, h, k_lo, k_hi, nt;
+};
+S1C_DEV AttcUnit attc_unit(const AttnTcArgs& args, int u) {
+  AttcUnit w;
+  const int4 item = args.items[u / args.heads];
+  w.h = u % args.heads;
+  w.q_first = item.y;
+  w.q_count = item.z;
+  w.mode = item.w;
+  w.k_lo = w.k_hi = w.nt = 0;
+  if (w.q_count <= 0) return w;
+  const int s_begin = args.cu_seqlens[item.x], s_end = args.cu_seqlens[item.x + 1];
+  w.k_lo = s_begin;
+  w.k_hi = s_end;
+  if (args.window >= 0 && w.mode == 0) {
+    w.k_lo = max(s_begin, w.q_first - args.window);
+    w.k_hi = min(s_end, w.q_first + w.q_count + args.window);
+  }
+  w.nt = max(0, w.k_hi - w.k_lo + ATTC_BK - 1) / ATTC_BK;
+  return w;
+}
+// The next unit with work at or after u (in steps of the grid), or false.
+S1C_DEV bool attc_seek(const AttnTcArgs& args, int& u, AttcUnit& w) {
+  const int n_units = args.n_items * args.heads;
+  for (; u < n_units; u += gridDim.x) {
+    w = attc_unit(args, u);
+    if (w.nt > 0) return true;
+  }
+  return false;
+}
+// Grid of the persistent launch: two CTAs per SM, or one per unit when there are fewer units.
+inline int attc_grid(int n_items, int heads, int num_sms) {
+  const long units = (long)n_items * heads;
+  return (int)(units < 2L * num_sms ? units : 2L * num_sms);
+}
 
 // Shared-memory descriptor of a V tile used as the MN-major B operand: rows are keys (the K
 // dimension, 128 B apart, 8-row atoms of 1024 B), the 64 head dims (N) contiguous in a row.
@@ -182,21 +227,7 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int groups = (args.heads + ATTC_HEADS - 1) / ATTC_HEADS;  // block b: item b / groups
-  const int4 item = args.items[blockIdx.x / groups];
-  const int seq = item.x, q_first = item.y, q_count = item.z, mode = item.w;
-  if (q_count <= 0) return;  // an empty item (work lists filled up to a bucket's fixed length)
-  const int s_begin = args.cu_seqlens[seq], s_end = args.cu_seqlens[seq + 1];
-  const int h0 = (blockIdx.x % groups) * ATTC_HEADS;
-  const int nh = min(ATTC_HEADS, args.heads - h0);
-  const bool local = args.window >= 0 && mode == 0;
-  int k_lo = s_begin, k_hi = s_end;
-  if (local) {
-    k_lo = max(s_begin, q_first - args.window);
-    k_hi = min(s_end, q_first + q_count + args.window);
-  }
-  const int nt = max(0, k_hi - k_lo + ATTC_BK - 1) / ATTC_BK;
-  const int nsteps = nh * nt;
+  const int G = gridDim.x;  // this CTA's units: blockIdx.x, blockIdx.x + G, ...
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
@@ -230,27 +261,28 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
   pdl_wait();
 
   if (warp == 0) {
-    if (lane == 0 && nsteps > 0) {
+    if (lane == 0) {
       prefetch_tmap(&tmQ);
       prefetch_tmap(&tmKV);
-      int issued_q = 0, issued_kv = 0;
+      int issued_q = 0, issued_kv = 0;  // units (= Q loads) and key steps (= K/V stages) issued
       bool ok = true;
-      for (int hi = 0; ok && hi < nh; ++hi) {
-        const int h = h0 + hi, qb = hi & 1;
-        // Q buffer qb is free once the last S MMA of head hi - 2 has completed
-        if (!mbar_wait(&q_empty[qb], ((hi >> 1) & 1) ^ 1u, args.status, DEV_TIMEOUT_PRODUCER, abort_flag)) break;
+      AttcUnit w;
+      for (int u = blockIdx.x; ok && attc_seek(args, u, w); u += G) {
+        const int qb = issued_q & 1;
+        // Q buffer qb is free once the last S MMA of the unit two before has completed
+        if (!mbar_wait(&q_empty[qb], ((issued_q >> 1) & 1) ^ 1u, args.status, DEV_TIMEOUT_PRODUCER, abort_flag)) break;
         mbar_arrive_expect_tx(&q_full[qb], ATTC_Q_BYTES);
-        tma_load_2d(sQ + qb * ATTC_Q_BYTES, &tmQ, &q_full[qb], args.q_col0 + h * 64, q_first);
+        tma_load_2d(sQ + qb * ATTC_Q_BYTES, &tmQ, &q_full[qb], args.q_col0 + w.h * 64, w.q_first);
         ++issued_q;
-        for (int j = 0; j < nt; ++j) {
-          const int step = hi * nt + j, s = step % NS;
+        for (int j = 0; j < w.nt; ++j) {
+          const int step = issued_kv, s = step % NS;
           if (!mbar_wait(&kv_empty[s], ((step / NS) & 1) ^ 1u, args.status, DEV_TIMEOUT_PRODUCER, abort_flag)) {
             ok = false;
             break;
           }
           mbar_arrive_expect_tx(&kv_full[s], 2 * ATTC_KV_BYTES);
-          tma_load_2d(sK + s * ATTC_KV_BYTES, &tmKV, &kv_full[s], args.k_col0 + h * 64, k_lo + j * ATTC_BK);
-          tma_load_2d(sV + s * ATTC_KV_BYTES, &tmKV, &kv_full[s], args.v_col0 + h * 64, k_lo + j * ATTC_BK);
+          tma_load_2d(sK + s * ATTC_KV_BYTES, &tmKV, &kv_full[s], args.k_col0 + w.h * 64, w.k_lo + j * ATTC_BK);
+          tma_load_2d(sV + s * ATTC_KV_BYTES, &tmKV, &kv_full[s], args.v_col0 + w.h * 64, w.k_lo + j * ATTC_BK);
           ++issued_kv;
         }
       }
@@ -261,17 +293,21 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
         mbar_wait(&kv_full[i % NS], (i / NS) & 1, args.status, DEV_TIMEOUT_DRAIN, nullptr);
     }
   } else if (warp == 1) {
-    if (lane == 0 && nsteps > 0) {
+    if (lane == 0) {
       constexpr uint32_t idS = idesc_bf16_f32(128, ATTC_BK);
       constexpr uint32_t idO = idesc_bf16_f32_bmn(128, 64);
-      bool ok = true;
-      // S for step `st` into TMEM buffer st & 1: needs Q of its head and K of its stage; issued
-      // after P V of step st - 2, which read the P held in that buffer.
-      auto issue_s = [&](int st) -> bool {
-        const int hi = st / nt, j = st % nt, s = st % NS, qb = hi & 1, sb = st & 1;
-        if (j == 0 && !mbar_wait(&q_full[qb], (hi >> 1) & 1, args.status, DEV_TIMEOUT_MMA_FULL, abort_flag))
+      // S cursor: the next key step whose S is issued (unit su, its count sui among this CTA's
+      // units, key step sj of it, global step sst). S of step st goes into TMEM buffer st & 1 and
+      // is issued right after P V of step st - 2, which read the P held in that buffer.
+      int su = blockIdx.x, sui = 0, sj = 0, sst = 0;
+      AttcUnit sw;
+      bool s_more = attc_seek(args, su, sw);
+      auto issue_next_s = [&]() -> bool {
+        if (!s_more) return true;
+        const int qb = sui & 1, s = sst % NS, sb = sst & 1;
+        if (sj == 0 && !mbar_wait(&q_full[qb], (sui >> 1) & 1, args.status, DEV_TIMEOUT_MMA_FULL, abort_flag))
           return false;
-        if (!mbar_wait(&kv_full[s], (st / NS) & 1, args.status, DEV_TIMEOUT_MMA_FULL, abort_flag)) return false;
+        if (!mbar_wait(&kv_full[s], (sst / NS) & 1, args.status, DEV_TIMEOUT_MMA_FULL, abort_flag)) return false;
         tc_fence_after();
         const uint32_t qa = smem_u32(sQ + qb * ATTC_Q_BYTES), ka = smem_u32(sK + s * ATTC_KV_BYTES);
         const uint32_t tS = tmem + 64 * sb;
@@ -279,27 +315,49 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
         for (int k = 0; k < 4; ++k)
           umma_bf16(tS, sdesc_kmajor_sw128(qa + k * 32), sdesc_kmajor_sw128(ka + k * 32), idS, k ? 1u : 0u);
         umma_commit(&s_full[sb]);
-        if (j == nt - 1) umma_commit(&q_empty[qb]);  // Q of this head is no longer read
+        if (sj == sw.nt - 1) umma_commit(&q_empty[qb]);  // Q of this unit is no longer read
+        ++sst;
+        if (++sj == sw.nt) {
+          sj = 0;
+          ++sui;
+          su += G;
+          s_more = attc_seek(args, su, sw);
+        }
         return true;
       };
-      ok = issue_s(0) && (nsteps < 2 || issue_s(1));
-      for (int st = 0; ok && st < nsteps; ++st) {
-        const int hi = st / nt, j = st % nt, s = st % NS, ob = hi & 1, sb = st & 1;
-        if (!mbar_wait(&p_full[sb], (st >> 1) & 1, args.status, DEV_TIMEOUT_MMA_FULL, abort_flag)) break;
-        // the first P V of a head overwrites its O buffer: head hi - 2's O must have been read
-        if (j == 0 && hi >= 2 &&
-            !mbar_wait(&o_free[ob], ((hi >> 1) - 1) & 1, args.status, DEV_TIMEOUT_MMA_TEMPTY, abort_flag))
-          break;
-        tc_fence_after();
-        const uint32_t va = smem_u32(sV + s * ATTC_KV_BYTES), tO = tmem + ATTC_TMEM_O + 64 * ob;
-        const uint32_t tP = tmem + 64 * sb;
+      bool ok = issue_next_s() && issue_next_s();
+      int st = 0, pui = 0, pu = blockIdx.x;
+      AttcUnit pw;
+      for (bool more = ok && attc_seek(args, pu, pw); ok && more; more = attc_seek(args, pu, pw)) {
+        const int ob = pui & 1;
+        for (int j = 0; j < pw.nt; ++j, ++st) {
+          const int s = st % NS, sb = st & 1;
+          if (!mbar_wait(&p_full[sb], (st >> 1) & 1, args.status, DEV_TIMEOUT_MMA_FULL, abort_flag)) {
+            ok = false;
+            break;
+          }
+          // the first P V of a unit overwrites its O buffer: the O of the unit two before must have been read
+          if (j == 0 && pui >= 2 &&
+              !mbar_wait(&o_free[ob], ((pui >> 1) - 1) & 1, args.status, DEV_TIMEOUT_MMA_TEMPTY, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t va = smem_u32(sV + s * ATTC_KV_BYTES), tO = tmem + ATTC_TMEM_O + 64 * ob;
+          const uint32_t tP = tmem + 64 * sb;
 #pragma unroll
-        for (int k = 0; k < ATTC_BK / 16; ++k)
-          umma_bf16_ts(tO, tP + 8 * k, sdesc_mnmajor_sw128(va + k * 2048), idO, (j > 0 || k > 0) ? 1u : 0u);
-        umma_commit(&kv_empty[s]);
-        umma_commit(&p_free[sb]);
-        if (j == nt - 1) umma_commit(&o_full[ob]);
-        if (st + 2 < nsteps && !issue_s(st + 2)) break;
+          for (int k = 0; k < ATTC_BK / 16; ++k)
+            umma_bf16_ts(tO, tP + 8 * k, sdesc_mnmajor_sw128(va + k * 2048), idO, (j > 0 || k > 0) ? 1u : 0u);
+          umma_commit(&kv_empty[s]);
+          umma_commit(&p_free[sb]);
+          if (j == pw.nt - 1) umma_commit(&o_full[ob]);
+          if (!issue_next_s()) {
+            ok = false;
+            break;
+          }
+        }
+        ++pui;
+        pu += G;
       }
       umma_commit(drain);
       mbar_wait(drain, 0, args.status, DEV_TIMEOUT_DRAIN, nullptr);
@@ -308,25 +366,25 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
     const int quad = warp & 3;
     const int r = quad * 32 + lane;  // query row of this thread
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-    const int qtok = q_first + r;  // query token (mode 0)
     const float sc = args.scale_log2;
     float m_ref = -INFINITY, l = 0.f;
-    // O / l of a finished head -> bf16, row q_first + r, columns of head h0 + hd. Deferred to the
-    // next step's exponentials so that the last P V of the head has completed by then.
-    int pend = -1;
+    // O / l of a finished unit -> bf16, row pq_first + r, columns of head ph. Deferred to the next
+    // step's exponentials so that the last P V of the unit has completed by then. `hd` is the
+    // unit's count among this CTA's units (its O buffer and barrier phase).
+    int pend = -1, pq_first = 0, pq_count = 0, ph = 0;
     float l_pend = 0.f;
     auto epilogue = [&](int hd, float lsum) -> bool {
       const int ob = hd & 1;
       if (!mbar_wait_warp(&o_full[ob], (hd >> 1) & 1, args.status, DEV_TIMEOUT_EPILOGUE, abort_flag)) return false;
       tc_fence_after();
       const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
-      uint4* dst = reinterpret_cast<uint4*>(args.o + (size_t)(q_first + r) * args.o_stride + (h0 + hd) * 64);
+      uint4* dst = reinterpret_cast<uint4*>(args.o + (size_t)(pq_first + r) * args.o_stride + ph * 64);
       const uint32_t tO = tmem + lane_off + ATTC_TMEM_O + 64 * ob;
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         float t[32];
         tmem_ld32(tO + half * 32, t);
-        if (r < q_count) {
+        if (r < pq_count) {
 #pragma unroll
           for (int q = 0; q < 4; ++q)
             dst[half * 4 + q] = make_uint4(pack_bf16x2(t[8 * q] * inv, t[8 * q + 1] * inv),
@@ -341,123 +399,130 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
       return true;
     };
     bool ok = true;
-    for (int st = 0; st < nsteps; ++st) {
-      const int hi = st / nt, j = st % nt;
-      if (j == 0) {
-        m_ref = -INFINITY;
-        l = 0.f;
-      }
-      // Keys this row may see, as column offsets [lo, hi_c) inside the tile; which 32-column
-      // halves any row of this warp may see.
-      const int kt0 = k_lo + j * ATTC_BK;
-      int lo = 0, hi_c = k_hi - kt0;
-      if (local) {
-        lo = max(lo, qtok - args.window - kt0);
-        hi_c = min(hi_c, qtok + args.window + 1 - kt0);
-      }
-      const bool need0 = __any_sync(0xffffffffu, lo < 32 && hi_c > 0);
-      const bool need1 = __any_sync(0xffffffffu, lo < 64 && hi_c > 32);
-      const int sb = st & 1;
-      const uint32_t tS = tmem + lane_off + 64 * sb;
-      if (!mbar_wait_warp(&s_full[sb], (st >> 1) & 1, args.status, DEV_TIMEOUT_EPILOGUE, abort_flag)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      float s[64];
-      tmem_ld32x2(tS, need0, need1, s);
-      // Keys outside [lo, hi_c) are masked only in the halves where some row of the warp has a
-      // boundary (halves no row sees were not read and hold -inf): one bit test per column. Tiles
-      // every row of the warp sees whole (most key steps of global layers) skip all of it.
-      if (!__all_sync(0xffffffffu, lo <= 0 && hi_c >= ATTC_BK)) {
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          const int c0 = half * 32;
-          if ((half ? need1 : need0) && !__all_sync(0xffffffffu, lo <= c0 && hi_c >= c0 + 32)) {
-            const int a = min(max(lo - c0, 0), 32), b = min(max(hi_c - c0, 0), 32);
-            const uint32_t vis = (b >= 32 ? 0xffffffffu : (1u << b) - 1u) & ~(a >= 32 ? 0xffffffffu : (1u << a) - 1u);
-#pragma unroll
-            for (int c = 0; c < 32; ++c) s[c0 + c] = (vis & (1u << c)) ? s[c0 + c] : -INFINITY;
-          }
+    int st = 0, ui = 0, u = blockIdx.x;
+    AttcUnit w;
+    for (; ok && attc_seek(args, u, w); u += G, ++ui) {
+      m_ref = -INFINITY;
+      l = 0.f;
+      const bool local = args.window >= 0 && w.mode == 0;
+      const int qtok = w.q_first + r;  // query token (mode 0)
+      const int k_lo = w.k_lo, k_hi = w.k_hi, hi = ui;
+      for (int j = 0; j < w.nt; ++j, ++st) {
+        // Keys this row may see, as column offsets [lo, hi_c) inside the tile; which 32-column
+        // halves any row of this warp may see.
+        const int kt0 = k_lo + j * ATTC_BK;
+        int lo = 0, hi_c = k_hi - kt0;
+        if (local) {
+          lo = max(lo, qtok - args.window - kt0);
+          hi_c = min(hi_c, qtok + args.window + 1 - kt0);
         }
-      }
-      float pm[8];  // 8 independent partial maxima over the halves read, then a tree
-#pragma unroll
-      for (int i = 0; i < 8; ++i) pm[i] = -INFINITY;
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        if (half ? need1 : need0) {
-#pragma unroll
-          for (int c = half * 32; c < half * 32 + 32; ++c) pm[c & 7] = fmaxf(pm[c & 7], s[c]);
-        }
-      }
-      const float mx =
-          fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])), fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7]))) * sc;
-      // Raise the reference maximum only when this tile's maximum passes it by more than 2^8.
-      float factor = 1.f;
-      bool rescale_o = false;
-      if (mx > m_ref + ATTC_RESCALE_LOG2) {
-        factor = ex2f_approx(m_ref - mx);  // 0 while m_ref is -inf
-        rescale_o = l > 0.f;               // O holds earlier P V products of this head
-        l *= factor;
-        m_ref = mx;
-      }
-      const float base = (m_ref == -INFINITY) ? 0.f : m_ref;
-      float rsum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        if (half ? need1 : need0) {
-#pragma unroll
-          for (int c = half * 32; c < half * 32 + 32; ++c) {
-            s[c] = ex2f_approx(fmaf(s[c], sc, -base));
-            rsum[c & 7] += s[c];
-          }
-        } else {
-#pragma unroll
-          for (int c = half * 32; c < half * 32 + 32; ++c) s[c] = 0.f;
-        }
-      }
-      l += ((rsum[0] + rsum[1]) + (rsum[2] + rsum[3])) + ((rsum[4] + rsum[5]) + (rsum[6] + rsum[7]));
-      if (pend >= 0) {
-        if (!epilogue(pend, l_pend)) {
-          ok = false;
-          break;
-        }
-        pend = -1;
-      }
-      {
-        // P over the S it came from (S of this step is in registers; P V of step st - 2, which
-        // read the P held here before, ran ahead of the S MMA that wrote this step's S)
-        float pk[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) pk[i] = __uint_as_float(pack_bf16x2(s[2 * i], s[2 * i + 1]));
-        tmem_st32(tS, pk);
-      }
-      if (__any_sync(0xffffffffu, rescale_o)) {
-        // O is rescaled after the previous step's P V has completed
-        if (st > 0 &&
-            !mbar_wait_warp(&p_free[sb ^ 1], ((st - 1) >> 1) & 1, args.status, DEV_TIMEOUT_EPILOGUE, abort_flag)) {
+        const bool need0 = __any_sync(0xffffffffu, lo < 32 && hi_c > 0);
+        const bool need1 = __any_sync(0xffffffffu, lo < 64 && hi_c > 32);
+        const int sb = st & 1;
+        const uint32_t tS = tmem + lane_off + 64 * sb;
+        if (!mbar_wait_warp(&s_full[sb], (st >> 1) & 1, args.status, DEV_TIMEOUT_EPILOGUE, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t tO = tmem + lane_off + ATTC_TMEM_O + 64 * (hi & 1);
+        float s[64];
+        tmem_ld32x2(tS, need0, need1, s);
+        // Keys outside [lo, hi_c) are masked only in the halves where some row of the warp has a
+        // boundary (halves no row sees were not read and hold -inf): one bit test per column. Tiles
+        // every row of the warp sees whole (most key steps of global layers) skip all of it.
+        if (!__all_sync(0xffffffffu, lo <= 0 && hi_c >= ATTC_BK)) {
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            const int c0 = half * 32;
+            if ((half ? need1 : need0) && !__all_sync(0xffffffffu, lo <= c0 && hi_c >= c0 + 32)) {
+              const int a = min(max(lo - c0, 0), 32), b = min(max(hi_c - c0, 0), 32);
+              const uint32_t vis = (b >= 32 ? 0xffffffffu : (1u << b) - 1u) & ~(a >= 32 ? 0xffffffffu : (1u << a) - 1u);
+#pragma unroll
+              for (int c = 0; c < 32; ++c) s[c0 + c] = (vis & (1u << c)) ? s[c0 + c] : -INFINITY;
+            }
+          }
+        }
+        float pm[8];  // 8 independent partial maxima over the halves read, then a tree
+#pragma unroll
+        for (int i = 0; i < 8; ++i) pm[i] = -INFINITY;
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
-          float t[32];
-          tmem_ld32(tO + half * 32, t);
+          if (half ? need1 : need0) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) t[i] *= factor;
-          tmem_st32(tO + half * 32, t);
+            for (int c = half * 32; c < half * 32 + 32; ++c) pm[c & 7] = fmaxf(pm[c & 7], s[c]);
+          }
         }
-      }
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[sb]);
-      if (j == nt - 1) {
-        pend = hi;
-        l_pend = l;
+        const float mx =
+            fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])), fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7]))) * sc;
+        // Raise the reference maximum only when this tile's maximum passes it by more than 2^8.
+        float factor = 1.f;
+        bool rescale_o = false;
+        if (mx > m_ref + ATTC_RESCALE_LOG2) {
+          factor = ex2f_approx(m_ref - mx);  // 0 while m_ref is -inf
+          rescale_o = l > 0.f;               // O holds earlier P V products of this head
+          l *= factor;
+          m_ref = mx;
+        }
+        const float base = (m_ref == -INFINITY) ? 0.f : m_ref;
+        float rsum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          if (half ? need1 : need0) {
+#pragma unroll
+            for (int c = half * 32; c < half * 32 + 32; ++c) {
+              s[c] = ex2f_approx(fmaf(s[c], sc, -base));
+              rsum[c & 7] += s[c];
+            }
+          } else {
+#pragma unroll
+            for (int c = half * 32; c < half * 32 + 32; ++c) s[c] = 0.f;
+          }
+        }
+        l += ((rsum[0] + rsum[1]) + (rsum[2] + rsum[3])) + ((rsum[4] + rsum[5]) + (rsum[6] + rsum[7]));
+        if (pend >= 0) {
+          if (!epilogue(pend, l_pend)) {
+            ok = false;
+            break;
+          }
+          pend = -1;
+        }
+        {
+          // P over the S it came from (S of this step is in registers; P V of step st - 2, which
+          // read the P held here before, ran ahead of the S MMA that wrote this step's S)
+          float pk[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) pk[i] = __uint_as_float(pack_bf16x2(s[2 * i], s[2 * i + 1]));
+          tmem_st32(tS, pk);
+        }
+        if (__any_sync(0xffffffffu, rescale_o)) {
+          // O is rescaled after the previous step's P V has completed
+          if (st > 0 &&
+              !mbar_wait_warp(&p_free[sb ^ 1], ((st - 1) >> 1) & 1, args.status, DEV_TIMEOUT_EPILOGUE, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t tO = tmem + lane_off + ATTC_TMEM_O + 64 * (hi & 1);
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            float t[32];
+            tmem_ld32(tO + half * 32, t);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) t[i] *= factor;
+            tmem_st32(tO + half * 32, t);
+          }
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[sb]);
+        if (j == w.nt - 1) {
+          pend = hi;
+          l_pend = l;
+          pq_first = w.q_first;
+          pq_count = w.q_count;
+          ph = w.h;
+        }
       }
     }
     if (ok && pend >= 0) epilogue(pend, l_pend);

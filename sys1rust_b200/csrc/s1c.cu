@@ -1149,7 +1149,7 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
   auto attn = [&](const char* name, const CUtensorMap& tq, const CUtensorMap& tkv, int q_col0, int k_col0,
                   int v_col0, const bf16* q, const bf16* k, const bf16* v, bf16* o, int qs, int ks, int vs, int os,
                   bool rows, int window, double pairs) {
-    // auto: the tcgen05 kernel when its grid (query tiles of 128 x groups of ATTC_HEADS heads) fills
+    // auto: the tcgen05 kernel when its work (query tiles of 128 x heads, ATTC_HEADS per SM at least) fills
     // the SMs; below that (single short requests) the mma.sync kernel's 64-row, one-head blocks
     // spread the work wider
     const size_t tc_blocks = m.items_full_tc.size() * (size_t)((d / 64 + ATTC_HEADS - 1) / ATTC_HEADS);
@@ -1160,9 +1160,9 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
                                  : (rows ? m.items_rows.size() : m.items_full.size()));
     if (n_items == 0) return;
     if (tc) {
-      AttnTcArgs a{dm.acu, items, o, os, q_col0, k_col0, v_col0, d / 64, window, scale_log2, B.d_status};
+      AttnTcArgs a{dm.acu, items, o, os, q_col0, k_col0, v_col0, d / 64, window, scale_log2, B.d_status, n_items};
       launch(B, nl, name, 4.0 * d * pairs, 0, [&] {
-        const dim3 grid((unsigned)n_items * ((d / 64 + ATTC_HEADS - 1) / ATTC_HEADS));
+        const dim3 grid((unsigned)attc_grid(n_items, d / 64, nsm));
         launch_k(attention_tc_kernel, grid, dim3(ATTC_THREADS), ATTC_SMEM, st, tq, tkv, a);
       });
     } else {
@@ -2532,8 +2532,11 @@ s1c_status s1c_attention(const void* d_q, const void* d_k, const void* d_v, void
       CK(cudaMemsetAsync(d_status, 0, sizeof(int), st));
       const CUtensorMap tq = make_tmap(d_q, T, heads * 64, q_stride, ATTC_BQ);
       const CUtensorMap tkv = make_tmap(d_k, T, dv + heads * 64, k_stride, ATTC_BK);
-      AttnTcArgs a{d_cu, d_items, static_cast<bf16*>(d_o), o_stride, 0, 0, (int)dv, heads, window, scale_log2, d_status};
-      const dim3 grid((unsigned)items.size() * ((heads + ATTC_HEADS - 1) / ATTC_HEADS));
+      AttnTcArgs a{d_cu, d_items, static_cast<bf16*>(d_o), o_stride, 0, 0, (int)dv, heads, window, scale_log2, d_status,
+                   (int)items.size()};
+      int n_sms = 0;
+      CK(cudaDeviceGetAttribute(&n_sms, cudaDevAttrMultiProcessorCount, dev));
+      const dim3 grid((unsigned)attc_grid((int)items.size(), heads, n_sms));
       launch_k(attention_tc_kernel, grid, dim3(ATTC_THREADS), ATTC_SMEM, st, tq, tkv, a);
       cudaError_t e = cudaGetLastError();
       cudaError_t e2 = cudaStreamSynchronize(st);
