@@ -1149,12 +1149,17 @@ void run_forward(s1c_backend& B, const HostMeta& m, const DevMeta& dm, const uin
   auto attn = [&](const char* name, const CUtensorMap& tq, const CUtensorMap& tkv, int q_col0, int k_col0,
                   int v_col0, const bf16* q, const bf16* k, const bf16* v, bf16* o, int qs, int ks, int vs, int os,
                   bool rows, int window, double pairs) {
-    // auto: the tcgen05 kernel when its work (query tiles of 128 x heads, ATTC_HEADS per SM at least) fills
-    // the SMs; below that (single short requests) the mma.sync kernel's 64-row, one-head blocks
-    // spread the work wider
+    // auto: the tcgen05 kernel when its work (query tiles of 128 x heads, ATTC_HEADS per SM at least)
+    // fills the SMs, or when the batch has at least 256 tokens in rows of 128 on average (long
+    // single requests: one row of 256 / 512 / 1000 / 2000 tokens measured 1 / 2 / 10 / 14 % faster
+    // per forward); below that (short requests) the mma.sync kernel's 64-row, one-head blocks
+    // spread the work wider (one row of 128 tokens: 1.26 against 1.33 ms). The rule reads only
+    // the batch's shape (tokens, rows with dummy rows, work-list lengths), so a bucket's graph
+    // always holds the same kernel.
     const size_t tc_blocks = m.items_full_tc.size() * (size_t)((d / 64 + ATTC_HEADS - 1) / ATTC_HEADS);
+    const bool long_rows = T >= 2 * ATTC_BQ && T >= ATTC_BQ * std::max(m.n, 1);
     const bool tc = B.attn_mode == s1c_backend::ATTN_TC ||
-                    (B.attn_mode == s1c_backend::ATTN_AUTO && !rows && tc_blocks >= (size_t)nsm);
+                    (B.attn_mode == s1c_backend::ATTN_AUTO && !rows && (tc_blocks >= (size_t)nsm || long_rows));
     const int4* items = tc ? (rows ? dm.items_rows_tc : dm.items_full_tc) : (rows ? dm.items_rows : dm.items_full);
     const int n_items = (int)(tc ? (rows ? m.items_rows_tc.size() : m.items_full_tc.size())
                                  : (rows ? m.items_rows.size() : m.items_full.size()));
