@@ -459,7 +459,7 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
         bool rescale_o = false;
         if (mx > m_ref + ATTC_RESCALE_LOG2) {
           factor = ex2f_approx(m_ref - mx);  // 0 while m_ref is -inf
-          rescale_o = l > 0.f;               // O holds earlier P V products of this head
+          rescale_o = l > 0.f;               // O holds earlier P V products of this unit
           l *= factor;
           m_ref = mx;
         }
