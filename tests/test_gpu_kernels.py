@@ -196,6 +196,26 @@ def test_attention_varlen_matches_torch(cuda_lib, window, impl):
     assert _rel_err(o, ref) < 1e-2
 
 
+@pytest.mark.parametrize("window", [-1, 64])
+def test_attention_many_units_per_cta(cuda_lib, window):
+    """The persistent tcgen05 kernel with several units per CTA: 60 sequences of 17..700 tokens
+    (~180 query tiles x 16 heads, about ten units for each of the 296 CTAs), so the Q and O
+    buffers alternate across units of different lengths and the deferred epilogue of one unit
+    runs inside the next; against torch fp32."""
+    from sys1rust_b200.backend import attention
+    heads, d = 16, 1024
+    rng = np.random.default_rng(5)
+    lens = [int(x) for x in rng.integers(17, 700, size=60)]
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    T = int(cu[-1])
+    qkv = _rand((T, 3 * d), 51)
+    o = torch.empty(T, d, dtype=torch.bfloat16, device="cuda")
+    attention(qkv.data_ptr(), qkv[:, d:].data_ptr(), qkv[:, 2 * d:].data_ptr(), o.data_ptr(), 3 * d, 3 * d, 3 * d, d,
+              heads, cu, window, 0.125, impl=0)
+    ref = _attn_ref(qkv[:, :d], qkv[:, d:2 * d], qkv[:, 2 * d:], cu, window, 0.125, heads)
+    assert _rel_err(o, ref) < 1e-2
+
+
 @pytest.mark.parametrize("impl", [1, 0])
 @pytest.mark.parametrize("window", [-1, 64])
 def test_attention_growing_scores(cuda_lib, window, impl):
