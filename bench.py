@@ -373,15 +373,15 @@ def main():
     # ---- latency of one 128-token request (cfg1), host API ---------------------------------
     lat = None
     one = Varlen.from_rows(cfg1())
-    for _ in range(5):
+    for _ in range(20):
         be.forward_varlen(one)
     ts = []
-    for _ in range(50):
+    for _ in range(100):
         t = time.perf_counter()
         be.forward_varlen(one)
         ts.append((time.perf_counter() - t) * 1e3)
     lat = {"p50_ms": float(np.median(ts)), "p90_ms": float(np.percentile(ts, 90)), "n": len(ts),
-           "path": "s1c_forward_varlen, host buffers, copies included; the same request 50 times"}
+           "path": "s1c_forward_varlen, host buffers, copies included; the same request 100 times after 20"}
     # ---- latency over single requests whose shapes never repeat --------------------------
     from sys1rust_b200.latency import stream_latency
     from sys1rust_b200.workloads import latency_stream
