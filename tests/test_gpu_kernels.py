@@ -147,7 +147,7 @@ def test_gemm_rope_epilogue(cuda_lib, theta, variant):
 
 
 @pytest.mark.parametrize("variant", VARIANTS)
-@pytest.mark.parametrize("I", [2624, 384])
+@pytest.mark.parametrize("I", [2624, 2600, 384])
 def test_gemm_geglu_epilogue(cuda_lib, I, variant):
     from sys1rust_b200.backend import EPI_GEGLU, gemm, interleave_wi
     if variant == 5:
