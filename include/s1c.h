@@ -226,7 +226,8 @@ S1C_API s1c_status s1c_profile(s1c_backend* b, int32_t on);
 S1C_API size_t s1c_profile_report(const s1c_backend* b, char* buf, size_t cap);
 
 /* Split-K GEMM that allocates nothing (no counterpart in the reference). Same arguments and result
- * as s1c_gemm with variant 3, for callers that cannot allocate device memory: a serving loop that
+ * as s1c_gemm with variant 3 for epilogues 0 to 3 (epi 4, the f16 residual add, is refused with
+ * S1C_ERR_ARG), for callers that cannot allocate device memory: a serving loop that
  * must not stall in cudaMalloc / cudaFree (both can synchronise the whole device), or a host whose
  * framework owns all device memory through its own pool. The fp32 partial sums go to a fixed
  * 4 MiB array compiled into this library (held by every GPU that loads it until the process
