@@ -7,8 +7,8 @@
 //
 // Persistent: a unit of work is one head of one tile of up to 128 query rows (unit u = item
 // u / heads, head u % heads; items sorted longest first); the grid is two CTAs per SM (98 KB of
-// shared memory and 256 TMEM columns each) and CTA b takes units b, b + grid, b + 2 grid, ...
-// back to back, so the TMA/MMA pipeline never drains between units and the last wave is one unit
+// shared memory and 256 TMEM columns each) and CTA b takes one unit of every round of grid units
+// (b, then grid - 1 - b of the next round, ...) back to back, so the TMA/MMA pipeline never drains between units and the last wave is one unit
 // deep, not four heads. 192 threads:
 //   warp 0      TMA producer: Q tile [128 x 64] per unit (double buffered, so the next unit's Q
 //               arrives while this one runs), K and V tiles [64 keys x 64] per key step (4-stage
@@ -92,10 +92,15 @@ S1C_DEV AttcUnit attc_unit(const AttnTcArgs& args, int u) {
   w.nt = max(0, w.k_hi - w.k_lo + ATTC_BK - 1) / ATTC_BK;
   return w;
 }
-// The next unit with work at or after u (in steps of the grid), or false.
-S1C_DEV bool attc_seek(const AttnTcArgs& args, int& u, AttcUnit& w) {
-  const int n_units = args.n_items * args.heads;
-  for (; u < n_units; u += gridDim.x) {
+// This CTA's unit of round k is k * grid + blockIdx.x in even rounds and k * grid + (grid - 1 -
+// blockIdx.x) in odd ones: units come longest item first, so walking each round in the other
+// direction evens out the CTAs' sums (the first CTAs would otherwise take the longest unit of every
+// round). Advances k to the next round whose unit has work; false when none is left.
+S1C_DEV bool attc_seek(const AttnTcArgs& args, int& k, AttcUnit& w) {
+  const int n_units = args.n_items * args.heads, G = gridDim.x;
+  for (; k * G < n_units; ++k) {
+    const int u = k * G + ((k & 1) ? G - 1 - (int)blockIdx.x : (int)blockIdx.x);
+    if (u >= n_units) continue;
     w = attc_unit(args, u);
     if (w.nt > 0) return true;
   }
@@ -227,7 +232,6 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int G = gridDim.x;  // this CTA's units: blockIdx.x, blockIdx.x + G, ...
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
@@ -267,7 +271,7 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
       int issued_q = 0, issued_kv = 0;  // units (= Q loads) and key steps (= K/V stages) issued
       bool ok = true;
       AttcUnit w;
-      for (int u = blockIdx.x; ok && attc_seek(args, u, w); u += G) {
+      for (int k = 0; ok && attc_seek(args, k, w); ++k) {
         const int qb = issued_q & 1;
         // Q buffer qb is free once the last S MMA of the unit two before has completed
         if (!mbar_wait(&q_empty[qb], ((issued_q >> 1) & 1) ^ 1u, args.status, DEV_TIMEOUT_PRODUCER, abort_flag)) break;
@@ -299,7 +303,7 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
       // S cursor: the next key step whose S is issued (unit su, its count sui among this CTA's
       // units, key step sj of it, global step sst). S of step st goes into TMEM buffer st & 1 and
       // is issued right after P V of step st - 2, which read the P held in that buffer.
-      int su = blockIdx.x, sui = 0, sj = 0, sst = 0;
+      int su = 0, sui = 0, sj = 0, sst = 0;  // su: round
       AttcUnit sw;
       bool s_more = attc_seek(args, su, sw);
       auto issue_next_s = [&]() -> bool {
@@ -320,13 +324,13 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
         if (++sj == sw.nt) {
           sj = 0;
           ++sui;
-          su += G;
+          ++su;
           s_more = attc_seek(args, su, sw);
         }
         return true;
       };
       bool ok = issue_next_s() && issue_next_s();
-      int st = 0, pui = 0, pu = blockIdx.x;
+      int st = 0, pui = 0, pu = 0;  // pu: round
       AttcUnit pw;
       for (bool more = ok && attc_seek(args, pu, pw); ok && more; more = attc_seek(args, pu, pw)) {
         const int ob = pui & 1;
@@ -357,7 +361,7 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
           }
         }
         ++pui;
-        pu += G;
+        ++pu;
       }
       umma_commit(drain);
       mbar_wait(drain, 0, args.status, DEV_TIMEOUT_DRAIN, nullptr);
@@ -399,9 +403,9 @@ __global__ void __launch_bounds__(ATTC_THREADS, 2)
       return true;
     };
     bool ok = true;
-    int st = 0, ui = 0, u = blockIdx.x;
+    int st = 0, ui = 0, u = 0;  // u: round
     AttcUnit w;
-    for (; ok && attc_seek(args, u, w); u += G, ++ui) {
+    for (; ok && attc_seek(args, u, w); ++u, ++ui) {
       m_ref = -INFINITY;
       l = 0.f;
       const bool local = args.window >= 0 && w.mode == 0;
